@@ -1,0 +1,442 @@
+"""Benchmark of the FlashAttention-2 hot path (BASELINE.json metric):
+FA2 forward + backward TFLOPS at B=4, H=32, N=4096, D=64, causal, FP32 in and
+out, on 1..8 B200s, as a fraction of dense TF32 tensor peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--precision 3xtf32|tf32]
+
+One step = FA2 forward (O, LSE) + backward (delta, dQ, dK/dV) over this
+rank's share of the 128 (batch, head) pairs: the pairs are split into equal
+contiguous slices, one per rank, with no collective on the data path
+(total work fixed: strong scaling).  FLOPs follow benchmark/cuda_bench.py:63-69
+of the reference (fwd = 4 B H N^2 D, halved for causal; bwd = 2.5 x fwd).
+
+Printed (rank 0, one JSON line): whole-job TFLOPS from CUDA events (max over
+ranks), the same metric end to end through the torch operators with host
+buffers (pinned H2D inputs + D2H outputs inside the timed region), the
+roofline of the dominant kernel, the reference FP32 math path timed on the
+host cores (CPU baseline), SM clocks sampled during the timed region, and the
+TF32-mode run beside the default FP32-accurate (3xTF32) one.
+
+--impl reference times the reference's math path on the host CPU (torch's
+fused CPU attention kernel, forward with log-sum-exp plus autograd backward,
+all host threads) on a bounded sample of the same workload; under torchrun
+only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B_FULL, H_FULL, N, D, CAUSAL = 4, 32, 4096, 64, True
+PAIRS = B_FULL * H_FULL
+METRIC = "FA2 fwd+bwd TFLOPS (B4,H32,N4096,D64) at 1/2/4/8 B200; % of TF32 peak"
+WORKLOAD = "FA2 fwd+bwd B4 H32 N4096 D64 causal fp32 (BASELINE config 2)"
+
+
+def fa2_flops(pairs: int, n: int, d: int, causal: bool, mode: str) -> float:
+    fwd = 4.0 * pairs * n * n * d * (0.5 if causal else 1.0)
+    return {"fwd": fwd, "bwd": 2.5 * fwd, "fwd+bwd": 3.5 * fwd}[mode]
+
+
+def shard(pairs: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, stop) slice of the (batch, head) pairs for `rank`."""
+    base, extra = divmod(pairs, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return {"hbm_gbs": j.get("hbm_gbs", 6650.0), "bf16_tflops": j.get("bf16_tflops", 1590.0),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples for one GPU while a region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.tmp.flush()
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), max=float(f[2]), power=float(f[3]),
+                                 hw=f[5], hwt=f[6], swt=f[7], pcap=f[8]))
+            except ValueError:
+                continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r["power"] > 300.0] or rows
+        reasons = sorted({name for r in loaded for name, key in
+                          (("hw_slowdown", "hw"), ("hw_thermal_slowdown", "hwt"),
+                           ("sw_thermal_slowdown", "swt"), ("sw_power_cap", "pcap"))
+                          if r[key].lower() == "active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
+                "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+# ----------------------------------------------------------------- CPU side
+def cpu_reference_throughput(pairs: int, min_seconds: float, max_steps: int | None = None,
+                             threads: int | None = None) -> dict:
+    """The reference's FP32 math path on the host: torch's fused CPU attention
+    forward (with log-sum-exp) and autograd backward, one (batch, head) slice
+    of `pairs` pairs at N=4096, D=64, causal, repeated for >= min_seconds."""
+    import torch
+
+    from oracle.torch_ref import cpu_flash_fwd_bwd
+
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(123)
+    q, k, v, do = (torch.randn(1, pairs, N, D, generator=g) for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    cpu_flash_fwd_bwd(q, k, v, do, CAUSAL)  # warm-up
+    steps, t0 = 0, time.perf_counter()
+    times = []
+    while True:
+        for t in (q, k, v):
+            t.grad = None
+        s0 = time.perf_counter()
+        cpu_flash_fwd_bwd(q, k, v, do, CAUSAL)
+        times.append(time.perf_counter() - s0)
+        steps += 1
+        if time.perf_counter() - t0 >= min_seconds or (max_steps and steps >= max_steps):
+            break
+    per = statistics.median(times)
+    tflops = fa2_flops(pairs, N, D, CAUSAL, "fwd+bwd") / per / 1e12
+    return {"value": tflops, "unit": "TFLOPS", "cores": torch.get_num_threads(),
+            "seconds_per_step": per, "steps": steps,
+            "sample": f"{pairs} of 128 (b,h) pairs at N={N}, D={D}, causal, fwd+bwd, "
+                      f"torch CPU fused attention (FP32), median of {steps} steps"}
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    pairs = 8
+    res = cpu_reference_throughput(pairs, min_seconds=0.0, max_steps=args.steps + args.warmup,
+                                   threads=os.cpu_count())
+    out = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": WORKLOAD, "B": B_FULL, "H": H_FULL, "N": N, "D": D,
+                   "causal": CAUSAL, "sample_pairs": pairs},
+        "cpu_baseline": {"value": res["value"], "unit": "TFLOPS", "cores": res["cores"],
+                         "kind": "port", "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------- GPU side
+class Fa2Runner:
+    """Holds one rank's inputs/outputs in HBM and launches the kernels through
+    the C ABI (libct_b200.so) on the current stream."""
+
+    def __init__(self, pairs: int, dev, precision: int, seed: int):
+        import torch
+
+        import cuda_transformer_b200 as cb
+
+        self.cb, self.lib, self.torch = cb, cb.lib(), torch
+        self.P, self.prec, self.dev = pairs, precision, dev
+        g = torch.Generator(device=dev).manual_seed(seed)
+        shape = (1, pairs, N, D)
+        self.q, self.k, self.v, self.do = (torch.randn(shape, device=dev, generator=g) for _ in range(4))
+        self.o, self.dq, self.dk, self.dv = (torch.empty(shape, device=dev) for _ in range(4))
+        self.lse = torch.empty(1, pairs, N, device=dev)
+        self.delta = torch.empty(1, pairs, N, device=dev)
+        self.s4 = (ctypes.c_int64 * 4)(*self.q.stride())
+        self.s3 = (ctypes.c_int64 * 3)(*self.lse.stride())
+        self.launches_per_step = 4
+
+    def _p(self, t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def _st(self):
+        return ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+
+    def fwd(self):
+        p, s4 = self._p, self.s4
+        self.cb.check(self.lib.ct_fa2_fwd(p(self.q), s4, p(self.k), s4, p(self.v), s4, p(self.o),
+                                          p(self.lse), 1, self.P, N, D, int(CAUSAL), self.prec,
+                                          self._st()), "fwd")
+
+    def delta_k(self):
+        p, s4 = self._p, self.s4
+        self.cb.check(self.lib.ct_fa2_bwd_delta(p(self.o), s4, p(self.do), s4, p(self.delta), 1,
+                                                self.P, N, D, self._st()), "delta")
+
+    def dq_k(self):
+        p, s4 = self._p, self.s4
+        self.cb.check(self.lib.ct_fa2_bwd_dq(p(self.q), s4, p(self.k), s4, p(self.v), s4,
+                                             p(self.do), s4, p(self.lse), self.s3, p(self.delta),
+                                             p(self.dq), 1, self.P, N, D, int(CAUSAL), self.prec,
+                                             self._st()), "dq")
+
+    def dkdv_k(self):
+        p, s4 = self._p, self.s4
+        self.cb.check(self.lib.ct_fa2_bwd_dkdv(p(self.q), s4, p(self.k), s4, p(self.v), s4,
+                                               p(self.do), s4, p(self.lse), self.s3,
+                                               p(self.delta), p(self.dk), p(self.dv), 1, self.P,
+                                               N, D, int(CAUSAL), self.prec, self._st()), "dkdv")
+
+    def step(self):
+        self.fwd()
+        self.delta_k()
+        self.dq_k()
+        self.dkdv_k()
+
+    def kernel_times_ms(self, reps: int = 3) -> dict:
+        torch = self.torch
+        out = {}
+        for name, fn in (("fa2_fwd", self.fwd), ("fa2_bwd_delta", self.delta_k),
+                         ("fa2_bwd_dq", self.dq_k), ("fa2_bwd_dkdv", self.dkdv_k)):
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(reps)]
+            for a, b in evs:
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize()
+            out[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return out
+
+
+def timed_steps(runner, steps: int, warmup: int, dist, world: int):
+    torch = runner.torch
+    for _ in range(warmup):
+        runner.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        runner.step()
+    b.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=runner.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def e2e_steps(pairs: int, dev, precision: int, steps: int, dist, world: int, seed: int) -> dict:
+    """Same metric through the torch operators, inputs from pinned host memory
+    and outputs back to pinned host memory inside the timed region."""
+    import torch
+
+    from cuda_transformer import ops
+
+    shape = (1, pairs, N, D)
+    g = torch.Generator().manual_seed(seed)
+    host_in = [torch.randn(shape, generator=g).pin_memory() for _ in range(4)]
+    host_out = [torch.empty(shape).pin_memory() for _ in range(4)] + [torch.empty(1, pairs, N).pin_memory()]
+    dev_in = [torch.empty(shape, device=dev) for _ in range(4)]
+
+    def one():
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        q, k, v, do = dev_in
+        o, lse = ops.flash_attention_fwd_ex(q, k, v, CAUSAL, precision)
+        dq, dk, dv = ops.flash_attention_bwd_ex(q, k, v, o, do, lse, CAUSAL, precision)
+        for h, d in zip(host_out, (o, dq, dk, dv, lse)):
+            h.copy_(d, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    h2d = sum(t.numel() * 4 for t in host_in)
+    d2h = sum(t.numel() * 4 for t in host_out)
+    return {"ms": ms, "h2d": h2d * world, "d2h": d2h * world}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import cuda_transformer_b200 as cb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    s0, s1 = shard(PAIRS, world, rank)
+    pairs = s1 - s0
+    prec = cb.PRECISION_3XTF32 if args.precision == "3xtf32" else cb.PRECISION_TF32
+    alt = cb.PRECISION_TF32 if prec == cb.PRECISION_3XTF32 else cb.PRECISION_3XTF32
+
+    runner = Fa2Runner(pairs, dev, prec, seed=1000 + s0)
+    with ClockSampler(local) as clk:
+        ms = timed_steps(runner, args.steps, args.warmup, dist, world)
+    clocks = clk.summary()
+    kern = runner.kernel_times_ms()
+    assert cb.device_status(local, clear=True) == 0, "device watchdog raised during the bench"
+
+    total_flops = fa2_flops(PAIRS, N, D, CAUSAL, "fwd+bwd")
+    value = total_flops * args.steps / (ms * 1e-3) / 1e12
+
+    # alternate precision mode on the same inputs (TF32 beside 3xTF32)
+    runner.prec = alt
+    ms_alt = timed_steps(runner, max(5, args.steps // 2), 3, dist, world)
+    kern_alt = runner.kernel_times_ms()
+    runner.prec = prec
+    value_alt = total_flops * max(5, args.steps // 2) / (ms_alt * 1e-3) / 1e12
+    del runner
+    torch.cuda.empty_cache()
+
+    e2e = e2e_steps(pairs, dev, prec, max(3, args.steps // 4), dist, world, seed=2000 + s0)
+    e2e_value = total_flops * max(3, args.steps // 4) / (e2e["ms"] * 1e-3) / 1e12
+
+    pk = peaks()
+    tf32_peak = pk["bf16_tflops"] / 2.0
+    # dominant kernel and its algorithmic FLOPs per launch (this rank's pairs):
+    # fwd = 2 GEMMs, dq = 3 (S, dP, dQ), dkdv = 4 (S, dP, dV, dK), each GEMM
+    # 2 N^2 D per pair (halved for causal)
+    gemm = 2.0 * pairs * N * N * D * (0.5 if CAUSAL else 1.0)
+    algo = {"fa2_fwd": 2 * gemm, "fa2_bwd_dq": 3 * gemm, "fa2_bwd_dkdv": 4 * gemm}
+    top = max(algo, key=lambda k: kern[k])
+    achieved = algo[top] / (kern[top] * 1e-3) / 1e12
+    mult = 3.0 if prec == cb.PRECISION_3XTF32 else 1.0
+    roofline = {"bound": "tensor", "kernel": top, "achieved": achieved,
+                "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
+                "frac_of_issued_mma": achieved * mult / tf32_peak,
+                "peak_source": f"{pk['source']} bf16 burst {pk['bf16_tflops']} / 2 (dense TF32 = half BF16 rate)",
+                "traffic": None,
+                "algorithmic_flop_per_launch": algo[top], "launch_ms": kern[top]}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            r = cpu_reference_throughput(8, min_seconds=args.cpu_seconds)
+            cpu = {"value": r["value"], "unit": "TFLOPS", "cores": r["cores"], "kind": "port",
+                   "sample": r["sample"]}
+        out = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32", "precision": args.precision,
+            "frac_of_tf32_peak": value / tf32_peak,
+            "data": "synthetic: Q, K, V, dO ~ N(0,1) fp32, seeded per (b,h) slice",
+            "config": {"workload": WORKLOAD, "B": B_FULL, "H": H_FULL, "N": N, "D": D,
+                       "causal": CAUSAL, "pairs_per_rank": pairs,
+                       "sharding": "(batch, head) pairs split contiguously across ranks, no collective",
+                       "l2": "inputs larger than L2 (Q, K, V, dO = 512 MiB per step at N=1)",
+                       "parallelism": f"bh-shard{world}"},
+            "kernel_ms": kern,
+            "gpu_launches": runner_launches(args.steps),
+            "roofline": roofline,
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"]},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "alt_precision": {"precision": "tf32" if alt == cb.PRECISION_TF32 else "3xtf32",
+                              "value": value_alt, "unit": "TFLOPS",
+                              "ms_per_step": ms_alt / max(5, args.steps // 2),
+                              "frac_of_tf32_peak": value_alt / tf32_peak, "kernel_ms": kern_alt},
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def runner_launches(steps: int) -> int:
+    return 4 * steps  # fwd, delta, dq, dkdv per step
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,35 @@
+"""Linear layer autograd function (reference: cuda_autograd_fns/cuda_linear_layer.py:4-28).
+
+Forward: out = x @ W + b with W stored (in, out).  Backward: dx = dy @ W^T;
+dW is one GEMM with the (batch, seq) dimensions folded into the reduction
+(x^T @ dy over batch*seq rows) instead of a per-batch product followed by a
+torch sum; db is the bias-gradient column sum.  Zero biases are created on the
+input's device."""
+import torch
+from cuda_transformer.ops import cuda_fma, db_calculation
+
+
+class CudaLinearLayer(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weights, bias):
+        out = cuda_fma(x, weights, bias)
+        ctx.save_for_backward(x, weights, bias)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        x, weights, _ = ctx.saved_tensors
+        dy = grad_output
+        w = weights.unsqueeze(0) if weights.dim() == 2 else weights
+        dx = cuda_fma(dy, w.transpose(1, 2),
+                      torch.zeros(x.shape[-1], dtype=torch.float32, device=x.device))
+        zero_n = torch.zeros(dy.shape[-1], dtype=torch.float32, device=dy.device)
+        if weights.dim() == 2:
+            rows = x.shape[0] * x.shape[1]
+            x2 = x.reshape(1, rows, x.shape[-1])
+            dy2 = dy.reshape(1, rows, dy.shape[-1])
+            dw = cuda_fma(x2.transpose(1, 2), dy2, zero_n)[0]
+        else:
+            dw = cuda_fma(x.transpose(1, 2), dy, zero_n)
+        db = db_calculation(dy)
+        return dx, dw, db

@@ -1,0 +1,114 @@
+// ct_internal.h -- host-side declarations shared by the kernel translation
+// units and the C-ABI layer (capi.cu).  No torch types anywhere.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/ct_b200.h"
+
+namespace ct {
+
+// Per-device state, created on first use with the device current.
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t* status = nullptr;  // device address of the watchdog word
+};
+
+// Returns the state of the current device (initialising it on first use), or
+// nullptr with *err set on failure.
+const DeviceInfo* current_device(int* err);
+
+// Encodes a TMA descriptor for an FP32 tensor of rank 3 or 4 with a 32-float
+// (128-byte) inner box and CU_TENSOR_MAP_SWIZZLE_128B.  dims[0] is the
+// contiguous dimension; strides_bytes[i] is the stride of dims[i + 1].
+// Returns CT_OK or CT_ERR_UNSUPPORTED_LAYOUT when TMA cannot address it.
+int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box);
+
+// True when a float tensor with these element strides (innermost first
+// omitted) can be described by a TMA map: unit inner stride, 16-byte aligned
+// base and outer strides.
+bool tma_compatible(const void* base, int64_t inner_stride, const int64_t* outer, int n_outer);
+
+inline int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CT_OK : CT_ERR_LAUNCH_FAILED;
+}
+
+// ---------------------------------------------------------------- FA2 args
+struct Fa2Problem {
+  int64_t B, H, T, D;
+  bool causal;
+  int precision;
+};
+struct Strided4 {
+  const float* ptr;
+  int64_t s[4];  // batch, head, seq, dim (elements)
+};
+
+// Kernel launchers (one translation unit each).  All return a ct status.
+int launch_fa2_fwd_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, float* o,
+                      float* lse, const DeviceInfo& dev, cudaStream_t st);
+int launch_fa2_bwd_dq_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
+                         const float* lse, const int64_t lse_s[3], const float* delta, float* dq,
+                         const DeviceInfo& dev, cudaStream_t st);
+int launch_fa2_bwd_dkdv_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
+                           const float* lse, const int64_t lse_s[3], const float* delta,
+                           float* dk, float* dv, const DeviceInfo& dev, cudaStream_t st);
+// Whether the tensor-core kernels cover this problem (head dim / precision).
+bool fa2_fwd_tc_supported(const Fa2Problem& p);
+bool fa2_bwd_tc_supported(const Fa2Problem& p);
+
+// CUDA-core FP32 kernels: any strides, head_dim in {32, 64, 128}.
+int launch_fa2_fwd_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, float* o,
+                        float* lse, cudaStream_t st);
+int launch_fa2_bwd_dq_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
+                           const float* lse, const int64_t lse_s[3], const float* delta,
+                           float* dq, cudaStream_t st);
+int launch_fa2_bwd_dkdv_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v,
+                             Strided4 dO, const float* lse, const int64_t lse_s[3],
+                             const float* delta, float* dk, float* dv, cudaStream_t st);
+int launch_fa2_delta(const Fa2Problem& p, Strided4 o, Strided4 dO, float* delta, cudaStream_t st);
+
+// ------------------------------------------------------------- GEMM args
+struct GemmProblem {
+  int64_t batch, m, k, n;
+  const float* x;
+  int64_t xs[3];  // batch, row (m), col (k)
+  const float* w;
+  int64_t ws[3];  // batch (0 = shared), row (k), col (n)
+  const float* bias;
+  int64_t bias_s;
+  float* out;     // contiguous [batch, m, n]
+  int precision;
+};
+int launch_linear_tc(const GemmProblem& g, const DeviceInfo& dev, cudaStream_t st);
+bool linear_tc_supported(const GemmProblem& g);
+int launch_linear_simt(const GemmProblem& g, cudaStream_t st);
+
+// -------------------------------------------------------- row-wise kernels
+size_t bias_grad_workspace(int64_t rows, int64_t n);
+int launch_bias_grad(const float* dy, const int64_t s[3], float* db, int64_t batch, int64_t m,
+                     int64_t n, float* ws, cudaStream_t st);
+int launch_softmax_fwd(const float* x, float* y, int64_t rows, int64_t n, cudaStream_t st);
+int launch_softmax_bwd(const float* p, const float* dp, float* dx, int64_t rows, int64_t n,
+                       cudaStream_t st);
+int launch_gelu_fwd(const float* x, float* y, int64_t numel, cudaStream_t st);
+int launch_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, cudaStream_t st);
+int launch_layernorm_fwd(const float* x, const float* g, const float* b, float* y, float* mean,
+                         float* rstd, int64_t rows, int64_t n, float eps, cudaStream_t st);
+size_t layernorm_bwd_workspace(int64_t rows, int64_t n);
+int launch_layernorm_bwd(const float* x, const float* g, const float* mean, const float* rstd,
+                         const float* dy, float* dx, float* dg, float* db, int64_t rows,
+                         int64_t n, float* ws, cudaStream_t st);
+
+// -------------------------------------------------------------- diagnostics
+int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
+                     const DeviceInfo& dev, cudaStream_t st);
+
+}  // namespace ct

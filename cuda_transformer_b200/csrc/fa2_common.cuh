@@ -1,0 +1,148 @@
+// fa2_common.cuh -- pieces shared by the tcgen05 FlashAttention-2 kernels.
+//
+// Conventions of every FA2 tensor-core kernel here:
+//  * 128-row stationary tile per CTA (M = 128 MMAs); row r of the tile lives
+//    in TMEM lane r and is owned by thread r of the 4-warp "row" warpgroup
+//    (warps 4..7, warp w reading lanes 32*(w%4) .. +31).
+//  * Streamed tiles (K/V in the forward and dQ pass, Q/dO in the dK/dV pass)
+//    arrive by TMA into 1024-byte aligned shared memory in the 128-byte swizzle
+//    with 32-float boxes, and are read by the tensor core either K-major (the
+//    head dim is the reduction) or MN-major (the sequence is the reduction).
+//  * Precision: SPLIT == 3 stores every operand as a TF32 hi/lo pair and issues
+//    hi*hi + hi*lo + lo*hi; SPLIT == 1 issues one TF32 MMA on the raw FP32 bits.
+#pragma once
+
+#include <cmath>
+
+#include "ct_internal.h"
+#include "tc_ptx.cuh"
+
+namespace ct {
+namespace fa2 {
+
+constexpr int kRows = 128;        // stationary rows per CTA
+constexpr int kThreads = 256;     // 8 warps
+constexpr int kRowWarp0 = 4;      // first warp of the row warpgroup
+constexpr int kSplitWarp0 = 2;    // first of the two split warps
+constexpr int kSplitThreads = 64;
+constexpr float kLn2 = 0.69314718055994530942f;
+constexpr float kLog2e = 1.44269504088896340736f;
+
+struct Ptr4 {
+  const float* p;
+  int64_t s0, s1, s2, s3;
+  __device__ __forceinline__ const float* row(int64_t b, int64_t h, int64_t t) const {
+    return p + b * s0 + h * s1 + t * s2;
+  }
+};
+
+// Loads 32 consecutive head-dim values of one row (zeros when !valid).
+__device__ __forceinline__ void load_row32(const Ptr4& t, const float* rowp, int c0, bool valid,
+                                           bool vec, float (&x)[32]) {
+  if (!valid) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = 0.0f;
+    return;
+  }
+  if (vec) {
+    const float4* p4 = reinterpret_cast<const float4*>(rowp + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldg(p4 + i);
+      x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = __ldg(rowp + (int64_t)(c0 + i) * t.s3);
+  }
+}
+
+// Writes one D-wide row into TMEM columns [col, col + D) (and its TF32 low
+// part into [col + D, col + 2D) when SPLIT == 3).  Caller waits/fences.
+template <int D, int SPLIT>
+__device__ __forceinline__ void row_to_tmem(const Ptr4& t, const float* rowp, bool valid,
+                                            bool vec, uint32_t lane_base, uint32_t col) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    float x[32];
+    load_row32(t, rowp, 32 * c, valid, vec, x);
+    if constexpr (SPLIT == 3) {
+      float lo[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float h, l;
+        tf32_split(x[i], h, l);
+        x[i] = h;
+        lo[i] = l;
+      }
+      tmem_st32(lane_base + col + D + 32 * c, lo);
+    }
+    tmem_st32(lane_base + col + 32 * c, x);
+  }
+}
+
+// Stores a D-wide row of TMEM columns [col, col+D) times `scale` to a dense
+// global row.
+template <int D>
+__device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t col, float scale,
+                                                   float* dst, bool valid) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    float v[32];
+    tmem_ld32(lane_base + col + 32 * c, v);
+    if (valid) {
+      float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        d4[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
+                            v[4 * i + 3] * scale);
+    }
+  }
+}
+
+// Drain-wait used on teardown: ignores the CTA abort flag, bounded by time.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > CT_WAIT_TIMEOUT_NS) return;
+  }
+}
+
+// Warp-uniform bounded wait (all 32 lanes must call it).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                          uint32_t* status) {
+  const bool ok = mbar_wait(bar, parity, ctl, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ bool status_raised(const uint32_t* status) {
+  return *reinterpret_cast<const volatile uint32_t*>(status) != 0u;
+}
+
+}  // namespace fa2
+
+// Host helper: TMA map for an FP32 [B,H,T,D] tensor with a {32, rows} box.
+inline int make_tmap_bhtd(CUtensorMap* map, const Strided4& t, const Fa2Problem& p, int rows) {
+  const uint64_t dims[4] = {(uint64_t)p.D, (uint64_t)p.T, (uint64_t)p.H, (uint64_t)p.B};
+  const uint64_t strides[3] = {(uint64_t)t.s[2] * 4u, (uint64_t)t.s[1] * 4u, (uint64_t)t.s[0] * 4u};
+  const uint32_t box[4] = {32u, (uint32_t)rows, 1u, 1u};
+  return make_tmap_f32(map, t.ptr, 4, dims, strides, box);
+}
+
+inline bool fa2_tma_ok(const Strided4& t) {
+  return tma_compatible(t.ptr, t.s[3], t.s, 3);
+}
+
+// Enables large dynamic shared memory once per (kernel, device).
+template <typename K>
+inline int ensure_smem_attr(K kernel, size_t bytes, int device, unsigned long long* done_mask) {
+  const unsigned long long bit = 1ull << (device & 63);
+  if (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit) return CT_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+      cudaSuccess)
+    return CT_ERR_CUDA;
+  __atomic_fetch_or(done_mask, bit, __ATOMIC_RELEASE);
+  return CT_OK;
+}
+
+}  // namespace ct

@@ -1,0 +1,376 @@
+// fa2_fwd_tc.cu -- FlashAttention-2 forward on the sm_100a tensor cores.
+//
+// Computes what flash_attention_fwd_kernel computes
+// (Transformer_kernels/flash_attention.cuh:27-170): S = Q K^T / sqrt(D) with
+// the mask (!causal || q >= k) && q < T && k < T (:117), an online softmax
+// (:124-141), O = sum P V rescaled (:150), then O /= l and L = m + ln(l)
+// (:163, :167).
+//
+// Per CTA: one (batch, head) and 128 query rows.  Warp roles:
+//   warp 0      TMA producer of K/V tiles (NS-stage ring)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-3   TF32 hi/lo split of each landed K/V tile (SPLIT == 3)
+//   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
+//               epilogue (thread r <-> query row r <-> TMEM lane r)
+// TMEM columns: Q (hi[,lo]) | O | two S/P buffers (S overwritten by P hi, then
+// P lo).  S_{j+1} = Q K_{j+1}^T runs on the tensor core while the row warps
+// turn S_j into P_j.  O is rescaled only when a row maximum grows by more
+// than 2^8 (exact: l and O always share the stale maximum).
+#include "fa2_common.cuh"
+
+namespace ct {
+namespace {
+
+using namespace fa2;
+
+template <int D_, int BN_, int SPLIT_, int NS_>
+struct FwdCfg {
+  static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_;
+  static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
+  static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;  // one K or V tile
+  static constexpr uint32_t STAGE = 2u * NCOPY * TILE;
+  static constexpr uint32_t OFF_K = 0, OFF_V = NCOPY * TILE;  // lo copy at +TILE
+  static constexpr uint32_t TC_Q = 0;
+  static constexpr uint32_t TC_O = NCOPY * D;
+  static constexpr uint32_t TC_S = TC_O + D;
+  static constexpr uint32_t SBUF = NCOPY * BN;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(TC_S + 2 * SBUF <= TMEM_COLS, "TMEM budget");
+  static_assert(D % 32 == 0 && BN % 32 == 0, "tile shape");
+};
+
+template <int NS>
+struct FwdBars {
+  uint64_t full_k[NS], full_v[NS], ready_k[NS], ready_v[NS], empty_k[NS], empty_v[NS];
+  uint64_t s_full[2], p_full[2], pv_done[2], q_ready, mma_final;
+  CtaCtl ctl;
+};
+
+struct FwdParams {
+  Ptr4 q;
+  float* o;
+  float* lse;
+  int H, T, n_qt, bh_total;
+  int causal;
+  float scale_log2;  // log2(e) / sqrt(D)
+  uint32_t* status;
+};
+
+template <class C>
+constexpr size_t fwd_smem_bytes() {
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
+}
+
+template <class C>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  auto* bars = reinterpret_cast<FwdBars<NS>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(FwdBars<NS>) + 1023u) & ~1023u;
+  CtaCtl* ctl = &bars->ctl;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // Heaviest (last) query tiles first so causal work balances across waves.
+  const int qt = p.n_qt - 1 - (int)(blockIdx.x / p.bh_total);
+  const int bh = (int)(blockIdx.x % p.bh_total);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qt * kRows;
+  const int T = p.T;
+  const int last_row = min(q0 + kRows - 1, T - 1);
+  const int n_kv = p.causal ? last_row / BN + 1 : (T + BN - 1) / BN;
+
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(B(bars->full_k[s]), 1);
+      mbar_init(B(bars->full_v[s]), 1);
+      mbar_init(B(bars->ready_k[s]), kSplitThreads);
+      mbar_init(B(bars->ready_v[s]), kSplitThreads);
+      mbar_init(B(bars->empty_k[s]), 1);
+      mbar_init(B(bars->empty_v[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(B(bars->s_full[i]), 1);
+      mbar_init(B(bars->p_full[i]), 128);
+      mbar_init(B(bars->pv_done[i]), 1);
+    }
+    mbar_init(B(bars->q_ready), 128);
+    mbar_init(B(bars->mma_final), 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int last_k[NS], last_v[NS];
+      for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % NS, r = j / NS;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (r > 0 && !mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status)) break;
+        mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tma_load_4d(st + C::OFF_K + c * BN * 128, &tmK, B(bars->full_k[s]), 32 * c, j * BN, h, b);
+        last_k[s] = r;
+        if (r > 0 && !mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status)) break;
+        mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tma_load_4d(st + C::OFF_V + c * BN * 128, &tmV, B(bars->full_v[s]), 32 * c, j * BN, h, b);
+        last_v[s] = r;
+      }
+      if (ctl->abort) {  // let every issued copy land before the CTA exits
+        for (int s = 0; s < NS; ++s) {
+          if (last_k[s] >= 0) mbar_drain(B(bars->full_k[s]), last_k[s] & 1);
+          if (last_v[s] >= 0) mbar_drain(B(bars->full_v[s]), last_v[s] & 1);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      if (mbar_wait(B(bars->q_ready), 0, ctl, p.status)) {
+        tc_fence_after();
+        for (int j = 0; j <= n_kv; ++j) {
+          if (j < n_kv) {  // S_j = Q K_j^T
+            const int s = j % NS, r = j / NS, bb = j & 1;
+            const uint64_t& kb = SPLIT == 3 ? bars->ready_k[s] : bars->full_k[s];
+            if (!mbar_wait(B(kb), r & 1, ctl, p.status)) break;
+            tc_fence_after();
+            const uint32_t kt = tiles + s * C::STAGE + C::OFF_K;
+            const uint32_t dS = tmem + C::TC_S + bb * C::SBUF;
+#pragma unroll
+            for (int k = 0; k < D / 8; ++k) {
+              const uint32_t off = (k / 4) * BN * 128 + (k % 4) * 32;
+              const uint64_t bh_ = sdesc_kmajor(kt + off);
+              umma_tf32_ts(dS, tmem + C::TC_Q + 8 * k, bh_, idS, k > 0);
+              if constexpr (SPLIT == 3) {
+                umma_tf32_ts(dS, tmem + C::TC_Q + 8 * k, sdesc_kmajor(kt + C::TILE + off), idS, 1);
+                umma_tf32_ts(dS, tmem + C::TC_Q + D + 8 * k, bh_, idS, 1);
+              }
+            }
+            umma_commit(B(bars->empty_k[s]));
+            umma_commit(B(bars->s_full[bb]));
+          }
+          if (j >= 1) {  // O += P_{j-1} V_{j-1}
+            const int jj = j - 1, s = jj % NS, r = jj / NS, bb = jj & 1;
+            if (!mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status)) break;
+            const uint64_t& vb = SPLIT == 3 ? bars->ready_v[s] : bars->full_v[s];
+            if (!mbar_wait(B(vb), r & 1, ctl, p.status)) break;
+            tc_fence_after();
+            const uint32_t vt = tiles + s * C::STAGE + C::OFF_V;
+            const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
+#pragma unroll
+            for (int k = 0; k < BN / 8; ++k) {
+              const uint64_t vh = sdesc_mnmajor(vt + k * 1024, BN * 128);
+              umma_tf32_ts(tmem + C::TC_O, pA + 8 * k, vh, idO, (jj > 0 || k > 0) ? 1u : 0u);
+              if constexpr (SPLIT == 3) {
+                umma_tf32_ts(tmem + C::TC_O, pA + 8 * k,
+                             sdesc_mnmajor(vt + C::TILE + k * 1024, BN * 128), idO, 1);
+                umma_tf32_ts(tmem + C::TC_O, pA + BN + 8 * k, vh, idO, 1);
+              }
+            }
+            umma_commit(B(bars->empty_v[s]));
+            umma_commit(B(bars->pv_done[bb]));
+          }
+        }
+      }
+      umma_commit(B(bars->mma_final));  // nothing of ours in flight after this
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp < kRowWarp0) {
+    // ------------------------------------------------------- split warps
+    if constexpr (SPLIT == 3) {
+      const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % NS, r = j / NS;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (!mbar_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
+        split_tile_smem(st + C::OFF_K, st + C::OFF_K + C::TILE, C::TILE, tid, kSplitThreads);
+        fence_proxy_async_smem();
+        mbar_arrive(B(bars->ready_k[s]));
+        if (!mbar_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
+        split_tile_smem(st + C::OFF_V, st + C::OFF_V + C::TILE, C::TILE, tid, kSplitThreads);
+        fence_proxy_async_smem();
+        mbar_arrive(B(bars->ready_v[s]));
+      }
+    }
+  } else {
+    // --------------------------------------------------------- row warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int row = q0 + r;
+    const bool valid = row < T;
+    const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    {
+      const float* qrow = p.q.row(b, h, valid ? row : 0);
+      const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
+      row_to_tmem<D, SPLIT>(p.q, qrow, valid, vec, lb, C::TC_Q);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->q_ready));
+    }
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int bb = j & 1;
+      if (!(ok = warp_wait(B(bars->s_full[bb]), (j >> 1) & 1, ctl, p.status))) break;
+      tc_fence_after();
+      const uint32_t sc = lb + C::TC_S + bb * C::SBUF;
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        tmem_ld32(sc + 32 * c, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[32 * c + i] = t[i];
+      }
+      const int kv0 = j * BN;
+      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        float x = sv[i] * p.scale_log2;
+        if (need_mask) {
+          const int kv = kv0 + i;
+          if (!(kv < T && (!p.causal || kv <= row))) x = -INFINITY;
+        }
+        sv[i] = x;
+        mt = fmaxf(mt, x);
+      }
+      const float m_new = fmaxf(m_used, mt);
+      const bool resc = m_new > m_used + 8.0f;
+      if (__any_sync(0xffffffffu, resc)) {
+        const float alpha = resc ? ex2_approx(m_used - m_new) : 1.0f;
+        if (resc) m_used = m_new;
+        l *= alpha;
+        if (j > 0) {
+          const int jj = j - 1;
+          if (!(ok = warp_wait(B(bars->pv_done[jj & 1]), (jj >> 1) & 1, ctl, p.status))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            tmem_ld32(lb + C::TC_O + 32 * c, ov);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(lb + C::TC_O + 32 * c, ov);
+          }
+        }
+      }
+      float ls = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float ph[32], pl[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float pv = ex2_approx(sv[32 * c + i] - m_used);
+          ls += pv;
+          if constexpr (SPLIT == 3) tf32_split(pv, ph[i], pl[i]);
+          else ph[i] = pv;
+        }
+        tmem_st32(sc + 32 * c, ph);
+        if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, pl);
+      }
+      l += ls;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->p_full[bb]));
+    }
+    if (ok) {
+      const int jj = n_kv - 1;
+      if (warp_wait(B(bars->pv_done[jj & 1]), (jj >> 1) & 1, ctl, p.status)) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;
+        tmem_row_to_global<D>(lb, C::TC_O, inv_l, orow, valid);
+        if (valid) p.lse[(int64_t)bh * T + row] = (m_used + log2f(l)) * kLn2;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <class C>
+int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, float* lse,
+            const DeviceInfo& dev, cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap tmK, tmV;
+  int rc = make_tmap_bhtd(&tmK, k, pr, C::BN);
+  if (rc != CT_OK) return rc;
+  rc = make_tmap_bhtd(&tmV, v, pr, C::BN);
+  if (rc != CT_OK) return rc;
+  const size_t smem = fwd_smem_bytes<C>();
+  rc = ensure_smem_attr(fa2_fwd_tc_kernel<C>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  FwdParams p;
+  p.q = Ptr4{q.ptr, q.s[0], q.s[1], q.s[2], q.s[3]};
+  p.o = o;
+  p.lse = lse;
+  p.H = (int)pr.H;
+  p.T = (int)pr.T;
+  p.n_qt = (int)((pr.T + kRows - 1) / kRows);
+  p.bh_total = (int)(pr.B * pr.H);
+  p.causal = pr.causal ? 1 : 0;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
+  p.status = dev.status;
+  const int64_t grid = (int64_t)p.n_qt * p.bh_total;
+  fa2_fwd_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tmK, tmV, p);
+  return check_launch();
+}
+
+}  // namespace
+
+bool fa2_fwd_tc_supported(const Fa2Problem& p) {
+  return (p.D == 32 || p.D == 64 || p.D == 128) &&
+         (p.precision == CT_PRECISION_3XTF32 || p.precision == CT_PRECISION_TF32) &&
+         p.T < (1ll << 31) && p.B * p.H < (1ll << 31) &&
+         ((p.T + kRows - 1) / kRows) * p.B * p.H < (1ll << 31);
+}
+
+int launch_fa2_fwd_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o,
+                      float* lse, const DeviceInfo& dev, cudaStream_t st) {
+  if (!fa2_tma_ok(k) || !fa2_tma_ok(v)) return CT_ERR_UNSUPPORTED_LAYOUT;
+  const bool split = pr.precision == CT_PRECISION_3XTF32;
+  switch (pr.D) {
+    case 32:
+      return split ? run_fwd<FwdCfg<32, 64, 3, 4>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<32, 128, 1, 4>>(pr, q, k, v, o, lse, dev, st);
+    case 64:
+      return split ? run_fwd<FwdCfg<64, 64, 3, 3>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<64, 128, 1, 3>>(pr, q, k, v, o, lse, dev, st);
+    case 128:
+      return split ? run_fwd<FwdCfg<128, 32, 3, 3>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<128, 64, 1, 3>>(pr, q, k, v, o, lse, dev, st);
+    default:
+      return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+}
+
+}  // namespace ct

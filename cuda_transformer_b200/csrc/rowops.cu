@@ -1,0 +1,676 @@
+// rowops.cu -- HBM-bound row-wise kernels: softmax fwd/bwd, erf-GELU
+// fwd/bwd, LayerNorm fwd/bwd, the linear layer's bias gradient and the
+// FlashAttention-2 backward delta.  Each keeps a row resident in registers so
+// that it is read from HBM once and written once (128-bit accesses where the
+// layout allows), and every reduction over rows is a fixed-order two-stage
+// sum, so results are bit-reproducible run to run.
+#include <cfloat>
+#include <cmath>
+
+#include "ct_internal.h"
+
+namespace ct {
+namespace {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide reduction for THREADS threads; `red` holds THREADS/32 floats.
+template <int THREADS, bool IS_MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+  v = IS_MAX ? warp_max(v) : warp_sum(v);
+  if constexpr (THREADS > kWarp) {
+    const int w = threadIdx.x / kWarp, l = threadIdx.x % kWarp;
+    __syncthreads();  // protect `red` against the previous reduction
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = (l < THREADS / kWarp) ? red[l] : (IS_MAX ? -INFINITY : 0.0f);
+    v = IS_MAX ? warp_max(v) : warp_sum(v);
+  }
+  return v;
+}
+
+// A row slice owned by one thread: V slots of 4 floats.  In vector mode slot
+// j covers elements 4*(j*THREADS+tid) .. +3 (one 128-bit access); in scalar
+// mode slot j, lane q covers element (4*j+q)*THREADS+tid (coalesced scalars).
+template <int THREADS, int V, bool VEC>
+struct RowSlice {
+  float v[V][4];
+  __device__ __forceinline__ static int64_t idx(int j, int q) {
+    return VEC ? (int64_t)4 * (j * THREADS + (int)threadIdx.x) + q
+               : (int64_t)(4 * j + q) * THREADS + (int)threadIdx.x;
+  }
+  __device__ __forceinline__ void load(const float* __restrict__ p, int64_t n, float fill) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (VEC) {
+        const int64_t e = idx(j, 0);
+        if (e < n) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(p + e));
+          v[j][0] = x.x; v[j][1] = x.y; v[j][2] = x.z; v[j][3] = x.w;
+        } else {
+          v[j][0] = v[j][1] = v[j][2] = v[j][3] = fill;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int64_t e = idx(j, q);
+          v[j][q] = e < n ? __ldg(p + e) : fill;
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* __restrict__ p, int64_t n) const {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (VEC) {
+        const int64_t e = idx(j, 0);
+        if (e < n) *reinterpret_cast<float4*>(p + e) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int64_t e = idx(j, q);
+          if (e < n) p[e] = v[j][q];
+        }
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------------ softmax
+// One row per CTA (THREADS threads, up to THREADS*V*4 elements).  Follows
+// naive_softmax (Transformer_kernels/softmax.cuh:25-106): max, sum of exp,
+// then exp(x - max) * (1/sum); here the row is read once instead of three times.
+template <int THREADS, int V, bool VEC>
+__global__ void __launch_bounds__(THREADS) softmax_fwd_kernel(const float* __restrict__ x,
+                                                              float* __restrict__ y, int64_t n) {
+  __shared__ float red[THREADS / kWarp > 0 ? THREADS / kWarp : 1];
+  const int64_t row = blockIdx.x;
+  RowSlice<THREADS, V, VEC> r;
+  r.load(x + row * n, n, -INFINITY);
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) m = fmaxf(m, r.v[j][q]);
+  m = block_reduce<THREADS, true>(m, red);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float e = (r.v[j][q] == -INFINITY) ? 0.0f : expf(r.v[j][q] - m);
+      r.v[j][q] = e;
+      s += e;
+    }
+  s = block_reduce<THREADS, false>(s, red);
+  const float inv = 1.0f / s;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r.v[j][q] *= inv;
+  r.store(y + row * n, n);
+}
+
+// dx = p * (dp - sum(p * dp)), naive_softmax_bwd (Transformer_kernels/softmax.cuh:108-159).
+template <int THREADS, int V, bool VEC>
+__global__ void __launch_bounds__(THREADS) softmax_bwd_kernel(const float* __restrict__ p,
+                                                              const float* __restrict__ dp,
+                                                              float* __restrict__ dx, int64_t n) {
+  __shared__ float red[THREADS / kWarp > 0 ? THREADS / kWarp : 1];
+  const int64_t row = blockIdx.x;
+  RowSlice<THREADS, V, VEC> a, b;
+  a.load(p + row * n, n, 0.0f);
+  b.load(dp + row * n, n, 0.0f);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s += a.v[j][q] * b.v[j][q];
+  s = block_reduce<THREADS, false>(s, red);
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) a.v[j][q] = a.v[j][q] * (b.v[j][q] - s);
+  a.store(dx + row * n, n);
+}
+
+// Rows longer than the register-resident variants: online max/sum in one
+// pass, then a second pass writes exp(x - m) / s.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) softmax_fwd_long_kernel(const float* __restrict__ x,
+                                                                   float* __restrict__ y,
+                                                                   int64_t n) {
+  __shared__ float red[THREADS / kWarp];
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  float m = -INFINITY, s = 0.0f;
+  for (int64_t i = threadIdx.x; i < n; i += THREADS) {
+    const float v = __ldg(xr + i);
+    if (v > m) {
+      s = (m == -INFINITY) ? 0.0f : s * expf(m - v);
+      m = v;
+    }
+    if (v != -INFINITY) s += expf(v - m);
+  }
+  const float gm = block_reduce<THREADS, true>(m, red);
+  s = (m == -INFINITY) ? 0.0f : s * expf(m - gm);
+  s = block_reduce<THREADS, false>(s, red);
+  const float inv = 1.0f / s;
+  float* yr = y + row * n;
+  for (int64_t i = threadIdx.x; i < n; i += THREADS) {
+    const float v = __ldg(xr + i);
+    yr[i] = (v == -INFINITY) ? 0.0f : expf(v - gm) * inv;
+  }
+}
+
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) softmax_bwd_long_kernel(const float* __restrict__ p,
+                                                                   const float* __restrict__ dp,
+                                                                   float* __restrict__ dx,
+                                                                   int64_t n) {
+  __shared__ float red[THREADS / kWarp];
+  const int64_t row = blockIdx.x;
+  const float* pr = p + row * n;
+  const float* dr = dp + row * n;
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < n; i += THREADS) s += __ldg(pr + i) * __ldg(dr + i);
+  s = block_reduce<THREADS, false>(s, red);
+  float* xr = dx + row * n;
+  for (int64_t i = threadIdx.x; i < n; i += THREADS) xr[i] = __ldg(pr + i) * (__ldg(dr + i) - s);
+}
+
+// ------------------------------------------------------------------ GELU
+// gelu / gelu_bwd (Transformer_kernels/GeLU.cuh:7-29): y = x * Phi(x) and
+// dx = dy * (Phi(x) + x * phi(x)), phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
+__device__ __forceinline__ float gelu_f(float x) { return x * normcdff(x); }
+__device__ __forceinline__ float gelu_g(float x, float dy) {
+  const float inv_sqrt_2pi = 0.3989422804014327f;
+  return dy * (normcdff(x) + x * inv_sqrt_2pi * expf(-0.5f * x * x));
+}
+
+__global__ void gelu_fwd_vec(const float4* __restrict__ x, float4* __restrict__ y, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldg(x + i);
+    y[i] = make_float4(gelu_f(a.x), gelu_f(a.y), gelu_f(a.z), gelu_f(a.w));
+  }
+}
+__global__ void gelu_bwd_vec(const float4* __restrict__ x, const float4* __restrict__ dy,
+                             float4* __restrict__ dx, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldg(x + i), g = __ldg(dy + i);
+    dx[i] = make_float4(gelu_g(a.x, g.x), gelu_g(a.y, g.y), gelu_g(a.z, g.z), gelu_g(a.w, g.w));
+  }
+}
+__global__ void gelu_fwd_scalar(const float* __restrict__ x, float* __restrict__ y, int64_t n,
+                                int64_t start) {
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = gelu_f(__ldg(x + i));
+}
+__global__ void gelu_bwd_scalar(const float* __restrict__ x, const float* __restrict__ dy,
+                                float* __restrict__ dx, int64_t n, int64_t start) {
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dx[i] = gelu_g(__ldg(x + i), __ldg(dy + i));
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row; lane holds V slots of 4 columns (the same columns for
+// every row, so per-column gradient partials stay in registers).  Math of the
+// reference module gpt/gpt.py:55-58: biased variance, eps inside the sqrt.
+template <int V, bool VEC>
+struct WarpRow {
+  float v[V][4];
+  __device__ __forceinline__ static int col(int lane, int j, int q) {
+    return VEC ? 4 * (j * kWarp + lane) + q : (4 * j + q) * kWarp + lane;
+  }
+  __device__ __forceinline__ void load(const float* __restrict__ p, int n, int lane) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (VEC) {
+        const int c = col(lane, j, 0);
+        if (c < n) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(p + c));
+          v[j][0] = x.x; v[j][1] = x.y; v[j][2] = x.z; v[j][3] = x.w;
+        } else {
+          v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.0f;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = col(lane, j, q);
+          v[j][q] = c < n ? __ldg(p + c) : 0.0f;
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* __restrict__ p, int n, int lane) const {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (VEC) {
+        const int c = col(lane, j, 0);
+        if (c < n) *reinterpret_cast<float4*>(p + c) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = col(lane, j, q);
+          if (c < n) p[c] = v[j][q];
+        }
+      }
+    }
+  }
+};
+
+constexpr int kLnWarps = 8;
+
+template <int V, bool VEC>
+__global__ void __launch_bounds__(kLnWarps* kWarp)
+    layernorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                         const float* __restrict__ beta, float* __restrict__ y,
+                         float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                         int64_t rows, int n, float eps) {
+  const int lane = threadIdx.x % kWarp;
+  const int64_t row = (int64_t)blockIdx.x * kLnWarps + threadIdx.x / kWarp;
+  if (row >= rows) return;
+  WarpRow<V, VEC> r, g, b;
+  r.load(x + row * n, n, lane);
+  g.load(gamma, n, lane);
+  b.load(beta, n, lane);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s += r.v[j][q];
+  const float mean = warp_sum(s) / (float)n;
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = WarpRow<V, VEC>::col(lane, j, q);
+      const float d = (c < n) ? r.v[j][q] - mean : 0.0f;
+      ss += d * d;
+    }
+  const float var = warp_sum(ss) / (float)n;
+  const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r.v[j][q] = (r.v[j][q] - mean) * rstd * g.v[j][q] + b.v[j][q];
+  r.store(y + row * n, n, lane);
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = rstd;
+  }
+}
+
+// dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma.
+// Per-CTA column partials of dy*xhat and dy go to ws[blockIdx.x][2][n].
+template <int V, bool VEC>
+__global__ void __launch_bounds__(kLnWarps* kWarp)
+    layernorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                         const float* __restrict__ dy, float* __restrict__ dx,
+                         float* __restrict__ ws, int64_t rows, int n) {
+  extern __shared__ float lnsm[];  // [2][n]
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  WarpRow<V, VEC> gam;
+  gam.load(gamma, n, lane);
+  float pg[V][4], pb[V][4];
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) pg[j][q] = pb[j][q] = 0.0f;
+  for (int64_t row = (int64_t)blockIdx.x * kLnWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kLnWarps) {
+    WarpRow<V, VEC> xr, g;
+    xr.load(x + row * n, n, lane);
+    g.load(dy + row * n, n, lane);
+    const float mu = __ldg(mean_in + row), rs = __ldg(rstd_in + row);
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float xh = (xr.v[j][q] - mu) * rs;
+        const float gg = g.v[j][q] * gam.v[j][q];
+        pg[j][q] += g.v[j][q] * xh;
+        pb[j][q] += g.v[j][q];
+        xr.v[j][q] = xh;
+        g.v[j][q] = gg;
+        s1 += gg;
+        s2 += gg * xh;
+      }
+    s1 = warp_sum(s1) / (float)n;
+    s2 = warp_sum(s2) / (float)n;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) g.v[j][q] = rs * (g.v[j][q] - s1 - xr.v[j][q] * s2);
+    g.store(dx + row * n, n, lane);
+  }
+  // CTA-level fixed-order reduction of the per-warp column partials: warps
+  // add their partials into lnsm[2][n] one after another.
+  for (int w = 0; w < kLnWarps; ++w) {
+    if (warp == w) {
+#pragma unroll
+      for (int j = 0; j < V; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = WarpRow<V, VEC>::col(lane, j, q);
+          if (c < n) {
+            lnsm[c] = (w == 0 ? 0.0f : lnsm[c]) + pg[j][q];
+            lnsm[n + c] = (w == 0 ? 0.0f : lnsm[n + c]) + pb[j][q];
+          }
+        }
+    }
+    __syncthreads();
+  }
+  float* out = ws + (size_t)blockIdx.x * 2 * n;
+  for (int c = threadIdx.x; c < 2 * n; c += blockDim.x) out[c] = lnsm[c];
+}
+
+// Sums `parts` partial rows of length `len` (row stride `len`) column-wise.
+__global__ void column_sum_parts(const float* __restrict__ ws, int parts, int64_t len,
+                                 float* __restrict__ out_a, float* __restrict__ out_b,
+                                 int64_t split) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < len;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int p = 0; p < parts; ++p) acc += ws[(int64_t)p * len + c];
+    if (c < split) out_a[c] = acc;
+    else out_b[c - split] = acc;
+  }
+}
+
+// ------------------------------------------------------------ bias gradient
+// Stage 1: CTA (column block, row chunk) sums its rows for 4 columns per
+// thread; stage 2 (column_sum_parts) adds the chunks.  Replaces the
+// one-block-per-column warp_sum_kernel (Transformer_kernels/warp_sum_kernel.cuh:13-51).
+constexpr int kBgThreads = 256;
+constexpr int kBgRowsPerChunk = 64;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kBgThreads)
+    bias_grad_partial(const float* __restrict__ dy, int64_t s0, int64_t s1, int64_t s2, int64_t m,
+                      int64_t rows, int64_t n, float* __restrict__ ws) {
+  const int64_t c0 = ((int64_t)blockIdx.x * kBgThreads + threadIdx.x) * 4;
+  if (c0 >= n) return;
+  const int64_t r0 = (int64_t)blockIdx.y * kBgRowsPerChunk;
+  const int64_t r1 = min(rows, r0 + kBgRowsPerChunk);
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int64_t r = r0; r < r1; ++r) {
+    const int64_t b = r / m, i = r % m;
+    const float* p = dy + b * s0 + i * s1;
+    if (VEC && c0 + 3 < n) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p + c0));
+      a[0] += v.x; a[1] += v.y; a[2] += v.z; a[3] += v.w;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (c0 + q < n) a[q] += __ldg(p + (c0 + q) * s2);
+    }
+  }
+  float* out = ws + (int64_t)blockIdx.y * n;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (c0 + q < n) out[c0 + q] = a[q];
+}
+
+// ---------------------------------------------------------- FA2 bwd delta
+// delta[b,h,t] = sum_d O * dO (flash_attention_bwd_delta,
+// Transformer_kernels/flash_attention.cuh:175-213).  D/4 lanes share a row,
+// each lane reading 4 consecutive head-dim elements.
+template <int D, bool VEC>
+__global__ void __launch_bounds__(256)
+    fa2_delta_kernel(const float* __restrict__ o, int64_t o0, int64_t o1, int64_t o2, int64_t o3,
+                     const float* __restrict__ g, int64_t g0, int64_t g1, int64_t g2, int64_t g3,
+                     float* __restrict__ delta, int64_t H, int64_t T, int64_t rows) {
+  constexpr int LPR = D / 4;  // lanes per row
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = tid / LPR;
+  const int sub = (int)(tid % LPR);
+  float acc = 0.0f;
+  if (row < rows) {
+    const int64_t b = row / (H * T), rem = row % (H * T), h = rem / T, t = rem % T;
+    const float* po = o + b * o0 + h * o1 + t * o2;
+    const float* pg = g + b * g0 + h * g1 + t * g2;
+    const int d = 4 * sub;
+    if (VEC) {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(po + d));
+      const float4 y = __ldg(reinterpret_cast<const float4*>(pg + d));
+      acc = x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc += __ldg(po + (d + q) * o3) * __ldg(pg + (d + q) * g3);
+    }
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off, LPR);
+  if (row < rows && sub == 0) delta[row] = acc;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int THREADS, int V>
+int softmax_dispatch_fwd(const float* x, float* y, int64_t rows, int64_t n, bool vec,
+                         cudaStream_t st) {
+  if (vec) softmax_fwd_kernel<THREADS, V, true><<<(unsigned)rows, THREADS, 0, st>>>(x, y, n);
+  else softmax_fwd_kernel<THREADS, V, false><<<(unsigned)rows, THREADS, 0, st>>>(x, y, n);
+  return check_launch();
+}
+template <int THREADS, int V>
+int softmax_dispatch_bwd(const float* p, const float* dp, float* dx, int64_t rows, int64_t n,
+                         bool vec, cudaStream_t st) {
+  if (vec) softmax_bwd_kernel<THREADS, V, true><<<(unsigned)rows, THREADS, 0, st>>>(p, dp, dx, n);
+  else softmax_bwd_kernel<THREADS, V, false><<<(unsigned)rows, THREADS, 0, st>>>(p, dp, dx, n);
+  return check_launch();
+}
+
+template <int V, bool VEC>
+void ln_fwd_launch(const float* x, const float* g, const float* b, float* y, float* mean,
+                   float* rstd, int64_t rows, int n, float eps, cudaStream_t st) {
+  const unsigned grid = (unsigned)((rows + kLnWarps - 1) / kLnWarps);
+  layernorm_fwd_kernel<V, VEC><<<grid, kLnWarps * kWarp, 0, st>>>(x, g, b, y, mean, rstd, rows, n,
+                                                                  eps);
+}
+
+int ln_bwd_grid(int64_t rows) {
+  const int64_t want = (rows + kLnWarps - 1) / kLnWarps;
+  return (int)(want < 512 ? (want < 1 ? 1 : want) : 512);
+}
+
+template <int V, bool VEC>
+int ln_bwd_launch(const float* x, const float* g, const float* mean, const float* rstd,
+                  const float* dy, float* dx, float* ws, int64_t rows, int n, int grid,
+                  cudaStream_t st) {
+  const size_t smem = (size_t)2 * n * sizeof(float);
+  auto kern = layernorm_bwd_kernel<V, VEC>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return CT_ERR_CUDA;
+  }
+  kern<<<grid, kLnWarps * kWarp, smem, st>>>(x, g, mean, rstd, dy, dx, ws, rows, n);
+  return check_launch();
+}
+
+}  // namespace
+
+// =============================================================== launchers
+int launch_softmax_fwd(const float* x, float* y, int64_t rows, int64_t n, cudaStream_t st) {
+  if (rows == 0 || n == 0) return CT_OK;
+  const bool vec = (n % 4 == 0) && aligned16(x) && aligned16(y);
+  if (n <= 128) return softmax_dispatch_fwd<32, 1>(x, y, rows, n, vec, st);
+  if (n <= 512) return softmax_dispatch_fwd<128, 1>(x, y, rows, n, vec, st);
+  if (n <= 1024) return softmax_dispatch_fwd<256, 1>(x, y, rows, n, vec, st);
+  if (n <= 2048) return softmax_dispatch_fwd<256, 2>(x, y, rows, n, vec, st);
+  if (n <= 4096) return softmax_dispatch_fwd<256, 4>(x, y, rows, n, vec, st);
+  if (n <= 8192) return softmax_dispatch_fwd<512, 4>(x, y, rows, n, vec, st);
+  if (n <= 16384) return softmax_dispatch_fwd<512, 8>(x, y, rows, n, vec, st);
+  softmax_fwd_long_kernel<512><<<(unsigned)rows, 512, 0, st>>>(x, y, n);
+  return check_launch();
+}
+
+int launch_softmax_bwd(const float* p, const float* dp, float* dx, int64_t rows, int64_t n,
+                       cudaStream_t st) {
+  if (rows == 0 || n == 0) return CT_OK;
+  const bool vec = (n % 4 == 0) && aligned16(p) && aligned16(dp) && aligned16(dx);
+  if (n <= 128) return softmax_dispatch_bwd<32, 1>(p, dp, dx, rows, n, vec, st);
+  if (n <= 512) return softmax_dispatch_bwd<128, 1>(p, dp, dx, rows, n, vec, st);
+  if (n <= 1024) return softmax_dispatch_bwd<256, 1>(p, dp, dx, rows, n, vec, st);
+  if (n <= 2048) return softmax_dispatch_bwd<256, 2>(p, dp, dx, rows, n, vec, st);
+  if (n <= 4096) return softmax_dispatch_bwd<256, 4>(p, dp, dx, rows, n, vec, st);
+  if (n <= 8192) return softmax_dispatch_bwd<512, 4>(p, dp, dx, rows, n, vec, st);
+  if (n <= 16384) return softmax_dispatch_bwd<512, 8>(p, dp, dx, rows, n, vec, st);
+  softmax_bwd_long_kernel<512><<<(unsigned)rows, 512, 0, st>>>(p, dp, dx, n);
+  return check_launch();
+}
+
+static unsigned elementwise_grid(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  const int64_t cap = 148 * 32;
+  if (g > cap) g = cap;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
+int launch_gelu_fwd(const float* x, float* y, int64_t numel, cudaStream_t st) {
+  if (numel == 0) return CT_OK;
+  int64_t done = 0;
+  if (aligned16(x) && aligned16(y)) {
+    const int64_t n4 = numel / 4;
+    if (n4 > 0) {
+      gelu_fwd_vec<<<elementwise_grid(n4, 256), 256, 0, st>>>(
+          reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n4);
+      done = n4 * 4;
+    }
+  }
+  if (done < numel) gelu_fwd_scalar<<<elementwise_grid(numel - done, 256), 256, 0, st>>>(x, y, numel, done);
+  return check_launch();
+}
+
+int launch_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, cudaStream_t st) {
+  if (numel == 0) return CT_OK;
+  int64_t done = 0;
+  if (aligned16(x) && aligned16(dy) && aligned16(dx)) {
+    const int64_t n4 = numel / 4;
+    if (n4 > 0) {
+      gelu_bwd_vec<<<elementwise_grid(n4, 256), 256, 0, st>>>(
+          reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(dy),
+          reinterpret_cast<float4*>(dx), n4);
+      done = n4 * 4;
+    }
+  }
+  if (done < numel)
+    gelu_bwd_scalar<<<elementwise_grid(numel - done, 256), 256, 0, st>>>(x, dy, dx, numel, done);
+  return check_launch();
+}
+
+int launch_layernorm_fwd(const float* x, const float* g, const float* b, float* y, float* mean,
+                         float* rstd, int64_t rows, int64_t n, float eps, cudaStream_t st) {
+  if (rows == 0) return CT_OK;
+  if (n <= 0 || n > 1024) return CT_ERR_INVALID_ARGUMENT;
+  const bool vec = (n % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(b) && aligned16(y);
+  const int nn = (int)n;
+#define CT_LN_FWD(V) \
+  (vec ? ln_fwd_launch<V, true>(x, g, b, y, mean, rstd, rows, nn, eps, st) \
+       : ln_fwd_launch<V, false>(x, g, b, y, mean, rstd, rows, nn, eps, st))
+  if (n <= 128) CT_LN_FWD(1);
+  else if (n <= 256) CT_LN_FWD(2);
+  else if (n <= 512) CT_LN_FWD(4);
+  else CT_LN_FWD(8);
+#undef CT_LN_FWD
+  return check_launch();
+}
+
+size_t layernorm_bwd_workspace(int64_t rows, int64_t n) {
+  return (size_t)ln_bwd_grid(rows) * 2 * (size_t)n * sizeof(float);
+}
+
+int launch_layernorm_bwd(const float* x, const float* g, const float* mean, const float* rstd,
+                         const float* dy, float* dx, float* dg, float* db, int64_t rows,
+                         int64_t n, float* ws, cudaStream_t st) {
+  if (n <= 0 || n > 1024) return CT_ERR_INVALID_ARGUMENT;
+  if (rows == 0) {
+    if (cudaMemsetAsync(dg, 0, n * sizeof(float), st) != cudaSuccess) return CT_ERR_CUDA;
+    if (cudaMemsetAsync(db, 0, n * sizeof(float), st) != cudaSuccess) return CT_ERR_CUDA;
+    return CT_OK;
+  }
+  const bool vec = (n % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(dy) && aligned16(dx);
+  const int nn = (int)n, grid = ln_bwd_grid(rows);
+  int rc;
+#define CT_LN_BWD(V) \
+  rc = vec ? ln_bwd_launch<V, true>(x, g, mean, rstd, dy, dx, ws, rows, nn, grid, st) \
+           : ln_bwd_launch<V, false>(x, g, mean, rstd, dy, dx, ws, rows, nn, grid, st)
+  if (n <= 128) CT_LN_BWD(1);
+  else if (n <= 256) CT_LN_BWD(2);
+  else if (n <= 512) CT_LN_BWD(4);
+  else CT_LN_BWD(8);
+#undef CT_LN_BWD
+  if (rc != CT_OK) return rc;
+  column_sum_parts<<<elementwise_grid(2 * n, 256), 256, 0, st>>>(ws, grid, 2 * n, dg, db, n);
+  return check_launch();
+}
+
+size_t bias_grad_workspace(int64_t rows, int64_t n) {
+  const int64_t chunks = (rows + kBgRowsPerChunk - 1) / kBgRowsPerChunk;
+  return (size_t)(chunks < 1 ? 1 : chunks) * (size_t)n * sizeof(float);
+}
+
+int launch_bias_grad(const float* dy, const int64_t s[3], float* db, int64_t batch, int64_t m,
+                     int64_t n, float* ws, cudaStream_t st) {
+  if (n == 0) return CT_OK;
+  const int64_t rows = batch * m;
+  if (rows == 0) return cudaMemsetAsync(db, 0, n * sizeof(float), st) == cudaSuccess ? CT_OK : CT_ERR_CUDA;
+  const int64_t chunks = (rows + kBgRowsPerChunk - 1) / kBgRowsPerChunk;
+  if (chunks > 65535) return CT_ERR_INVALID_ARGUMENT;
+  const bool vec = s[2] == 1 && s[1] % 4 == 0 && s[0] % 4 == 0 && aligned16(dy);
+  dim3 grid((unsigned)((n + 4 * kBgThreads - 1) / (4 * kBgThreads)), (unsigned)chunks);
+  if (vec) bias_grad_partial<true><<<grid, kBgThreads, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  else bias_grad_partial<false><<<grid, kBgThreads, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  int rc = check_launch();
+  if (rc != CT_OK) return rc;
+  column_sum_parts<<<elementwise_grid(n, 256), 256, 0, st>>>(ws, (int)chunks, n, db, db, n);
+  return check_launch();
+}
+
+int launch_fa2_delta(const Fa2Problem& p, Strided4 o, Strided4 dO, float* delta, cudaStream_t st) {
+  const int64_t rows = p.B * p.H * p.T;
+  if (rows == 0) return CT_OK;
+  const bool vec = o.s[3] == 1 && dO.s[3] == 1 && aligned16(o.ptr) && aligned16(dO.ptr) &&
+                   o.s[0] % 4 == 0 && o.s[1] % 4 == 0 && o.s[2] % 4 == 0 && dO.s[0] % 4 == 0 &&
+                   dO.s[1] % 4 == 0 && dO.s[2] % 4 == 0;
+  const int64_t threads = rows * (p.D / 4);
+  const unsigned grid = (unsigned)((threads + 255) / 256);
+#define CT_DELTA(DD)                                                                          \
+  if (vec)                                                                                    \
+    fa2_delta_kernel<DD, true><<<grid, 256, 0, st>>>(o.ptr, o.s[0], o.s[1], o.s[2], o.s[3],   \
+                                                     dO.ptr, dO.s[0], dO.s[1], dO.s[2],       \
+                                                     dO.s[3], delta, p.H, p.T, rows);         \
+  else                                                                                        \
+    fa2_delta_kernel<DD, false><<<grid, 256, 0, st>>>(o.ptr, o.s[0], o.s[1], o.s[2], o.s[3],  \
+                                                      dO.ptr, dO.s[0], dO.s[1], dO.s[2],      \
+                                                      dO.s[3], delta, p.H, p.T, rows);
+  switch (p.D) {
+    case 32: CT_DELTA(32) break;
+    case 64: CT_DELTA(64) break;
+    case 128: CT_DELTA(128) break;
+    default: return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+#undef CT_DELTA
+  return check_launch();
+}
+
+}  // namespace ct

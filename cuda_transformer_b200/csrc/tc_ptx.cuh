@@ -1,0 +1,330 @@
+// tc_ptx.cuh -- thin inline-PTX layer for sm_100a: mbarriers with bounded
+// waits, TMA tile loads, Tensor Memory (TMEM) allocation / load / store, and
+// tcgen05.mma (kind::tf32) with shared-memory matrix descriptors.
+//
+// Every wait in this file is bounded: after CT_WAIT_TIMEOUT_NS of spinning it
+// records CT_DEVSTAT_TIMEOUT in the device status word, raises the CTA's abort
+// flag and returns false.  Callers then skip the rest of their work and fall
+// through to the kernel teardown (drain in-flight copies, release TMEM).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#ifndef CT_WAIT_TIMEOUT_NS
+#define CT_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: legitimate waits are microseconds
+#endif
+
+namespace ct {
+
+// Device status word bits (see ct_device_status in the C ABI).
+constexpr uint32_t CT_DEVSTAT_TIMEOUT = 1u;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Per-CTA control block placed in shared memory by every tcgen05 kernel.
+struct CtaCtl {
+  volatile uint32_t abort;   // set when any wait in this CTA expired
+  uint32_t tmem_base;        // written by tcgen05.alloc
+};
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy accesses (TMA writes, tensor-core operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits until the phase with the given parity of barrier `bar` has completed.
+// Returns false (and raises ctl->abort and the device status word) if the
+// wait exceeds CT_WAIT_TIMEOUT_NS or another wait of this CTA already failed.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                          uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (ctl->abort) return false;
+      if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {  // another CTA gave up
+        ctl->abort = 1u;
+        return false;
+      }
+      if (globaltimer_ns() - t0 > CT_WAIT_TIMEOUT_NS) {
+        ctl->abort = 1u;
+        atomicOr(status, CT_DEVSTAT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// ------------------------------------------------------------ tcgen05 sync
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------- TMEM allocation
+// Executed by one full warp.  The allocated base address is written to smem.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// TMEM address of (lane, column): lane in bits 31..16, column in 15..0.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+// ------------------------------------------------------- TMEM load/store
+// 32 lanes x 32 columns of 32-bit: thread t of the warp gets lane (quadrant
+// base + t), columns col..col+31.  The wait is inside the same asm statement
+// so the registers are valid when the statement retires.
+#define CT_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), \
+                 "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+#define CT_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), \
+                 "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : CT_R8(0), CT_R8(8), CT_R8(16), CT_R8(24)
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : CT_R8(0), CT_R8(8)
+      : "r"(taddr)
+      : "memory");
+}
+// Stores do not wait; call tmem_wait_st() before publishing them.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      CT_W8(0), CT_W8(8), CT_W8(16), CT_W8(24)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      CT_W8(0), CT_W8(8)
+      : "memory");
+}
+#undef CT_R8
+#undef CT_W8
+
+// --------------------------------------------------- UMMA descriptors
+// Shared-memory matrix descriptor for the 128-byte swizzle layout (the layout
+// TMA writes with CU_TENSOR_MAP_SWIZZLE_128B; atoms of 8 rows x 128 bytes,
+// 1024-byte aligned):
+//   bits  0-13 start address >> 4      bits 16-29 leading byte offset >> 4
+//   bits 32-45 stride byte offset >> 4 bits 46-47 version (1 on sm_100)
+//   bits 49-51 base offset (0)         bits 61-63 layout (2 = SWIZZLE_128B)
+// K-major operand: rows of 128 bytes (32 fp32 along K); SBO = distance between
+//   8-row groups (1024 when dense), LBO unused (16).  Stepping K by 8 fp32
+//   inside the 128-byte row advances the start address by 32 bytes.
+// MN-major operand: 128-byte rows hold 32 consecutive M (or N) elements, one
+//   row per K index; LBO = distance between consecutive 32-element M/N chunks,
+//   SBO = distance between 8-row K groups (1024).  Stepping K by 8 advances the
+//   start address by 1024 bytes.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr) {
+  return sdesc_sw128(saddr, 16u, 1024u);
+}
+__device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t saddr, uint32_t chunk_stride_bytes) {
+  return sdesc_sw128(saddr, chunk_stride_bytes, 1024u);
+}
+
+// Instruction descriptor for kind::tf32 with an FP32 accumulator:
+//   bits 4-5 D format (1 = F32), 7-9 A format (2 = TF32), 10-12 B format,
+//   15 A major (1 = MN), 16 B major, 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ------------------------------------------------------------- MMA issue
+// D[tmem] (+)= A * B, A and B from shared memory.
+__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A * B, A from TMEM (rows = lanes, K = columns), B from smem.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on `bar` when all previously issued tcgen05 async ops of this
+// thread have completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// --------------------------------------------------------- TF32 helpers
+// Round-to-nearest (ties away) to TF32; the low 13 bits of the result are 0.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// x = hi + lo with hi, lo both exactly representable in TF32 up to the
+// rounding of lo (|x - hi - lo| <= 2^-22 |x|).
+__device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
+  hi = tf32_round(x);
+  lo = tf32_round(x - hi);
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 128-bit shared-memory accessors on 32-bit shared addresses.
+__device__ __forceinline__ float4 lds128(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// Splits a shared-memory tile in place: every fp32 word x at raw+i becomes
+// tf32(x) and lo+i receives the TF32-rounded remainder.  Both buffers share
+// the same swizzled layout, so the element correspondence is positional.
+__device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint32_t bytes,
+                                                uint32_t tid, uint32_t nthreads) {
+  for (uint32_t off = tid * 16u; off < bytes; off += nthreads * 16u) {
+    float4 x = lds128(raw + off);
+    float4 h, l;
+    tf32_split(x.x, h.x, l.x);
+    tf32_split(x.y, h.y, l.y);
+    tf32_split(x.z, h.z, l.z);
+    tf32_split(x.w, h.w, l.w);
+    sts128(raw + off, h);
+    sts128(lo + off, l);
+  }
+}
+
+// Byte offset of element (row, col) in a tile written by TMA with
+// SWIZZLE_128B and 32-float boxes: column chunk c = col / 32 occupies
+// rows * 128 bytes; inside it the 16-byte unit index is XORed with row % 8.
+__host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col,
+                                                          uint32_t rows) {
+  const uint32_t chunk = col >> 5;
+  const uint32_t in_row = (col & 31u) * 4u;
+  const uint32_t unit = (in_row >> 4) ^ (row & 7u);
+  return chunk * rows * 128u + row * 128u + (unit << 4) + (in_row & 15u);
+}
+
+}  // namespace ct

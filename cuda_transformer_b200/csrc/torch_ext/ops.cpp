@@ -1,0 +1,400 @@
+// ops.cpp -- torch.ops.cuda_transformer.* registrations over the C ABI.
+//
+// Keeps the reference's operator library name and every schema string
+// verbatim (Transformer_launchers/bindings.cpp:3, linear_layer.cu:101-102,
+// softmax_layer.cu:83-84, gelu_activation.cu:80-81, flash_attn_launcher.cu:145-146,
+// causal_self_attn_layer.cu:135-136) so cuda_transformer/ops.py, the autograd
+// functions and gpt/gpt.py bind unchanged.  Like the reference launchers this
+// shim owns allocation: outputs are dense torch tensors on the input's device
+// and scratch comes from the caching allocator.  Unlike them it guards the
+// device, checks dtypes, and maps C-ABI status codes to RuntimeError.
+//
+// Precision of the tensor-core kernels: CUDA_TRANSFORMER_PRECISION =
+// "3xtf32" (default, FP32-accurate), "tf32" or "fp32" (CUDA cores); the *_ex
+// operators take it explicitly (0 = 3xtf32, 1 = tf32, 2 = fp32).
+#include <Python.h>
+
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <tuple>
+
+#include "ct_b200.h"
+
+namespace cuda_transformer {
+namespace {
+
+using at::Tensor;
+
+int default_precision() {
+  static const int p = [] {
+    const char* e = std::getenv("CUDA_TRANSFORMER_PRECISION");
+    if (!e || !*e) return (int)CT_PRECISION_3XTF32;
+    std::string s(e);
+    if (s == "3xtf32" || s == "fp32acc") return (int)CT_PRECISION_3XTF32;
+    if (s == "tf32") return (int)CT_PRECISION_TF32;
+    if (s == "fp32" || s == "simt") return (int)CT_PRECISION_FP32;
+    TORCH_CHECK(false, "CUDA_TRANSFORMER_PRECISION must be 3xtf32, tf32 or fp32, got ", s);
+  }();
+  return p;
+}
+
+void check_rc(int rc, const char* op) {
+  TORCH_CHECK(rc == CT_OK, op, ": ", ct_status_string(rc));
+}
+
+void check_cuda_f32(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kFloat, name, " must be float32");
+}
+
+void* cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Attention operands must be addressable by TMA (unit stride along head_dim,
+// 16-byte aligned base and strides); anything else is copied once.
+Tensor tma_ready(const Tensor& t) {
+  bool ok = t.stride(3) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
+  for (int i = 0; i < 3 && ok; ++i) ok = (t.stride(i) % 4) == 0;
+  return ok ? t : t.contiguous();
+}
+
+void strides4(const Tensor& t, int64_t out[4]) {
+  for (int i = 0; i < 4; ++i) out[i] = t.stride(i);
+}
+
+// ------------------------------------------------------------ FlashAttention
+std::tuple<Tensor, Tensor> fa2_fwd_impl(const Tensor& Q0, const Tensor& K0, const Tensor& V0,
+                                        bool causal, int64_t precision) {
+  check_cuda_f32(Q0, "Q");
+  check_cuda_f32(K0, "K");
+  check_cuda_f32(V0, "V");
+  TORCH_CHECK(Q0.dim() == 4 && K0.sizes() == Q0.sizes() && V0.sizes() == Q0.sizes(),
+              "Q, K, V must be [B, nh, T, hs] of equal shape");
+  c10::cuda::CUDAGuard guard(Q0.device());
+  const Tensor Q = tma_ready(Q0), K = tma_ready(K0), V = tma_ready(V0);
+  const int64_t B = Q.size(0), H = Q.size(1), T = Q.size(2), D = Q.size(3);
+  auto opt = Q.options();
+  Tensor O = at::empty({B, H, T, D}, opt);
+  Tensor L = at::empty({B, H, T}, opt);
+  int64_t qs[4], ks[4], vs[4];
+  strides4(Q, qs);
+  strides4(K, ks);
+  strides4(V, vs);
+  check_rc(ct_fa2_fwd(Q.data_ptr<float>(), qs, K.data_ptr<float>(), ks, V.data_ptr<float>(), vs,
+                      O.data_ptr<float>(), L.data_ptr<float>(), B, H, T, D, causal ? 1 : 0,
+                      (int)precision, cur_stream()),
+           "flash_attention_fwd");
+  return {O, L};
+}
+
+std::tuple<Tensor, Tensor, Tensor> fa2_bwd_impl(const Tensor& Q0, const Tensor& K0,
+                                                const Tensor& V0, const Tensor& O0,
+                                                const Tensor& dO0, const Tensor& L, bool causal,
+                                                int64_t precision) {
+  check_cuda_f32(Q0, "Q");
+  check_cuda_f32(K0, "K");
+  check_cuda_f32(V0, "V");
+  check_cuda_f32(O0, "O");
+  check_cuda_f32(dO0, "dO");
+  check_cuda_f32(L, "L");
+  TORCH_CHECK(Q0.dim() == 4 && K0.sizes() == Q0.sizes() && V0.sizes() == Q0.sizes() &&
+                  O0.sizes() == Q0.sizes() && dO0.sizes() == Q0.sizes(),
+              "Q, K, V, O, dO must be [B, nh, T, hs] of equal shape");
+  TORCH_CHECK(L.dim() == 3 && L.size(0) == Q0.size(0) && L.size(1) == Q0.size(1) &&
+                  L.size(2) == Q0.size(2),
+              "L must be [B, nh, T]");
+  c10::cuda::CUDAGuard guard(Q0.device());
+  const Tensor Q = tma_ready(Q0), K = tma_ready(K0), V = tma_ready(V0), O = O0,
+               dO = tma_ready(dO0);
+  const int64_t B = Q.size(0), H = Q.size(1), T = Q.size(2), D = Q.size(3);
+  auto opt = Q.options();
+  Tensor dQ = at::empty({B, H, T, D}, opt);
+  Tensor dK = at::empty({B, H, T, D}, opt);
+  Tensor dV = at::empty({B, H, T, D}, opt);
+  const size_t ws_bytes = ct_fa2_bwd_workspace_size(B, H, T, D);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 16)}, opt.dtype(at::kByte));
+  int64_t qs[4], ks[4], vs[4], os[4], gs[4], ls[3] = {L.stride(0), L.stride(1), L.stride(2)};
+  strides4(Q, qs);
+  strides4(K, ks);
+  strides4(V, vs);
+  strides4(O, os);
+  strides4(dO, gs);
+  check_rc(ct_fa2_bwd(Q.data_ptr<float>(), qs, K.data_ptr<float>(), ks, V.data_ptr<float>(), vs,
+                      O.data_ptr<float>(), os, dO.data_ptr<float>(), gs, L.data_ptr<float>(), ls,
+                      dQ.data_ptr<float>(), dK.data_ptr<float>(), dV.data_ptr<float>(),
+                      ws.data_ptr(), ws_bytes, B, H, T, D, causal ? 1 : 0, (int)precision,
+                      cur_stream()),
+           "flash_attention_bwd");
+  return {dQ, dK, dV};
+}
+
+std::tuple<Tensor, Tensor> flash_attention_fwd(Tensor Q, Tensor K, Tensor V, bool causal) {
+  return fa2_fwd_impl(Q, K, V, causal, default_precision());
+}
+std::tuple<Tensor, Tensor, Tensor> flash_attention_bwd(Tensor Q, Tensor K, Tensor V, Tensor O,
+                                                       Tensor dO, Tensor L, bool causal) {
+  return fa2_bwd_impl(Q, K, V, O, dO, L, causal, default_precision());
+}
+std::tuple<Tensor, Tensor> flash_attention_fwd_ex(Tensor Q, Tensor K, Tensor V, bool causal,
+                                                  int64_t precision) {
+  return fa2_fwd_impl(Q, K, V, causal, precision);
+}
+std::tuple<Tensor, Tensor, Tensor> flash_attention_bwd_ex(Tensor Q, Tensor K, Tensor V, Tensor O,
+                                                          Tensor dO, Tensor L, bool causal,
+                                                          int64_t precision) {
+  return fa2_bwd_impl(Q, K, V, O, dO, L, causal, precision);
+}
+
+// ----------------------------------------------------------------- Linear
+// x: (batch, m, k); weights: (k, n) or (1 | batch, k, n) "pre-transposed";
+// bias: (n,); out: (batch, m, n)  -- linear_layer.cu:24-70.
+Tensor fma_impl(const Tensor& x, Tensor weights, const Tensor& bias, int64_t precision) {
+  if (weights.dim() == 2) weights = weights.unsqueeze(0);
+  TORCH_CHECK(x.dim() == 3, "x must be a 3D tensor (batch, m, k)");
+  const int64_t batch = x.size(0), m = x.size(1), k = x.size(2), n = weights.size(2);
+  TORCH_CHECK(weights.size(1) == k, "weights.size(1) must match x.size(2)");
+  TORCH_CHECK(bias.size(0) == n, "bias.size(0) must match weights.size(2)");
+  check_cuda_f32(x, "x");
+  check_cuda_f32(weights, "weights");
+  check_cuda_f32(bias, "bias");
+  TORCH_CHECK(weights.size(0) == 1 || weights.size(0) == batch,
+              "weights batch must be 1 or match x");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty({batch, m, n}, x.options());
+  const int64_t xs[3] = {x.stride(0), x.stride(1), x.stride(2)};
+  const int64_t wsd[3] = {weights.stride(0), weights.stride(1), weights.stride(2)};
+  check_rc(ct_linear_fwd(x.data_ptr<float>(), xs, weights.data_ptr<float>(), wsd,
+                         bias.data_ptr<float>(), bias.stride(0), out.data_ptr<float>(), batch, m,
+                         k, n, weights.size(0), (int)precision, cur_stream()),
+           "cuda_fma");
+  return out;
+}
+
+Tensor cuda_fma(Tensor x, Tensor weights, Tensor bias) {
+  return fma_impl(x, weights, bias, default_precision());
+}
+Tensor cuda_fma_ex(Tensor x, Tensor weights, Tensor bias, int64_t precision) {
+  return fma_impl(x, weights, bias, precision);
+}
+
+// dy: (batch, m, n) -> db: (n,)  -- linear_layer.cu:72-97.
+Tensor db_calculation(Tensor dy) {
+  check_cuda_f32(dy, "dy");
+  TORCH_CHECK(dy.dim() == 3, "dy must be a 3D tensor");
+  c10::cuda::CUDAGuard guard(dy.device());
+  const int64_t batch = dy.size(0), m = dy.size(1), n = dy.size(2);
+  Tensor db = at::empty({n}, dy.options());
+  const size_t wsb = ct_bias_grad_workspace_size(batch, m, n);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(wsb, 16)}, dy.options().dtype(at::kByte));
+  const int64_t s[3] = {dy.stride(0), dy.stride(1), dy.stride(2)};
+  check_rc(ct_bias_grad(dy.data_ptr<float>(), s, db.data_ptr<float>(), batch, m, n, ws.data_ptr(),
+                        wsb, cur_stream()),
+           "db_calculation");
+  return db;
+}
+
+// ---------------------------------------------------------------- Softmax
+Tensor cuda_softmax(Tensor x) {
+  TORCH_CHECK(x.dim() == 3, "x must be a 3D tensor");
+  check_cuda_f32(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty_like(x);
+  const int64_t n = x.size(2);
+  check_rc(ct_softmax_fwd(x.data_ptr<float>(), out.data_ptr<float>(), x.size(0) * x.size(1), n,
+                          cur_stream()),
+           "cuda_softmax");
+  return out;
+}
+
+Tensor cuda_softmax_bwd(Tensor probs, Tensor dp) {
+  TORCH_CHECK(probs.dim() == 3, "probs must be a 3D tensor");
+  check_cuda_f32(probs, "probs");
+  TORCH_CHECK(probs.is_contiguous(), "probs must be contiguous");
+  TORCH_CHECK(dp.dim() == 3, "dp must be a 3D tensor");
+  check_cuda_f32(dp, "dp");
+  TORCH_CHECK(dp.is_contiguous(), "dp must be contiguous");
+  TORCH_CHECK(dp.sizes() == probs.sizes(), "dp must match probs");
+  c10::cuda::CUDAGuard guard(probs.device());
+  Tensor out = at::empty_like(probs);
+  check_rc(ct_softmax_bwd(probs.data_ptr<float>(), dp.data_ptr<float>(), out.data_ptr<float>(),
+                          probs.size(0) * probs.size(1), probs.size(2), cur_stream()),
+           "cuda_softmax_bwd");
+  return out;
+}
+
+// ------------------------------------------------------------------- GELU
+Tensor gelu_activation(Tensor x) {
+  check_cuda_f32(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty_like(x);
+  check_rc(ct_gelu_fwd(x.data_ptr<float>(), out.data_ptr<float>(), x.numel(), cur_stream()),
+           "gelu_activation");
+  return out;
+}
+
+Tensor gelu_activation_bwd(Tensor x, Tensor dy) {
+  check_cuda_f32(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  check_cuda_f32(dy, "dy");
+  TORCH_CHECK(dy.is_contiguous(), "dy must be contiguous");
+  TORCH_CHECK(dy.numel() == x.numel(), "dy must match x");
+  c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = at::empty_like(x);
+  check_rc(ct_gelu_bwd(x.data_ptr<float>(), dy.data_ptr<float>(), out.data_ptr<float>(),
+                       x.numel(), cur_stream()),
+           "gelu_activation_bwd");
+  return out;
+}
+
+// -------------------------------------------------------------- LayerNorm
+// New surface (the reference's LayerNorm is a torch module, gpt/gpt.py:47-59).
+std::tuple<Tensor, Tensor, Tensor> layernorm_fwd(Tensor x, Tensor gamma, Tensor beta, double eps) {
+  check_cuda_f32(x, "x");
+  check_cuda_f32(gamma, "gamma");
+  check_cuda_f32(beta, "beta");
+  TORCH_CHECK(x.is_contiguous() && gamma.is_contiguous() && beta.is_contiguous(),
+              "layernorm inputs must be contiguous");
+  const int64_t n = x.size(-1);
+  TORCH_CHECK(gamma.numel() == n && beta.numel() == n, "gamma/beta must have x.size(-1) elements");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = n ? x.numel() / n : 0;
+  Tensor y = at::empty_like(x);
+  Tensor mean = at::empty({rows}, x.options());
+  Tensor rstd = at::empty({rows}, x.options());
+  check_rc(ct_layernorm_fwd(x.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(),
+                            y.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                            rows, n, (float)eps, cur_stream()),
+           "layernorm_fwd");
+  return {y, mean, rstd};
+}
+
+std::tuple<Tensor, Tensor, Tensor> layernorm_bwd(Tensor x, Tensor gamma, Tensor mean, Tensor rstd,
+                                                 Tensor dy0) {
+  check_cuda_f32(x, "x");
+  check_cuda_f32(gamma, "gamma");
+  check_cuda_f32(mean, "mean");
+  check_cuda_f32(rstd, "rstd");
+  check_cuda_f32(dy0, "dy");
+  TORCH_CHECK(x.is_contiguous() && gamma.is_contiguous(), "layernorm inputs must be contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  const Tensor dy = dy0.contiguous();
+  const int64_t n = x.size(-1), rows = n ? x.numel() / n : 0;
+  Tensor dx = at::empty_like(x);
+  Tensor dg = at::empty({n}, x.options());
+  Tensor db = at::empty({n}, x.options());
+  const size_t wsb = ct_layernorm_bwd_workspace_size(rows, n);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(wsb, 16)}, x.options().dtype(at::kByte));
+  check_rc(ct_layernorm_bwd(x.data_ptr<float>(), gamma.data_ptr<float>(), mean.data_ptr<float>(),
+                            rstd.data_ptr<float>(), dy.data_ptr<float>(), dx.data_ptr<float>(),
+                            dg.data_ptr<float>(), db.data_ptr<float>(), rows, n, ws.data_ptr(),
+                            wsb, cur_stream()),
+           "layernorm_bwd");
+  return {dx, dg, db};
+}
+
+// ------------------------------------------- materialised (naive) attention
+// Kept registered so cuda_autograd_fns imports; composed from this library's
+// own GEMM and softmax kernels.  qkv: (B, T, 3C) contiguous.
+std::tuple<Tensor, Tensor> causal_self_attention_fwd(Tensor qkv, int64_t nh, bool causal) {
+  check_cuda_f32(qkv, "qkv");
+  TORCH_CHECK(qkv.is_contiguous(), "qkv must be contiguous");
+  TORCH_CHECK(qkv.dim() == 3 && qkv.size(2) % (3 * nh) == 0, "qkv must be (B, T, 3*nh*hs)");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int64_t B = qkv.size(0), T = qkv.size(1), C = qkv.size(2) / 3, hs = C / nh;
+  const int prec = default_precision();
+  auto heads = [&](int64_t part) {  // (B*nh, T, hs) view of one third of qkv
+    return qkv.narrow(2, part * C, C).reshape({B, T, nh, hs}).transpose(1, 2).reshape({B * nh, T, hs});
+  };
+  Tensor q = heads(0), k = heads(1), v = heads(2);
+  Tensor zero_t = at::zeros({T}, qkv.options());
+  // S = q k^T / sqrt(hs): weights = k^T viewed (B*nh, hs, T)
+  Tensor s = fma_impl(q, k.transpose(1, 2), zero_t, prec).mul_(1.0 / std::sqrt((double)hs));
+  if (causal) s.masked_fill_(at::ones({T, T}, qkv.options().dtype(at::kBool)).triu(1), -INFINITY);
+  Tensor probs = at::empty_like(s);
+  check_rc(ct_softmax_fwd(s.data_ptr<float>(), probs.data_ptr<float>(), B * nh * T, T, cur_stream()),
+           "causal_self_attention_fwd");
+  Tensor zero_h = at::zeros({hs}, qkv.options());
+  Tensor o = fma_impl(probs, v, zero_h, prec);  // (B*nh, T, hs)
+  Tensor out = o.reshape({B, nh, T, hs}).transpose(1, 2).reshape({B, T, C}).contiguous();
+  return {out, probs.reshape({B, nh, T, T})};
+}
+
+// Gradients with the test's convention (test/test_causal_self_attn.py:60-67):
+// returns dq and dk multiplied by sqrt(hs) and dv unscaled.
+std::tuple<Tensor, Tensor, Tensor> causal_self_attention_bwd(Tensor Q, Tensor K, Tensor V,
+                                                             Tensor probs, Tensor dO) {
+  check_cuda_f32(Q, "Q");
+  check_cuda_f32(K, "K");
+  check_cuda_f32(V, "V");
+  check_cuda_f32(probs, "probs");
+  check_cuda_f32(dO, "dO");
+  c10::cuda::CUDAGuard guard(Q.device());
+  const int64_t BH = Q.size(0), T = Q.size(1), hs = Q.size(2);
+  const int prec = default_precision();
+  Tensor P = probs.reshape({BH, T, T}).contiguous();
+  Tensor zT = at::zeros({T}, Q.options()), zH = at::zeros({hs}, Q.options());
+  Tensor dV = fma_impl(P.transpose(1, 2), dO, zH, prec);         // P^T dO
+  Tensor dP = fma_impl(dO, V.transpose(1, 2), zT, prec);         // dO V^T
+  Tensor dS = at::empty_like(P);
+  check_rc(ct_softmax_bwd(P.data_ptr<float>(), dP.contiguous().data_ptr<float>(),
+                          dS.data_ptr<float>(), BH * T, T, cur_stream()),
+           "causal_self_attention_bwd");
+  Tensor dQ = fma_impl(dS, K, zH, prec);                          // dS K
+  Tensor dK = fma_impl(dS.transpose(1, 2), Q, zH, prec);          // dS^T Q
+  return {dQ, dK, dV};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(cuda_transformer, m) {
+  m.def("cuda_fma(Tensor x, Tensor weights, Tensor bias) -> Tensor");
+  m.def("db_calculation(Tensor dy) -> Tensor");
+  m.def("cuda_softmax(Tensor x) -> Tensor");
+  m.def("cuda_softmax_bwd(Tensor probs, Tensor dp) -> Tensor");
+  m.def("gelu_activation(Tensor x) -> Tensor");
+  m.def("gelu_activation_bwd(Tensor x, Tensor dy) -> Tensor");
+  m.def("flash_attention_fwd(Tensor Q, Tensor K, Tensor V, bool causal) -> (Tensor, Tensor)");
+  m.def("flash_attention_bwd(Tensor Q, Tensor K, Tensor V, Tensor O, Tensor dO, Tensor L, bool causal) -> (Tensor, Tensor, Tensor)");
+  m.def("causal_self_attention_fwd(Tensor qkv, int nh, bool causal) -> (Tensor, Tensor)");
+  m.def("causal_self_attention_bwd(Tensor Q, Tensor K, Tensor V, Tensor probs, Tensor dO) -> (Tensor, Tensor, Tensor)");
+  // additions of this implementation
+  m.def("flash_attention_fwd_ex(Tensor Q, Tensor K, Tensor V, bool causal, int precision) -> (Tensor, Tensor)");
+  m.def("flash_attention_bwd_ex(Tensor Q, Tensor K, Tensor V, Tensor O, Tensor dO, Tensor L, bool causal, int precision) -> (Tensor, Tensor, Tensor)");
+  m.def("cuda_fma_ex(Tensor x, Tensor weights, Tensor bias, int precision) -> Tensor");
+  m.def("layernorm_fwd(Tensor x, Tensor gamma, Tensor beta, float eps) -> (Tensor, Tensor, Tensor)");
+  m.def("layernorm_bwd(Tensor x, Tensor gamma, Tensor mean, Tensor rstd, Tensor dy) -> (Tensor, Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(cuda_transformer, CUDA, m) {
+  m.impl("cuda_fma", &cuda_fma);
+  m.impl("db_calculation", &db_calculation);
+  m.impl("cuda_softmax", &cuda_softmax);
+  m.impl("cuda_softmax_bwd", &cuda_softmax_bwd);
+  m.impl("gelu_activation", &gelu_activation);
+  m.impl("gelu_activation_bwd", &gelu_activation_bwd);
+  m.impl("flash_attention_fwd", &flash_attention_fwd);
+  m.impl("flash_attention_bwd", &flash_attention_bwd);
+  m.impl("causal_self_attention_fwd", &causal_self_attention_fwd);
+  m.impl("causal_self_attention_bwd", &causal_self_attention_bwd);
+  m.impl("flash_attention_fwd_ex", &flash_attention_fwd_ex);
+  m.impl("flash_attention_bwd_ex", &flash_attention_bwd_ex);
+  m.impl("cuda_fma_ex", &cuda_fma_ex);
+  m.impl("layernorm_fwd", &layernorm_fwd);
+  m.impl("layernorm_bwd", &layernorm_bwd);
+}
+
+}  // namespace cuda_transformer
+
+// Python module object for `import cuda_transformer._C`; loading the shared
+// object runs the static operator registrations above.
+static PyModuleDef ct_module = {PyModuleDef_HEAD_INIT, "_C",
+                                "custom cuda kernels for transformer architecture (sm_100a)", -1,
+                                nullptr};
+PyMODINIT_FUNC PyInit__C(void) { return PyModule_Create(&ct_module); }

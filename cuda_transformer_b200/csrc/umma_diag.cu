@@ -1,0 +1,123 @@
+// umma_diag.cu -- a single-CTA 128 x n x 32 TF32 tensor-core product used by
+// the test-suite to check, on the device, the operand layouts that the
+// FlashAttention and GEMM kernels rely on: K-major and MN-major shared-memory
+// operands in the 128-byte swizzle, A read from Tensor Memory, and how the
+// tensor core treats the 13 low mantissa bits of an FP32 operand.
+#include "ct_internal.h"
+#include "tc_ptx.cuh"
+
+namespace ct {
+namespace {
+
+struct DiagSmem {
+  uint64_t bar;
+  CtaCtl ctl;
+};
+
+// 128 threads.  smem: [header][pad to 1024][A 16 KB][B n*128 bytes].
+__global__ void __launch_bounds__(128, 1)
+    umma_diag_kernel(int mode, const float* __restrict__ a, const float* __restrict__ b,
+                     float* __restrict__ d, int n, uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DiagSmem* hs = reinterpret_cast<DiagSmem*>(smem_raw);
+  const uint32_t base = (smem_u32(smem_raw) + sizeof(DiagSmem) + 1023u) & ~1023u;
+  const uint32_t sa = base, sb = base + 128u * 128u;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const bool a_tmem = (mode == 2 || mode == 3);
+  const bool a_mn = (mode == 4);
+  const bool b_mn = (mode == 1 || mode == 3 || mode == 4);
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&hs->bar), 1);
+    hs->ctl.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&hs->ctl.tmem_base), 256);
+    tmem_relinquish();
+  }
+  // Operands into swizzled smem exactly as TMA would lay them out.
+  for (int e = tid; e < 128 * 32; e += 128) {
+    if (!a_tmem) {
+      if (a_mn) {  // a is [32 (k)][128 (m)], m contiguous
+        const int kk = e / 128, mm = e % 128;
+        *reinterpret_cast<float*>(smem_raw + (sa - smem_u32(smem_raw)) + sw128_offset(kk, mm, 32)) = a[e];
+      } else {  // a is [128 (m)][32 (k)]
+        const int mm = e / 32, kk = e % 32;
+        *reinterpret_cast<float*>(smem_raw + (sa - smem_u32(smem_raw)) + sw128_offset(mm, kk, 128)) = a[e];
+      }
+    }
+  }
+  for (int e = tid; e < n * 32; e += 128) {
+    if (b_mn) {  // b is [32 (k)][n], n contiguous
+      const int kk = e / n, nn = e % n;
+      *reinterpret_cast<float*>(smem_raw + (sb - smem_u32(smem_raw)) + sw128_offset(kk, nn, 32)) = b[e];
+    } else {  // b is [n][32 (k)]
+      const int nn = e / 32, kk = e % 32;
+      *reinterpret_cast<float*>(smem_raw + (sb - smem_u32(smem_raw)) + sw128_offset(nn, kk, n)) = b[e];
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = hs->ctl.tmem_base;
+  const uint32_t lane_base = tmem_addr(tmem, 32u * warp, 0);
+  if (a_tmem) {  // row tid of A into columns 128..159 of lane tid
+    float row[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) row[i] = a[tid * 32 + i];
+    tmem_st32(lane_base + 128u, row);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_tf32(128, n, a_mn, b_mn);
+    for (int k = 0; k < 4; ++k) {
+      const uint64_t bd = b_mn ? sdesc_mnmajor(sb + k * 1024u, 32u * 128u)
+                               : sdesc_kmajor(sb + k * 32u);
+      if (a_tmem) {
+        umma_tf32_ts(tmem, tmem + 128u + 8u * k, bd, idesc, k > 0);
+      } else {
+        const uint64_t ad = a_mn ? sdesc_mnmajor(sa + k * 1024u, 32u * 128u)
+                                 : sdesc_kmajor(sa + k * 32u);
+        umma_tf32_ss(tmem, ad, bd, idesc, k > 0);
+      }
+    }
+    umma_commit(smem_u32(&hs->bar));
+  }
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&hs->bar), 0, &hs->ctl, status));
+  if (ok) {
+    tc_fence_after();
+    for (int c = 0; c < n; c += 32) {
+      float v[32];
+      tmem_ld32(lane_base + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) d[tid * n + c + i] = v[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace
+
+int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
+                     const DeviceInfo& dev, cudaStream_t st) {
+  if (mode < 0 || mode > 4 || !(n == 32 || n == 64 || n == 128)) return CT_ERR_INVALID_ARGUMENT;
+  const size_t smem = 1024 + 1024 + 128 * 128 + (size_t)n * 128;
+  cudaError_t e = cudaFuncSetAttribute(umma_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return CT_ERR_CUDA;
+  umma_diag_kernel<<<1, 128, smem, st>>>(mode, a, b, d, n, dev.status);
+  return check_launch();
+}
+
+}  // namespace ct

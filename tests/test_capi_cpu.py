@@ -1,0 +1,118 @@
+"""CPU tests of the boundary: the C-ABI library loads and exports every symbol
+include/ct_b200.h declares; the torch extension registers the reference's
+operator schemas verbatim; fake (meta) kernels give the reference's shapes.
+No compute is launched (no GPU here)."""
+import ctypes
+import re
+
+import pytest
+import torch
+
+import cuda_transformer_b200 as cb
+
+from .conftest import ROOT
+
+REFERENCE_SCHEMAS = {
+    # Transformer_launchers/*.cu m.def(...) strings
+    "cuda_fma": "cuda_fma(Tensor x, Tensor weights, Tensor bias) -> Tensor",
+    "db_calculation": "db_calculation(Tensor dy) -> Tensor",
+    "cuda_softmax": "cuda_softmax(Tensor x) -> Tensor",
+    "cuda_softmax_bwd": "cuda_softmax_bwd(Tensor probs, Tensor dp) -> Tensor",
+    "gelu_activation": "gelu_activation(Tensor x) -> Tensor",
+    "gelu_activation_bwd": "gelu_activation_bwd(Tensor x, Tensor dy) -> Tensor",
+    "flash_attention_fwd":
+        "flash_attention_fwd(Tensor Q, Tensor K, Tensor V, bool causal) -> (Tensor, Tensor)",
+    "flash_attention_bwd":
+        "flash_attention_bwd(Tensor Q, Tensor K, Tensor V, Tensor O, Tensor dO, Tensor L, "
+        "bool causal) -> (Tensor, Tensor, Tensor)",
+    "causal_self_attention_fwd":
+        "causal_self_attention_fwd(Tensor qkv, int nh, bool causal) -> (Tensor, Tensor)",
+    "causal_self_attention_bwd":
+        "causal_self_attention_bwd(Tensor Q, Tensor K, Tensor V, Tensor probs, Tensor dO) -> "
+        "(Tensor, Tensor, Tensor)",
+}
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "ct_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ct_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = cb.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in ct_b200.h but not exported"
+    assert set(syms) == set(cb.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_status_strings_and_version():
+    lib = cb.lib()
+    assert lib.ct_version() >= 10000
+    assert cb.status_string(cb.CT_ERR_UNSUPPORTED_HEAD_DIM).startswith("Unsupported head dimension")
+    for rc in range(0, 9):
+        assert cb.status_string(rc)
+
+
+def test_workspace_queries():
+    lib = cb.lib()
+    assert lib.ct_fa2_bwd_workspace_size(4, 32, 4096, 64) == 4 * 32 * 4096 * 4
+    assert lib.ct_bias_grad_workspace_size(1, 16384, 1536) >= 1536 * 4
+    assert lib.ct_layernorm_bwd_workspace_size(16384, 384) >= 2 * 384 * 4
+
+
+def test_invalid_arguments_rejected_before_any_device_work():
+    lib = cb.lib()
+    s = (ctypes.c_int64 * 4)(1, 1, 1, 1)
+    # head_dim 48 is unsupported: rejected during validation
+    rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, 1, 1, 8, 48, 0, 0, None)
+    assert rc == cb.CT_ERR_UNSUPPORTED_HEAD_DIM
+    rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, -1, 1, 8, 64, 0, 0, None)
+    assert rc == cb.CT_ERR_INVALID_ARGUMENT
+    rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, 1, 1, 8, 64, 0, 7, None)
+    assert rc == cb.CT_ERR_INVALID_ARGUMENT
+
+
+def test_torch_schemas_match_reference():
+    import cuda_transformer  # noqa: F401  (loads _C)
+    for name, schema in REFERENCE_SCHEMAS.items():
+        op = getattr(torch.ops.cuda_transformer, name).default
+        assert str(op._schema) == "cuda_transformer::" + schema
+
+
+def test_ops_module_surface():
+    from cuda_transformer import ops
+    for name in ["cuda_fma", "db_calculation", "cuda_softmax", "cuda_softmax_bwd",
+                 "gelu_activation", "gelu_activation_bwd", "causal_self_attention_fwd",
+                 "causal_self_attention_bwd", "flash_attention_fwd", "flash_attention_bwd"]:
+        assert callable(getattr(ops, name)) and name in ops.__all__
+    import cuda_autograd_fns
+    for name in ['CudaCausalSelfAttention', 'CudaFlashAttention', 'CudaGeluLayer',
+                 'CudaLinearLayer', 'CudaSoftmaxLayer']:
+        assert issubclass(getattr(cuda_autograd_fns, name), torch.autograd.Function)
+
+
+def test_fake_kernels_give_reference_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from cuda_transformer import ops
+    with FakeTensorMode():
+        q = torch.empty(2, 4, 33, 64)
+        o, l = ops.flash_attention_fwd(q, q, q, True)
+        assert o.shape == (2, 4, 33, 64) and l.shape == (2, 4, 33)
+        dq, dk, dv = ops.flash_attention_bwd(q, q, q, o, o, l, True)
+        assert dq.shape == q.shape and dk.shape == q.shape and dv.shape == q.shape
+        x = torch.empty(3, 5, 7)
+        w = torch.empty(7, 11)
+        assert ops.cuda_fma(x, w, torch.empty(11)).shape == (3, 5, 11)
+        assert ops.db_calculation(torch.empty(3, 5, 11)).shape == (11,)
+        y, m, r = ops.layernorm_fwd(torch.empty(6, 384), torch.empty(384), torch.empty(384))
+        assert y.shape == (6, 384) and m.shape == (6,) and r.shape == (6,)
+
+
+def test_product_path_does_not_import_oracle():
+    for pkg in ("cuda_transformer", "cuda_autograd_fns", "cuda_transformer_b200"):
+        for f in (ROOT / pkg).rglob("*.py"):
+            src = f.read_text()
+            assert "import oracle" not in src and "from oracle" not in src, f

@@ -1,0 +1,59 @@
+"""On-device checks of the tensor-core operand layouts the kernels rely on
+(K-major / MN-major shared-memory operands in the 128-byte swizzle, A from
+Tensor Memory) and of how the tensor core treats the low mantissa bits of an
+FP32 operand (the 3xTF32 split writes explicit TF32 hi/lo values, so it is
+correct either way; this records which rule the hardware applies)."""
+import pytest
+import torch
+
+from . import ct_helpers as H
+
+MODES = {0: "ss_kk", 1: "ss_k_mn", 2: "ts_k", 3: "ts_mn", 4: "ss_mn_mn"}
+
+
+def _tf32_exact(shape, gen, device):
+    x = torch.randn(*shape, generator=gen, dtype=torch.float32)
+    x = (x.view(torch.int32) & ~0x1FFF).view(torch.float32)  # low 13 bits zero: exact in TF32
+    return x.to(device)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", sorted(MODES))
+@pytest.mark.parametrize("n", [32, 64, 128])
+def test_umma_layouts(cuda_device, mode, n):
+    g = torch.Generator().manual_seed(100 + 10 * mode + n)
+    if mode == 4:
+        a = _tf32_exact((32, 128), g, cuda_device)      # [k][m]
+        amat = a.t()
+    else:
+        a = _tf32_exact((128, 32), g, cuda_device)      # [m][k]
+        amat = a
+    if mode in (1, 3, 4):
+        b = _tf32_exact((32, n), g, cuda_device)        # [k][n]
+        bmat = b
+    else:
+        b = _tf32_exact((n, 32), g, cuda_device)        # [n][k]
+        bmat = b.t()
+    d = H.diag_umma(mode, a.contiguous(), b.contiguous(), n)
+    ref = amat.double() @ bmat.double()
+    assert H.rel_err(d, ref) < 1e-6, MODES[mode]
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+def test_tf32_operand_rounding_rule(cuda_device, record_property):
+    """A holds values whose 13 low mantissa bits are set; B is the identity, so
+    D shows the TF32 value the tensor core used for each A element."""
+    base = torch.linspace(1.0, 2.0, 128 * 32).reshape(128, 32)
+    bits = base.view(torch.int32) | 0x1FFF | 0x1000  # above the half-way point of a TF32 ulp
+    a = bits.view(torch.float32).contiguous()
+    b = torch.zeros(32, 32)
+    b.fill_diagonal_(1.0)
+    d = H.diag_umma(0, a.to(cuda_device), b.to(cuda_device), 32).cpu()
+    trunc = (a.view(torch.int32) & ~0x1FFF).view(torch.float32)
+    is_trunc = torch.equal(d, trunc)
+    is_round = torch.equal(d, (trunc.double() + 2.0 ** -10 * 2.0 ** torch.floor(torch.log2(trunc.double()))).float())
+    record_property("tf32_operand_rule", "truncate" if is_trunc else ("round" if is_round else "other"))
+    print("tf32 operand rule:", "truncate" if is_trunc else ("round" if is_round else "other"))
+    assert is_trunc or is_round
+    H.assert_device_clean()

@@ -1,0 +1,180 @@
+"""GPU parity of the FlashAttention-2 kernels through the C ABI against the
+NumPy FP64 oracle (oracle/fa2.py), on the reference test grid, BASELINE
+config 1, the committed golden vectors, gpt.py-style strided views and a
+config-2-length subset.  Tolerances (max |err| / max |ref|):
+  3xTF32 (default)  1e-4 relative   (north star; plus the reference tests'
+                                      absolute atol 1e-5 on O/L, 1e-4 on grads)
+  TF32              2e-3 relative
+  FP32 (CUDA cores) 1e-5 relative"""
+import numpy as np
+import pytest
+import torch
+
+import cuda_transformer_b200 as cb
+from oracle import fa2 as orc
+
+from . import ct_helpers as H
+from .conftest import ROOT
+
+TOL = {cb.PRECISION_3XTF32: 1e-4, cb.PRECISION_TF32: 2e-3, cb.PRECISION_FP32: 1e-5}
+PRECISIONS = [cb.PRECISION_3XTF32, cb.PRECISION_TF32, cb.PRECISION_FP32]
+
+REF_GRID = [
+    (1, 1, 64, 128, False), (1, 1, 64, 128, True), (1, 1, 65, 64, True),
+    (2, 4, 128, 32, False), (2, 4, 128, 64, True), (2, 4, 257, 64, True),
+    (1, 2, 512, 128, True),
+]
+
+
+def _rand(shape, seed, dev, uniform=False):
+    g = torch.Generator().manual_seed(seed)
+    t = torch.rand(*shape, generator=g) if uniform else torch.randn(*shape, generator=g)
+    return t.to(dev)
+
+
+def _check_fwd_bwd(q, k, v, do, causal, prec, bwd=True):
+    o, lse = H.fa2_fwd(q, k, v, causal, prec)
+    qn, kn, vn, don = (t.detach().cpu().double().numpy() for t in (q, k, v, do))
+    o_ref, l_ref = orc.attention_fwd(qn, kn, vn, causal)
+    tol = TOL[prec]
+    assert H.rel_err(o, o_ref) < tol, ("O", H.rel_err(o, o_ref))
+    assert H.rel_err(lse, l_ref) < tol, ("LSE", H.rel_err(lse, l_ref))
+    if prec == cb.PRECISION_3XTF32:  # the reference tests' absolute tolerances
+        assert np.abs(o.cpu().double().numpy() - o_ref).max() < 1e-5
+        assert np.abs(lse.cpu().double().numpy() - l_ref).max() < 1e-5
+    if not bwd:
+        return
+    dq, dk, dv = H.fa2_bwd(q, k, v, o, do, lse, causal, prec)
+    refs = orc.attention_bwd(qn, kn, vn, o_ref, don, l_ref, causal)
+    for name, got, ref in zip(("dQ", "dK", "dV"), (dq, dk, dv), refs):
+        assert H.rel_err(got, ref) < tol, (name, H.rel_err(got, ref))
+        if prec == cb.PRECISION_3XTF32:
+            assert np.abs(got.cpu().double().numpy() - ref).max() < 1e-4, name
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", PRECISIONS)
+@pytest.mark.parametrize("B,Hh,T,D,causal", REF_GRID)
+def test_reference_grid(cuda_device, prec, B, Hh, T, D, causal):
+    q, k, v = (_rand((B, Hh, T, D), s, cuda_device) for s in (1, 2, 3))
+    do = _rand((B, Hh, T, D), 4, cuda_device, uniform=True)  # the reference test uses U[0,1)
+    _check_fwd_bwd(q, k, v, do, causal, prec)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", PRECISIONS)
+@pytest.mark.parametrize("causal", [True, False])
+def test_baseline_config1(cuda_device, prec, causal):
+    """B=2, H=4, N=256, D=64; Q, K, V, dO ~ N(0,1) drawn in that order from seed 0."""
+    torch.manual_seed(0)
+    q, k, v, do = (torch.randn(2, 4, 256, 64).to(cuda_device) for _ in range(4))
+    _check_fwd_bwd(q, k, v, do, causal, prec)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", PRECISIONS)
+@pytest.mark.parametrize("T,D", [(1, 64), (15, 64), (17, 32), (127, 64), (129, 64), (200, 32),
+                                 (300, 128)])
+def test_ragged_lengths(cuda_device, prec, T, D):
+    q, k, v, do = (_rand((1, 3, T, D), 10 + s, cuda_device) for s in range(4))
+    for causal in (True, False):
+        _check_fwd_bwd(q, k, v, do, causal, prec)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_gpt_strided_views(cuda_device, prec):
+    """gpt/gpt.py:104-107 passes q, k, v as transposed views of one (B, T, 3C)
+    projection; the kernels read those strides directly."""
+    B, T, nh, hs = 2, 256, 4, 64
+    C = nh * hs
+    qkv = _rand((B, T, 3 * C), 21, cuda_device)
+    q, k, v = (t.reshape(B, T, nh, hs).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+    assert not q.is_contiguous()
+    do = _rand((B, nh, T, hs), 22, cuda_device)
+    _check_fwd_bwd(q, k, v, do, True, prec)
+
+
+@pytest.mark.gpu
+def test_golden_vectors(cuda_device):
+    z = np.load(ROOT / "tests" / "golden" / "fa2_golden.npz")
+    for n in sorted({k.split("/")[0] for k in z.files}):
+        causal = bool(z[f"{n}/causal"])
+        q, k, v, do = (torch.from_numpy(z[f"{n}/{x}"]).to(cuda_device) for x in ("q", "k", "v", "do"))
+        o, lse = H.fa2_fwd(q, k, v, causal)
+        dq, dk, dv = H.fa2_bwd(q, k, v, o, do, lse, causal)
+        for name, got in (("o", o), ("lse", lse), ("dq", dq), ("dk", dk), ("dv", dv)):
+            assert H.rel_err(got, z[f"{n}/{name}"]) < 1e-4, (n, name)
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
+def test_no_out_of_bounds_writes(cuda_device, prec):
+    """Outputs placed inside guard bands of NaN sentinels; ragged T so the last
+    tiles are partial.  compute-sanitizer is not available on this pool, so the
+    guard bands stand in for it."""
+    B, Hh, T, D = 2, 3, 200, 64
+    q, k, v, do = (_rand((B, Hh, T, D), 30 + s, cuda_device) for s in range(4))
+    pad = 4096
+    numel = B * Hh * T * D
+
+    def guarded(n):
+        buf = torch.full((n + 2 * pad,), float("nan"), device=cuda_device)
+        return buf, buf[pad:pad + n]
+
+    ob, o = guarded(numel)
+    lb, lse = guarded(B * Hh * T)
+    o, lse = o.view(B, Hh, T, D), lse.view(B, Hh, T)
+    rc = cb.lib().ct_fa2_fwd(H._p(q), cb.strides(q), H._p(k), cb.strides(k), H._p(v),
+                             cb.strides(v), H._p(o), H._p(lse), B, Hh, T, D, 1, prec, H._stream())
+    cb.check(rc)
+    grads = [guarded(numel) for _ in range(3)]
+    dq, dk, dv = (g[1].view(B, Hh, T, D) for g in grads)
+    ws = torch.empty(B * Hh * T * 4, dtype=torch.uint8, device=cuda_device)
+    rc = cb.lib().ct_fa2_bwd(H._p(q), cb.strides(q), H._p(k), cb.strides(k), H._p(v),
+                             cb.strides(v), H._p(o), cb.strides(o), H._p(do), cb.strides(do),
+                             H._p(lse), cb.strides(lse), H._p(dq), H._p(dk), H._p(dv), H._p(ws),
+                             ws.numel(), B, Hh, T, D, 1, prec, H._stream())
+    cb.check(rc)
+    torch.cuda.synchronize()
+    for buf, inner in [(ob, o), (lb, lse)] + [(g[0], t) for g, t in zip(grads, (dq, dk, dv))]:
+        assert torch.isnan(buf[:pad]).all() and torch.isnan(buf[-pad:]).all()
+        assert torch.isfinite(inner).all()
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_deterministic(cuda_device, prec):
+    """Atomics-free backward: bit-identical results run to run."""
+    q, k, v, do = (_rand((2, 4, 384, 64), 40 + s, cuda_device) for s in range(4))
+    o1, l1 = H.fa2_fwd(q, k, v, True, prec)
+    g1 = H.fa2_bwd(q, k, v, o1, do, l1, True, prec)
+    o2, l2 = H.fa2_fwd(q, k, v, True, prec)
+    g2 = H.fa2_bwd(q, k, v, o2, do, l2, True, prec)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
+def test_config2_length_subset(cuda_device, prec):
+    """BASELINE config 2 sequence length (N=4096, D=64, causal) on 2 (b,h)
+    pairs, compared in full with the FP64 oracle."""
+    q, k, v, do = (_rand((1, 2, 4096, 64), 50 + s, cuda_device) for s in range(4))
+    _check_fwd_bwd(q, k, v, do, True, prec)
+
+
+@pytest.mark.gpu
+def test_delta_kernel(cuda_device):
+    o, do = (_rand((2, 3, 77, 64), 60 + s, cuda_device) for s in range(2))
+    d = H.fa2_delta(o, do)
+    ref = orc.attention_bwd_delta(o.cpu().numpy(), do.cpu().numpy())
+    assert H.rel_err(d, ref) < 1e-6
+    # strided inputs (non-unit head-dim stride)
+    ot = o.transpose(2, 3).contiguous().transpose(2, 3)
+    d2 = H.fa2_delta(ot, do)
+    assert H.rel_err(d2, ref) < 1e-6
