@@ -78,7 +78,7 @@ bool tma_compatible(const void* base, int64_t inner_stride, const int64_t* outer
 }
 
 int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                  const uint64_t* strides_bytes, const uint32_t* box) {
+                  const uint64_t* strides_bytes, const uint32_t* box, bool mn_major) {
   std::call_once(g_encode_once, load_encode);
   if (!g_encode) return CT_ERR_CUDA;
   cuuint64_t gd[5];
@@ -97,7 +97,8 @@ int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* 
   }
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
                         const_cast<void*>(base), gd, gs, bd, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? CT_OK : CT_ERR_UNSUPPORTED_LAYOUT;
 }

@@ -24,11 +24,13 @@ struct DeviceInfo {
 const DeviceInfo* current_device(int* err);
 
 // Encodes a TMA descriptor for an FP32 tensor of rank 3 or 4 with a 32-float
-// (128-byte) inner box and CU_TENSOR_MAP_SWIZZLE_128B.  dims[0] is the
-// contiguous dimension; strides_bytes[i] is the stride of dims[i + 1].
-// Returns CT_OK or CT_ERR_UNSUPPORTED_LAYOUT when TMA cannot address it.
+// (128-byte) inner box.  `mn_major` selects CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+// (tiles the tensor core reads MN-major) instead of CU_TENSOR_MAP_SWIZZLE_128B
+// (tiles read K-major).  dims[0] is the contiguous dimension; strides_bytes[i]
+// is the stride of dims[i + 1].  Returns CT_OK or CT_ERR_UNSUPPORTED_LAYOUT
+// when TMA cannot address the tensor.
 int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                  const uint64_t* strides_bytes, const uint32_t* box);
+                  const uint64_t* strides_bytes, const uint32_t* box, bool mn_major = false);
 
 // True when a float tensor with these element strides (innermost first
 // omitted) can be described by a TMA map: unit inner stride, 16-byte aligned

@@ -1,20 +1,685 @@
-// fa2_bwd_tc.cu -- tensor-core FlashAttention-2 backward.  Not wired yet:
-// every problem is reported unsupported so the C ABI uses the CUDA-core path.
-#include "ct_internal.h"
+// fa2_bwd_tc.cu -- FlashAttention-2 backward on the sm_100a tensor cores,
+// atomics-free like the reference (flash_attention.cuh:216-504): a
+// query-stationary kernel produces dQ and a key/value-stationary kernel
+// produces dK and dV, each recomputing P = exp(S - L) and dP = dO V^T.
+// Unlike flash_attention_bwd_dk_dv (:409-411) the dK/dV pass starts at the
+// causal diagonal instead of scanning every query tile.
+//
+// Warp roles as in the forward: warp 0 TMA producer, warp 1 TMEM allocator and
+// MMA issuer, warps 2-3 TF32 hi/lo split (SPLIT == 3), warps 4-7 row warps
+// (one stationary row per thread / TMEM lane).
+//
+// dQ kernel, per 128 query rows, per key tile j (BN keys):
+//   S  = Q K_j^T     (A = Q in TMEM, B = K_j K-major)
+//   dP = dO V_j^T    (A = dO in TMEM, B = V_j K-major)
+//   dS = P * (dP - delta), P = exp2(S * log2e / sqrt(D) - L * log2e)   [row warps]
+//   dQ += dS K_j     (A = dS in TMEM, B = K_j read MN-major)
+// dK/dV kernel, per 128 key rows, per query tile j (BN queries):
+//   S^T  = K Q_j^T,  dP^T = V dO_j^T,  P^T, dS^T in the row warps
+//   dV += P^T dO_j,  dK += dS^T Q_j   (B = Q_j / dO_j read MN-major)
+// The MMA issuer runs one phase ahead of the row warps (S_{j+1} while dS_j is
+// formed), ordering reuse of the single S / dP buffers by issue order.
+#include "fa2_common.cuh"
 
 namespace ct {
+namespace {
 
-bool fa2_bwd_tc_supported(const Fa2Problem&) { return false; }
+using namespace fa2;
 
-int launch_fa2_bwd_dq_tc(const Fa2Problem&, Strided4, Strided4, Strided4, Strided4, const float*,
-                         const int64_t*, const float*, float*, const DeviceInfo&, cudaStream_t) {
-  return CT_ERR_INVALID_ARGUMENT;
+// ------------------------------------------------------------ configuration
+// A stage holds the two streamed tiles of one step (dQ pass: K_j and V_j;
+// dK/dV pass: Q_j and dO_j).  A tile the tensor core reads both K-major and
+// MN-major is loaded twice, once per shared-memory layout (the TF32 MN-major
+// operand layout differs from the K-major one).  Per stage, in order:
+//   A K-major [raw, lo] | A MN-major [raw, lo] (LA == 2) | B K-major [raw, lo] |
+//   B MN-major [raw, lo] (LB == 2), the lo copies present when SPLIT == 3.
+template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_>
+struct BwdTiles {
+  static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, LA = LA_, LB = LB_;
+  static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
+  static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;
+  static constexpr uint32_t OFF_A0 = 0, OFF_A1 = NCOPY * TILE;
+  static constexpr uint32_t OFF_B0 = LA * NCOPY * TILE, OFF_B1 = OFF_B0 + NCOPY * TILE;
+  static constexpr uint32_t STAGE = (LA + LB) * NCOPY * TILE;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+// dQ pass: A = K (K-major for S, MN-major for dQ), B = V (K-major for dP).
+template <int D_, int BN_, int SPLIT_, int NS_>
+struct DqCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1>;
+  static constexpr uint32_t TC_Q = 0, TC_G = T_::NCOPY * D_, TC_DQ = 2 * T_::NCOPY * D_;
+  static constexpr uint32_t TC_S = TC_DQ + D_, TC_DP = TC_S + BN_, TC_DSL = TC_DP + BN_;
+  static_assert(TC_DP + T_::NCOPY * BN_ <= T_::TMEM_COLS, "TMEM budget");
+};
+
+template <int NS>
+struct BwdBars {
+  uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
+  uint64_t s_full, dp_full, s_free, p_full, ds_full, rows_ready, done, mma_final;
+  CtaCtl ctl;
+};
+
+struct BwdParams {
+  Ptr4 st0, st1;       // stationary operands (dQ: Q, dO; dK/dV: K, V)
+  const float* lse;
+  int64_t l0, l1, l2;
+  const float* delta;  // contiguous [B,H,T]
+  float* out0;         // dQ | dK
+  float* out1;         // -  | dV
+  int H, T, n_tiles, bh_total, causal;
+  float scale_log2, scale;
+  uint32_t* status;
+};
+
+template <class C>
+constexpr size_t bwd_smem_bytes() {
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
 }
 
-int launch_fa2_bwd_dkdv_tc(const Fa2Problem&, Strided4, Strided4, Strided4, Strided4,
-                           const float*, const int64_t*, const float*, float*, float*,
-                           const DeviceInfo&, cudaStream_t) {
-  return CT_ERR_INVALID_ARGUMENT;
+template <class C>
+__device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars) {
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  for (int s = 0; s < C::NS; ++s) {
+    mbar_init(B(bars->full_a[s]), 1);
+    mbar_init(B(bars->full_b[s]), 1);
+    mbar_init(B(bars->ready_a[s]), kSplitThreads);
+    mbar_init(B(bars->ready_b[s]), kSplitThreads);
+    mbar_init(B(bars->empty_a[s]), 1);
+    mbar_init(B(bars->empty_b[s]), 1);
+  }
+  mbar_init(B(bars->s_full), 1);
+  mbar_init(B(bars->dp_full), 1);
+  mbar_init(B(bars->s_free), 128);
+  mbar_init(B(bars->p_full), 128);
+  mbar_init(B(bars->ds_full), 128);
+  mbar_init(B(bars->rows_ready), 128);
+  mbar_init(B(bars->done), 1);
+  mbar_init(B(bars->mma_final), 1);
+  bars->ctl.abort = 0;
+  fence_barrier_init();
+}
+
+// TMA producer: tiles j0..j1-1 of two [B,H,T,D] tensors into the stage ring;
+// maps[0..1] = A in the K-major / MN-major layouts, maps[2..3] = B likewise.
+template <class C>
+__device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles,
+                                             const CUtensorMap* const* maps, int j0, int j1,
+                                             int h, int b, uint32_t* status) {
+  constexpr int NS = C::NS, BN = C::BN, D = C::D;
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  CtaCtl* ctl = &bars->ctl;
+  for (int m = 0; m < 4; ++m)
+    if (maps[m]) tma_prefetch_desc(maps[m]);
+  int last_a[NS], last_b[NS];
+  for (int s = 0; s < NS; ++s) last_a[s] = last_b[s] = -1;
+  for (int j = j0; j < j1; ++j) {
+    const int i = j - j0, s = i % NS, r = i / NS;
+    const uint32_t st = tiles + s * C::STAGE;
+    if (r > 0 && !mbar_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
+    mbar_arrive_expect_tx(B(bars->full_a[s]), C::LA * C::TILE);
+#pragma unroll
+    for (int l = 0; l < C::LA; ++l)
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tma_load_4d(st + (l ? C::OFF_A1 : C::OFF_A0) + c * BN * 128, maps[l], B(bars->full_a[s]),
+                    32 * c, j * BN, h, b);
+    last_a[s] = r;
+    if (r > 0 && !mbar_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
+    mbar_arrive_expect_tx(B(bars->full_b[s]), C::LB * C::TILE);
+#pragma unroll
+    for (int l = 0; l < C::LB; ++l)
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tma_load_4d(st + (l ? C::OFF_B1 : C::OFF_B0) + c * BN * 128, maps[2 + l],
+                    B(bars->full_b[s]), 32 * c, j * BN, h, b);
+    last_b[s] = r;
+  }
+  if (ctl->abort) {
+    for (int s = 0; s < NS; ++s) {
+      if (last_a[s] >= 0) mbar_drain(B(bars->full_a[s]), last_a[s] & 1);
+      if (last_b[s] >= 0) mbar_drain(B(bars->full_b[s]), last_b[s] & 1);
+    }
+  }
+}
+
+template <class C>
+__device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
+                                             uint32_t* status) {
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
+  for (int i = 0; i < n; ++i) {
+    const int s = i % C::NS, r = i / C::NS;
+    const uint32_t st = tiles + s * C::STAGE;
+    if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
+    for (int l = 0; l < C::LA; ++l) {
+      const uint32_t t = st + (l ? C::OFF_A1 : C::OFF_A0);
+      split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(B(bars->ready_a[s]));
+    if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
+    for (int l = 0; l < C::LB; ++l) {
+      const uint32_t t = st + (l ? C::OFF_B1 : C::OFF_B0);
+      split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(B(bars->ready_b[s]));
+  }
+}
+
+// Issues D(+)= A(TMEM, K columns) x B over K = kdim in steps of 8, with the
+// 3xTF32 hi/lo terms when SPLIT == 3.  b_desc(k) / b_lo_desc(k) give the B
+// descriptors of k-step k.
+template <int SPLIT, int KDIM, class FB, class FBL>
+__device__ __forceinline__ void mma_ts_chain(uint32_t d, uint32_t a_hi, uint32_t a_lo,
+                                             uint32_t idesc, bool accumulate, FB b_desc,
+                                             FBL b_lo_desc) {
+#pragma unroll
+  for (int k = 0; k < KDIM / 8; ++k) {
+    const uint64_t bh = b_desc(k);
+    umma_tf32_ts(d, a_hi + 8 * k, bh, idesc, (accumulate || k > 0) ? 1u : 0u);
+    if constexpr (SPLIT == 3) {
+      umma_tf32_ts(d, a_hi + 8 * k, b_lo_desc(k), idesc, 1u);
+      umma_tf32_ts(d, a_lo + 8 * k, bh, idesc, 1u);
+    }
+  }
+}
+
+template <class C>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmKmn,
+                         const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(BwdBars<NS>) + 1023u) & ~1023u;
+  CtaCtl* ctl = &bars->ctl;
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  const int qt = p.n_tiles - 1 - (int)(blockIdx.x / p.bh_total);  // heavy tiles first
+  const int bh = (int)(blockIdx.x % p.bh_total);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qt * kRows, T = p.T;
+  const int last_row = min(q0 + kRows - 1, T - 1);
+  const int n_kv = p.causal ? last_row / BN + 1 : (T + BN - 1) / BN;
+
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const CUtensorMap* maps[4] = {&tmK, &tmKmn, &tmV, nullptr};
+      bwd_producer<C>(bars, tiles, maps, 0, n_kv, h, b, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      constexpr uint32_t idQ = idesc_tf32(128, D, false, true);
+      auto kt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A0; };
+      auto kmn = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A1; };
+      auto vt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_B0; };
+      auto& rk = SPLIT == 3 ? bars->ready_a : bars->full_a;
+      auto& rv = SPLIT == 3 ? bars->ready_b : bars->full_b;
+      auto issue_S = [&](int j) {
+        const uint32_t base = kt(j);
+        mma_ts_chain<SPLIT, D>(
+            tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D, idS, false,
+            [&](int k) { return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32); },
+            [&](int k) { return sdesc_kmajor(base + C::TILE + (k / 4) * BN * 128 + (k % 4) * 32); });
+        umma_commit(B(bars->s_full));
+      };
+      auto issue_dP = [&](int j) {
+        const uint32_t base = vt(j);
+        mma_ts_chain<SPLIT, D>(
+            tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D, idS, false,
+            [&](int k) { return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32); },
+            [&](int k) { return sdesc_kmajor(base + C::TILE + (k / 4) * BN * 128 + (k % 4) * 32); });
+        umma_commit(B(bars->empty_b[j % NS]));
+        umma_commit(B(bars->dp_full));
+      };
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      if (ok) {
+        tc_fence_after();
+        ok = mbar_wait(B(rk[0]), 0, ctl, p.status);
+        if (ok) { tc_fence_after(); issue_S(0); }
+        if (ok) ok = mbar_wait(B(rv[0]), 0, ctl, p.status);
+        if (ok) { tc_fence_after(); issue_dP(0); }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          if (j + 1 < n_kv) {  // S_{j+1} once the row warps hold S_j in registers
+            if (!(ok = mbar_wait(B(bars->s_free), j & 1, ctl, p.status))) break;
+            if (!(ok = mbar_wait(B(rk[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_S(j + 1);
+          }
+          if (!(ok = mbar_wait(B(bars->ds_full), j & 1, ctl, p.status))) break;
+          tc_fence_after();
+          const uint32_t base = kmn(j);
+          mma_ts_chain<SPLIT, BN>(
+              tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL, idQ, j > 0,
+              [&](int k) { return sdesc_mnmajor(base + k * 1024, BN * 128); },
+              [&](int k) { return sdesc_mnmajor(base + C::TILE + k * 1024, BN * 128); });
+          umma_commit(B(bars->empty_a[j % NS]));
+          if (j + 1 < n_kv) {
+            if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_dP(j + 1);
+          }
+        }
+        if (ok) umma_commit(B(bars->done));
+      }
+      umma_commit(B(bars->mma_final));
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp < kRowWarp0) {
+    if constexpr (SPLIT == 3) bwd_splitter<C>(bars, tiles, n_kv, p.status);
+  } else {
+    const int quad = warp & 3;
+    const int row = q0 + quad * 32 + lane;
+    const bool valid = row < T;
+    const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    float l2 = 0.0f, dl = 0.0f;
+    {
+      const float* qr = p.st0.row(b, h, valid ? row : 0);
+      const float* gr = p.st1.row(b, h, valid ? row : 0);
+      const bool vq = p.st0.s3 == 1 && ((reinterpret_cast<uintptr_t>(qr) & 15u) == 0);
+      const bool vg = p.st1.s3 == 1 && ((reinterpret_cast<uintptr_t>(gr) & 15u) == 0);
+      row_to_tmem<D, SPLIT>(p.st0, qr, valid, vq, lb, C::TC_Q);
+      row_to_tmem<D, SPLIT>(p.st1, gr, valid, vg, lb, C::TC_G);
+      if (valid) {
+        l2 = __ldg(p.lse + b * p.l0 + h * p.l1 + (int64_t)row * p.l2) * kLog2e;
+        dl = __ldg(p.delta + (int64_t)bh * T + row);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->rows_ready));
+    }
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!(ok = warp_wait(B(bars->s_full), j & 1, ctl, p.status))) break;
+      tc_fence_after();
+      float pv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        tmem_ld32(lb + C::TC_S + 32 * c, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pv[32 * c + i] = t[i];
+      }
+      tc_fence_before();
+      mbar_arrive(B(bars->s_free));
+      const int kv0 = j * BN;
+      const bool need_mask = !valid || (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        float e = ex2_approx(pv[i] * p.scale_log2 - l2);
+        if (need_mask) {
+          const int kv = kv0 + i;
+          if (!(valid && kv < T && (!p.causal || kv <= row))) e = 0.0f;
+        }
+        pv[i] = e;
+      }
+      if (!(ok = warp_wait(B(bars->dp_full), j & 1, ctl, p.status))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32], lo[32];
+        tmem_ld32(lb + C::TC_DP + 32 * c, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float ds = pv[32 * c + i] * (t[i] - dl);
+          if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
+          else t[i] = ds;
+        }
+        tmem_st32(lb + C::TC_DP + 32 * c, t);
+        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->ds_full));
+    }
+    if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
+      tc_fence_after();
+      tmem_row_to_global<D>(lb, C::TC_DQ, p.scale, p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D,
+                            valid);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// -------------------------------------------------------------- dK/dV pass
+// dK/dV pass: A = Q (K-major for S^T, MN-major for dK), B = dO (K-major for
+// dP^T, MN-major for dV).
+template <int D_, int BN_, int SPLIT_, int NS_>
+struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2>;
+  static constexpr uint32_t TC_K = 0, TC_V = T_::NCOPY * D_, TC_DK = 2 * T_::NCOPY * D_;
+  static constexpr uint32_t TC_DV = TC_DK + D_, TC_S = TC_DV + D_, TC_PL = TC_S + BN_;
+  static constexpr uint32_t TC_DP = TC_S + T_::NCOPY * BN_, TC_DSL = TC_DP + BN_;
+  static_assert(TC_DP + T_::NCOPY * BN_ <= T_::TMEM_COLS, "TMEM budget");
+};
+
+template <class C>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                           const __grid_constant__ CUtensorMap tmQmn,
+                           const __grid_constant__ CUtensorMap tmG,
+                           const __grid_constant__ CUtensorMap tmGmn, const BwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(BwdBars<NS>) + 1023u) & ~1023u;
+  CtaCtl* ctl = &bars->ctl;
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  const int kt_ = (int)(blockIdx.x / p.bh_total);  // causal: low key tiles are heaviest
+  const int bh = (int)(blockIdx.x % p.bh_total);
+  const int b = bh / p.H, h = bh % p.H;
+  const int k0 = kt_ * kRows, T = p.T;
+  const int j0 = p.causal ? k0 / BN : 0;
+  const int j1 = (T + BN - 1) / BN;
+  const int n = j1 - j0;
+
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
+      bwd_producer<C>(bars, tiles, maps, j0, j1, h, b, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      auto qt = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_A0; };
+      auto gt = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B0; };
+      auto qmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_A1; };
+      auto gmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B1; };
+      auto& rq = SPLIT == 3 ? bars->ready_a : bars->full_a;
+      auto& rg = SPLIT == 3 ? bars->ready_b : bars->full_b;
+      auto kdesc = [&](uint32_t base, int k) {
+        return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32);
+      };
+      auto issue_S = [&](int i) {
+        const uint32_t base = qt(i);
+        mma_ts_chain<SPLIT, D>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D, idS, false,
+                               [&](int k) { return kdesc(base, k); },
+                               [&](int k) { return kdesc(base + C::TILE, k); });
+        umma_commit(B(bars->s_full));
+      };
+      auto issue_dP = [&](int i) {
+        const uint32_t base = gt(i);
+        mma_ts_chain<SPLIT, D>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D, idS, false,
+                               [&](int k) { return kdesc(base, k); },
+                               [&](int k) { return kdesc(base + C::TILE, k); });
+        umma_commit(B(bars->dp_full));
+      };
+      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      if (ok) {
+        tc_fence_after();
+        ok = mbar_wait(B(rq[0]), 0, ctl, p.status);
+        if (ok) { tc_fence_after(); issue_S(0); }
+        if (ok) ok = mbar_wait(B(rg[0]), 0, ctl, p.status);
+        if (ok) { tc_fence_after(); issue_dP(0); }
+        for (int i = 0; ok && i < n; ++i) {
+          if (!(ok = mbar_wait(B(bars->p_full), i & 1, ctl, p.status))) break;
+          tc_fence_after();
+          const uint32_t gb = gmn(i), qb = qmn(i);
+          mma_ts_chain<SPLIT, BN>(  // dV += P^T dO_i
+              tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, idO, i > 0,
+              [&](int k) { return sdesc_mnmajor(gb + k * 1024, BN * 128); },
+              [&](int k) { return sdesc_mnmajor(gb + C::TILE + k * 1024, BN * 128); });
+          if (i + 1 < n) {
+            if (!(ok = mbar_wait(B(rq[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_S(i + 1);
+          }
+          if (!(ok = mbar_wait(B(bars->ds_full), i & 1, ctl, p.status))) break;
+          tc_fence_after();
+          mma_ts_chain<SPLIT, BN>(  // dK += dS^T Q_i
+              tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, idO, i > 0,
+              [&](int k) { return sdesc_mnmajor(qb + k * 1024, BN * 128); },
+              [&](int k) { return sdesc_mnmajor(qb + C::TILE + k * 1024, BN * 128); });
+          umma_commit(B(bars->empty_a[i % NS]));
+          umma_commit(B(bars->empty_b[i % NS]));
+          if (i + 1 < n) {
+            if (!(ok = mbar_wait(B(rg[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_dP(i + 1);
+          }
+        }
+        if (ok) umma_commit(B(bars->done));
+      }
+      umma_commit(B(bars->mma_final));
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp < kRowWarp0) {
+    if constexpr (SPLIT == 3) bwd_splitter<C>(bars, tiles, n, p.status);
+  } else {
+    const int quad = warp & 3;
+    const int row = k0 + quad * 32 + lane;  // key row
+    const bool valid = row < T;
+    const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    {
+      const float* kr = p.st0.row(b, h, valid ? row : 0);
+      const float* vr = p.st1.row(b, h, valid ? row : 0);
+      const bool vk = p.st0.s3 == 1 && ((reinterpret_cast<uintptr_t>(kr) & 15u) == 0);
+      const bool vv = p.st1.s3 == 1 && ((reinterpret_cast<uintptr_t>(vr) & 15u) == 0);
+      row_to_tmem<D, SPLIT>(p.st0, kr, valid, vk, lb, C::TC_K);
+      row_to_tmem<D, SPLIT>(p.st1, vr, valid, vv, lb, C::TC_V);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->rows_ready));
+    }
+    const float* lse_bh = p.lse + b * p.l0 + h * p.l1;
+    const float* del_bh = p.delta + (int64_t)bh * T;
+    bool ok = n > 0;
+    for (int i = 0; ok && i < n; ++i) {
+      const int qs = (j0 + i) * BN;
+      if (!(ok = warp_wait(B(bars->s_full), i & 1, ctl, p.status))) break;
+      tc_fence_after();
+      const bool need_mask = !valid || (qs + BN > T) || (p.causal && qs < k0 + kRows - 1);
+      float pv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32], lo[32], lq[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {  // broadcast loads, L1 resident
+          const int q = qs + 32 * c + x;
+          lq[x] = q < T ? __ldg(lse_bh + (int64_t)q * p.l2) * kLog2e : 0.0f;
+        }
+        tmem_ld32(lb + C::TC_S + 32 * c, t);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const int cc = 32 * c + x;
+          float e = ex2_approx(t[x] * p.scale_log2 - lq[x]);
+          if (need_mask) {
+            const int q = qs + cc;
+            if (!(valid && q < T && (!p.causal || q >= row))) e = 0.0f;
+          }
+          pv[cc] = e;
+          if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
+          else t[x] = e;
+        }
+        tmem_st32(lb + C::TC_S + 32 * c, t);
+        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_PL + 32 * c, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->p_full));
+      if (!(ok = warp_wait(B(bars->dp_full), i & 1, ctl, p.status))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32], lo[32], dlt[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const int q = qs + 32 * c + x;
+          dlt[x] = q < T ? __ldg(del_bh + q) : 0.0f;
+        }
+        tmem_ld32(lb + C::TC_DP + 32 * c, t);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const int cc = 32 * c + x;
+          const float ds = pv[cc] * (t[x] - dlt[x]);
+          if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
+          else t[x] = ds;
+        }
+        tmem_st32(lb + C::TC_DP + 32 * c, t);
+        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B(bars->ds_full));
+    }
+    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
+    if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
+      if (valid) {
+        for (int d = 0; d < D; ++d) p.out0[orow + d] = 0.0f, p.out1[orow + d] = 0.0f;
+      }
+    } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
+      tc_fence_after();
+      tmem_row_to_global<D>(lb, C::TC_DK, p.scale, p.out0 + orow, valid);
+      tmem_row_to_global<D>(lb, C::TC_DV, 1.0f, p.out1 + orow, valid);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+BwdParams make_params(const Fa2Problem& pr, Strided4 a, Strided4 b, const float* lse,
+                      const int64_t ls[3], const float* delta, float* out0, float* out1,
+                      const DeviceInfo& dev) {
+  BwdParams p;
+  p.st0 = Ptr4{a.ptr, a.s[0], a.s[1], a.s[2], a.s[3]};
+  p.st1 = Ptr4{b.ptr, b.s[0], b.s[1], b.s[2], b.s[3]};
+  p.lse = lse;
+  p.l0 = ls[0];
+  p.l1 = ls[1];
+  p.l2 = ls[2];
+  p.delta = delta;
+  p.out0 = out0;
+  p.out1 = out1;
+  p.H = (int)pr.H;
+  p.T = (int)pr.T;
+  p.n_tiles = (int)((pr.T + kRows - 1) / kRows);
+  p.bh_total = (int)(pr.B * pr.H);
+  p.causal = pr.causal ? 1 : 0;
+  p.scale = (float)(1.0 / std::sqrt((double)pr.D));
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
+  p.status = dev.status;
+  return p;
+}
+
+template <class C>
+int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g, const float* lse,
+           const int64_t ls[3], const float* delta, float* dq, const DeviceInfo& dev,
+           cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap tk, tkmn, tv;
+  int rc = make_tmap_bhtd(&tk, k, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tkmn, k, pr, C::BN, /*mn_major=*/true);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tv, v, pr, C::BN);
+  if (rc != CT_OK) return rc;
+  const size_t smem = bwd_smem_bytes<C>();
+  rc = ensure_smem_attr(fa2_bwd_dq_tc_kernel<C>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  BwdParams p = make_params(pr, q, g, lse, ls, delta, dq, nullptr, dev);
+  const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
+  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tk, tkmn, tv, p);
+  return check_launch();
+}
+
+template <class C>
+int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
+             const float* lse, const int64_t ls[3], const float* delta, float* dk, float* dv,
+             const DeviceInfo& dev, cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap tq, tqmn, tg, tgmn;
+  int rc = make_tmap_bhtd(&tq, q, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tqmn, q, pr, C::BN, /*mn_major=*/true);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tg, g, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tgmn, g, pr, C::BN, /*mn_major=*/true);
+  if (rc != CT_OK) return rc;
+  const size_t smem = bwd_smem_bytes<C>();
+  rc = ensure_smem_attr(fa2_bwd_dkdv_tc_kernel<C>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
+  const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
+  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tq, tqmn, tg, tgmn, p);
+  return check_launch();
+}
+
+}  // namespace
+
+bool fa2_bwd_tc_supported(const Fa2Problem& p) {
+  return (p.D == 32 || p.D == 64) &&
+         (p.precision == CT_PRECISION_3XTF32 || p.precision == CT_PRECISION_TF32) &&
+         p.T < (1ll << 31) && ((p.T + kRows - 1) / kRows) * p.B * p.H < (1ll << 31);
+}
+
+int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
+                         const float* lse, const int64_t ls[3], const float* delta, float* dq,
+                         const DeviceInfo& dev, cudaStream_t st) {
+  if (!fa2_tma_ok(k) || !fa2_tma_ok(v)) return CT_ERR_UNSUPPORTED_LAYOUT;
+  const bool split = pr.precision == CT_PRECISION_3XTF32;
+  if (pr.D == 64)
+    return split ? run_dq<DqCfg<64, 64, 3, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
+                 : run_dq<DqCfg<64, 128, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
+  if (pr.D == 32)
+    return split ? run_dq<DqCfg<32, 64, 3, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
+                 : run_dq<DqCfg<32, 128, 1, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
+  return CT_ERR_UNSUPPORTED_HEAD_DIM;
+}
+
+int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
+                           const float* lse, const int64_t ls[3], const float* delta, float* dk,
+                           float* dv, const DeviceInfo& dev, cudaStream_t st) {
+  if (!fa2_tma_ok(q) || !fa2_tma_ok(g)) return CT_ERR_UNSUPPORTED_LAYOUT;
+  const bool split = pr.precision == CT_PRECISION_3XTF32;
+  if (pr.D == 64)
+    return split ? run_dkdv<DkvCfg<64, 32, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
+                 : run_dkdv<DkvCfg<64, 64, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+  if (pr.D == 32)
+    return split ? run_dkdv<DkvCfg<32, 64, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
+                 : run_dkdv<DkvCfg<32, 128, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+  return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
 
 }  // namespace ct

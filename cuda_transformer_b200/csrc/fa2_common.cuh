@@ -121,12 +121,14 @@ __device__ __forceinline__ bool status_raised(const uint32_t* status) {
 
 }  // namespace fa2
 
-// Host helper: TMA map for an FP32 [B,H,T,D] tensor with a {32, rows} box.
-inline int make_tmap_bhtd(CUtensorMap* map, const Strided4& t, const Fa2Problem& p, int rows) {
+// Host helper: TMA map for an FP32 [B,H,T,D] tensor with a {32, rows} box, in
+// the K-major (SWIZZLE_128B) or MN-major (SWIZZLE_128B_ATOM_32B) tile layout.
+inline int make_tmap_bhtd(CUtensorMap* map, const Strided4& t, const Fa2Problem& p, int rows,
+                          bool mn_major = false) {
   const uint64_t dims[4] = {(uint64_t)p.D, (uint64_t)p.T, (uint64_t)p.H, (uint64_t)p.B};
   const uint64_t strides[3] = {(uint64_t)t.s[2] * 4u, (uint64_t)t.s[1] * 4u, (uint64_t)t.s[0] * 4u};
   const uint32_t box[4] = {32u, (uint32_t)rows, 1u, 1u};
-  return make_tmap_f32(map, t.ptr, 4, dims, strides, box);
+  return make_tmap_f32(map, t.ptr, 4, dims, strides, box, mn_major);
 }
 
 inline bool fa2_tma_ok(const Strided4& t) {

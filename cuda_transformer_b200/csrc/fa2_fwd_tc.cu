@@ -12,6 +12,7 @@
 //   warps 2-3   TF32 hi/lo split of each landed K/V tile (SPLIT == 3)
 //   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
 //               epilogue (thread r <-> query row r <-> TMEM lane r)
+// K tiles use the K-major tile layout, V tiles the MN-major one.
 // TMEM columns: Q (hi[,lo]) | O | two S/P buffers (S overwritten by P hi, then
 // P lo).  S_{j+1} = Q K_{j+1}^T runs on the tensor core while the row warps
 // turn S_j into P_j.  O is rescaled only when a row maximum grows by more
@@ -58,6 +59,7 @@ struct FwdParams {
 
 template <class C>
 constexpr size_t fwd_smem_bytes() {
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
   return 1024 + 1024 + (size_t)C::NS * C::STAGE;
 }
 
@@ -324,7 +326,7 @@ int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, 
   CUtensorMap tmK, tmV;
   int rc = make_tmap_bhtd(&tmK, k, pr, C::BN);
   if (rc != CT_OK) return rc;
-  rc = make_tmap_bhtd(&tmV, v, pr, C::BN);
+  rc = make_tmap_bhtd(&tmV, v, pr, C::BN, /*mn_major=*/true);
   if (rc != CT_OK) return rc;
   const size_t smem = fwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_fwd_tc_kernel<C>, smem, dev.device, &attr_done);

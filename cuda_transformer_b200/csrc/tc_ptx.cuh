@@ -198,34 +198,37 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 #undef CT_W8
 
 // --------------------------------------------------- UMMA descriptors
-// Shared-memory matrix descriptor for the 128-byte swizzle layout (the layout
-// TMA writes with CU_TENSOR_MAP_SWIZZLE_128B; atoms of 8 rows x 128 bytes,
-// 1024-byte aligned):
+// Shared-memory matrix descriptor (64-bit):
 //   bits  0-13 start address >> 4      bits 16-29 leading byte offset >> 4
 //   bits 32-45 stride byte offset >> 4 bits 46-47 version (1 on sm_100)
-//   bits 49-51 base offset (0)         bits 61-63 layout (2 = SWIZZLE_128B)
-// K-major operand: rows of 128 bytes (32 fp32 along K); SBO = distance between
-//   8-row groups (1024 when dense), LBO unused (16).  Stepping K by 8 fp32
-//   inside the 128-byte row advances the start address by 32 bytes.
-// MN-major operand: 128-byte rows hold 32 consecutive M (or N) elements, one
-//   row per K index; LBO = distance between consecutive 32-element M/N chunks,
-//   SBO = distance between 8-row K groups (1024).  Stepping K by 8 advances the
-//   start address by 1024 bytes.
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                uint32_t sbo_bytes) {
+//   bits 49-51 base offset (0)         bits 61-63 layout (2 = SWIZZLE_128B,
+//                                                  1 = SWIZZLE_128B_BASE32B)
+// K-major operand (layout 2, the pattern TMA writes with
+//   CU_TENSOR_MAP_SWIZZLE_128B): rows of 128 bytes hold 32 fp32 along K; 16-byte
+//   units are XOR-swizzled with row % 8; SBO = distance between 8-row groups
+//   (1024 when dense), LBO unused (16).  Stepping K by 8 fp32 inside the
+//   128-byte row advances the start address by 32 bytes.
+// MN-major operand (layout 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B; the only
+//   MN-major layout the tensor core accepts for TF32): 128-byte rows hold 32
+//   consecutive M (or N) elements, one row per K index; 32-byte units are
+//   XOR-swizzled with row % 4; LBO = distance between consecutive 32-element
+//   M/N chunks, SBO = distance between 4-row K groups (512 when dense).
+//   Stepping K by 8 advances the start address by 1024 bytes.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                          uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
+  d |= (uint64_t)layout << 61;
   return d;
 }
 __device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr) {
-  return sdesc_sw128(saddr, 16u, 1024u);
+  return sdesc(saddr, 16u, 1024u, 2u);
 }
 __device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t saddr, uint32_t chunk_stride_bytes) {
-  return sdesc_sw128(saddr, chunk_stride_bytes, 1024u);
+  return sdesc(saddr, chunk_stride_bytes, 512u, 1u);
 }
 
 // Instruction descriptor for kind::tf32 with an FP32 accumulator:
@@ -316,15 +319,24 @@ __device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint3
   }
 }
 
-// Byte offset of element (row, col) in a tile written by TMA with
-// SWIZZLE_128B and 32-float boxes: column chunk c = col / 32 occupies
-// rows * 128 bytes; inside it the 16-byte unit index is XORed with row % 8.
+// Byte offset of element (row, col) in a tile of `rows` rows written by TMA
+// with 32-float boxes: column chunk c = col / 32 occupies rows * 128 bytes.
+// K-major tiles (SWIZZLE_128B): the 16-byte unit index is XORed with row % 8.
 __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col,
                                                           uint32_t rows) {
   const uint32_t chunk = col >> 5;
   const uint32_t in_row = (col & 31u) * 4u;
   const uint32_t unit = (in_row >> 4) ^ (row & 7u);
   return chunk * rows * 128u + row * 128u + (unit << 4) + (in_row & 15u);
+}
+// MN-major tiles (SWIZZLE_128B_ATOM_32B): the 32-byte unit index is XORed
+// with row % 4.
+__host__ __device__ __forceinline__ uint32_t sw128_32b_offset(uint32_t row, uint32_t col,
+                                                              uint32_t rows) {
+  const uint32_t chunk = col >> 5;
+  const uint32_t in_row = (col & 31u) * 4u;
+  const uint32_t unit = (in_row >> 5) ^ (row & 3u);
+  return chunk * rows * 128u + row * 128u + (unit << 5) + (in_row & 31u);
 }
 
 }  // namespace ct

@@ -36,12 +36,13 @@ __global__ void __launch_bounds__(128, 1)
     tmem_alloc(smem_u32(&hs->ctl.tmem_base), 256);
     tmem_relinquish();
   }
-  // Operands into swizzled smem exactly as TMA would lay them out.
+  // Operands into swizzled smem exactly as TMA would lay them out (K-major:
+  // SWIZZLE_128B; MN-major: SWIZZLE_128B_ATOM_32B).
   for (int e = tid; e < 128 * 32; e += 128) {
     if (!a_tmem) {
       if (a_mn) {  // a is [32 (k)][128 (m)], m contiguous
         const int kk = e / 128, mm = e % 128;
-        *reinterpret_cast<float*>(smem_raw + (sa - smem_u32(smem_raw)) + sw128_offset(kk, mm, 32)) = a[e];
+        *reinterpret_cast<float*>(smem_raw + (sa - smem_u32(smem_raw)) + sw128_32b_offset(kk, mm, 32)) = a[e];
       } else {  // a is [128 (m)][32 (k)]
         const int mm = e / 32, kk = e % 32;
         *reinterpret_cast<float*>(smem_raw + (sa - smem_u32(smem_raw)) + sw128_offset(mm, kk, 128)) = a[e];
@@ -51,7 +52,7 @@ __global__ void __launch_bounds__(128, 1)
   for (int e = tid; e < n * 32; e += 128) {
     if (b_mn) {  // b is [32 (k)][n], n contiguous
       const int kk = e / n, nn = e % n;
-      *reinterpret_cast<float*>(smem_raw + (sb - smem_u32(smem_raw)) + sw128_offset(kk, nn, 32)) = b[e];
+      *reinterpret_cast<float*>(smem_raw + (sb - smem_u32(smem_raw)) + sw128_32b_offset(kk, nn, 32)) = b[e];
     } else {  // b is [n][32 (k)]
       const int nn = e / 32, kk = e % 32;
       *reinterpret_cast<float*>(smem_raw + (sb - smem_u32(smem_raw)) + sw128_offset(nn, kk, n)) = b[e];
