@@ -6,7 +6,7 @@
 // causal diagonal instead of scanning every query tile.
 //
 // Warp roles as in the forward: warp 0 TMA producer, warp 1 TMEM allocator and
-// MMA issuer, warps 2-3 TF32 hi/lo split (SPLIT == 3), warps 4-7 row warps
+// MMA issuer, warps 2-3 TF32 hi/lo split or rounding of landed tiles, warps 4-7 row warps
 // (one stationary row per thread / TMEM lane).
 //
 // dQ kernel, per 128 query rows, per key tile j (BN keys):
@@ -155,14 +155,16 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
     for (int l = 0; l < C::LA; ++l) {
       const uint32_t t = st + (l ? C::OFF_A1 : C::OFF_A0);
-      split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+      if constexpr (C::SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
     }
     fence_proxy_async_smem();
     mbar_arrive(B(bars->ready_a[s]));
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
     for (int l = 0; l < C::LB; ++l) {
       const uint32_t t = st + (l ? C::OFF_B1 : C::OFF_B0);
-      split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+      if constexpr (C::SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
     }
     fence_proxy_async_smem();
     mbar_arrive(B(bars->ready_b[s]));
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto kt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A0; };
       auto kmn = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A1; };
       auto vt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_B0; };
-      auto& rk = SPLIT == 3 ? bars->ready_a : bars->full_a;
-      auto& rv = SPLIT == 3 ? bars->ready_b : bars->full_b;
+      auto& rk = bars->ready_a;
+      auto& rv = bars->ready_b;
       auto issue_S = [&](int j) {
         const uint32_t base = kt(j);
         mma_ts_chain<SPLIT, D>(
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
-    if constexpr (SPLIT == 3) bwd_splitter<C>(bars, tiles, n_kv, p.status);
+    bwd_splitter<C>(bars, tiles, n_kv, p.status);
   } else {
     const int quad = warp & 3;
     const int row = q0 + quad * 32 + lane;
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) {
           const float ds = pv[32 * c + i] * (t[i] - dl);
           if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
-          else t[i] = ds;
+          else t[i] = tf32_round(ds);
         }
         tmem_st32(lb + C::TC_DP + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
@@ -425,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto gt = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B0; };
       auto qmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_A1; };
       auto gmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B1; };
-      auto& rq = SPLIT == 3 ? bars->ready_a : bars->full_a;
-      auto& rg = SPLIT == 3 ? bars->ready_b : bars->full_b;
+      auto& rq = bars->ready_a;
+      auto& rg = bars->ready_b;
       auto kdesc = [&](uint32_t base, int k) {
         return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32);
       };
@@ -485,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
-    if constexpr (SPLIT == 3) bwd_splitter<C>(bars, tiles, n, p.status);
+    bwd_splitter<C>(bars, tiles, n, p.status);
   } else {
     const int quad = warp & 3;
     const int row = k0 + quad * 32 + lane;  // key row
@@ -530,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           pv[cc] = e;
           if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
-          else t[x] = e;
+          else t[x] = tf32_round(e);
         }
         tmem_st32(lb + C::TC_S + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_PL + 32 * c, lo);
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int cc = 32 * c + x;
           const float ds = pv[cc] * (t[x] - dlt[x]);
           if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
-          else t[x] = ds;
+          else t[x] = tf32_round(ds);
         }
         tmem_st32(lb + C::TC_DP + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);

@@ -9,7 +9,10 @@
 //    with 32-float boxes, and are read by the tensor core either K-major (the
 //    head dim is the reduction) or MN-major (the sequence is the reduction).
 //  * Precision: SPLIT == 3 stores every operand as a TF32 hi/lo pair and issues
-//    hi*hi + hi*lo + lo*hi; SPLIT == 1 issues one TF32 MMA on the raw FP32 bits.
+//    hi*hi + hi*lo + lo*hi; SPLIT == 1 issues one TF32 MMA per product on
+//    operands rounded to the nearest TF32 (the tensor core truncates raw FP32).
+//  * Warps 2-3 prepare every landed tile before the MMA reads it: the hi/lo
+//    split (SPLIT == 3) or the in-place rounding (SPLIT == 1).
 #pragma once
 
 #include <cmath>
@@ -57,8 +60,9 @@ __device__ __forceinline__ void load_row32(const Ptr4& t, const float* rowp, int
   }
 }
 
-// Writes one D-wide row into TMEM columns [col, col + D) (and its TF32 low
-// part into [col + D, col + 2D) when SPLIT == 3).  Caller waits/fences.
+// Writes one D-wide row into TMEM columns [col, col + D): the TF32 hi part and
+// its low part into [col + D, col + 2D) when SPLIT == 3, the value rounded to
+// the nearest TF32 when SPLIT == 1.  Caller waits/fences.
 template <int D, int SPLIT>
 __device__ __forceinline__ void row_to_tmem(const Ptr4& t, const float* rowp, bool valid,
                                             bool vec, uint32_t lane_base, uint32_t col) {
@@ -76,6 +80,9 @@ __device__ __forceinline__ void row_to_tmem(const Ptr4& t, const float* rowp, bo
         lo[i] = l;
       }
       tmem_st32(lane_base + col + D + 32 * c, lo);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = tf32_round(x[i]);
     }
     tmem_st32(lane_base + col + 32 * c, x);
   }

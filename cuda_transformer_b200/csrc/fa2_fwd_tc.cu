@@ -9,7 +9,8 @@
 // Per CTA: one (batch, head) and 128 query rows.  Warp roles:
 //   warp 0      TMA producer of K/V tiles (NS-stage ring)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-3   TF32 hi/lo split of each landed K/V tile (SPLIT == 3)
+//   warps 2-3   TF32 hi/lo split (SPLIT == 3) or rounding (SPLIT == 1) of
+//               each landed K/V tile
 //   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
 //               epilogue (thread r <-> query row r <-> TMEM lane r)
 // K tiles use the K-major tile layout, V tiles the MN-major one.
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j <= n_kv; ++j) {
           if (j < n_kv) {  // S_j = Q K_j^T
             const int s = j % NS, r = j / NS, bb = j & 1;
-            const uint64_t& kb = SPLIT == 3 ? bars->ready_k[s] : bars->full_k[s];
+            const uint64_t& kb = bars->ready_k[s];
             if (!mbar_wait(B(kb), r & 1, ctl, p.status)) break;
             tc_fence_after();
             const uint32_t kt = tiles + s * C::STAGE + C::OFF_K;
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= 1) {  // O += P_{j-1} V_{j-1}
             const int jj = j - 1, s = jj % NS, r = jj / NS, bb = jj & 1;
             if (!mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status)) break;
-            const uint64_t& vb = SPLIT == 3 ? bars->ready_v[s] : bars->full_v[s];
+            const uint64_t& vb = bars->ready_v[s];
             if (!mbar_wait(B(vb), r & 1, ctl, p.status)) break;
             tc_fence_after();
             const uint32_t vt = tiles + s * C::STAGE + C::OFF_V;
@@ -201,21 +202,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
-    // ------------------------------------------------------- split warps
-    if constexpr (SPLIT == 3) {
-      const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % NS, r = j / NS;
-        const uint32_t st = tiles + s * C::STAGE;
-        if (!mbar_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
-        split_tile_smem(st + C::OFF_K, st + C::OFF_K + C::TILE, C::TILE, tid, kSplitThreads);
-        fence_proxy_async_smem();
-        mbar_arrive(B(bars->ready_k[s]));
-        if (!mbar_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
-        split_tile_smem(st + C::OFF_V, st + C::OFF_V + C::TILE, C::TILE, tid, kSplitThreads);
-        fence_proxy_async_smem();
-        mbar_arrive(B(bars->ready_v[s]));
-      }
+    // ---------------------------------------- split / rounding warps
+    const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
+    auto prep = [&](uint32_t t) {
+      if constexpr (SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
+      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
+    };
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j % NS, r = j / NS;
+      const uint32_t st = tiles + s * C::STAGE;
+      if (!mbar_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
+      prep(st + C::OFF_K);
+      fence_proxy_async_smem();
+      mbar_arrive(B(bars->ready_k[s]));
+      if (!mbar_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
+      prep(st + C::OFF_V);
+      fence_proxy_async_smem();
+      mbar_arrive(B(bars->ready_v[s]));
     }
   } else {
     // --------------------------------------------------------- row warps
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float pv = ex2_approx(sv[32 * c + i] - m_used);
           ls += pv;
           if constexpr (SPLIT == 3) tf32_split(pv, ph[i], pl[i]);
-          else ph[i] = pv;
+          else ph[i] = tf32_round(pv);
         }
         tmem_st32(sc + 32 * c, ph);
         if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, pl);

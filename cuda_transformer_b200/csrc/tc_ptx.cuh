@@ -319,6 +319,20 @@ __device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint3
   }
 }
 
+// TF32 mode: rounds a shared-memory tile in place to the nearest TF32 value
+// (the tensor core itself truncates the 13 low mantissa bits).
+__device__ __forceinline__ void round_tile_smem(uint32_t raw, uint32_t bytes, uint32_t tid,
+                                                uint32_t nthreads) {
+  for (uint32_t off = tid * 16u; off < bytes; off += nthreads * 16u) {
+    float4 x = lds128(raw + off);
+    x.x = tf32_round(x.x);
+    x.y = tf32_round(x.y);
+    x.z = tf32_round(x.z);
+    x.w = tf32_round(x.w);
+    sts128(raw + off, x);
+  }
+}
+
 // Byte offset of element (row, col) in a tile of `rows` rows written by TMA
 // with 32-float boxes: column chunk c = col / 32 occupies rows * 128 bytes.
 // K-major tiles (SWIZZLE_128B): the 16-byte unit index is XORed with row % 8.
