@@ -28,6 +28,7 @@ CT_ERR_WORKSPACE_TOO_SMALL = 8
 PRECISION_3XTF32 = 0
 PRECISION_TF32 = 1
 PRECISION_FP32 = 2
+CT_FA2_BWD_NOALLOC_MAX_ROWS = 2097152  # batch * heads * seq_len limit of ct_fa2_bwd_noalloc
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _fp = ctypes.c_void_p
@@ -50,6 +51,8 @@ SIGNATURES = {
     "ct_fa2_bwd_workspace_size": ([_i64, _i64, _i64, _i64], _sz),
     "ct_fa2_bwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp,
                     _fp, _fp, _fp, _sz, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
+    "ct_fa2_bwd_noalloc": ([_fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp,
+                            _i64p, _fp, _fp, _fp, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
     "ct_linear_fwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64, _int,
                        _fp], _int),
     "ct_bias_grad_workspace_size": ([_i64, _i64, _i64], _sz),

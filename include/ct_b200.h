@@ -122,6 +122,31 @@ int ct_fa2_bwd(const float* q, const int64_t q_stride[4],
                int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
                int causal, int precision, void* stream);
 
+/* Largest batch * heads * seq_len ct_fa2_bwd_noalloc accepts. */
+#define CT_FA2_BWD_NOALLOC_MAX_ROWS 2097152
+
+/* The full backward of ct_fa2_bwd for callers that cannot allocate device
+ * memory (for example a plugin given only tensor pointers by a host whose
+ * allocator it cannot reach, or a service that allows no cudaMalloc after
+ * start-up).  This entry point has no counterpart in the reference, whose
+ * launcher allocates the delta temporary with torch::empty.  Delta lives in a
+ * fixed array inside this library (8 MiB held on every GPU that loads it
+ * until the process exits); the call itself allocates nothing.  Returns
+ * CT_ERR_WORKSPACE_TOO_SMALL when batch * heads * seq_len exceeds
+ * CT_FA2_BWD_NOALLOC_MAX_ROWS.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race, so order them on one
+ * stream (or with events). */
+int ct_fa2_bwd_noalloc(const float* q, const int64_t q_stride[4],
+                       const float* k, const int64_t k_stride[4],
+                       const float* v, const int64_t v_stride[4],
+                       const float* o, const int64_t o_stride[4],
+                       const float* d_o, const int64_t do_stride[4],
+                       const float* lse, const int64_t lse_stride[3],
+                       float* dq, float* dk, float* dv,
+                       int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                       int causal, int precision, void* stream);
+
 /* ======================================================================== */
 /* Linear layer                                                              */
 /* ======================================================================== */
