@@ -67,7 +67,7 @@ struct BwdParams {
   const float* delta;  // contiguous [B,H,T]
   float* out0;         // dQ | dK
   float* out1;         // -  | dV
-  int H, T, n_tiles, bh_total, causal;
+  int H, T, n_tiles, bh_total, head_group, causal;
   float scale_log2, scale;
   uint32_t* status;
 };
@@ -171,24 +171,6 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
-// Issues D(+)= A(TMEM, K columns) x B over K = kdim in steps of 8, with the
-// 3xTF32 hi/lo terms when SPLIT == 3.  b_desc(k) / b_lo_desc(k) give the B
-// descriptors of k-step k.
-template <int SPLIT, int KDIM, class FB, class FBL>
-__device__ __forceinline__ void mma_ts_chain(uint32_t d, uint32_t a_hi, uint32_t a_lo,
-                                             uint32_t idesc, bool accumulate, FB b_desc,
-                                             FBL b_lo_desc) {
-#pragma unroll
-  for (int k = 0; k < KDIM / 8; ++k) {
-    const uint64_t bh = b_desc(k);
-    umma_tf32_ts(d, a_hi + 8 * k, bh, idesc, (accumulate || k > 0) ? 1u : 0u);
-    if constexpr (SPLIT == 3) {
-      umma_tf32_ts(d, a_hi + 8 * k, b_lo_desc(k), idesc, 1u);
-      umma_tf32_ts(d, a_lo + 8 * k, bh, idesc, 1u);
-    }
-  }
-}
-
 template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
     fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -203,8 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-  const int qt = p.n_tiles - 1 - (int)(blockIdx.x / p.bh_total);  // heavy tiles first
-  const int bh = (int)(blockIdx.x % p.bh_total);
+  int qt, bh;  // head-major (L2 reuse of K/V), last query tiles of a head first
+  cta_tile(p.n_tiles, p.bh_total, p.head_group, true, qt, bh);
   const int b = bh / p.H, h = bh % p.H;
   const int q0 = qt * kRows, T = p.T;
   const int last_row = min(q0 + kRows - 1, T - 1);
@@ -230,25 +212,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idQ = idesc_tf32(128, D, false, true);
-      auto kt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A0; };
-      auto kmn = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_A1; };
-      auto vt = [&](int j) { return tiles + (j % NS) * C::STAGE + C::OFF_B0; };
+      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_A0);           // stage-0 descriptors
+      const uint64_t kmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      const uint64_t vd0 = sdesc_kmajor(tiles + C::OFF_B0);
+      auto stg = [&](int j) { return (uint64_t)(((j % NS) * C::STAGE) >> 4); };
       auto& rk = bars->ready_a;
       auto& rv = bars->ready_b;
       auto issue_S = [&](int j) {
-        const uint32_t base = kt(j);
-        mma_ts_chain<SPLIT, D>(
-            tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D, idS, false,
-            [&](int k) { return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32); },
-            [&](int k) { return sdesc_kmajor(base + C::TILE + (k / 4) * BN * 128 + (k % 4) * 32); });
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D,
+                                                kd0 + stg(j), idS, false);
         umma_commit(B(bars->s_full));
       };
       auto issue_dP = [&](int j) {
-        const uint32_t base = vt(j);
-        mma_ts_chain<SPLIT, D>(
-            tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D, idS, false,
-            [&](int k) { return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32); },
-            [&](int k) { return sdesc_kmajor(base + C::TILE + (k / 4) * BN * 128 + (k % 4) * 32); });
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D,
+                                                vd0 + stg(j), idS, false);
         umma_commit(B(bars->empty_b[j % NS]));
         umma_commit(B(bars->dp_full));
       };
@@ -268,11 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!(ok = mbar_wait(B(bars->ds_full), j & 1, ctl, p.status))) break;
           tc_fence_after();
-          const uint32_t base = kmn(j);
-          mma_ts_chain<SPLIT, BN>(
-              tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL, idQ, j > 0,
-              [&](int k) { return sdesc_mnmajor(base + k * 1024, BN * 128); },
-              [&](int k) { return sdesc_mnmajor(base + C::TILE + k * 1024, BN * 128); });
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL,
+                                                  kmd0 + stg(j), idQ, j > 0);
           umma_commit(B(bars->empty_a[j % NS]));
           if (j + 1 < n_kv) {
             if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
@@ -327,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask = !valid || (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
-        float e = ex2_approx(pv[i] * p.scale_log2 - l2);
+        float e = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
         if (need_mask) {
           const int kv = kv0 + i;
           if (!(valid && kv < T && (!p.causal || kv <= row))) e = 0.0f;
@@ -395,8 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-  const int kt_ = (int)(blockIdx.x / p.bh_total);  // causal: low key tiles are heaviest
-  const int bh = (int)(blockIdx.x % p.bh_total);
+  int kt_, bh;  // head-major (L2 reuse of Q/dO); causal: low key tiles are heaviest
+  cta_tile(p.n_tiles, p.bh_total, p.head_group, false, kt_, bh);
   const int b = bh / p.H, h = bh % p.H;
   const int k0 = kt_ * kRows, T = p.T;
   const int j0 = p.causal ? k0 / BN : 0;
@@ -423,27 +397,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idO = idesc_tf32(128, D, false, true);
-      auto qt = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_A0; };
-      auto gt = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B0; };
-      auto qmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_A1; };
-      auto gmn = [&](int i) { return tiles + (i % NS) * C::STAGE + C::OFF_B1; };
+      const uint64_t qd0 = sdesc_kmajor(tiles + C::OFF_A0);           // stage-0 descriptors
+      const uint64_t gd0 = sdesc_kmajor(tiles + C::OFF_B0);
+      const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
+      auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
       auto& rq = bars->ready_a;
       auto& rg = bars->ready_b;
-      auto kdesc = [&](uint32_t base, int k) {
-        return sdesc_kmajor(base + (k / 4) * BN * 128 + (k % 4) * 32);
-      };
       auto issue_S = [&](int i) {
-        const uint32_t base = qt(i);
-        mma_ts_chain<SPLIT, D>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D, idS, false,
-                               [&](int k) { return kdesc(base, k); },
-                               [&](int k) { return kdesc(base + C::TILE, k); });
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D,
+                                                qd0 + stg(i), idS, false);
         umma_commit(B(bars->s_full));
       };
       auto issue_dP = [&](int i) {
-        const uint32_t base = gt(i);
-        mma_ts_chain<SPLIT, D>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D, idS, false,
-                               [&](int k) { return kdesc(base, k); },
-                               [&](int k) { return kdesc(base + C::TILE, k); });
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D,
+                                                gd0 + stg(i), idS, false);
         umma_commit(B(bars->dp_full));
       };
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
@@ -456,11 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; ok && i < n; ++i) {
           if (!(ok = mbar_wait(B(bars->p_full), i & 1, ctl, p.status))) break;
           tc_fence_after();
-          const uint32_t gb = gmn(i), qb = qmn(i);
-          mma_ts_chain<SPLIT, BN>(  // dV += P^T dO_i
-              tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, idO, i > 0,
-              [&](int k) { return sdesc_mnmajor(gb + k * 1024, BN * 128); },
-              [&](int k) { return sdesc_mnmajor(gb + C::TILE + k * 1024, BN * 128); });
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
+              tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, gmd0 + stg(i), idO, i > 0);
           if (i + 1 < n) {
             if (!(ok = mbar_wait(B(rq[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
@@ -468,10 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!(ok = mbar_wait(B(bars->ds_full), i & 1, ctl, p.status))) break;
           tc_fence_after();
-          mma_ts_chain<SPLIT, BN>(  // dK += dS^T Q_i
-              tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, idO, i > 0,
-              [&](int k) { return sdesc_mnmajor(qb + k * 1024, BN * 128); },
-              [&](int k) { return sdesc_mnmajor(qb + C::TILE + k * 1024, BN * 128); });
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
+              tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, qmd0 + stg(i), idO, i > 0);
           umma_commit(B(bars->empty_a[i % NS]));
           umma_commit(B(bars->empty_b[i % NS]));
           if (i + 1 < n) {
@@ -525,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
           const int cc = 32 * c + x;
-          float e = ex2_approx(t[x] * p.scale_log2 - lq[x]);
+          float e = ex2_approx(fmaf(t[x], p.scale_log2, -lq[x]));
           if (need_mask) {
             const int q = qs + cc;
             if (!(valid && q < T && (!p.causal || q >= row))) e = 0.0f;
@@ -602,6 +565,7 @@ BwdParams make_params(const Fa2Problem& pr, Strided4 a, Strided4 b, const float*
   p.T = (int)pr.T;
   p.n_tiles = (int)((pr.T + kRows - 1) / kRows);
   p.bh_total = (int)(pr.B * pr.H);
+  p.head_group = fa2_head_group(p.bh_total);
   p.causal = pr.causal ? 1 : 0;
   p.scale = (float)(1.0 / std::sqrt((double)pr.D));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));

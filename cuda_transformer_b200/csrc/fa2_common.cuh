@@ -16,6 +16,7 @@
 #pragma once
 
 #include <cmath>
+#include <cstdlib>
 
 #include "ct_internal.h"
 #include "tc_ptx.cuh"
@@ -88,6 +89,23 @@ __device__ __forceinline__ void row_to_tmem(const Ptr4& t, const float* rowp, bo
   }
 }
 
+// Causal / ragged mask of 32 consecutive score columns starting at key kv0:
+// column kv stays iff kv < T and (!causal || kv <= row); others become -inf.
+__device__ __forceinline__ void mask_cols32(float (&t)[32], int kv0, int T, int causal, int row) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int kv = kv0 + i;
+    if (!(kv < T && (!causal || kv <= row))) t[i] = -INFINITY;
+  }
+}
+
+__device__ __forceinline__ float max32(const float (&t)[32]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(fmaxf(t[4 * i], t[4 * i + 1]), fmaxf(t[4 * i + 2], t[4 * i + 3]));
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
 // Stores a D-wide row of TMEM columns [col, col+D) times `scale` to a dense
 // global row.
 template <int D>
@@ -105,6 +123,46 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t 
                             v[4 * i + 3] * scale);
     }
   }
+}
+
+// D (+)= A x B over K = KDIM in steps of 8: A from TMEM columns a_hi (+ a_lo
+// for the 3xTF32 low part), B from a shared-memory tile whose k-step-0
+// descriptor is `bd` (its low copy TILE bytes further).  Descriptors advance
+// by compile-time offsets (start address field counts 16-byte units):
+//   K-major tile of BN rows: k-step k at (k/4)*BN*128 + (k%4)*32 bytes
+//   MN-major tile:           k-step k at k*1024 bytes
+template <int SPLIT, int KDIM, bool MN_MAJOR, int BN, uint32_t TILE>
+__device__ __forceinline__ void mma_chain(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t bd,
+                                          uint32_t idesc, bool accumulate) {
+#pragma unroll
+  for (int k = 0; k < KDIM / 8; ++k) {
+    const uint32_t off = MN_MAJOR ? (uint32_t)k * 1024u
+                                  : (uint32_t)(k / 4) * BN * 128u + (uint32_t)(k % 4) * 32u;
+    const uint64_t bh = bd + (off >> 4);
+    umma_tf32_ts(d, a_hi + 8 * k, bh, idesc, (accumulate || k > 0) ? 1u : 0u);
+    if constexpr (SPLIT == 3) {
+      umma_tf32_ts(d, a_hi + 8 * k, bh + (TILE >> 4), idesc, 1u);
+      umma_tf32_ts(d, a_lo + 8 * k, bh, idesc, 1u);
+    }
+  }
+}
+
+// Maps a linear CTA index to (tile, batch*head).  Heads are taken in groups of
+// `group` (the last group may be smaller): all tiles of a group run before the
+// next group, so resident CTAs share a few heads' streamed operands in L2,
+// and inside a group consecutive CTAs alternate between its heads, so they do
+// not all stream the same tile at the same moment.  `heavy_first_desc` lists a
+// head's tiles from the last to the first (causal forward / dQ do the most
+// work on late query tiles; dK/dV on early key tiles keep ascending order).
+__device__ __forceinline__ void cta_tile(int n_tiles, int bh_total, int group,
+                                         bool heavy_first_desc, int& tile, int& bh) {
+  const int per_group = group * n_tiles;
+  const int g = (int)(blockIdx.x / per_group);
+  const int r = (int)(blockIdx.x % per_group);
+  const int gsize = min(group, bh_total - g * group);
+  const int t = r / gsize;
+  bh = g * group + r % gsize;
+  tile = heavy_first_desc ? n_tiles - 1 - t : t;
 }
 
 // Drain-wait used on teardown: ignores the CTA abort flag, bounded by time.
@@ -136,6 +194,17 @@ inline int make_tmap_bhtd(CUtensorMap* map, const Strided4& t, const Fa2Problem&
   const uint64_t strides[3] = {(uint64_t)t.s[2] * 4u, (uint64_t)t.s[1] * 4u, (uint64_t)t.s[0] * 4u};
   const uint32_t box[4] = {32u, (uint32_t)rows, 1u, 1u};
   return make_tmap_f32(map, t.ptr, 4, dims, strides, box, mn_major);
+}
+
+// Number of (b,h) heads interleaved per CTA-order group (see fa2::cta_tile).
+// The environment variable CT_FA2_HEAD_GROUP overrides the default (tuning).
+inline int fa2_head_group(int bh_total) {
+  static const int env = [] {
+    const char* e = std::getenv("CT_FA2_HEAD_GROUP");
+    return e ? std::atoi(e) : 0;
+  }();
+  int g = env > 0 ? env : 16;
+  return g < 1 ? 1 : (g > bh_total ? (bh_total > 0 ? bh_total : 1) : g);
 }
 
 inline bool fa2_tma_ok(const Strided4& t) {

@@ -52,7 +52,7 @@ struct FwdParams {
   Ptr4 q;
   float* o;
   float* lse;
-  int H, T, n_qt, bh_total;
+  int H, T, n_qt, bh_total, head_group;
   int causal;
   float scale_log2;  // log2(e) / sqrt(D)
   uint32_t* status;
@@ -76,9 +76,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   CtaCtl* ctl = &bars->ctl;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-  // Heaviest (last) query tiles first so causal work balances across waves.
-  const int qt = p.n_qt - 1 - (int)(blockIdx.x / p.bh_total);
-  const int bh = (int)(blockIdx.x % p.bh_total);
+  // Head-major order (L2 reuse of K/V), last query tiles of a head first.
+  int qt, bh;
+  cta_tile(p.n_qt, p.bh_total, p.head_group, true, qt, bh);
   const int b = bh / p.H, h = bh % p.H;
   const int q0 = qt * kRows;
   const int T = p.T;
@@ -151,47 +151,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);            // stage-0 descriptors
+      const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
       if (mbar_wait(B(bars->q_ready), 0, ctl, p.status)) {
         tc_fence_after();
         for (int j = 0; j <= n_kv; ++j) {
           if (j < n_kv) {  // S_j = Q K_j^T
             const int s = j % NS, r = j / NS, bb = j & 1;
-            const uint64_t& kb = bars->ready_k[s];
-            if (!mbar_wait(B(kb), r & 1, ctl, p.status)) break;
+            if (!mbar_wait(B(bars->ready_k[s]), r & 1, ctl, p.status)) break;
             tc_fence_after();
-            const uint32_t kt = tiles + s * C::STAGE + C::OFF_K;
-            const uint32_t dS = tmem + C::TC_S + bb * C::SBUF;
-#pragma unroll
-            for (int k = 0; k < D / 8; ++k) {
-              const uint32_t off = (k / 4) * BN * 128 + (k % 4) * 32;
-              const uint64_t bh_ = sdesc_kmajor(kt + off);
-              umma_tf32_ts(dS, tmem + C::TC_Q + 8 * k, bh_, idS, k > 0);
-              if constexpr (SPLIT == 3) {
-                umma_tf32_ts(dS, tmem + C::TC_Q + 8 * k, sdesc_kmajor(kt + C::TILE + off), idS, 1);
-                umma_tf32_ts(dS, tmem + C::TC_Q + D + 8 * k, bh_, idS, 1);
-              }
-            }
+            mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
+                                                    tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
+                                                    idS, false);
             umma_commit(B(bars->empty_k[s]));
             umma_commit(B(bars->s_full[bb]));
           }
           if (j >= 1) {  // O += P_{j-1} V_{j-1}
             const int jj = j - 1, s = jj % NS, r = jj / NS, bb = jj & 1;
             if (!mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status)) break;
-            const uint64_t& vb = bars->ready_v[s];
-            if (!mbar_wait(B(vb), r & 1, ctl, p.status)) break;
+            if (!mbar_wait(B(bars->ready_v[s]), r & 1, ctl, p.status)) break;
             tc_fence_after();
-            const uint32_t vt = tiles + s * C::STAGE + C::OFF_V;
             const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
-#pragma unroll
-            for (int k = 0; k < BN / 8; ++k) {
-              const uint64_t vh = sdesc_mnmajor(vt + k * 1024, BN * 128);
-              umma_tf32_ts(tmem + C::TC_O, pA + 8 * k, vh, idO, (jj > 0 || k > 0) ? 1u : 0u);
-              if constexpr (SPLIT == 3) {
-                umma_tf32_ts(tmem + C::TC_O, pA + 8 * k,
-                             sdesc_mnmajor(vt + C::TILE + k * 1024, BN * 128), idO, 1);
-                umma_tf32_ts(tmem + C::TC_O, pA + BN + 8 * k, vh, idO, 1);
-              }
-            }
+            mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
+                                                    vd0 + (s * C::STAGE >> 4), idO, jj > 0);
             umma_commit(B(bars->empty_v[s]));
             umma_commit(B(bars->pv_done[bb]));
           }
@@ -242,28 +224,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = warp_wait(B(bars->s_full[bb]), (j >> 1) & 1, ctl, p.status))) break;
       tc_fence_after();
       const uint32_t sc = lb + C::TC_S + bb * C::SBUF;
-      float sv[BN];
-#pragma unroll
+      const int kv0 = j * BN;
+      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
+      // Pass 1: row maximum of the raw scores, 32 columns at a time
+      // (scale_log2 > 0, so scaling after the maximum is exact).
+      float mraw = -INFINITY;
+#pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float t[32];
         tmem_ld32(sc + 32 * c, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[32 * c + i] = t[i];
+        if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
+        mraw = fmaxf(mraw, max32(t));
       }
-      const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
-      float mt = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        float x = sv[i] * p.scale_log2;
-        if (need_mask) {
-          const int kv = kv0 + i;
-          if (!(kv < T && (!p.causal || kv <= row))) x = -INFINITY;
-        }
-        sv[i] = x;
-        mt = fmaxf(mt, x);
-      }
-      const float m_new = fmaxf(m_used, mt);
+      const float m_new = fmaxf(m_used, mraw * p.scale_log2);
       const bool resc = m_new > m_used + 8.0f;
       if (__any_sync(0xffffffffu, resc)) {
         const float alpha = resc ? ex2_approx(m_used - m_new) : 1.0f;
@@ -283,20 +256,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      float ls = 0.0f;
-#pragma unroll
+      // Pass 2: P = exp2(s * scale_log2 - m), written over S (hi) and next to it (lo).
+      const float neg_m = -m_used;
+      float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
-        float ph[32], pl[32];
+        float t[32], lo[32];
+        tmem_ld32(sc + 32 * c, t);
+        if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float pv = ex2_approx(sv[32 * c + i] - m_used);
-          ls += pv;
-          if constexpr (SPLIT == 3) tf32_split(pv, ph[i], pl[i]);
-          else ph[i] = tf32_round(pv);
+          const float e = ex2_approx(fmaf(t[i], p.scale_log2, neg_m));
+          if (i & 1) ls1 += e;
+          else ls0 += e;
+          if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
+          else t[i] = tf32_round(e);
         }
-        tmem_st32(sc + 32 * c, ph);
-        if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, pl);
+        tmem_st32(sc + 32 * c, t);
+        if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, lo);
       }
+      const float ls = ls0 + ls1;
       l += ls;
       tmem_wait_st();
       tc_fence_before();
@@ -342,6 +321,7 @@ int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, 
   p.T = (int)pr.T;
   p.n_qt = (int)((pr.T + kRows - 1) / kRows);
   p.bh_total = (int)(pr.B * pr.H);
+  p.head_group = fa2_head_group(p.bh_total);
   p.causal = pr.causal ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
   p.status = dev.status;

@@ -275,11 +275,17 @@ __device__ __forceinline__ float tf32_round(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
-// x = hi + lo with hi, lo both exactly representable in TF32 up to the
-// rounding of lo (|x - hi - lo| <= 2^-22 |x|).
+// TF32 value the tensor core uses for an FP32 operand: the 13 low mantissa
+// bits are dropped (truncation; checked on the device by the test-suite).
+__device__ __forceinline__ float tf32_trunc(float x) {
+  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+// 3xTF32 split x = hi + lo: hi = tf32_trunc(x) is exact, lo = x - hi is exact
+// in FP32 and loses at most 2^-21 |x| when the tensor core truncates it.
+// Two ALU operations (no conversion instructions).
 __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
-  hi = tf32_round(x);
-  lo = tf32_round(x - hi);
+  hi = tf32_trunc(x);
+  lo = x - hi;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -302,20 +308,17 @@ __device__ __forceinline__ void sts128(uint32_t a, float4 v) {
                : "memory");
 }
 
-// Splits a shared-memory tile in place: every fp32 word x at raw+i becomes
-// tf32(x) and lo+i receives the TF32-rounded remainder.  Both buffers share
-// the same swizzled layout, so the element correspondence is positional.
+// 3xTF32 split of a shared-memory tile: lo + i receives x - tf32_trunc(x) for
+// every fp32 word x at raw + i.  The raw tile itself is the "hi" operand,
+// because the tensor core reads it truncated to tf32_trunc(x).  Both buffers
+// share the same swizzled layout, so the element correspondence is positional.
 __device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint32_t bytes,
                                                 uint32_t tid, uint32_t nthreads) {
+#pragma unroll 4
   for (uint32_t off = tid * 16u; off < bytes; off += nthreads * 16u) {
-    float4 x = lds128(raw + off);
-    float4 h, l;
-    tf32_split(x.x, h.x, l.x);
-    tf32_split(x.y, h.y, l.y);
-    tf32_split(x.z, h.z, l.z);
-    tf32_split(x.w, h.w, l.w);
-    sts128(raw + off, h);
-    sts128(lo + off, l);
+    const float4 x = lds128(raw + off);
+    sts128(lo + off, make_float4(x.x - tf32_trunc(x.x), x.y - tf32_trunc(x.y),
+                                 x.z - tf32_trunc(x.z), x.w - tf32_trunc(x.w)));
   }
 }
 

@@ -1,8 +1,8 @@
 """On-device checks of the tensor-core operand layouts the kernels rely on
 (K-major / MN-major shared-memory operands in the 128-byte swizzle, A from
 Tensor Memory) and of how the tensor core treats the low mantissa bits of an
-FP32 operand (the 3xTF32 split writes explicit TF32 hi/lo values, so it is
-correct either way; this records which rule the hardware applies)."""
+FP32 operand: it truncates them, which the 3xTF32 split relies on (a raw FP32
+tile in shared memory is read as its truncated "hi" part)."""
 import pytest
 import torch
 
@@ -55,5 +55,5 @@ def test_tf32_operand_rounding_rule(cuda_device, record_property):
     is_round = torch.equal(d, (trunc.double() + 2.0 ** -10 * 2.0 ** torch.floor(torch.log2(trunc.double()))).float())
     record_property("tf32_operand_rule", "truncate" if is_trunc else ("round" if is_round else "other"))
     print("tf32 operand rule:", "truncate" if is_trunc else ("round" if is_round else "other"))
-    assert is_trunc or is_round
+    assert is_trunc, "3xTF32 split assumes the tensor core truncates FP32 operands to TF32"
     H.assert_device_clean()
