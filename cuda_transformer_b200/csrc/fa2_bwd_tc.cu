@@ -72,10 +72,16 @@ struct BwdParams {
   uint32_t* status;
 };
 
+// Bytes of the per-stage vector slots (log-sum-exp and delta of BN queries).
+template <class C>
+constexpr size_t bwd_vec_bytes() {
+  return (size_t)C::NS * 2 * C::BN * sizeof(float);
+}
 template <class C>
 constexpr size_t bwd_smem_bytes() {
-  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
-  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>() <= 227 * 1024,
+                "shared memory budget");
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>();
 }
 
 template <class C>
@@ -101,42 +107,62 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars) {
   fence_barrier_init();
 }
 
-// TMA producer: tiles j0..j1-1 of two [B,H,T,D] tensors into the stage ring;
-// maps[0..1] = A in the K-major / MN-major layouts, maps[2..3] = B likewise.
-template <class C>
-__device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles,
+// Producer warp (all 32 lanes): lane 0 issues the TMA loads of tiles j0..j1-1
+// of two [B,H,T,D] tensors into the stage ring (maps[0..1] = A in the K-major /
+// MN-major layouts, maps[2..3] = B likewise).  With VEC, all lanes first stage
+// the step's per-query log-sum-exp (times log2 e) and delta into the stage's
+// vector slot, so the row warps read them from shared memory.
+template <class C, bool VEC>
+__device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles, float* vec,
                                              const CUtensorMap* const* maps, int j0, int j1,
-                                             int h, int b, uint32_t* status) {
+                                             int h, int b, const float* lse_bh, int64_t lse_t,
+                                             const float* del_bh, int T, uint32_t* status) {
   constexpr int NS = C::NS, BN = C::BN, D = C::D;
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   CtaCtl* ctl = &bars->ctl;
-  for (int m = 0; m < 4; ++m)
-    if (maps[m]) tma_prefetch_desc(maps[m]);
+  const int lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int m = 0; m < 4; ++m)
+      if (maps[m]) tma_prefetch_desc(maps[m]);
   int last_a[NS], last_b[NS];
   for (int s = 0; s < NS; ++s) last_a[s] = last_b[s] = -1;
   for (int j = j0; j < j1; ++j) {
     const int i = j - j0, s = i % NS, r = i / NS;
     const uint32_t st = tiles + s * C::STAGE;
-    if (r > 0 && !mbar_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
-    mbar_arrive_expect_tx(B(bars->full_a[s]), C::LA * C::TILE);
+    if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
+    if constexpr (VEC) {
+      float* vs = vec + s * 2 * BN;
+      for (int x = lane; x < BN; x += 32) {
+        const int q = j * BN + x;
+        vs[x] = q < T ? __ldg(lse_bh + (int64_t)q * lse_t) * kLog2e : 0.0f;
+        vs[BN + x] = q < T ? __ldg(del_bh + q) : 0.0f;
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      mbar_arrive_expect_tx(B(bars->full_a[s]), C::LA * C::TILE);
 #pragma unroll
-    for (int l = 0; l < C::LA; ++l)
+      for (int l = 0; l < C::LA; ++l)
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tma_load_4d(st + (l ? C::OFF_A1 : C::OFF_A0) + c * BN * 128, maps[l], B(bars->full_a[s]),
-                    32 * c, j * BN, h, b);
+        for (int c = 0; c < D / 32; ++c)
+          tma_load_4d(st + (l ? C::OFF_A1 : C::OFF_A0) + c * BN * 128, maps[l],
+                      B(bars->full_a[s]), 32 * c, j * BN, h, b);
+    }
     last_a[s] = r;
-    if (r > 0 && !mbar_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
-    mbar_arrive_expect_tx(B(bars->full_b[s]), C::LB * C::TILE);
+    if (r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(B(bars->full_b[s]), C::LB * C::TILE);
 #pragma unroll
-    for (int l = 0; l < C::LB; ++l)
+      for (int l = 0; l < C::LB; ++l)
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tma_load_4d(st + (l ? C::OFF_B1 : C::OFF_B0) + c * BN * 128, maps[2 + l],
-                    B(bars->full_b[s]), 32 * c, j * BN, h, b);
+        for (int c = 0; c < D / 32; ++c)
+          tma_load_4d(st + (l ? C::OFF_B1 : C::OFF_B0) + c * BN * 128, maps[2 + l],
+                      B(bars->full_b[s]), 32 * c, j * BN, h, b);
+    }
     last_b[s] = r;
   }
-  if (ctl->abort) {
+  __syncwarp();
+  if (ctl->abort && lane == 0) {
     for (int s = 0; s < NS; ++s) {
       if (last_a[s] >= 0) mbar_drain(B(bars->full_a[s]), last_a[s] & 1);
       if (last_b[s] >= 0) mbar_drain(B(bars->full_b[s]), last_b[s] & 1);
@@ -203,11 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0) {
-      const CUtensorMap* maps[4] = {&tmK, &tmKmn, &tmV, nullptr};
-      bwd_producer<C>(bars, tiles, maps, 0, n_kv, h, b, p.status);
-    }
-    __syncwarp();
+    const CUtensorMap* maps[4] = {&tmK, &tmKmn, &tmV, nullptr};
+    bwd_producer<C, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
+                           p.status);
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
@@ -365,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
   const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(BwdBars<NS>) + 1023u) & ~1023u;
+  float* vec = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) + NS * C::STAGE);
   CtaCtl* ctl = &bars->ctl;
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -388,11 +413,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0) {
-      const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
-      bwd_producer<C>(bars, tiles, maps, j0, j1, h, b, p.status);
-    }
-    __syncwarp();
+    const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
+    bwd_producer<C, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
+                          p.l2, p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
@@ -467,28 +490,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(B(bars->rows_ready));
     }
-    const float* lse_bh = p.lse + b * p.l0 + h * p.l1;
-    const float* del_bh = p.delta + (int64_t)bh * T;
     bool ok = n > 0;
     for (int i = 0; ok && i < n; ++i) {
       const int qs = (j0 + i) * BN;
+      // the step's log-sum-exp * log2(e) and delta, staged by the producer warp
+      if (!(ok = warp_wait(B(bars->full_a[i % NS]), (i / NS) & 1, ctl, p.status))) break;
+      const float* vl = vec + (i % NS) * 2 * BN;
       if (!(ok = warp_wait(B(bars->s_full), i & 1, ctl, p.status))) break;
       tc_fence_after();
       const bool need_mask = !valid || (qs + BN > T) || (p.causal && qs < k0 + kRows - 1);
       float pv[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32], lq[32];
-#pragma unroll
-        for (int x = 0; x < 32; ++x) {  // broadcast loads, L1 resident
-          const int q = qs + 32 * c + x;
-          lq[x] = q < T ? __ldg(lse_bh + (int64_t)q * p.l2) * kLog2e : 0.0f;
-        }
+        float t[32], lo[32];
         tmem_ld32(lb + C::TC_S + 32 * c, t);
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
           const int cc = 32 * c + x;
-          float e = ex2_approx(fmaf(t[x], p.scale_log2, -lq[x]));
+          float e = ex2_approx(fmaf(t[x], p.scale_log2, -vl[cc]));
           if (need_mask) {
             const int q = qs + cc;
             if (!(valid && q < T && (!p.causal || q >= row))) e = 0.0f;
@@ -507,17 +526,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32], dlt[32];
-#pragma unroll
-        for (int x = 0; x < 32; ++x) {
-          const int q = qs + 32 * c + x;
-          dlt[x] = q < T ? __ldg(del_bh + q) : 0.0f;
-        }
+        float t[32], lo[32];
         tmem_ld32(lb + C::TC_DP + 32 * c, t);
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
           const int cc = 32 * c + x;
-          const float ds = pv[cc] * (t[x] - dlt[x]);
+          const float ds = pv[cc] * (t[x] - vl[BN + cc]);
           if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
           else t[x] = tf32_round(ds);
         }
