@@ -69,6 +69,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase has not completed is
+// suspended by the hardware (woken when the phase completes or after at most
+// `hint_ns`) instead of spinning, so waiting warps leave their scheduler's
+// issue slots to the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits until the phase with the given parity of barrier `bar` has completed.
 // Returns false (and raises ctl->abort and the device status word) if the
 // wait exceeds CT_WAIT_TIMEOUT_NS or another wait of this CTA already failed.
@@ -77,8 +94,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, CtaCtl*
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if ((i & 15u) == 0u) {
       if (ctl->abort) return false;
       if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {  // another CTA gave up
         ctl->abort = 1u;
