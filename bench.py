@@ -259,6 +259,16 @@ class Fa2Runner:
         return out
 
 
+def max_over_ranks(ms: float, dist, world: int, device) -> float:
+    """Maximum of a per-rank time over all ranks (the job's time)."""
+    if world == 1:
+        return ms
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def timed_steps(runner, steps: int, warmup: int, dist, world: int):
     torch = runner.torch
     for _ in range(warmup):
@@ -275,12 +285,7 @@ def timed_steps(runner, steps: int, warmup: int, dist, world: int):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = a.elapsed_time(b)
-    if world > 1:
-        t = torch.tensor([ms], device=runner.dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms
+    return max_over_ranks(a.elapsed_time(b), dist, world, runner.dev)
 
 
 def e2e_steps(pairs: int, dev, precision: int, steps: int, dist, world: int, seed: int) -> dict:
@@ -315,11 +320,7 @@ def e2e_steps(pairs: int, dev, precision: int, steps: int, dist, world: int, see
         one()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(a.elapsed_time(b), dist, world, dev)
     h2d = sum(t.numel() * 4 for t in host_in)
     d2h = sum(t.numel() * 4 for t in host_out)
     return {"ms": ms, "h2d": h2d * world, "d2h": d2h * world}
@@ -417,7 +418,7 @@ def main() -> None:
                        "l2": "inputs larger than L2 (Q, K, V, dO = 512 MiB per step at N=1)",
                        "parallelism": f"bh-shard{world}"},
             "kernel_ms": kern,
-            "gpu_launches": runner_launches(args.steps),
+            "gpu_launches": runner_launches(args.steps) * world,
             "roofline": roofline,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"]},
@@ -435,7 +436,9 @@ def main() -> None:
 
 
 def runner_launches(steps: int) -> int:
-    return 4 * steps  # fwd, delta, dq, dkdv per step
+    """This library's kernel launches per rank in the timed region: fwd,
+    delta, dq and dkdv per step."""
+    return 4 * steps
 
 
 if __name__ == "__main__":
