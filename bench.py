@@ -68,61 +68,112 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples for one GPU while a region runs."""
+    """SM clock, power and clock-event reasons of one GPU, sampled every
+    10 ms by an NVML reader thread while a region runs (read-only queries;
+    nvidia-smi polling at 100 ms is the fallback when NVML is missing).  The
+    first sample is taken before __enter__ returns, so short regions are
+    still covered."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.tmp = None
+    def __init__(self, cuda_index: int, period_s: float = 0.01):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.rows: list[dict] = []
+        self.source = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
+        self._tmp = None
+
+    # -- NVML path
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _sample(self, nv, h, max_mhz, masks):
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append(dict(sm=float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                              max=max_mhz, power=nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                              reasons=[name for name, m in masks if r & m]))
 
     def __enter__(self):
+        import threading
+
         try:
-            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.tmp, stderr=subprocess.DEVNULL)
+            nv, h = self._nvml_handle()
+            max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+            self._sample(nv, h, max_mhz, masks)
+            self._stop = threading.Event()
+
+            def loop():
+                while not self._stop.wait(self.period):
+                    try:
+                        self._sample(nv, h, max_mhz, masks)
+                    except Exception:
+                        return
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+            self.source = "nvml"
+            return self
         except Exception:
-            self.proc = None
+            pass
+        try:
+            self._tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self._tmp, stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi"
+        except Exception:
+            self._proc = None
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except Exception:
-                self.proc.kill()
+                self._proc.kill()
+            self._tmp.flush()
+            names = [n for n, _ in self.REASONS]
+            for line in Path(self._tmp.name).read_text().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                try:
+                    self.rows.append(dict(sm=float(f[1]), max=float(f[2]), power=float(f[3]),
+                                          reasons=[n for n, v in zip(names, f[5:9])
+                                                   if v.lower() == "active"]))
+                except (ValueError, IndexError):
+                    continue
+            os.unlink(self._tmp.name)
 
     def summary(self) -> dict:
-        if self.proc is None or self.tmp is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.tmp.flush()
-        rows = []
-        for line in Path(self.tmp.name).read_text().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                rows.append(dict(sm=float(f[1]), max=float(f[2]), power=float(f[3]),
-                                 hw=f[5], hwt=f[6], swt=f[7], pcap=f[8]))
-            except ValueError:
-                continue
-        os.unlink(self.tmp.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [r for r in rows if r["power"] > 300.0] or rows
-        reasons = sorted({name for r in loaded for name, key in
-                          (("hw_slowdown", "hw"), ("hw_thermal_slowdown", "hwt"),
-                           ("sw_thermal_slowdown", "swt"), ("sw_power_cap", "pcap"))
-                          if r[key].lower() == "active"})
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"],
+                    "source": self.source}
+        loaded = [r for r in self.rows if r["power"] > 300.0] or self.rows
         return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
-                "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
-                "samples": len(rows), "samples_under_load": len(loaded)}
+                "sm_max_mhz": max(r["max"] for r in self.rows),
+                "reasons": sorted({x for r in loaded for x in r["reasons"]}),
+                "samples": len(self.rows), "samples_under_load": len(loaded),
+                "source": self.source}
 
 
 # ----------------------------------------------------------------- CPU side
