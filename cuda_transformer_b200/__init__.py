@@ -55,6 +55,9 @@ SIGNATURES = {
                             _i64p, _fp, _fp, _fp, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
     "ct_linear_fwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64, _int,
                        _fp], _int),
+    "ct_linear_workspace_size": ([_i64, _i64, _i64, _i64], _sz),
+    "ct_linear_fwd_ws": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64,
+                          _int, _fp, _sz, _fp], _int),
     "ct_bias_grad_workspace_size": ([_i64, _i64, _i64], _sz),
     "ct_bias_grad": ([_fp, _i64p, _fp, _i64, _i64, _i64, _fp, _sz, _fp], _int),
     "ct_softmax_fwd": ([_fp, _fp, _i64, _i64, _fp], _int),

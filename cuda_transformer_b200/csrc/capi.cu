@@ -292,15 +292,21 @@ int ct_fa2_bwd(const float* q, const int64_t q_stride[4], const float* k, const 
                            s4(d_o, do_stride), lse, lse_stride, delta, dk, dv, *dev, st);
 }
 
-int ct_linear_fwd(const float* x, const int64_t x_stride[3], const float* w,
-                  const int64_t w_stride[3], const float* bias, int64_t bias_stride, float* out,
-                  int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch, int precision,
-                  void* stream) {
+size_t ct_linear_workspace_size(int64_t batch, int64_t m, int64_t k, int64_t n) {
+  if (batch < 0 || m < 0 || k < 0 || n < 0) return 0;
+  return linear_workspace_bytes(batch, m, n);
+}
+
+int ct_linear_fwd_ws(const float* x, const int64_t x_stride[3], const float* w,
+                     const int64_t w_stride[3], const float* bias, int64_t bias_stride, float* out,
+                     int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
+                     int precision, void* workspace, size_t workspace_bytes, void* stream) {
   if (batch < 0 || m < 0 || k < 0 || n < 0 || !valid_precision(precision) ||
       !(w_batch == 1 || w_batch == batch))
     return CT_ERR_INVALID_ARGUMENT;
   if (batch * m * n == 0) return CT_OK;
   if (!x || !w || !bias || !out || !x_stride || !w_stride) return CT_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes > 0 && !workspace) return CT_ERR_INVALID_ARGUMENT;
   int err = CT_OK;
   const DeviceInfo* dev = current_device(&err);
   if (err != CT_OK) return err;
@@ -310,9 +316,19 @@ int ct_linear_fwd(const float* x, const int64_t x_stride[3], const float* w,
   for (int i = 0; i < 3; ++i) { g.xs[i] = x_stride[i]; g.ws[i] = w_stride[i]; }
   if (w_batch == 1) g.ws[0] = 0;
   g.precision = precision;
-  if (precision != CT_PRECISION_FP32 && linear_tc_supported(g))
-    return launch_linear_tc(g, *dev, as_stream(stream));
+  if (precision != CT_PRECISION_FP32 && linear_tc_supported(g)) {
+    const int rc = launch_linear_tc(g, workspace, workspace_bytes, *dev, as_stream(stream));
+    if (rc != CT_ERR_UNSUPPORTED_LAYOUT) return rc;  // else: TMA cannot address it
+  }
   return launch_linear_simt(g, as_stream(stream));
+}
+
+int ct_linear_fwd(const float* x, const int64_t x_stride[3], const float* w,
+                  const int64_t w_stride[3], const float* bias, int64_t bias_stride, float* out,
+                  int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch, int precision,
+                  void* stream) {
+  return ct_linear_fwd_ws(x, x_stride, w, w_stride, bias, bias_stride, out, batch, m, k, n,
+                          w_batch, precision, nullptr, 0, stream);
 }
 
 size_t ct_bias_grad_workspace_size(int64_t batch, int64_t m, int64_t n) {

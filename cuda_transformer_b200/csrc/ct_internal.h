@@ -89,7 +89,10 @@ struct GemmProblem {
   float* out;     // contiguous [batch, m, n]
   int precision;
 };
-int launch_linear_tc(const GemmProblem& g, const DeviceInfo& dev, cudaStream_t st);
+// ws / ws_bytes: optional per-tile counters that enable the split-K schedule.
+int launch_linear_tc(const GemmProblem& g, void* ws, size_t ws_bytes, const DeviceInfo& dev,
+                     cudaStream_t st);
+size_t linear_workspace_bytes(int64_t batch, int64_t m, int64_t n);
 bool linear_tc_supported(const GemmProblem& g);
 int launch_linear_simt(const GemmProblem& g, cudaStream_t st);
 

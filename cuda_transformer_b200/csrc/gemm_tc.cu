@@ -1,13 +1,584 @@
-// gemm_tc.cu -- tensor-core (tcgen05) linear layer.  Not wired yet: every
-// problem is reported unsupported so ct_linear_fwd uses the CUDA-core kernel.
-#include "ct_internal.h"
+// gemm_tc.cu -- linear layer out[b] = x[b] @ W[b | 0] + bias on the sm_100a
+// tensor cores (tcgen05, kind::tf32, accumulators in TMEM).
+//
+// Computes what fused_multiply_add computes
+// (Transformer_kernels/fused_multiply_add.cuh:10-93, launched by
+// Transformer_launchers/linear_layer.cu:28-70): for every batch b and output
+// element (i, j), out[b][i][j] = sum_k x[b][i][k] * W[b or 0][k][j] + bias[j].
+//
+// Persistent kernel, one CTA per SM.  Work units are (128 x BN output tile,
+// K slice), taken in the order (batch, tile row, tile column, slice) so that
+// the CTAs running at the same time share the x row block in L2.  Warp roles:
+//   warp 0      TMA producer (NS-stage ring of 32-deep K blocks of x and W)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-3   TF32 hi/lo split of each stage (3xTF32 mode)
+//   warps 4-7   epilogue: thread r <-> tile row r <-> TMEM lane r
+// TF32 mode feeds the tiles to the tensor core as loaded: it reads an FP32
+// operand as its TF32 truncation (the 13 low mantissa bits dropped), a
+// relative bias near 7e-4 on a product, inside the TF32 tolerance.  Rounding
+// the tiles in shared memory first would cost about as long as the MMAs.
+// Either operand may be K-major (the reduction index is contiguous: x as the
+// forward passes it, W^T views) or MN-major (rows/columns contiguous: W as
+// stored, x^T views); the layout is picked per call from the strides, so the
+// three GEMMs of the linear layer's forward and backward need no copies.
+//
+// Accumulation.  The tensor core's FP32 accumulator drops the bits below its
+// 24-bit mantissa on every addition (round toward zero), a bias that grows
+// with the number of MMAs folded into one accumulator.  The K loop is
+// therefore cut into chunks of at most kChunkKb K blocks (512 values of K,
+// about 1e-5 relative bias in 3xTF32, which issues three MMAs per K step):
+// each chunk accumulates in one of two TMEM buffers and the epilogue warps
+// add the chunks with round-to-nearest FP32 additions into a running sum kept
+// in a third TMEM region (BN = 128 only; the wider BN = 256 tiles are used
+// when K fits one chunk).  The two TMEM buffers also let the epilogue of one
+// unit overlap the main loop of the next.
+//
+// Split K.  When the output has fewer tiles than the GPU has SMs (weight
+// gradients, x^T dy over batch*seq rows) and the caller passes a workspace,
+// the K range is cut into `slices` and each slice is a work unit.  The slices
+// of a tile add into the output in slice order (deterministic): slice s waits
+// until the tile's counter in the workspace reads s, adds its partial sum to
+// what slices 0..s-1 stored, and sets the counter to s + 1.  Every slice of a
+// tile sits in the same round of the persistent loop (the grid is a multiple
+// of `slices`), on CTAs of increasing index, so each wait is on a CTA that is
+// already running; all waits are bounded.
+#include "fa2_common.cuh"
 
 namespace ct {
+namespace {
 
-bool linear_tc_supported(const GemmProblem&) { return false; }
+using fa2::mbar_drain;
+using fa2::status_raised;
+using fa2::warp_wait;
 
-int launch_linear_tc(const GemmProblem&, const DeviceInfo&, cudaStream_t) {
-  return CT_ERR_INVALID_ARGUMENT;
+constexpr int kBM = 128;
+constexpr int kBK = 32;
+constexpr int kChunkKb = 16;  // K blocks per TMEM accumulation chunk (K = 512)
+constexpr int kThreadsG = 256;
+constexpr int kPrepWarp0 = 2, kPrepThreads = 64, kEpiWarp0 = 4;
+
+template <int BN_, int SPLIT_, int NS_>
+struct GemmCfg {
+  static constexpr int BN = BN_, SPLIT = SPLIT_, NS = NS_;
+  static constexpr uint32_t A_TILE = kBM * kBK * 4u;      // 16 KB
+  static constexpr uint32_t B_TILE = (uint32_t)BN * kBK * 4u;
+  static constexpr uint32_t RAW = A_TILE + B_TILE;         // bytes TMA writes per stage
+  static constexpr uint32_t OFF_A = 0, OFF_B = A_TILE;
+  static constexpr uint32_t LO = RAW;                      // 3xTF32 low parts, same layout
+  static constexpr uint32_t STAGE = (SPLIT == 3 ? 2u : 1u) * RAW;
+  // TMEM: two accumulator buffers, then (BN = 128) the running sum of chunks
+  static constexpr uint32_t TC_SUM = 2u * BN;
+  static constexpr bool FOLD = BN <= 128;  // multi-chunk K allowed
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(BN == 128 || BN == 256, "tile width");
+  static_assert(!FOLD || TC_SUM + BN <= TMEM_COLS, "TMEM budget");
+  static_assert(STAGE % 1024 == 0, "stage alignment");
+};
+
+struct GemmBars {
+  uint64_t full[8], ready[8], empty[8];
+  uint64_t acc_full[2], acc_empty[2], stored, mma_final;
+  CtaCtl ctl;
+};
+
+struct GemmParams {
+  int m, n, batch;
+  int tiles_m, tiles_n, units;
+  int kb_total;  // number of 32-deep K blocks
+  int slices, kb_per_slice;
+  int a_mn, b_mn, w_batched;
+  const float* bias;
+  int64_t bias_s;
+  float* out;
+  uint32_t* sem;  // one counter per tile (slices > 1)
+  uint32_t* status;
+};
+
+template <class C>
+constexpr size_t gemm_smem_bytes() {
+  static_assert(sizeof(GemmBars) <= 1024, "barrier block");
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
+}
+
+struct Unit {
+  int tile, slice, b, m0, n0, kb0, kb1;
+};
+__device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p, int bn) {
+  Unit w;
+  w.slice = u % p.slices;
+  w.tile = u / p.slices;
+  const int tn = w.tile % p.tiles_n;
+  const int t = w.tile / p.tiles_n;
+  w.b = t / p.tiles_m;
+  w.m0 = (t % p.tiles_m) * kBM;
+  w.n0 = tn * bn;
+  w.kb0 = w.slice * p.kb_per_slice;
+  w.kb1 = min(p.kb_total, w.kb0 + p.kb_per_slice);
+  return w;
+}
+
+__device__ __forceinline__ int n_chunks(int kbs) { return (kbs + kChunkKb - 1) / kChunkKb; }
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *sem == want (split-K slice order).
+__device__ __forceinline__ bool sem_wait(const uint32_t* sem, uint32_t want, CtaCtl* ctl,
+                                         uint32_t* status) {
+  if (ld_acquire_gpu(sem) == want) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(128);
+    if (ld_acquire_gpu(sem) == want) return true;
+    if ((i & 15u) == 0u) {
+      if (ctl->abort || status_raised(status)) {
+        ctl->abort = 1u;
+        return false;
+      }
+      if (globaltimer_ns() - t0 > CT_WAIT_TIMEOUT_NS) {
+        ctl->abort = 1u;
+        atomicOr(status, CT_DEVSTAT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Epilogue of one 32-column slice of a tile row: adds the bias (first slice)
+// or the partial sum the earlier slices stored (later slices), then stores.
+__device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p, float* orow,
+                                            int col0, bool vec_ok, bool first_slice) {
+  const int n = p.n;
+  if (col0 >= n) return;
+  const bool full = col0 + 32 <= n;
+  if (!first_slice) {
+    if (full && vec_ok) {
+      const float4* o4 = reinterpret_cast<const float4*>(orow + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 q = __ldcg(o4 + i);  // written by another SM: read from L2
+        v[4 * i] += q.x; v[4 * i + 1] += q.y; v[4 * i + 2] += q.z; v[4 * i + 3] += q.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < n) v[i] += __ldcg(orow + col0 + i);
+    }
+  } else if (full && p.bias_s == 1 && ((reinterpret_cast<uintptr_t>(p.bias + col0) & 15u) == 0)) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 bb = __ldg(b4 + i);
+      v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < n) v[i] += __ldg(p.bias + (int64_t)(col0 + i) * p.bias_s);
+  }
+  if (full && vec_ok) {
+    float4* d4 = reinterpret_cast<float4*>(orow + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < n) orow[col0 + i] = v[i];
+  }
+}
+
+template <class C>
+__global__ void __launch_bounds__(kThreadsG, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  constexpr int BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  // the host never launches a multi-chunk unit without TMEM for the sum
+  if (!C::FOLD && n_chunks(min(p.kb_per_slice, p.kb_total)) > 1) return;
+  auto* bars = reinterpret_cast<GemmBars*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(GemmBars) + 1023u) & ~1023u;
+  CtaCtl* ctl = &bars->ctl;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(B(bars->full[s]), 1);
+      mbar_init(B(bars->ready[s]), kPrepThreads);
+      mbar_init(B(bars->empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(B(bars->acc_full[i]), 1);
+      mbar_init(B(bars->acc_empty[i]), 128);
+    }
+    mbar_init(B(bars->stored), 128);
+    mbar_init(B(bars->mma_final), 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int last[NS];
+      for (int s = 0; s < NS; ++s) last[s] = -1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        const Unit w = decode_unit(u, p, BN);
+        const int wb = p.w_batched ? w.b : 0;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          const int s = (int)(it % NS), r = (int)(it / NS);
+          const uint32_t st = tiles + s * C::STAGE;
+          if (r > 0 && !mbar_wait(B(bars->empty[s]), (r - 1) & 1, ctl, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = B(bars->full[s]);
+          mbar_arrive_expect_tx(bar, C::RAW);
+          const int k0 = kb * kBK;
+          if (p.a_mn) {
+#pragma unroll
+            for (int c = 0; c < kBM / 32; ++c)
+              tma_load_3d(st + C::OFF_A + c * 4096u, &tmA, bar, w.m0 + 32 * c, k0, w.b);
+          } else {
+            tma_load_3d(st + C::OFF_A, &tmA, bar, k0, w.m0, w.b);
+          }
+          if (p.b_mn) {
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c)
+              tma_load_3d(st + C::OFF_B + c * 4096u, &tmB, bar, w.n0 + 32 * c, k0, wb);
+          } else {
+            tma_load_3d(st + C::OFF_B, &tmB, bar, k0, w.n0, wb);
+          }
+          last[s] = r;
+        }
+      }
+      if (ctl->abort) {  // let every issued copy land before the CTA exits
+        for (int s = 0; s < NS; ++s)
+          if (last[s] >= 0) mbar_drain(B(bars->full[s]), last[s] & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(kBM, BN, p.a_mn != 0, p.b_mn != 0);
+      // stage-0 descriptors; MN-major tiles are 32-element chunks of 32 K rows
+      const uint64_t ad0 = p.a_mn ? sdesc_mnmajor(tiles + C::OFF_A, 4096u) : sdesc_kmajor(tiles + C::OFF_A);
+      const uint64_t bd0 = p.b_mn ? sdesc_mnmajor(tiles + C::OFF_B, 4096u) : sdesc_kmajor(tiles + C::OFF_B);
+      const uint32_t astep = p.a_mn ? 1024u >> 4 : 32u >> 4;  // per 8-deep k step
+      const uint32_t bstep = p.b_mn ? 1024u >> 4 : 32u >> 4;
+      uint32_t it = 0, ci = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        const Unit w = decode_unit(u, p, BN);
+        for (int kc = w.kb0; ok && kc < w.kb1; kc += kChunkKb, ++ci) {
+          const int acc = (int)(ci & 1);
+          if (ci >= 2 && !mbar_wait(B(bars->acc_empty[acc]), ((ci >> 1) - 1) & 1, ctl, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + acc * BN;
+          const int kce = min(w.kb1, kc + kChunkKb);
+          for (int kb = kc; kb < kce; ++kb, ++it) {
+            const int s = (int)(it % NS), r = (int)(it / NS);
+            const uint32_t rbar = SPLIT == 3 ? B(bars->ready[s]) : B(bars->full[s]);
+            if (!mbar_wait(rbar, r & 1, ctl, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t ad = ad0 + ((s * C::STAGE) >> 4);
+            const uint64_t bd = bd0 + ((s * C::STAGE) >> 4);
+#pragma unroll
+            for (int j = 0; j < kBK / 8; ++j) {
+              const uint64_t a = ad + j * astep, b = bd + j * bstep;
+              umma_tf32_ss(d, a, b, idesc, (kb > kc || j > 0) ? 1u : 0u);
+              if constexpr (SPLIT == 3) {
+                umma_tf32_ss(d, a, b + (C::LO >> 4), idesc, 1u);
+                umma_tf32_ss(d, a + (C::LO >> 4), b, idesc, 1u);
+              }
+            }
+            umma_commit(B(bars->empty[s]));
+          }
+          if (ok) umma_commit(B(bars->acc_full[acc]));
+        }
+      }
+      umma_commit(B(bars->mma_final));  // nothing of ours in flight after this
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    // ------------------------------------------------ 3xTF32 split warps
+    if constexpr (SPLIT == 3) {
+      const uint32_t tid = threadIdx.x - kPrepWarp0 * 32;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        const Unit w = decode_unit(u, p, BN);
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          const int s = (int)(it % NS), r = (int)(it / NS);
+          const uint32_t st = tiles + s * C::STAGE;
+          if (!mbar_wait(B(bars->full[s]), r & 1, ctl, p.status)) {
+            ok = false;
+            break;
+          }
+          split_tile_smem(st, st + C::LO, C::RAW, tid, kPrepThreads);
+          fence_proxy_async_smem();
+          mbar_arrive(B(bars->ready[s]));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    const bool vec_ok = (p.n & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0);
+    uint32_t ci = 0, n_split = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+      const Unit w = decode_unit(u, p, BN);
+      const int row = w.m0 + r;
+      const bool valid = row < p.m;
+      float* orow = p.out + ((int64_t)w.b * p.m + (valid ? row : 0)) * p.n;
+      const int nch = n_chunks(w.kb1 - w.kb0);
+      for (int c = 0; c < nch; ++c, ++ci) {
+        const int acc = (int)(ci & 1);
+        const bool last = c == nch - 1;
+        if (!warp_wait(B(bars->acc_full[acc]), (ci >> 1) & 1, ctl, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (last && w.slice > 0 && !sem_wait(p.sem + w.tile, (uint32_t)w.slice, ctl, p.status))
+          ok = false;  // finish the protocol (free the accumulator), write nothing
+#pragma unroll 1
+        for (int q = 0; q < BN / 32; ++q) {
+          float v[32];
+          tmem_ld32(lb + acc * BN + 32 * q, v);
+          if (c > 0) {  // running sum of the earlier chunks, round-to-nearest adds
+            float s[32];
+            tmem_ld32(lb + C::TC_SUM + 32 * q, s);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += s[i];
+          }
+          if (!last) tmem_st32(lb + C::TC_SUM + 32 * q, v);
+          else if (valid && ok) store_row32(v, p, orow, w.n0 + 32 * q, vec_ok, w.slice == 0);
+        }
+        if (!last) tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(B(bars->acc_empty[acc]));
+      }
+      if (!ok) break;
+      if (p.slices > 1) {  // publish this slice: counter = slice + 1
+        __threadfence();
+        mbar_arrive(B(bars->stored));
+        if (r == 0) {
+          if (mbar_wait(B(bars->stored), n_split & 1, ctl, p.status))
+            st_release_gpu(p.sem + w.tile, (uint32_t)w.slice + 1u);
+          else
+            ok = false;
+        }
+        ++n_split;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Operand layout of x (A) and W (B) from their strides: K-major when the
+// reduction index is contiguous, MN-major when the row (x) / column (W) index
+// is.  Returns false when neither holds.
+bool a_layout(const GemmProblem& g, bool* mn) {
+  if (g.xs[2] == 1) { *mn = false; return true; }
+  if (g.xs[1] == 1) { *mn = true; return true; }
+  return false;
+}
+bool b_layout(const GemmProblem& g, bool* mn) {
+  if (g.ws[2] == 1) { *mn = true; return true; }
+  if (g.ws[1] == 1) { *mn = false; return true; }
+  return false;
+}
+
+// Byte stride of a TMA dimension; a dimension of extent 1 gets a stride that
+// is never used but satisfies the encoder (a non-zero multiple of 16 that
+// spans the dimensions inside it).
+uint64_t dim_stride(int64_t elems, int64_t extent, uint64_t fallback) {
+  return extent > 1 ? (uint64_t)elems * 4u : fallback;
+}
+uint64_t row_bytes16(int64_t inner) { return ((uint64_t)inner * 4u + 15u) & ~15ull; }
+
+int make_maps(const GemmProblem& g, bool a_mn, bool b_mn, int bn, CUtensorMap* ta,
+              CUtensorMap* tb) {
+  const int64_t wb = g.ws[0] == 0 ? 1 : g.batch;
+  {
+    const int64_t inner = a_mn ? g.m : g.k, outer = a_mn ? g.k : g.m;
+    const int64_t os = a_mn ? g.xs[2] : g.xs[1];
+    const uint64_t s1 = dim_stride(os, outer, row_bytes16(inner));
+    const uint64_t dims[3] = {(uint64_t)inner, (uint64_t)outer, (uint64_t)g.batch};
+    const uint64_t strides[2] = {s1, dim_stride(g.xs[0], g.batch, s1 * (uint64_t)outer)};
+    const uint32_t box[3] = {32u, a_mn ? (uint32_t)kBK : (uint32_t)kBM, 1u};
+    const int rc = make_tmap_f32(ta, g.x, 3, dims, strides, box, a_mn);
+    if (rc != CT_OK) return rc;
+  }
+  {
+    const int64_t inner = b_mn ? g.n : g.k, outer = b_mn ? g.k : g.n;
+    const int64_t os = b_mn ? g.ws[1] : g.ws[2];
+    const uint64_t s1 = dim_stride(os, outer, row_bytes16(inner));
+    const uint64_t dims[3] = {(uint64_t)inner, (uint64_t)outer, (uint64_t)wb};
+    const uint64_t strides[2] = {s1, dim_stride(g.ws[0], wb, s1 * (uint64_t)outer)};
+    const uint32_t box[3] = {32u, b_mn ? (uint32_t)kBK : (uint32_t)bn, 1u};
+    return make_tmap_f32(tb, g.w, 3, dims, strides, box, b_mn);
+  }
+}
+
+int64_t tile_count(const GemmProblem& g, int bn) {
+  return g.batch * ((g.m + kBM - 1) / kBM) * ((g.n + bn - 1) / bn);
+}
+
+// K split: slices of whole accumulation chunks, enough to give every SM a
+// unit, each slice at least two chunks deep.
+void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int* slices, int* kbps) {
+  const int kb_total = (int)((g.k + kBK - 1) / kBK);
+  *slices = 1;
+  *kbps = kb_total;
+  const int64_t tiles = tile_count(g, bn);
+  if (!have_ws || tiles * 2 > sms) return;
+  int s = (int)(sms / tiles);
+  const int max_s = kb_total / (2 * kChunkKb);
+  if (s > max_s) s = max_s;
+  if (s < 2) return;
+  int per = (kb_total + s - 1) / s;
+  per = (per + kChunkKb - 1) / kChunkKb * kChunkKb;
+  *kbps = per;
+  *slices = (kb_total + per - 1) / per;
+}
+
+template <class C>
+int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_bytes,
+               const DeviceInfo& dev, cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap ta, tb;
+  int rc = make_maps(g, a_mn, b_mn, C::BN, &ta, &tb);
+  if (rc != CT_OK) return rc;
+  const size_t smem = gemm_smem_bytes<C>();
+  rc = ensure_smem_attr(linear_tc_kernel<C>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  GemmParams p;
+  p.m = (int)g.m;
+  p.n = (int)g.n;
+  p.batch = (int)g.batch;
+  p.tiles_m = (int)((g.m + kBM - 1) / kBM);
+  p.tiles_n = (int)((g.n + C::BN - 1) / C::BN);
+  p.kb_total = (int)((g.k + kBK - 1) / kBK);
+  const int64_t tiles = tile_count(g, C::BN);
+  const bool have_ws = ws != nullptr && ws_bytes >= (size_t)tiles * 4u;
+  pick_split(g, C::BN, dev.sm_count, have_ws, &p.slices, &p.kb_per_slice);
+  p.units = (int)(tiles * p.slices);
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.w_batched = g.ws[0] != 0;
+  p.bias = g.bias;
+  p.bias_s = g.bias_s;
+  p.out = g.out;
+  p.sem = static_cast<uint32_t*>(ws);
+  p.status = dev.status;
+  int grid = p.units < dev.sm_count ? p.units : dev.sm_count;
+  if (p.slices > 1) {
+    grid = grid / p.slices * p.slices;  // whole tiles per round of the persistent loop
+    if (cudaMemsetAsync(ws, 0, (size_t)tiles * 4u, st) != cudaSuccess) return CT_ERR_CUDA;
+  }
+  linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, p);
+  return check_launch();
+}
+
+// Tile width: BN = 256 needs K within one accumulation chunk; otherwise the
+// choice minimises (waves of tiles) x (tile cost), a 128-wide tile costing a
+// little more than half a 256-wide one (x re-read, per-tile overhead).  The
+// environment variable CT_GEMM_BN (128 or 256) overrides it (tuning).
+int pick_bn(const GemmProblem& g, int sms) {
+  const int64_t kb = (g.k + kBK - 1) / kBK;
+  if (kb > kChunkKb || g.n <= 128) return 128;
+  static const int env = [] {
+    const char* e = std::getenv("CT_GEMM_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (env == 128 || env == 256) return env;
+  auto cost = [&](int bn, double rel) {
+    const int64_t waves = (tile_count(g, bn) + sms - 1) / sms;
+    return (double)waves * rel;
+  };
+  return cost(256, 1.0) <= cost(128, 0.59) ? 256 : 128;
+}
+
+}  // namespace
+
+size_t linear_workspace_bytes(int64_t batch, int64_t m, int64_t n) {
+  if (batch <= 0 || m <= 0 || n <= 0) return 0;
+  const int64_t tiles = batch * ((m + kBM - 1) / kBM) * ((n + 127) / 128);
+  return (size_t)((tiles * 4 + 255) / 256 * 256);
+}
+
+bool linear_tc_supported(const GemmProblem& g) {
+  if (g.precision != CT_PRECISION_3XTF32 && g.precision != CT_PRECISION_TF32) return false;
+  if (g.m <= 0 || g.n <= 0 || g.k <= 0 || g.batch <= 0) return false;
+  if (g.m >= (1ll << 31) || g.n >= (1ll << 31) || g.k >= (1ll << 31) || g.batch >= (1ll << 31))
+    return false;
+  if (tile_count(g, 128) >= (1ll << 26)) return false;  // units (tiles x slices) fit an int
+  bool amn, bmn;
+  if (!a_layout(g, &amn) || !b_layout(g, &bmn)) return false;
+  const int64_t a_outer[2] = {amn ? g.xs[2] : g.xs[1], g.xs[0]};
+  const int64_t b_outer[2] = {bmn ? g.ws[1] : g.ws[2], g.ws[0]};
+  auto ok = [](const void* base, const int64_t* outer, int64_t ext1, int64_t ext2) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+    if (ext1 > 1 && (outer[0] <= 0 || (outer[0] * 4) % 16 != 0)) return false;
+    if (ext2 > 1 && (outer[1] <= 0 || (outer[1] * 4) % 16 != 0)) return false;
+    return true;
+  };
+  const int64_t wb = g.ws[0] == 0 ? 1 : g.batch;
+  return ok(g.x, a_outer, amn ? g.k : g.m, g.batch) && ok(g.w, b_outer, bmn ? g.k : g.n, wb);
+}
+
+int launch_linear_tc(const GemmProblem& g, void* ws, size_t ws_bytes, const DeviceInfo& dev,
+                     cudaStream_t st) {
+  if (!linear_tc_supported(g)) return CT_ERR_UNSUPPORTED_LAYOUT;
+  bool amn = false, bmn = false;
+  a_layout(g, &amn);
+  b_layout(g, &bmn);
+  const bool split = g.precision == CT_PRECISION_3XTF32;
+  if (pick_bn(g, dev.sm_count) == 256)
+    return split ? run_linear<GemmCfg<256, 3, 2>>(g, amn, bmn, ws, ws_bytes, dev, st)
+                 : run_linear<GemmCfg<256, 1, 4>>(g, amn, bmn, ws, ws_bytes, dev, st);
+  return split ? run_linear<GemmCfg<128, 3, 3>>(g, amn, bmn, ws, ws_bytes, dev, st)
+               : run_linear<GemmCfg<128, 1, 6>>(g, amn, bmn, ws, ws_bytes, dev, st);
 }
 
 }  // namespace ct

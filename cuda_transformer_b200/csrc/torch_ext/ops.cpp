@@ -168,9 +168,13 @@ Tensor fma_impl(const Tensor& x, Tensor weights, const Tensor& bias, int64_t pre
   Tensor out = at::empty({batch, m, n}, x.options());
   const int64_t xs[3] = {x.stride(0), x.stride(1), x.stride(2)};
   const int64_t wsd[3] = {weights.stride(0), weights.stride(1), weights.stride(2)};
-  check_rc(ct_linear_fwd(x.data_ptr<float>(), xs, weights.data_ptr<float>(), wsd,
-                         bias.data_ptr<float>(), bias.stride(0), out.data_ptr<float>(), batch, m,
-                         k, n, weights.size(0), (int)precision, cur_stream()),
+  // per-tile counters of the split-K schedule (a few hundred bytes)
+  const size_t wsb = ct_linear_workspace_size(batch, m, k, n);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(wsb, 16)}, x.options().dtype(at::kByte));
+  check_rc(ct_linear_fwd_ws(x.data_ptr<float>(), xs, weights.data_ptr<float>(), wsd,
+                            bias.data_ptr<float>(), bias.stride(0), out.data_ptr<float>(), batch,
+                            m, k, n, weights.size(0), (int)precision, ws.data_ptr(), wsb,
+                            cur_stream()),
            "cuda_fma");
   return out;
 }

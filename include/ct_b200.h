@@ -164,6 +164,24 @@ int ct_linear_fwd(const float* x, const int64_t x_stride[3],
                   int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
                   int precision, void* stream);
 
+/* Device workspace (bytes, possibly 0) that ct_linear_fwd_ws may use to split
+ * the K reduction across SMs when the output has few tiles (the weight
+ * gradient x^T dy over batch*seq rows). */
+size_t ct_linear_workspace_size(int64_t batch, int64_t m, int64_t k, int64_t n);
+
+/* ct_linear_fwd with a caller-owned device workspace of workspace_bytes
+ * (>= ct_linear_workspace_size for the split-K schedule; smaller or NULL
+ * disables it).  The slices of a split reduction are added in a fixed order,
+ * so results are deterministic.  The workspace must not be used by another
+ * call that can run concurrently.  Same reference counterpart as
+ * ct_linear_fwd (Transformer_launchers/linear_layer.cu:28-70). */
+int ct_linear_fwd_ws(const float* x, const int64_t x_stride[3],
+                     const float* w, const int64_t w_stride[3],
+                     const float* bias, int64_t bias_stride,
+                     float* out,
+                     int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
+                     int precision, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of workspace ct_bias_grad needs. */
 size_t ct_bias_grad_workspace_size(int64_t batch, int64_t m, int64_t n);
 

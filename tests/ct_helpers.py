@@ -51,13 +51,22 @@ def fa2_delta(o, do):
     return delta
 
 
-def linear_fwd(x, w, b, precision=cb.PRECISION_3XTF32):
+def linear_fwd(x, w, b, precision=cb.PRECISION_3XTF32, workspace=False):
+    """ct_linear_fwd, or ct_linear_fwd_ws with a workspace (split-K allowed)."""
     w3 = w if w.dim() == 3 else w.unsqueeze(0)
     batch, m, k = x.shape
     n = w3.shape[2]
     out = torch.empty(batch, m, n, device=x.device, dtype=torch.float32)
-    rc = cb.lib().ct_linear_fwd(_p(x), cb.strides(x), _p(w3), cb.strides(w3), _p(b), b.stride(0),
-                                _p(out), batch, m, k, n, w3.shape[0], precision, _stream())
+    if workspace:
+        wsb = cb.lib().ct_linear_workspace_size(batch, m, k, n)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x.device)
+        rc = cb.lib().ct_linear_fwd_ws(_p(x), cb.strides(x), _p(w3), cb.strides(w3), _p(b),
+                                       b.stride(0), _p(out), batch, m, k, n, w3.shape[0],
+                                       precision, _p(ws), wsb, _stream())
+    else:
+        rc = cb.lib().ct_linear_fwd(_p(x), cb.strides(x), _p(w3), cb.strides(w3), _p(b),
+                                    b.stride(0), _p(out), batch, m, k, n, w3.shape[0], precision,
+                                    _stream())
     cb.check(rc, "ct_linear_fwd")
     return out
 

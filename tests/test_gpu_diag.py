@@ -57,3 +57,4 @@ def test_tf32_operand_rounding_rule(cuda_device, record_property):
     print("tf32 operand rule:", "truncate" if is_trunc else ("round" if is_round else "other"))
     assert is_trunc, "3xTF32 split assumes the tensor core truncates FP32 operands to TF32"
     H.assert_device_clean()
+
