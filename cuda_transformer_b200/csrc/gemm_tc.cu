@@ -42,6 +42,8 @@
 // tile sits in the same round of the persistent loop (the grid is a multiple
 // of `slices`), on CTAs of increasing index, so each wait is on a CTA that is
 // already running; all waits are bounded.
+#include <cstring>
+
 #include "fa2_common.cuh"
 
 namespace ct {
@@ -92,13 +94,19 @@ struct GemmParams {
   float* out;
   uint32_t* sem;  // one counter per tile (slices > 1)
   uint32_t* status;
+  int tma_out;    // epilogue stores through TMA (tmO) instead of per-thread rows
 };
+
+// Epilogue staging: two 32 x 32 FP32 tiles (4 KB each, 128-byte swizzle) per
+// epilogue warp, after the stage ring.
+constexpr uint32_t kStageOut = 4u * 2u * 4096u;
 
 template <class C>
 constexpr size_t gemm_smem_bytes() {
   static_assert(sizeof(GemmBars) <= 1024, "barrier block");
-  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
-  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut <= 227 * 1024,
+                "shared memory budget");
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut;
 }
 
 struct Unit {
@@ -151,8 +159,26 @@ __device__ __forceinline__ bool sem_wait(const uint32_t* sem, uint32_t want, Cta
   }
 }
 
-// Epilogue of one 32-column slice of a tile row: adds the bias (first slice)
-// or the partial sum the earlier slices stored (later slices), then stores.
+// v[i] += bias[col0 + i] for the columns inside the output.
+__device__ __forceinline__ void add_bias32(float (&v)[32], const GemmParams& p, int col0) {
+  const int n = p.n;
+  if (col0 + 32 <= n && p.bias_s == 1 && ((reinterpret_cast<uintptr_t>(p.bias + col0) & 15u) == 0)) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 bb = __ldg(b4 + i);
+      v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < n) v[i] += __ldg(p.bias + (int64_t)(col0 + i) * p.bias_s);
+  }
+}
+
+// Per-thread epilogue of one 32-column slice of a tile row (outputs TMA
+// cannot address): adds the bias (first slice) or the partial sum the earlier
+// slices stored (later slices), then stores the row.
 __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p, float* orow,
                                             int col0, bool vec_ok, bool first_slice) {
   const int n = p.n;
@@ -171,17 +197,8 @@ __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p,
       for (int i = 0; i < 32; ++i)
         if (col0 + i < n) v[i] += __ldcg(orow + col0 + i);
     }
-  } else if (full && p.bias_s == 1 && ((reinterpret_cast<uintptr_t>(p.bias + col0) & 15u) == 0)) {
-    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 bb = __ldg(b4 + i);
-      v[4 * i] += bb.x; v[4 * i + 1] += bb.y; v[4 * i + 2] += bb.z; v[4 * i + 3] += bb.w;
-    }
   } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (col0 + i < n) v[i] += __ldg(p.bias + (int64_t)(col0 + i) * p.bias_s);
+    add_bias32(v, p, col0);
   }
   if (full && vec_ok) {
     float4* d4 = reinterpret_cast<float4*>(orow + col0);
@@ -198,7 +215,7 @@ __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p,
 template <class C>
 __global__ void __launch_bounds__(kThreadsG, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
   constexpr int BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
@@ -352,16 +369,22 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Warp q owns tile rows 32q..32q+31.  With tma_out each 32 x 32 piece is
+    // staged in this warp's swizzled buffer (thread = row) and written by one
+    // TMA store -- or, for split-K slices after the first, one TMA add.
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
     const bool vec_ok = (p.n & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0);
-    uint32_t ci = 0, n_split = 0;
+    const uint32_t stg = tiles + NS * C::STAGE + (uint32_t)quad * 2u * 4096u;
+    if (p.tma_out && lane == 0) tma_prefetch_desc(&tmO);
+    uint32_t ci = 0, n_split = 0, n_out = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const Unit w = decode_unit(u, p, BN);
       const int row = w.m0 + r;
       const bool valid = row < p.m;
+      const bool rows_in = w.m0 + 32 * quad < p.m;  // warp-uniform
       float* orow = p.out + ((int64_t)w.b * p.m + (valid ? row : 0)) * p.n;
       const int nch = n_chunks(w.kb1 - w.kb0);
       for (int c = 0; c < nch; ++c, ++ci) {
@@ -372,8 +395,12 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           break;
         }
         tc_fence_after();
-        if (last && w.slice > 0 && !sem_wait(p.sem + w.tile, (uint32_t)w.slice, ctl, p.status))
-          ok = false;  // finish the protocol (free the accumulator), write nothing
+        if (last && w.slice > 0) {
+          if (sem_wait(p.sem + w.tile, (uint32_t)w.slice, ctl, p.status))
+            fence_proxy_async_global();  // the TMA add below follows the acquire
+          else
+            ok = false;  // finish the protocol (free the accumulator), write nothing
+        }
 #pragma unroll 1
         for (int q = 0; q < BN / 32; ++q) {
           float v[32];
@@ -384,15 +411,45 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] += s[i];
           }
-          if (!last) tmem_st32(lb + C::TC_SUM + 32 * q, v);
-          else if (valid && ok) store_row32(v, p, orow, w.n0 + 32 * q, vec_ok, w.slice == 0);
+          const int col0 = w.n0 + 32 * q;
+          if (!last) {
+            tmem_st32(lb + C::TC_SUM + 32 * q, v);
+          } else if (!__all_sync(0xffffffffu, ok)) {
+            // a wait of this unit failed: nothing is written
+          } else if (p.tma_out) {
+            if (rows_in && col0 < p.n) {
+              if (w.slice == 0) add_bias32(v, p, col0);
+              const uint32_t buf = stg + (n_out & 1u) * 4096u;
+              if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                sts128(buf + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4),
+                       make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (w.slice == 0) tma_store_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
+                else tma_reduce_add_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
+                bulk_commit_group();
+              }
+              ++n_out;
+            }
+          } else if (valid) {
+            store_row32(v, p, orow, col0, vec_ok, w.slice == 0);
+          }
         }
         if (!last) tmem_wait_st();
         tc_fence_before();
         mbar_arrive(B(bars->acc_empty[acc]));
       }
-      if (!ok) break;
+      if (!__all_sync(0xffffffffu, ok)) break;
       if (p.slices > 1) {  // publish this slice: counter = slice + 1
+        if (p.tma_out && lane == 0) {
+          bulk_wait_group<0>();  // this warp's TMA writes are done
+          fence_proxy_async_global();
+        }
+        __syncwarp();
         __threadfence();
         mbar_arrive(B(bars->stored));
         if (r == 0) {
@@ -404,6 +461,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         ++n_split;
       }
     }
+    if (p.tma_out && lane == 0) bulk_wait_group<0>();  // staging buffers are read before exit
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -482,13 +541,26 @@ void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int* slices
   *slices = (kb_total + per - 1) / per;
 }
 
+// TMA map of the dense output [batch, m, n] with 32 x 32 boxes (epilogue);
+// false when TMA cannot address it (n not a multiple of 4, unaligned base).
+bool make_out_map(const GemmProblem& g, CUtensorMap* to) {
+  if ((g.n & 3) != 0 || (reinterpret_cast<uintptr_t>(g.out) & 15u) != 0) return false;
+  const uint64_t s1 = (uint64_t)g.n * 4u;
+  const uint64_t dims[3] = {(uint64_t)g.n, (uint64_t)g.m, (uint64_t)g.batch};
+  const uint64_t strides[2] = {s1, s1 * (uint64_t)g.m};
+  const uint32_t box[3] = {32u, 32u, 1u};
+  return make_tmap_f32(to, g.out, 3, dims, strides, box, false) == CT_OK;
+}
+
 template <class C>
 int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_bytes,
                const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   int rc = make_maps(g, a_mn, b_mn, C::BN, &ta, &tb);
   if (rc != CT_OK) return rc;
+  const bool tma_out = make_out_map(g, &to);
+  if (!tma_out) std::memset(&to, 0, sizeof(to));
   const size_t smem = gemm_smem_bytes<C>();
   rc = ensure_smem_attr(linear_tc_kernel<C>, smem, dev.device, &attr_done);
   if (rc != CT_OK) return rc;
@@ -511,12 +583,13 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   p.out = g.out;
   p.sem = static_cast<uint32_t*>(ws);
   p.status = dev.status;
+  p.tma_out = tma_out ? 1 : 0;
   int grid = p.units < dev.sm_count ? p.units : dev.sm_count;
   if (p.slices > 1) {
     grid = grid / p.slices * p.slices;  // whole tiles per round of the persistent loop
     if (cudaMemsetAsync(ws, 0, (size_t)tiles * 4u, st) != cudaSuccess) return CT_ERR_CUDA;
   }
-  linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, p);
+  linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, to, p);
   return check_launch();
 }
 

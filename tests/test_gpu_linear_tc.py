@@ -140,3 +140,17 @@ def test_unaligned_strides_fall_back(cuda_device):
     b = torch.randn(120, generator=_gen(16)).to(cuda_device)
     out = H.linear_fwd(x, w, b, cb.PRECISION_3XTF32)
     assert H.rel_err(out, ref_linear(x, w, b)) < 1e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("workspace", [False, True])
+@pytest.mark.parametrize("batch,m,k,n", [(1, 300, 96, 118), (2, 200, 3000, 70)])
+def test_output_rows_not_16_byte_aligned(cuda_device, workspace, batch, m, k, n):
+    """n not a multiple of 4: the output rows cannot be TMA-stored, so the
+    epilogue writes rows per thread (x and W^T still arrive by TMA)."""
+    x = make_x(batch, m, k, False, 20, cuda_device)
+    w = make_w(1, k, n, False, 21, cuda_device)
+    b = torch.randn(n, generator=_gen(22)).to(cuda_device)
+    out = H.linear_fwd(x, w, b, cb.PRECISION_3XTF32, workspace=workspace)
+    assert H.rel_err(out, ref_linear(x, w, b)) < 5e-6
+    H.assert_device_clean()
