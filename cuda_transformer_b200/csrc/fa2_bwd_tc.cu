@@ -323,14 +323,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(B(bars->s_free));
       const int kv0 = j * BN;
       const bool need_mask = !valid || (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
+      // straight-line exponentials, then the mask as a separate pass on the
+      // few boundary tiles (a test per column would split the unrolled loop
+      // into one basic block per column and serialise it)
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        float e = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
-        if (need_mask) {
+      for (int i = 0; i < BN; ++i) pv[i] = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
+      if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
           const int kv = kv0 + i;
-          if (!(valid && kv < T && (!p.causal || kv <= row))) e = 0.0f;
+          pv[i] = (valid && kv < T && (!p.causal || kv <= row)) ? pv[i] : 0.0f;
         }
-        pv[i] = e;
       }
       if (!(ok = warp_wait(B(bars->dp_full), j & 1, ctl, p.status))) break;
       tc_fence_after();
@@ -502,17 +505,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       float pv[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32];
+        float t[32], lo[32], lv[32];
         tmem_ld32(lb + C::TC_S + 32 * c, t);
+        load_vec32(vl + 32 * c, lv);
+        // straight-line exponentials; the mask is a separate pass on the few
+        // boundary tiles (a test per column would serialise the loop)
+#pragma unroll
+        for (int x = 0; x < 32; ++x) t[x] = ex2_approx(fmaf(t[x], p.scale_log2, -lv[x]));
+        if (need_mask) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int q = qs + 32 * c + x;
+            t[x] = (valid && q < T && (!p.causal || q >= row)) ? t[x] : 0.0f;
+          }
+        }
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
-          const int cc = 32 * c + x;
-          float e = ex2_approx(fmaf(t[x], p.scale_log2, -vl[cc]));
-          if (need_mask) {
-            const int q = qs + cc;
-            if (!(valid && q < T && (!p.causal || q >= row))) e = 0.0f;
-          }
-          pv[cc] = e;
+          const float e = t[x];
+          pv[32 * c + x] = e;
           if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
           else t[x] = tf32_round(e);
         }
@@ -526,12 +536,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32];
+        float t[32], lo[32], dv[32];
         tmem_ld32(lb + C::TC_DP + 32 * c, t);
+        load_vec32(vl + BN + 32 * c, dv);
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
           const int cc = 32 * c + x;
-          const float ds = pv[cc] * (t[x] - vl[BN + cc]);
+          const float ds = pv[cc] * (t[x] - dv[x]);
           if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
           else t[x] = tf32_round(ds);
         }

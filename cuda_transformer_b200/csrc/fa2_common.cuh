@@ -99,6 +99,17 @@ __device__ __forceinline__ void mask_cols32(float (&t)[32], int kv0, int T, int 
   }
 }
 
+// 32 consecutive floats from 16-byte aligned shared memory (every lane of a
+// warp reads the same address: broadcast).
+__device__ __forceinline__ void load_vec32(const float* src, float (&v)[32]) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 x = s4[i];
+    v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+  }
+}
+
 __device__ __forceinline__ float max32(const float (&t)[32]) {
   float m[8];
 #pragma unroll
