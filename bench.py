@@ -240,19 +240,21 @@ class Fa2Runner:
     """Holds one rank's inputs/outputs in HBM and launches the kernels through
     the C ABI (libct_b200.so) on the current stream."""
 
-    def __init__(self, pairs: int, dev, precision: int, seed: int):
+    def __init__(self, pairs: int, dev, precision: int, seed: int, n: int = N,
+                 causal: bool = CAUSAL):
         import torch
 
         import cuda_transformer_b200 as cb
 
         self.cb, self.lib, self.torch = cb, cb.lib(), torch
         self.P, self.prec, self.dev = pairs, precision, dev
+        self.n, self.causal = n, int(causal)
         g = torch.Generator(device=dev).manual_seed(seed)
-        shape = (1, pairs, N, D)
+        shape = (1, pairs, n, D)
         self.q, self.k, self.v, self.do = (torch.randn(shape, device=dev, generator=g) for _ in range(4))
         self.o, self.dq, self.dk, self.dv = (torch.empty(shape, device=dev) for _ in range(4))
-        self.lse = torch.empty(1, pairs, N, device=dev)
-        self.delta = torch.empty(1, pairs, N, device=dev)
+        self.lse = torch.empty(1, pairs, n, device=dev)
+        self.delta = torch.empty(1, pairs, n, device=dev)
         self.s4 = (ctypes.c_int64 * 4)(*self.q.stride())
         self.s3 = (ctypes.c_int64 * 3)(*self.lse.stride())
         self.launches_per_step = 4
@@ -266,27 +268,28 @@ class Fa2Runner:
     def fwd(self):
         p, s4 = self._p, self.s4
         self.cb.check(self.lib.ct_fa2_fwd(p(self.q), s4, p(self.k), s4, p(self.v), s4, p(self.o),
-                                          p(self.lse), 1, self.P, N, D, int(CAUSAL), self.prec,
-                                          self._st()), "fwd")
+                                          p(self.lse), 1, self.P, self.n, D, self.causal,
+                                          self.prec, self._st()), "fwd")
 
     def delta_k(self):
         p, s4 = self._p, self.s4
         self.cb.check(self.lib.ct_fa2_bwd_delta(p(self.o), s4, p(self.do), s4, p(self.delta), 1,
-                                                self.P, N, D, self._st()), "delta")
+                                                self.P, self.n, D, self._st()), "delta")
 
     def dq_k(self):
         p, s4 = self._p, self.s4
         self.cb.check(self.lib.ct_fa2_bwd_dq(p(self.q), s4, p(self.k), s4, p(self.v), s4,
                                              p(self.do), s4, p(self.lse), self.s3, p(self.delta),
-                                             p(self.dq), 1, self.P, N, D, int(CAUSAL), self.prec,
-                                             self._st()), "dq")
+                                             p(self.dq), 1, self.P, self.n, D, self.causal,
+                                             self.prec, self._st()), "dq")
 
     def dkdv_k(self):
         p, s4 = self._p, self.s4
         self.cb.check(self.lib.ct_fa2_bwd_dkdv(p(self.q), s4, p(self.k), s4, p(self.v), s4,
                                                p(self.do), s4, p(self.lse), self.s3,
                                                p(self.delta), p(self.dk), p(self.dv), 1, self.P,
-                                               N, D, int(CAUSAL), self.prec, self._st()), "dkdv")
+                                               self.n, D, self.causal, self.prec, self._st()),
+                      "dkdv")
 
     def step(self):
         self.fwd()
@@ -377,6 +380,33 @@ def e2e_steps(pairs: int, dev, precision: int, steps: int, dist, world: int, see
     return {"ms": ms, "h2d": h2d * world, "d2h": d2h * world}
 
 
+SWEEP_N = (1024, 2048, 4096, 8192, 16384)
+
+
+def run_sweep(args, pairs, s0, dev, prec, dist, world, rank) -> None:
+    """B=4, H=32, D=64, non-causal fwd+bwd at each sequence length; the 128
+    (b,h) pairs are split across ranks; one JSON line per length (max over
+    ranks of the device time)."""
+    import torch
+
+    for n in SWEEP_N:
+        runner = Fa2Runner(pairs, dev, prec, seed=3000 + s0, n=n, causal=False)
+        steps = max(1, min(args.steps, 4 if n >= 8192 else args.steps))
+        ms = timed_steps(runner, steps, args.warmup, dist, world)
+        kern = runner.kernel_times_ms(reps=1)
+        flops = fa2_flops(PAIRS, n, D, False, "fwd+bwd")
+        if rank == 0:
+            print(json.dumps({
+                "metric": "FA2 fwd+bwd TFLOPS, N sweep (B4,H32,D64, non-causal)", "N": n,
+                "value": flops * steps / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "n_gpus": world,
+                "steps": steps, "ms_per_step": ms / steps, "precision": args.precision,
+                "scaling": "strong", "gflop_per_step": flops / 1e9, "kernel_ms_rank0": kern,
+                "config": {"workload": f"FA2 fwd+bwd B4 H32 N{n} D64 non-causal (BASELINE config 3)",
+                           "pairs_per_rank": pairs}}), flush=True)
+        del runner
+        torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,6 +416,8 @@ def main() -> None:
     ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sweep", action="store_true",
+                    help="sequence-length sweep (non-causal N = 1024..16384) instead of the headline")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -409,6 +441,11 @@ def main() -> None:
     s0, s1 = shard(PAIRS, world, rank)
     pairs = s1 - s0
     prec = cb.PRECISION_3XTF32 if args.precision == "3xtf32" else cb.PRECISION_TF32
+    if args.sweep:
+        run_sweep(args, pairs, s0, dev, prec, dist, world, rank)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     alt = cb.PRECISION_TF32 if prec == cb.PRECISION_3XTF32 else cb.PRECISION_3XTF32
 
     runner = Fa2Runner(pairs, dev, prec, seed=1000 + s0)

@@ -1,0 +1,228 @@
+"""Data-parallel GPT training step built from the cuda_transformer operators.
+
+The model follows the reference GPT (gpt/gpt.py:47-175): token + position
+embedding, pre-LayerNorm decoder blocks (x + attn(ln1(x)), x + mlp(ln2(x))),
+causal FlashAttention-2 on the (B, nh, T, hs) views of the fused QKV
+projection, an exact-GELU 4x MLP, a final LayerNorm and the lm_head, with the
+cross-entropy loss.  Every linear layer, LayerNorm, GELU and attention runs on
+this package's kernels (CudaLinearLayer, CudaLayerNorm, CudaGeluLayer,
+CudaFlashAttention); the embeddings, the loss and AdamW are torch's.
+
+Default shape (the data-parallel benchmark configuration): 6 blocks,
+d_model 384, 6 heads of 64, context 256, vocabulary 65 with the lm_head tied to
+the token embedding, 64 sequences per GPU, AdamW lr 3e-4, weights
+N(0, 0.02).  Tokens are uniform in [0, vocab), seeded per rank, staged in
+pinned host memory and copied to the GPU inside every timed step (as the
+reference's Generate_Batch does, gpt/gpt.py:39-45).
+
+One process per GPU (torchrun); with more than one, gradients are averaged by
+torch DistributedDataParallel over NCCL: bucketed all-reduces that start
+while the backward is still running.  The step time is the maximum over ranks
+of the CUDA-event time of the timed steps.
+
+  python -m cuda_transformer_b200.gpt_case [--steps 20 --warmup 5]
+  torchrun --nproc-per-node N -m cuda_transformer_b200.gpt_case ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from cuda_autograd_fns import CudaFlashAttention, CudaGeluLayer, CudaLayerNorm, CudaLinearLayer
+
+
+class LayerNorm(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.alpha = nn.Parameter(torch.ones(d))
+        self.beta = nn.Parameter(torch.zeros(d))
+
+    def forward(self, x):
+        return CudaLayerNorm.apply(x, self.alpha, self.beta, 1e-5)
+
+
+class Attention(nn.Module):
+    def __init__(self, d, heads):
+        super().__init__()
+        self.heads, self.hs = heads, d // heads
+        self.qkv_weight = nn.Parameter(torch.empty(d, 3 * d).normal_(0.0, 0.02))
+        self.qkv_bias = nn.Parameter(torch.zeros(3 * d))
+        self.out_weight = nn.Parameter(torch.empty(d, d).normal_(0.0, 0.02))
+        self.out_bias = nn.Parameter(torch.zeros(d))
+
+    def forward(self, x):
+        B, T, C = x.shape
+        qkv = CudaLinearLayer.apply(x, self.qkv_weight, self.qkv_bias)
+        # strided (B, nh, T, hs) views: the attention kernels read them in place
+        q, k, v = (t.reshape(B, T, self.heads, self.hs).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+        o, _ = CudaFlashAttention.apply(q, k, v, True)
+        o = o.transpose(1, 2).reshape(B, T, C)
+        return CudaLinearLayer.apply(o, self.out_weight, self.out_bias)
+
+
+class MLP(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.fc1_weights = nn.Parameter(torch.empty(d, 4 * d).normal_(0.0, 0.02))
+        self.fc1_bias = nn.Parameter(torch.zeros(4 * d))
+        self.fc2_weights = nn.Parameter(torch.empty(4 * d, d).normal_(0.0, 0.02))
+        self.fc2_bias = nn.Parameter(torch.zeros(d))
+
+    def forward(self, x):
+        x = CudaLinearLayer.apply(x, self.fc1_weights, self.fc1_bias)
+        x = CudaGeluLayer.apply(x)
+        return CudaLinearLayer.apply(x, self.fc2_weights, self.fc2_bias)
+
+
+class Block(nn.Module):
+    def __init__(self, d, heads):
+        super().__init__()
+        self.ln1, self.attn, self.ln2, self.mlp = LayerNorm(d), Attention(d, heads), LayerNorm(d), MLP(d)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln1(x))
+        return x + self.mlp(self.ln2(x))
+
+
+class GPT(nn.Module):
+    def __init__(self, layers=6, d=384, heads=6, ctx=256, vocab=65, tied=True):
+        super().__init__()
+        self.tok = nn.Embedding(vocab, d)
+        self.pos = nn.Embedding(ctx, d)
+        nn.init.normal_(self.tok.weight, 0.0, 0.02)
+        nn.init.normal_(self.pos.weight, 0.0, 0.02)
+        self.blocks = nn.ModuleList([Block(d, heads) for _ in range(layers)])
+        self.ln = LayerNorm(d)
+        self.tied = tied
+        if not tied:
+            self.lm_head_weights = nn.Parameter(torch.empty(d, vocab).normal_(0.0, 0.02))
+        self.lm_head_bias = nn.Parameter(torch.zeros(vocab))
+
+    def forward(self, idx, targets=None):
+        T = idx.shape[1]
+        x = self.tok(idx) + self.pos(torch.arange(T, device=idx.device))
+        for blk in self.blocks:
+            x = blk(x)
+        x = self.ln(x)
+        w = self.tok.weight.t() if self.tied else self.lm_head_weights
+        logits = CudaLinearLayer.apply(x, w, self.lm_head_bias)
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), targets.reshape(-1))
+        return logits, loss
+
+
+def n_params(model: nn.Module) -> int:
+    return sum(p.numel() for p in model.parameters())
+
+
+def step_flops(params: int, layers: int, d: int, ctx: int, tokens: int) -> float:
+    """Training FLOPs of one step: 6 * params * tokens for the dense layers,
+    plus causal attention (2 * 2 * T * d per token per layer forward, half of
+    it masked, x3 for forward + backward)."""
+    return 6.0 * params * tokens + 3.0 * 2.0 * layers * ctx * d * tokens
+
+
+def rank_batches(seed: int, n: int, batch: int, ctx: int, vocab: int) -> list:
+    """n (input, target) token batches in pinned host memory, seeded per rank."""
+    g = torch.Generator().manual_seed(seed)
+    pin = torch.cuda.is_available()
+    out = []
+    for _ in range(n):
+        t = torch.randint(0, vocab, (batch, ctx + 1), generator=g, dtype=torch.int64)
+        x, y = t[:, :-1].contiguous(), t[:, 1:].contiguous()
+        out.append((x.pin_memory(), y.pin_memory()) if pin else (x, y))
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--layers", type=int, default=6)
+    ap.add_argument("--d", type=int, default=384)
+    ap.add_argument("--heads", type=int, default=6)
+    ap.add_argument("--ctx", type=int, default=256)
+    ap.add_argument("--vocab", type=int, default=65)
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--lr", type=float, default=3e-4)
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    torch.manual_seed(1234)  # identical initial weights on every rank
+    model = GPT(a.layers, a.d, a.heads, a.ctx, a.vocab).to(dev)
+    params = n_params(model)
+    net = model
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=a.lr, fused=True)
+    batches = rank_batches(1000 + rank, 8, a.batch, a.ctx, a.vocab)
+
+    losses = []
+
+    def step(i):
+        x, y = batches[i % len(batches)]
+        x = x.to(dev, non_blocking=True)
+        y = y.to(dev, non_blocking=True)
+        _, loss = net(x, y)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(a.warmup):
+        losses.append(step(i).item())
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    last = None
+    for i in range(a.steps):
+        last = step(a.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    losses.append(last.item())
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    tokens = world * a.batch * a.ctx
+    if rank == 0:
+        flops = step_flops(params, a.layers, a.d, a.ctx, tokens)
+        print(json.dumps({
+            "metric": "GPT DP training tokens/s", "value": tokens * a.steps / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms / a.steps, "steps": a.steps,
+            "warmup": a.warmup, "tflops": flops * a.steps / (ms * 1e-3) / 1e12,
+            "params": params, "loss_first": losses[0], "loss_last": losses[-1],
+            "loss_uniform": math.log(a.vocab),
+            "config": {"layers": a.layers, "d_model": a.d, "heads": a.heads, "ctx": a.ctx,
+                       "vocab": a.vocab, "batch_per_gpu": a.batch, "tied": True,
+                       "optimizer": "AdamW(fused) lr %g" % a.lr,
+                       "grad_sync": "DDP bucketed NCCL all-reduce" if world > 1 else "none"},
+            "data": "synthetic uniform tokens, pinned host -> device each step"}))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
