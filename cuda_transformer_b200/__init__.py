@@ -69,6 +69,7 @@ SIGNATURES = {
     "ct_layernorm_bwd": ([_fp, _fp, _fp, _fp, _fp, _fp, _fp, _fp, _i64, _i64, _fp, _sz, _fp],
                          _int),
     "ct_diag_umma_tf32": ([_int, _fp, _fp, _fp, _int, _fp], _int),
+    "ct_diag_mma_rate": ([_int, _int, _int, _int, _fp, _fp], _int),
 }
 
 _lib: ctypes.CDLL | None = None

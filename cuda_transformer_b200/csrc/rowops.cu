@@ -4,6 +4,7 @@
 // that it is read from HBM once and written once (128-bit accesses where the
 // layout allows), and every reduction over rows is a fixed-order two-stage
 // sum, so results are bit-reproducible run to run.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 
@@ -193,10 +194,17 @@ __global__ void __launch_bounds__(THREADS) softmax_bwd_long_kernel(const float* 
 // ------------------------------------------------------------------ GELU
 // gelu / gelu_bwd (Transformer_kernels/GeLU.cuh:7-29): y = x * Phi(x) and
 // dx = dy * (Phi(x) + x * phi(x)), phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
-__device__ __forceinline__ float gelu_f(float x) { return x * normcdff(x); }
+// Phi(x) = (1 + erf(x / sqrt 2)) / 2, the form torch's exact GELU uses; erff
+// costs fewer instructions than normcdff, which keeps these element-wise
+// kernels at the memory bound (normcdff's extra accuracy is in the far
+// negative tail, where the products are below 1e-6 in absolute value).
+__device__ __forceinline__ float phi_cdf(float x) {
+  return fmaf(0.5f, erff(x * 0.7071067811865476f), 0.5f);
+}
+__device__ __forceinline__ float gelu_f(float x) { return x * phi_cdf(x); }
 __device__ __forceinline__ float gelu_g(float x, float dy) {
   const float inv_sqrt_2pi = 0.3989422804014327f;
-  return dy * (normcdff(x) + x * inv_sqrt_2pi * expf(-0.5f * x * x));
+  return dy * (phi_cdf(x) + x * inv_sqrt_2pi * expf(-0.5f * x * x));
 }
 
 __global__ void gelu_fwd_vec(const float4* __restrict__ x, float4* __restrict__ y, int64_t n4) {
@@ -283,12 +291,16 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
                          float* __restrict__ mean_out, float* __restrict__ rstd_out,
                          int64_t rows, int n, float eps) {
   const int lane = threadIdx.x % kWarp;
-  const int64_t row = (int64_t)blockIdx.x * kLnWarps + threadIdx.x / kWarp;
-  if (row >= rows) return;
-  WarpRow<V, VEC> r, g, b;
-  r.load(x + row * n, n, lane);
+  WarpRow<V, VEC> g, b;
   g.load(gamma, n, lane);
   b.load(beta, n, lane);
+  const int64_t stride = (int64_t)gridDim.x * kLnWarps;
+  int64_t row = (int64_t)blockIdx.x * kLnWarps + threadIdx.x / kWarp;
+  WarpRow<V, VEC> nx;  // the next row of this warp, loaded one row ahead
+  if (row < rows) nx.load(x + row * n, n, lane);
+  for (; row < rows; row += stride) {
+  WarpRow<V, VEC> r = nx;
+  if (row + stride < rows) nx.load(x + (row + stride) * n, n, lane);
   float s = 0.0f;
 #pragma unroll
   for (int j = 0; j < V; ++j)
@@ -315,6 +327,7 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
     if (mean_out) mean_out[row] = mean;
     if (rstd_out) rstd_out[row] = rstd;
   }
+  }
 }
 
 // dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma.
@@ -334,12 +347,29 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
   for (int j = 0; j < V; ++j)
 #pragma unroll
     for (int q = 0; q < 4; ++q) pg[j][q] = pb[j][q] = 0.0f;
-  for (int64_t row = (int64_t)blockIdx.x * kLnWarps + warp; row < rows;
-       row += (int64_t)gridDim.x * kLnWarps) {
-    WarpRow<V, VEC> xr, g;
-    xr.load(x + row * n, n, lane);
-    g.load(dy + row * n, n, lane);
-    const float mu = __ldg(mean_in + row), rs = __ldg(rstd_in + row);
+  const int64_t stride = (int64_t)gridDim.x * kLnWarps;
+  int64_t row0 = (int64_t)blockIdx.x * kLnWarps + warp;
+  WarpRow<V, VEC> nx, ng;  // next row of this warp, loaded one row ahead
+  float nmu = 0.0f, nrs = 0.0f;
+  if (row0 < rows) {
+    nx.load(x + row0 * n, n, lane);
+    ng.load(dy + row0 * n, n, lane);
+    nmu = __ldg(mean_in + row0);
+    nrs = __ldg(rstd_in + row0);
+  }
+  constexpr bool kPrefetch = V <= 4;  // wider rows would not fit two in registers
+  for (int64_t row = row0; row < rows; row += stride) {
+    WarpRow<V, VEC> xr = nx, g = ng;
+    const float mu = nmu, rs = nrs;
+    const int64_t nrow = row + stride;
+    if (nrow < rows) {
+      if (kPrefetch) {
+        nx.load(x + nrow * n, n, lane);
+        ng.load(dy + nrow * n, n, lane);
+      }
+      nmu = __ldg(mean_in + nrow);
+      nrs = __ldg(rstd_in + nrow);
+    }
     float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int j = 0; j < V; ++j)
@@ -361,6 +391,10 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
 #pragma unroll
       for (int q = 0; q < 4; ++q) g.v[j][q] = rs * (g.v[j][q] - s1 - xr.v[j][q] * s2);
     g.store(dx + row * n, n, lane);
+    if (!kPrefetch && nrow < rows) {
+      nx.load(x + nrow * n, n, lane);
+      ng.load(dy + nrow * n, n, lane);
+    }
   }
   // CTA-level fixed-order reduction of the per-warp column partials: warps
   // add their partials into lnsm[2][n] one after another.
@@ -383,51 +417,95 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
   for (int c = threadIdx.x; c < 2 * n; c += blockDim.x) out[c] = lnsm[c];
 }
 
-// Sums `parts` partial rows of length `len` (row stride `len`) column-wise.
-__global__ void column_sum_parts(const float* __restrict__ ws, int parts, int64_t len,
-                                 float* __restrict__ out_a, float* __restrict__ out_b,
-                                 int64_t split) {
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < len;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    float acc = 0.0f;
-    for (int p = 0; p < parts; ++p) acc += ws[(int64_t)p * len + c];
-    if (c < split) out_a[c] = acc;
-    else out_b[c - split] = acc;
+// Sums `parts` partial rows of length `len` (row stride `len`) column-wise;
+// columns [0, split) go to out_a, the rest to out_b.  A 1024-thread block
+// covers 32 columns: its 32 warps take every 32nd part (eight loads in flight
+// per thread), then warp 0 adds the 32 partial sums.  The order of the
+// additions depends only on (parts, len), so results are reproducible.
+constexpr int kCsCols = 32, kCsGroups = 32;
+__global__ void __launch_bounds__(kCsCols* kCsGroups)
+    column_sum_parts(const float* __restrict__ ws, int parts, int64_t len,
+                     float* __restrict__ out_a, float* __restrict__ out_b, int64_t split) {
+  __shared__ float red[kCsGroups][kCsCols + 1];
+  const int cx = threadIdx.x % kCsCols, gy = threadIdx.x / kCsCols;
+  const int64_t c = (int64_t)blockIdx.x * kCsCols + cx;
+  float acc = 0.0f;
+  if (c < len) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int p = gy;
+    for (; p + 7 * kCsGroups < parts; p += 8 * kCsGroups) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] += ws[(int64_t)(p + u * kCsGroups) * len + c];
+    }
+    for (; p < parts; p += kCsGroups) a[0] += ws[(int64_t)p * len + c];
+    acc = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+  }
+  red[gy][cx] = acc;
+  __syncthreads();
+  if (gy == 0 && c < len) {
+    float s = 0.0f;
+#pragma unroll
+    for (int g = 0; g < kCsGroups; ++g) s += red[g][cx];
+    if (c < split) out_a[c] = s;
+    else out_b[c - split] = s;
   }
 }
 
-// ------------------------------------------------------------ bias gradient
-// Stage 1: CTA (column block, row chunk) sums its rows for 4 columns per
-// thread; stage 2 (column_sum_parts) adds the chunks.  Replaces the
-// one-block-per-column warp_sum_kernel (Transformer_kernels/warp_sum_kernel.cuh:13-51).
-constexpr int kBgThreads = 256;
-constexpr int kBgRowsPerChunk = 64;
+static unsigned column_sum_grid(int64_t len) { return (unsigned)((len + kCsCols - 1) / kCsCols); }
 
-template <bool VEC>
+// ------------------------------------------------------------ bias gradient
+// Stage 1: a CTA of up to kBgThreads threads owns 4 * blockDim consecutive
+// columns (4 per thread, float4 loads; one CTA spans a whole row when
+// n <= 1536) and sums a chunk of kBgRowsPerChunk rows, all of them in flight
+// per thread; it writes one partial row per chunk.  Stage 2
+// (column_sum_parts) adds the chunks in fixed order.  The shape was picked by
+// measurement on B200: throughput grows with the CTAs in flight, not with
+// deeper per-thread loops.  Replaces the one-block-per-column warp_sum_kernel
+// (Transformer_kernels/warp_sum_kernel.cuh:13-51).
+constexpr int kBgThreads = 384;
+constexpr int kBgRowsPerChunk = 32;
+constexpr int kBgUnroll = 8;
+
+// FLAT: the batch stride is m row strides, so row r of the flattened
+// (batch * m) rows starts at r * s1 (no division per row).
+template <bool VEC, bool FLAT>
 __global__ void __launch_bounds__(kBgThreads)
     bias_grad_partial(const float* __restrict__ dy, int64_t s0, int64_t s1, int64_t s2, int64_t m,
                       int64_t rows, int64_t n, float* __restrict__ ws) {
-  const int64_t c0 = ((int64_t)blockIdx.x * kBgThreads + threadIdx.x) * 4;
+  // grid.x: row chunks (may exceed 65535), grid.y: column blocks
+  const int64_t c0 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (c0 >= n) return;
-  const int64_t r0 = (int64_t)blockIdx.y * kBgRowsPerChunk;
+  const int64_t r0 = (int64_t)blockIdx.x * kBgRowsPerChunk;
   const int64_t r1 = min(rows, r0 + kBgRowsPerChunk);
-  float a[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t r = r0; r < r1; ++r) {
-    const int64_t b = r / m, i = r % m;
-    const float* p = dy + b * s0 + i * s1;
-    if (VEC && c0 + 3 < n) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(p + c0));
-      a[0] += v.x; a[1] += v.y; a[2] += v.z; a[3] += v.w;
-    } else {
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t r = r0; r < r1; r += kBgUnroll) {
+    float4 v[kBgUnroll];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (c0 + q < n) a[q] += __ldg(p + (c0 + q) * s2);
+    for (int u = 0; u < kBgUnroll; ++u) {  // independent loads in flight
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int64_t rr = r + u;
+      if (rr < r1) {
+        const float* p = FLAT ? dy + rr * s1 : dy + (rr / m) * s0 + (rr % m) * s1;
+        if (VEC && c0 + 3 < n) {
+          v[u] = __ldg(reinterpret_cast<const float4*>(p + c0));
+        } else {
+          v[u].x = __ldg(p + c0 * s2);
+          if (c0 + 1 < n) v[u].y = __ldg(p + (c0 + 1) * s2);
+          if (c0 + 2 < n) v[u].z = __ldg(p + (c0 + 2) * s2);
+          if (c0 + 3 < n) v[u].w = __ldg(p + (c0 + 3) * s2);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBgUnroll; ++u) {
+      a.x += v[u].x; a.y += v[u].y; a.z += v[u].z; a.w += v[u].w;
     }
   }
-  float* out = ws + (int64_t)blockIdx.y * n;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    if (c0 + q < n) out[c0 + q] = a[q];
+  float* out = ws + (int64_t)blockIdx.x * n;
+  out[c0] = a.x;
+  if (c0 + 1 < n) out[c0 + 1] = a.y;
+  if (c0 + 2 < n) out[c0 + 2] = a.z;
+  if (c0 + 3 < n) out[c0 + 3] = a.w;
 }
 
 // ---------------------------------------------------------- FA2 bwd delta
@@ -483,14 +561,18 @@ int softmax_dispatch_bwd(const float* p, const float* dp, float* dx, int64_t row
 template <int V, bool VEC>
 void ln_fwd_launch(const float* x, const float* g, const float* b, float* y, float* mean,
                    float* rstd, int64_t rows, int n, float eps, cudaStream_t st) {
-  const unsigned grid = (unsigned)((rows + kLnWarps - 1) / kLnWarps);
+  // persistent: about four resident CTAs per SM, each warp taking rows in turn
+  const int64_t want = (rows + kLnWarps - 1) / kLnWarps;
+  const unsigned grid = (unsigned)(want < 148 * 4 ? want : 148 * 4);
   layernorm_fwd_kernel<V, VEC><<<grid, kLnWarps * kWarp, 0, st>>>(x, g, b, y, mean, rstd, rows, n,
                                                                   eps);
 }
 
+// Two CTAs per SM (each warp loops over rows); the per-CTA column partials
+// are then few enough for one short reduction pass.
 int ln_bwd_grid(int64_t rows) {
   const int64_t want = (rows + kLnWarps - 1) / kLnWarps;
-  return (int)(want < 512 ? (want < 1 ? 1 : want) : 512);
+  return (int)(want < 296 ? (want < 1 ? 1 : want) : 296);
 }
 
 template <int V, bool VEC>
@@ -589,6 +671,7 @@ int launch_layernorm_fwd(const float* x, const float* g, const float* b, float* 
        : ln_fwd_launch<V, false>(x, g, b, y, mean, rstd, rows, nn, eps, st))
   if (n <= 128) CT_LN_FWD(1);
   else if (n <= 256) CT_LN_FWD(2);
+  else if (n <= 384) CT_LN_FWD(3);
   else if (n <= 512) CT_LN_FWD(4);
   else CT_LN_FWD(8);
 #undef CT_LN_FWD
@@ -616,11 +699,12 @@ int launch_layernorm_bwd(const float* x, const float* g, const float* mean, cons
            : ln_bwd_launch<V, false>(x, g, mean, rstd, dy, dx, ws, rows, nn, grid, st)
   if (n <= 128) CT_LN_BWD(1);
   else if (n <= 256) CT_LN_BWD(2);
+  else if (n <= 384) CT_LN_BWD(3);
   else if (n <= 512) CT_LN_BWD(4);
   else CT_LN_BWD(8);
 #undef CT_LN_BWD
   if (rc != CT_OK) return rc;
-  column_sum_parts<<<elementwise_grid(2 * n, 256), 256, 0, st>>>(ws, grid, 2 * n, dg, db, n);
+  column_sum_parts<<<column_sum_grid(2 * n), kCsCols * kCsGroups, 0, st>>>(ws, grid, 2 * n, dg, db, n);
   return check_launch();
 }
 
@@ -635,14 +719,20 @@ int launch_bias_grad(const float* dy, const int64_t s[3], float* db, int64_t bat
   const int64_t rows = batch * m;
   if (rows == 0) return cudaMemsetAsync(db, 0, n * sizeof(float), st) == cudaSuccess ? CT_OK : CT_ERR_CUDA;
   const int64_t chunks = (rows + kBgRowsPerChunk - 1) / kBgRowsPerChunk;
-  if (chunks > 65535) return CT_ERR_INVALID_ARGUMENT;
+  if (chunks >= (1ll << 31)) return CT_ERR_INVALID_ARGUMENT;
   const bool vec = s[2] == 1 && s[1] % 4 == 0 && s[0] % 4 == 0 && aligned16(dy);
-  dim3 grid((unsigned)((n + 4 * kBgThreads - 1) / (4 * kBgThreads)), (unsigned)chunks);
-  if (vec) bias_grad_partial<true><<<grid, kBgThreads, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
-  else bias_grad_partial<false><<<grid, kBgThreads, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  const int64_t quads = (n + 3) / 4;
+  const unsigned th = (unsigned)std::min<int64_t>((quads + 31) / 32 * 32, kBgThreads);
+  if ((quads + th - 1) / th > 65535) return CT_ERR_INVALID_ARGUMENT;
+  dim3 grid((unsigned)chunks, (unsigned)((quads + th - 1) / th));
+  const bool flat = batch == 1 || s[0] == m * s[1];
+  if (vec && flat) bias_grad_partial<true, true><<<grid, th, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  else if (vec) bias_grad_partial<true, false><<<grid, th, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  else if (flat) bias_grad_partial<false, true><<<grid, th, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
+  else bias_grad_partial<false, false><<<grid, th, 0, st>>>(dy, s[0], s[1], s[2], m, rows, n, ws);
   int rc = check_launch();
   if (rc != CT_OK) return rc;
-  column_sum_parts<<<elementwise_grid(n, 256), 256, 0, st>>>(ws, (int)chunks, n, db, db, n);
+  column_sum_parts<<<column_sum_grid(n), kCsCols * kCsGroups, 0, st>>>(ws, (int)chunks, n, db, db, n);
   return check_launch();
 }
 

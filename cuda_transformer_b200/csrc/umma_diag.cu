@@ -2,7 +2,9 @@
 // the test-suite to check, on the device, the operand layouts that the
 // FlashAttention and GEMM kernels rely on: K-major and MN-major shared-memory
 // operands in the 128-byte swizzle, A read from Tensor Memory, and how the
-// tensor core treats the 13 low mantissa bits of an FP32 operand.
+// tensor core treats the 13 low mantissa bits of an FP32 operand.  Also a
+// throughput probe: back-to-back kind::tf32 MMAs of one shape, timed in SM
+// cycles on every SM (the tensor-pipe ceiling the roofline figures use).
 #include "ct_internal.h"
 #include "tc_ptx.cuh"
 
@@ -108,7 +110,95 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// One CTA per SM (the shared-memory request keeps a second CTA off the SM):
+// thread 0 issues `reps` x 4 MMAs D[128 x N] += A[128 x 8] B[8 x N] on zeroed
+// operands (A in TMEM when TS, else shared memory; B K-major in shared
+// memory) and records the clock64 span from the first issue to the commit's
+// completion in cycles[blockIdx.x].
+template <int N, bool TS>
+__global__ void __launch_bounds__(128, 1)
+    mma_rate_kernel(int reps, long long* __restrict__ cycles, uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DiagSmem* hs = reinterpret_cast<DiagSmem*>(smem_raw);
+  const uint32_t base = (smem_u32(smem_raw) + sizeof(DiagSmem) + 1023u) & ~1023u;
+  const uint32_t sa = base, sb = base + 16384u;
+  float* f = reinterpret_cast<float*>(smem_raw + (base - smem_u32(smem_raw)));
+  for (int i = threadIdx.x; i < (16384 + N * 128) / 4; i += 128) f[i] = 0.0f;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&hs->bar), 1);
+    hs->ctl.abort = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(smem_u32(&hs->ctl.tmem_base), 512);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = hs->ctl.tmem_base;
+  if (threadIdx.x < 128 && TS) {  // A operand columns 256..287: zeros
+    float z[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) z[i] = 0.0f;
+    tmem_st32(tmem_addr(tmem, 32u * (threadIdx.x / 32), 256), z);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    const uint32_t id = idesc_tf32(128, N, false, false);
+    const uint64_t ad = sdesc_kmajor(sa), bd = sdesc_kmajor(sb);
+    const long long t0 = clock64();
+    for (int r = 0; r < reps; ++r) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (TS) umma_tf32_ts(tmem, tmem + 256 + 8 * k, bd + (32u * k >> 4), id, (r | k) ? 1u : 0u);
+        else umma_tf32_ss(tmem, ad + (32u * k >> 4), bd + (32u * k >> 4), id, (r | k) ? 1u : 0u);
+      }
+    }
+    umma_commit(smem_u32(&hs->bar));
+    const bool ok = mbar_wait(smem_u32(&hs->bar), 0, &hs->ctl, status);
+    cycles[blockIdx.x] = ok ? clock64() - t0 : -1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int N, bool TS>
+int run_mma_rate(int reps, int blocks, long long* cycles, const DeviceInfo& dev, cudaStream_t st) {
+  const size_t smem = 120 * 1024;  // one CTA per SM: each allocates all 512 TMEM columns
+  if (cudaFuncSetAttribute(mma_rate_kernel<N, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return CT_ERR_CUDA;
+  mma_rate_kernel<N, TS><<<blocks, 128, smem, st>>>(reps, cycles, dev.status);
+  return check_launch();
+}
+
 }  // namespace
+
+int launch_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles,
+                         const DeviceInfo& dev, cudaStream_t st) {
+  if (reps <= 0 || reps > (1 << 20) || blocks <= 0 || blocks > dev.sm_count || !cycles)
+    return CT_ERR_INVALID_ARGUMENT;
+  switch (n) {
+    case 32: return a_tmem ? run_mma_rate<32, true>(reps, blocks, cycles, dev, st)
+                           : run_mma_rate<32, false>(reps, blocks, cycles, dev, st);
+    case 64: return a_tmem ? run_mma_rate<64, true>(reps, blocks, cycles, dev, st)
+                           : run_mma_rate<64, false>(reps, blocks, cycles, dev, st);
+    case 128: return a_tmem ? run_mma_rate<128, true>(reps, blocks, cycles, dev, st)
+                            : run_mma_rate<128, false>(reps, blocks, cycles, dev, st);
+    case 256: return a_tmem ? run_mma_rate<256, true>(reps, blocks, cycles, dev, st)
+                            : run_mma_rate<256, false>(reps, blocks, cycles, dev, st);
+    default: return CT_ERR_INVALID_ARGUMENT;
+  }
+}
 
 int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
                      const DeviceInfo& dev, cudaStream_t st) {

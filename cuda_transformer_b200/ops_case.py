@@ -10,8 +10,8 @@ measurement shapes and prints one JSON line per kernel with its roofline:
 
 The linear layer runs through ct_linear_fwd_ws with its workspace, as the
 cuda_fma operator calls it.  Each launch is timed alone with CUDA events on
-the current stream; a 256 MiB
-buffer is rewritten between launches so every launch starts with a cold L2.
+the current stream after a read of a 256 MiB buffer, so every launch starts
+with a cold L2.
 Peaks come from MEASURED_PEAKS.json at the repository root (dense TF32 is
 half the measured dense BF16 rate).
 
@@ -42,15 +42,19 @@ def peaks() -> dict:
 
 
 class Timer:
+    """Cold-L2 timing: before each launch a 256 MiB buffer is read, so L2
+    holds only clean, unrelated lines (a write flush would leave dirty lines
+    whose write-back the timed kernel would pay for)."""
+
     def __init__(self, dev):
-        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
 
     def __call__(self, fn, iters: int, warmup: int = 3) -> float:
         for _ in range(warmup):
             fn()
         total = 0.0
         for _ in range(iters):
-            self.flush.fill_(1)
+            self.flush.max()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()

@@ -250,6 +250,14 @@ int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean,
 int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
                       void* stream);
 
+/* Diagnostic: tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in
+ * {32, 64, 128, 256}, A from TMEM (a_tmem != 0) or shared memory.  `blocks`
+ * CTAs (at most one per SM) each issue reps x 4 MMAs back to back and write
+ * the clock64 cycles from first issue to completion into the device array
+ * cycles[blocks] (-1 if the completion wait timed out).  No reference
+ * counterpart. */
+int ct_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

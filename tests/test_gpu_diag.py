@@ -58,3 +58,18 @@ def test_tf32_operand_rounding_rule(cuda_device, record_property):
     assert is_trunc, "3xTF32 split assumes the tensor core truncates FP32 operands to TF32"
     H.assert_device_clean()
 
+
+
+@pytest.mark.gpu
+def test_mma_rate_probe_runs(cuda_device):
+    """The tensor-pipe probe completes on every SM and wider N never costs
+    fewer cycles per MMA than narrower N."""
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    cyc = torch.zeros(sms, dtype=torch.int64, device=cuda_device)
+    per = {}
+    for n in (32, 128):
+        H.cb.check(H.cb.lib().ct_diag_mma_rate(n, 1, 200, sms, H._p(cyc), H._stream()), "rate")
+        torch.cuda.synchronize()
+        assert bool((cyc > 0).all())
+        per[n] = cyc.double().mean().item() / 800
+    assert per[128] >= per[32] * 0.95

@@ -116,3 +116,17 @@ def test_rowops_golden_vectors(cuda_device):
     assert H.rel_err(db, z["ln/dbeta"]) < 1e-5
     out = H.linear_fwd(t("linear/x"), t("linear/w"), t("linear/b"))
     assert np.abs(out.cpu().double().numpy() - z["linear/y"]).max() < 1e-5
+
+
+@pytest.mark.gpu
+def test_gelu_wide_range(cuda_device):
+    """Exact GELU over [-12, 12] (both tails) against the FP64 oracle: error
+    within a few FP32 ulps of max(1, |value|)."""
+    x = torch.linspace(-12.0, 12.0, 200001, dtype=torch.float32)
+    dy = torch.ones_like(x)
+    xd = x.to(cuda_device)
+    y = H.gelu_fwd(xd).cpu().double().numpy()
+    dx = H.gelu_bwd(xd, dy.to(cuda_device)).cpu().double().numpy()
+    ry, rdx = orc.gelu_fwd(x.numpy()), orc.gelu_bwd(x.numpy(), dy.numpy())
+    assert (np.abs(y - ry) / np.maximum(1.0, np.abs(ry))).max() < 5e-7
+    assert (np.abs(dx - rdx) / np.maximum(1.0, np.abs(rdx))).max() < 5e-7
