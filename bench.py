@@ -43,6 +43,10 @@ sys.path.insert(0, str(ROOT))
 B_FULL, H_FULL, N, D, CAUSAL = 4, 32, 4096, 64, True
 PAIRS = B_FULL * H_FULL
 METRIC = "FA2 fwd+bwd TFLOPS (B4,H32,N4096,D64) at 1/2/4/8 B200; % of TF32 peak"
+# DRAM bytes of one 3xTF32 dK/dV launch at config 2 (ncu capture at half size, x2) and the
+# kernel's algorithmic bytes: reads Q, K, V, dO (4 x 128 MiB) + LSE, delta, writes dK, dV.
+DKDV_TRAFFIC_BYTES = 2 * 377.0e6
+DKDV_ALGO_BYTES = 4 * 134217728 + 2 * 2097152 + 2 * 134217728
 WORKLOAD = "FA2 fwd+bwd B4 H32 N4096 D64 causal fp32 (BASELINE config 2)"
 
 
@@ -517,7 +521,12 @@ def main() -> None:
                 "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
                 "frac_of_issued_mma": achieved * mult / tf32_peak,
                 "peak_source": f"{pk['source']} bf16 burst {pk['bf16_tflops']} / 2 (dense TF32 = half BF16 rate)",
-                "traffic": None,
+                "traffic": DKDV_TRAFFIC_BYTES if (top == "fa2_bwd_dkdv" and prec == cb.PRECISION_3XTF32
+                                                  and world == 1) else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one dK/dV "
+                                  "launch at B4 H16 (64 pairs, 377 MB), scaled x2 to the 128 pairs "
+                                  "of a launch here (profiles/fa2_kernels_B4H32N4096D64_causal_3xtf32.md)",
+                "algorithmic_bytes": DKDV_ALGO_BYTES,
                 "algorithmic_flop_per_launch": algo[top], "launch_ms": kern[top]}
 
     if rank == 0:
