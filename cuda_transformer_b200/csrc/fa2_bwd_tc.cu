@@ -55,6 +55,9 @@ struct DqCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1> {
 
 template <int NS>
 struct BwdBars {
+  // full_*: TMA landed (A / B tiles); ready_*: split or rounded; empty_*: no
+  // longer read by the tensor core.  With MERGED stages (dK/dV pass) only the
+  // _a barriers are used and cover both tiles.
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
   uint64_t s_full, dp_full, s_free, p_full, ds_full, rows_ready, done, mma_final;
   CtaCtl ctl;
@@ -112,7 +115,7 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars) {
 // MN-major layouts, maps[2..3] = B likewise).  With VEC, all lanes first stage
 // the step's per-query log-sum-exp (times log2 e) and delta into the stage's
 // vector slot, so the row warps read them from shared memory.
-template <class C, bool VEC>
+template <class C, bool VEC, bool MERGED>
 __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles, float* vec,
                                              const CUtensorMap* const* maps, int j0, int j1,
                                              int h, int b, const float* lse_bh, int64_t lse_t,
@@ -149,7 +152,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
                       B(bars->full_a[s]), 32 * c, j * BN, h, b);
     }
     last_a[s] = r;
-    if (r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
+    if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
     if (lane == 0) {
       mbar_arrive_expect_tx(B(bars->full_b[s]), C::LB * C::TILE);
 #pragma unroll
@@ -170,7 +173,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
-template <class C>
+template <class C, bool MERGED>
 __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
                                              uint32_t* status) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
@@ -184,8 +187,10 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
       if constexpr (C::SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
       else round_tile_smem(t, C::TILE, tid, kSplitThreads);
     }
-    fence_proxy_async_smem();
-    mbar_arrive(B(bars->ready_a[s]));
+    if (!MERGED) {
+      fence_proxy_async_smem();
+      mbar_arrive(B(bars->ready_a[s]));
+    }
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
     for (int l = 0; l < C::LB; ++l) {
       const uint32_t t = st + (l ? C::OFF_B1 : C::OFF_B0);
@@ -193,7 +198,7 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
       else round_tile_smem(t, C::TILE, tid, kSplitThreads);
     }
     fence_proxy_async_smem();
-    mbar_arrive(B(bars->ready_b[s]));
+    mbar_arrive(B(MERGED ? bars->ready_a[s] : bars->ready_b[s]));
   }
 }
 
@@ -230,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     const CUtensorMap* maps[4] = {&tmK, &tmKmn, &tmV, nullptr};
-    bwd_producer<C, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
+    bwd_producer<C, false, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
                            p.status);
   } else if (warp == 1) {
     if (lane == 0) {
@@ -250,16 +255,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_dP = [&](int j) {
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D,
                                                 vd0 + stg(j), idS, false);
-        umma_commit(B(bars->empty_b[j % NS]));
+        umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full));
       };
-      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      // Every wait or commit of this thread idles the tensor pipe, so waits
+      // are grouped where their barriers are usually complete already.  K
+      // and V keep separate ready/empty barriers: V_j is released after dP_j,
+      // well before K_j, which keeps the producer ahead with two stages.
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
+                mbar_wait(B(rk[0]), 0, ctl, p.status) && mbar_wait(B(rv[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
-        ok = mbar_wait(B(rk[0]), 0, ctl, p.status);
-        if (ok) { tc_fence_after(); issue_S(0); }
-        if (ok) ok = mbar_wait(B(rv[0]), 0, ctl, p.status);
-        if (ok) { tc_fence_after(); issue_dP(0); }
+        issue_S(0);
+        issue_dP(0);
         for (int j = 0; ok && j < n_kv; ++j) {
           if (j + 1 < n_kv) {  // S_{j+1} once the row warps hold S_j in registers
             if (!(ok = mbar_wait(B(bars->s_free), j & 1, ctl, p.status))) break;
@@ -271,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL,
                                                   kmd0 + stg(j), idQ, j > 0);
-          umma_commit(B(bars->empty_a[j % NS]));
-          if (j + 1 < n_kv) {
+          umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
+          if (j + 1 < n_kv) {  // V_{j+1} often lands late with two stages: wait here,
+                               // not before dQ_j
             if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
             issue_dP(j + 1);
@@ -285,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
-    bwd_splitter<C>(bars, tiles, n_kv, p.status);
+    bwd_splitter<C, false>(bars, tiles, n_kv, p.status);
   } else {
     const int quad = warp & 3;
     const int row = q0 + quad * 32 + lane;
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
-    bwd_producer<C, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
+    bwd_producer<C, true, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
                           p.l2, p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
     if (lane == 0) {
@@ -428,45 +437,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
       auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
-      auto& rq = bars->ready_a;
-      auto& rg = bars->ready_b;
+      auto& rdy = bars->ready_a;  // merged stages: Q_i and dO_i both prepared
       auto issue_S = [&](int i) {
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D,
                                                 qd0 + stg(i), idS, false);
-        umma_commit(B(bars->s_full));
       };
       auto issue_dP = [&](int i) {
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D,
                                                 gd0 + stg(i), idS, false);
-        umma_commit(B(bars->dp_full));
       };
-      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      // Two synchronisation points per step with back-to-back MMA groups
+      // between them (every wait or commit of this thread idles the pipe):
+      //   [P_i ready, tiles i+1 split]  dV += P_i^T dO_i;  S_{i+1}     -> s_full
+      //   [dS_i ready]                  dK += dS_i^T Q_i -> empty_i;  dP_{i+1} -> dp_full
+      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
+                mbar_wait(B(rdy[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
-        ok = mbar_wait(B(rq[0]), 0, ctl, p.status);
-        if (ok) { tc_fence_after(); issue_S(0); }
-        if (ok) ok = mbar_wait(B(rg[0]), 0, ctl, p.status);
-        if (ok) { tc_fence_after(); issue_dP(0); }
+        issue_S(0);
+        umma_commit(B(bars->s_full));
+        issue_dP(0);
+        umma_commit(B(bars->dp_full));
         for (int i = 0; ok && i < n; ++i) {
           if (!(ok = mbar_wait(B(bars->p_full), i & 1, ctl, p.status))) break;
+          if (i + 1 < n && !(ok = mbar_wait(B(rdy[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status)))
+            break;
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
               tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, gmd0 + stg(i), idO, i > 0);
           if (i + 1 < n) {
-            if (!(ok = mbar_wait(B(rq[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
-            tc_fence_after();
             issue_S(i + 1);
+            umma_commit(B(bars->s_full));
           }
           if (!(ok = mbar_wait(B(bars->ds_full), i & 1, ctl, p.status))) break;
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
               tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, qmd0 + stg(i), idO, i > 0);
-          umma_commit(B(bars->empty_a[i % NS]));
-          umma_commit(B(bars->empty_b[i % NS]));
+          umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
           if (i + 1 < n) {
-            if (!(ok = mbar_wait(B(rg[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
-            tc_fence_after();
             issue_dP(i + 1);
+            umma_commit(B(bars->dp_full));
           }
         }
         if (ok) umma_commit(B(bars->done));
@@ -476,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
-    bwd_splitter<C>(bars, tiles, n, p.status);
+    bwd_splitter<C, true>(bars, tiles, n, p.status);
   } else {
     const int quad = warp & 3;
     const int row = k0 + quad * 32 + lane;  // key row

@@ -38,11 +38,15 @@ struct FwdCfg {
   static constexpr uint32_t SBUF = NCOPY * BN;
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(TC_S + 2 * SBUF <= TMEM_COLS, "TMEM budget");
+  static_assert(NS >= 3, "K_{j+2} is needed before V_j is released");
   static_assert(D % 32 == 0 && BN % 32 == 0, "tile shape");
 };
 
 template <int NS>
 struct FwdBars {
+  // full_*: TMA landed; ready_*: split or rounded; empty_*: free again.  K and V
+  // keep separate barriers: K_j is released when S_j is done, well before V_j,
+  // which gives the producer more lead on the next K tiles.
   uint64_t full_k[NS], full_v[NS], ready_k[NS], ready_v[NS], empty_k[NS], empty_v[NS];
   uint64_t s_full[2], p_full[2], pv_done[2], q_ready, mma_final;
   CtaCtl ctl;
@@ -153,30 +157,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idO = idesc_tf32(128, D, false, true);
       const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);            // stage-0 descriptors
       const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
-      if (mbar_wait(B(bars->q_ready), 0, ctl, p.status)) {
+      // One synchronisation point per key tile (every wait or commit of this
+      // thread idles the tensor pipe): once P_jj is in TMEM, V_jj and K_{jj+2}
+      // are prepared, O += P_jj V_jj and S_{jj+2} = Q K_{jj+2}^T go out back
+      // to back.  S_{jj+2} reuses P_jj's buffer; the tensor core executes the
+      // two in order, so P_jj is read first.
+      auto issue_S = [&](int j) {
+        const int s = j % NS, bb = j & 1;
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
+                                                tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
+                                                idS, false);
+        umma_commit(B(bars->empty_k[s]));
+        umma_commit(B(bars->s_full[bb]));
+      };
+      bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status) &&
+                mbar_wait(B(bars->ready_k[0]), 0, ctl, p.status) &&
+                (n_kv < 2 || mbar_wait(B(bars->ready_k[1 % NS]), (1 / NS) & 1, ctl, p.status));
+      if (ok) {
         tc_fence_after();
-        for (int j = 0; j <= n_kv; ++j) {
-          if (j < n_kv) {  // S_j = Q K_j^T
-            const int s = j % NS, r = j / NS, bb = j & 1;
-            if (!mbar_wait(B(bars->ready_k[s]), r & 1, ctl, p.status)) break;
-            tc_fence_after();
-            mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
-                                                    tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
-                                                    idS, false);
-            umma_commit(B(bars->empty_k[s]));
-            umma_commit(B(bars->s_full[bb]));
-          }
-          if (j >= 1) {  // O += P_{j-1} V_{j-1}
-            const int jj = j - 1, s = jj % NS, r = jj / NS, bb = jj & 1;
-            if (!mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status)) break;
-            if (!mbar_wait(B(bars->ready_v[s]), r & 1, ctl, p.status)) break;
-            tc_fence_after();
-            const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
-            mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
-                                                    vd0 + (s * C::STAGE >> 4), idO, jj > 0);
-            umma_commit(B(bars->empty_v[s]));
-            umma_commit(B(bars->pv_done[bb]));
-          }
+        issue_S(0);
+        if (n_kv > 1) issue_S(1);
+        for (int jj = 0; ok && jj < n_kv; ++jj) {
+          const int s = jj % NS, bb = jj & 1, j2 = jj + 2;
+          if (!(ok = mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(bars->ready_v[s]), (jj / NS) & 1, ctl, p.status))) break;
+          if (j2 < n_kv &&
+              !(ok = mbar_wait(B(bars->ready_k[j2 % NS]), (j2 / NS) & 1, ctl, p.status)))
+            break;
+          tc_fence_after();
+          const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
+                                                  vd0 + (s * C::STAGE >> 4), idO, jj > 0);
+          umma_commit(B(bars->empty_v[s]));
+          umma_commit(B(bars->pv_done[bb]));
+          if (j2 < n_kv) issue_S(j2);
         }
       }
       umma_commit(B(bars->mma_final));  // nothing of ours in flight after this

@@ -86,12 +86,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
-// Waits until the phase with the given parity of barrier `bar` has completed.
-// Returns false (and raises ctl->abort and the device status word) if the
-// wait exceeds CT_WAIT_TIMEOUT_NS or another wait of this CTA already failed.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, CtaCtl* ctl,
-                                          uint32_t* status) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait: suspend-hinted polls bounded by CT_WAIT_TIMEOUT_NS.
+// Kept out of line so the fast path is one try_wait and a branch.
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                                   uint32_t* status) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
@@ -108,6 +106,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, CtaCtl*
       }
     }
   }
+}
+
+// Waits until the phase with the given parity of barrier `bar` has completed.
+// Returns false (and raises ctl->abort and the device status word) if the
+// wait exceeds CT_WAIT_TIMEOUT_NS or another wait of this CTA already failed.
+// The common case -- the phase has completed -- costs one try_wait: the MMA
+// issuing thread pays for every instruction between two MMA groups, because
+// the tensor pipe idles while that thread is away (measured on B200).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                          uint32_t* status) {
+  if (__builtin_expect(mbar_try_wait(bar, parity), 1)) return true;
+  return mbar_wait_slow(bar, parity, ctl, status);
 }
 
 // ------------------------------------------------------------------- TMA
