@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) {
           const float ds = pv[32 * c + i] * (t[i] - dl);
           if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
-          else t[i] = tf32_round(ds);
+          else t[i] = tf32_round_finite(ds);
         }
         tmem_st32(lb + C::TC_DP + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float e = t[x];
           pv[32 * c + x] = e;
           if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
-          else t[x] = tf32_round(e);
+          else t[x] = tf32_round_finite(e);
         }
         tmem_st32(lb + C::TC_S + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_PL + 32 * c, lo);
@@ -554,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int cc = 32 * c + x;
           const float ds = pv[cc] * (t[x] - dv[x]);
           if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
-          else t[x] = tf32_round(ds);
+          else t[x] = tf32_round_finite(ds);
         }
         tmem_st32(lb + C::TC_DP + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);

@@ -48,7 +48,10 @@ struct FwdBars {
   // keep separate barriers: K_j is released when S_j is done, well before V_j,
   // which gives the producer more lead on the next K tiles.
   uint64_t full_k[NS], full_v[NS], ready_k[NS], ready_v[NS], empty_k[NS], empty_v[NS];
-  uint64_t s_full[2], p_full[2], pv_done[2], q_ready, mma_final;
+  // The row warps learn that S_j is done from empty_k of its stage and that
+  // O += P_j V_j is done from empty_v (both complete exactly then); a stage's
+  // barrier cannot run a phase ahead of the row warps, whose P feeds it.
+  uint64_t p_full[2], q_ready, mma_final;
   CtaCtl ctl;
 };
 
@@ -101,9 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(B(bars->empty_v[s]), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(B(bars->s_full[i]), 1);
       mbar_init(B(bars->p_full[i]), 128);
-      mbar_init(B(bars->pv_done[i]), 1);
     }
     mbar_init(B(bars->q_ready), 128);
     mbar_init(B(bars->mma_final), 1);
@@ -167,8 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
                                                 tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
                                                 idS, false);
-        umma_commit(B(bars->empty_k[s]));
-        umma_commit(B(bars->s_full[bb]));
+        umma_commit(B(bars->empty_k[s]));  // also tells the row warps S_j is ready
       };
       bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status) &&
                 mbar_wait(B(bars->ready_k[0]), 0, ctl, p.status) &&
@@ -188,8 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
                                                   vd0 + (s * C::STAGE >> 4), idO, jj > 0);
-          umma_commit(B(bars->empty_v[s]));
-          umma_commit(B(bars->pv_done[bb]));
+          umma_commit(B(bars->empty_v[s]));  // also: O += P_jj V_jj is done
           if (j2 < n_kv) issue_S(j2);
         }
       }
@@ -235,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int bb = j & 1;
-      if (!(ok = warp_wait(B(bars->s_full[bb]), (j >> 1) & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->empty_k[j % NS]), (j / NS) & 1, ctl, p.status))) break;
       tc_fence_after();
       const uint32_t sc = lb + C::TC_S + bb * C::SBUF;
       const int kv0 = j * BN;
@@ -258,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         if (j > 0) {
           const int jj = j - 1;
-          if (!(ok = warp_wait(B(bars->pv_done[jj & 1]), (jj >> 1) & 1, ctl, p.status))) break;
+          if (!(ok = warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -284,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (i & 1) ls1 += e;
           else ls0 += e;
           if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
-          else t[i] = tf32_round(e);
+          else t[i] = tf32_round_finite(e);
         }
         tmem_st32(sc + 32 * c, t);
         if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, lo);
@@ -297,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) {
       const int jj = n_kv - 1;
-      if (warp_wait(B(bars->pv_done[jj & 1]), (jj >> 1) & 1, ctl, p.status)) {
+      if (warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status)) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
         float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;

@@ -340,6 +340,16 @@ __device__ __forceinline__ float tf32_round(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
+// The same rounding for values known to be finite (softmax probabilities and
+// score gradients): adding half of the dropped 13-bit field carries into the
+// kept bits -- and on into the exponent -- exactly when the dropped part is at
+// least half a TF32 ulp, ties going away from zero (sign-magnitude).  Two
+// integer operations instead of a conversion, which shares its pipe with the
+// exponentials.  Identical to cvt.rna.tf32.f32 on finite inputs (checked on
+// the device bit for bit, ties, subnormals and the overflow edge included).
+__device__ __forceinline__ float tf32_round_finite(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
 // TF32 value the tensor core uses for an FP32 operand: the 13 low mantissa
 // bits are dropped (truncation; checked on the device by the test-suite).
 __device__ __forceinline__ float tf32_trunc(float x) {
