@@ -25,8 +25,10 @@
 // Accumulation.  The tensor core's FP32 accumulator drops the bits below its
 // 24-bit mantissa on every addition (round toward zero), a bias that grows
 // with the number of MMAs folded into one accumulator.  The K loop is
-// therefore cut into chunks of at most kChunkKb K blocks (512 values of K,
-// about 1e-5 relative bias in 3xTF32, which issues three MMAs per K step):
+// therefore cut into chunks of at most chunk_kb(precision) K blocks: 256
+// values of K in 3xTF32 (which issues three MMAs per K step; about 5e-6
+// relative bias even when every product is positive), 1024 in TF32 (its
+// tolerance is 2e-3):
 // each chunk accumulates in one of two TMEM buffers and the epilogue warps
 // add the chunks with round-to-nearest FP32 additions into a running sum kept
 // in a third TMEM region (BN = 128 only; the wider BN = 256 tiles are used
@@ -55,7 +57,8 @@ using fa2::warp_wait;
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;
-constexpr int kChunkKb = 16;  // K blocks per TMEM accumulation chunk (K = 512)
+// K blocks per TMEM accumulation chunk
+__host__ __device__ constexpr int chunk_kb(int split) { return split == 3 ? 8 : 32; }
 constexpr int kThreadsG = 256;
 constexpr int kPrepWarp0 = 2, kPrepThreads = 64, kEpiWarp0 = 4;
 
@@ -126,7 +129,7 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p, int bn) 
   return w;
 }
 
-__device__ __forceinline__ int n_chunks(int kbs) { return (kbs + kChunkKb - 1) / kChunkKb; }
+__device__ __forceinline__ int n_chunks(int kbs, int ckb) { return (kbs + ckb - 1) / ckb; }
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
@@ -220,7 +223,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
   // the host never launches a multi-chunk unit without TMEM for the sum
-  if (!C::FOLD && n_chunks(min(p.kb_per_slice, p.kb_total)) > 1) return;
+  // the host launches multi-chunk BN = 256 tiles only with TMA stores and no split
+  if (!C::FOLD && n_chunks(min(p.kb_per_slice, p.kb_total), chunk_kb(SPLIT)) > 1 &&
+      (!p.tma_out || p.slices > 1))
+    return;
   auto* bars = reinterpret_cast<GemmBars*>(smem_raw);
   const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(GemmBars) + 1023u) & ~1023u;
   CtaCtl* ctl = &bars->ctl;
@@ -309,7 +315,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
         const Unit w = decode_unit(u, p, BN);
-        for (int kc = w.kb0; ok && kc < w.kb1; kc += kChunkKb, ++ci) {
+        for (int kc = w.kb0; ok && kc < w.kb1; kc += chunk_kb(SPLIT), ++ci) {
           const int acc = (int)(ci & 1);
           if (ci >= 2 && !mbar_wait(B(bars->acc_empty[acc]), ((ci >> 1) - 1) & 1, ctl, p.status)) {
             ok = false;
@@ -317,7 +323,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           }
           tc_fence_after();
           const uint32_t d = tmem + acc * BN;
-          const int kce = min(w.kb1, kc + kChunkKb);
+          const int kce = min(w.kb1, kc + chunk_kb(SPLIT));
           for (int kb = kc; kb < kce; ++kb, ++it) {
             const int s = (int)(it % NS), r = (int)(it / NS);
             const uint32_t rbar = SPLIT == 3 ? B(bars->ready[s]) : B(bars->full[s]);
@@ -386,39 +392,54 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const bool valid = row < p.m;
       const bool rows_in = w.m0 + 32 * quad < p.m;  // warp-uniform
       float* orow = p.out + ((int64_t)w.b * p.m + (valid ? row : 0)) * p.n;
-      const int nch = n_chunks(w.kb1 - w.kb0);
+      const int nch = n_chunks(w.kb1 - w.kb0, chunk_kb(SPLIT));
       for (int c = 0; c < nch; ++c, ++ci) {
         const int acc = (int)(ci & 1);
         const bool last = c == nch - 1;
+        // FOLD (BN = 128): chunks add into the TMEM running sum, the last one
+        // writes.  Otherwise (BN = 256, no TMEM left for a sum) every chunk
+        // writes: the first stores, later ones add in L2 by TMA, each after
+        // this warp's previous writes have completed (fixed order).
+        const bool writes = last || !C::FOLD;
+        const bool first_write = C::FOLD ? last : c == 0;
+        const bool add_mode = w.slice > 0 || (!C::FOLD && c > 0);
+        const bool with_bias = w.slice == 0 && first_write;
         if (!warp_wait(B(bars->acc_full[acc]), (ci >> 1) & 1, ctl, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (last && w.slice > 0) {
+        if (first_write && w.slice > 0) {
           if (sem_wait(p.sem + w.tile, (uint32_t)w.slice, ctl, p.status))
             fence_proxy_async_global();  // the TMA add below follows the acquire
           else
             ok = false;  // finish the protocol (free the accumulator), write nothing
         }
+        if (!C::FOLD && c > 0 && p.tma_out) {
+          if (lane == 0) {
+            bulk_wait_group<0>();  // the previous chunk's rows of this warp have landed
+            fence_proxy_async_global();
+          }
+          __syncwarp();
+        }
 #pragma unroll 1
         for (int q = 0; q < BN / 32; ++q) {
           float v[32];
           tmem_ld32(lb + acc * BN + 32 * q, v);
-          if (c > 0) {  // running sum of the earlier chunks, round-to-nearest adds
+          if (C::FOLD && c > 0) {  // running sum of the earlier chunks, round-to-nearest adds
             float s[32];
             tmem_ld32(lb + C::TC_SUM + 32 * q, s);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] += s[i];
           }
           const int col0 = w.n0 + 32 * q;
-          if (!last) {
+          if (!writes) {
             tmem_st32(lb + C::TC_SUM + 32 * q, v);
           } else if (!__all_sync(0xffffffffu, ok)) {
             // a wait of this unit failed: nothing is written
           } else if (p.tma_out) {
             if (rows_in && col0 < p.n) {
-              if (w.slice == 0) add_bias32(v, p, col0);
+              if (with_bias) add_bias32(v, p, col0);
               const uint32_t buf = stg + (n_out & 1u) * 4096u;
               if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
               __syncwarp();
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
-                if (w.slice == 0) tma_store_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
+                if (!add_mode) tma_store_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
                 else tma_reduce_add_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
                 bulk_commit_group();
               }
@@ -525,18 +546,19 @@ int64_t tile_count(const GemmProblem& g, int bn) {
 
 // K split: slices of whole accumulation chunks, enough to give every SM a
 // unit, each slice at least two chunks deep.
-void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int* slices, int* kbps) {
+void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int ckb, int* slices,
+                int* kbps) {
   const int kb_total = (int)((g.k + kBK - 1) / kBK);
   *slices = 1;
   *kbps = kb_total;
   const int64_t tiles = tile_count(g, bn);
   if (!have_ws || tiles * 2 > sms) return;
   int s = (int)(sms / tiles);
-  const int max_s = kb_total / (2 * kChunkKb);
+  const int max_s = kb_total / (2 * ckb);
   if (s > max_s) s = max_s;
   if (s < 2) return;
   int per = (kb_total + s - 1) / s;
-  per = (per + kChunkKb - 1) / kChunkKb * kChunkKb;
+  per = (per + ckb - 1) / ckb * ckb;
   *kbps = per;
   *slices = (kb_total + per - 1) / per;
 }
@@ -573,7 +595,9 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   p.kb_total = (int)((g.k + kBK - 1) / kBK);
   const int64_t tiles = tile_count(g, C::BN);
   const bool have_ws = ws != nullptr && ws_bytes >= (size_t)tiles * 4u;
-  pick_split(g, C::BN, dev.sm_count, have_ws, &p.slices, &p.kb_per_slice);
+  pick_split(g, C::BN, dev.sm_count, have_ws, chunk_kb(C::SPLIT), &p.slices, &p.kb_per_slice);
+  if (!C::FOLD && p.kb_per_slice > chunk_kb(C::SPLIT) && (!tma_out || p.slices > 1))
+    return CT_ERR_UNSUPPORTED_LAYOUT;  // the L2 fold needs TMA stores (caller falls back)
   p.units = (int)(tiles * p.slices);
   p.a_mn = a_mn;
   p.b_mn = b_mn;
@@ -593,13 +617,19 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   return check_launch();
 }
 
-// Tile width: BN = 256 needs K within one accumulation chunk; otherwise the
-// choice minimises (waves of tiles) x (tile cost), a 128-wide tile costing a
+// Tile width: BN = 256 has no TMEM left for a running sum, so K beyond one
+// accumulation chunk is folded in L2 (at most four chunks, TMA-storable
+// output, no split-K); otherwise the choice minimises (waves of tiles) x (tile cost), a 128-wide tile costing a
 // little more than half a 256-wide one (x re-read, per-tile overhead).  The
 // environment variable CT_GEMM_BN (128 or 256) overrides it (tuning).
 int pick_bn(const GemmProblem& g, int sms) {
   const int64_t kb = (g.k + kBK - 1) / kBK;
-  if (kb > kChunkKb || g.n <= 128) return 128;
+  const int ckb = chunk_kb(g.precision == CT_PRECISION_3XTF32 ? 3 : 1);
+  if (g.n <= 128) return 128;
+  if (kb > ckb) {  // several chunks: BN = 256 folds them in L2 (TMA stores, no split-K)
+    const bool tma_out = (g.n & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15u) == 0;
+    if (!tma_out || kb > 4 * ckb || tile_count(g, 256) * 2 <= sms) return 128;
+  }
   static const int env = [] {
     const char* e = std::getenv("CT_GEMM_BN");
     return e ? std::atoi(e) : 0;

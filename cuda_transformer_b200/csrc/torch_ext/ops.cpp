@@ -153,18 +153,42 @@ std::tuple<Tensor, Tensor, Tensor> flash_attention_bwd_ex(Tensor Q, Tensor K, Te
 // ----------------------------------------------------------------- Linear
 // x: (batch, m, k); weights: (k, n) or (1 | batch, k, n) "pre-transposed";
 // bias: (n,); out: (batch, m, n)  -- linear_layer.cu:24-70.
-Tensor fma_impl(const Tensor& x, Tensor weights, const Tensor& bias, int64_t precision) {
-  if (weights.dim() == 2) weights = weights.unsqueeze(0);
-  TORCH_CHECK(x.dim() == 3, "x must be a 3D tensor (batch, m, k)");
+// A [b, r, c] operand of the tensor-core linear layer must have a unit stride
+// in one of its last two dimensions, the other strides 16-byte multiples (or
+// extent 1) and a 16-byte aligned base (TMA).  Otherwise it is copied into a
+// layout with unit last stride and rows padded to 4 floats, viewed back at its
+// logical size (the kernel never reads the padding: TMA zero-fills past the
+// logical extent).  Vocabulary-sized outputs (n = 65) and their gradients need
+// this; the FP32 CUDA-core path takes any strides.
+Tensor linear_operand(const Tensor& t) {
+  auto al = [](int64_t stride, int64_t extent) { return extent <= 1 || (stride % 4) == 0; };
+  const bool base = (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
+  const bool batch_ok = al(t.stride(0), t.size(0));
+  const bool kmaj = t.stride(2) == 1 && al(t.stride(1), t.size(1));
+  const bool mnmaj = t.stride(1) == 1 && al(t.stride(2), t.size(2));
+  if (base && batch_ok && (kmaj || mnmaj)) return t;
+  const int64_t cpad = (t.size(2) + 3) / 4 * 4;
+  Tensor buf = at::empty({t.size(0), t.size(1), cpad}, t.options());
+  Tensor view = buf.narrow(2, 0, t.size(2));
+  view.copy_(t);
+  return view;
+}
+
+Tensor fma_impl(const Tensor& x0, Tensor weights0, const Tensor& bias, int64_t precision) {
+  if (weights0.dim() == 2) weights0 = weights0.unsqueeze(0);
+  TORCH_CHECK(x0.dim() == 3, "x must be a 3D tensor (batch, m, k)");
+  check_cuda_f32(x0, "x");
+  check_cuda_f32(weights0, "weights");
+  c10::cuda::CUDAGuard guard0(x0.device());
+  const bool tc = precision != (int64_t)CT_PRECISION_FP32;
+  const Tensor x = tc && x0.numel() > 0 ? linear_operand(x0) : x0;
+  Tensor weights = tc && weights0.numel() > 0 ? linear_operand(weights0) : weights0;
   const int64_t batch = x.size(0), m = x.size(1), k = x.size(2), n = weights.size(2);
   TORCH_CHECK(weights.size(1) == k, "weights.size(1) must match x.size(2)");
   TORCH_CHECK(bias.size(0) == n, "bias.size(0) must match weights.size(2)");
-  check_cuda_f32(x, "x");
-  check_cuda_f32(weights, "weights");
   check_cuda_f32(bias, "bias");
   TORCH_CHECK(weights.size(0) == 1 || weights.size(0) == batch,
               "weights batch must be 1 or match x");
-  c10::cuda::CUDAGuard guard(x.device());
   Tensor out = at::empty({batch, m, n}, x.options());
   const int64_t xs[3] = {x.stride(0), x.stride(1), x.stride(2)};
   const int64_t wsd[3] = {weights.stride(0), weights.stride(1), weights.stride(2)};
