@@ -3,10 +3,22 @@
 Forward: out = x @ W + b with W stored (in, out).  Backward: dx = dy @ W^T;
 dW is one GEMM with the (batch, seq) dimensions folded into the reduction
 (x^T @ dy over batch*seq rows) instead of a per-batch product followed by a
-torch sum; db is the bias-gradient column sum.  Zero biases are created on the
-input's device."""
+torch sum; db is the bias-gradient column sum.  The zero biases of the two
+backward products are cached per device and length (the operator only reads
+them)."""
 import torch
 from cuda_transformer.ops import cuda_fma, db_calculation
+
+_ZEROS = {}
+
+
+def _zeros(n, device):
+    """A cached all-zero bias of length n (the operator only reads it)."""
+    key = (device, n)
+    z = _ZEROS.get(key)
+    if z is None:
+        z = _ZEROS[key] = torch.zeros(n, dtype=torch.float32, device=device)
+    return z
 
 
 class CudaLinearLayer(torch.autograd.Function):
@@ -21,9 +33,8 @@ class CudaLinearLayer(torch.autograd.Function):
         x, weights, _ = ctx.saved_tensors
         dy = grad_output
         w = weights.unsqueeze(0) if weights.dim() == 2 else weights
-        dx = cuda_fma(dy, w.transpose(1, 2),
-                      torch.zeros(x.shape[-1], dtype=torch.float32, device=x.device))
-        zero_n = torch.zeros(dy.shape[-1], dtype=torch.float32, device=dy.device)
+        dx = cuda_fma(dy, w.transpose(1, 2), _zeros(x.shape[-1], x.device))
+        zero_n = _zeros(dy.shape[-1], dy.device)
         if weights.dim() == 2:
             rows = x.shape[0] * x.shape[1]
             x2 = x.reshape(1, rows, x.shape[-1])
