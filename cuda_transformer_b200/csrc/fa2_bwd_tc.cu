@@ -6,8 +6,10 @@
 // causal diagonal instead of scanning every query tile.
 //
 // Warp roles as in the forward: warp 0 TMA producer, warp 1 TMEM allocator and
-// MMA issuer, warps 2-3 TF32 hi/lo split or rounding of landed tiles, warps 4-7 row warps
-// (one stationary row per thread / TMEM lane).
+// first MMA issuer, warps 2-3 TF32 hi/lo split or rounding of landed tiles,
+// warps 4-7 row warps (one stationary row per thread / TMEM lane), warp 8 the
+// second MMA issuer.  dQ: warp 1 issues S, warp 8 dP and dQ.  dK/dV: warp 1
+// issues S^T and dV, warp 8 dP^T and dK.
 //
 // dQ kernel, per 128 query rows, per key tile j (BN keys):
 //   S  = Q K_j^T     (A = Q in TMEM, B = K_j K-major)
@@ -17,8 +19,9 @@
 // dK/dV kernel, per 128 key rows, per query tile j (BN queries):
 //   S^T  = K Q_j^T,  dP^T = V dO_j^T,  P^T, dS^T in the row warps
 //   dV += P^T dO_j,  dK += dS^T Q_j   (B = Q_j / dO_j read MN-major)
-// The MMA issuer runs one phase ahead of the row warps (S_{j+1} while dS_j is
-// formed), ordering reuse of the single S / dP buffers by issue order.
+// The issuers run one phase ahead of the row warps (S_{j+1} while dS_j is
+// formed).  Each single S / dP buffer is written and read by MMAs of one
+// issuer, which order its reuse by issue order.
 #include "fa2_common.cuh"
 
 namespace ct {
@@ -59,7 +62,7 @@ struct BwdBars {
   // longer read by the tensor core.  With MERGED stages (dK/dV pass) only the
   // _a barriers are used and cover both tiles.
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
-  uint64_t s_full, dp_full, s_free, p_full, ds_full, rows_ready, done, mma_final;
+  uint64_t s_full, dp_full, s_free, p_full, ds_full, rows_ready, done, mma_final, mma_final2;
   CtaCtl ctl;
 };
 
@@ -87,15 +90,18 @@ constexpr size_t bwd_smem_bytes() {
   return 1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>();
 }
 
+// empty_count: MMA issuers that read a stage; done_count: issuers whose
+// accumulators the epilogue reads.
 template <class C>
-__device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars) {
+__device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_count,
+                                              int done_count) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
     mbar_init(B(bars->full_b[s]), 1);
     mbar_init(B(bars->ready_a[s]), kSplitThreads);
     mbar_init(B(bars->ready_b[s]), kSplitThreads);
-    mbar_init(B(bars->empty_a[s]), 1);
+    mbar_init(B(bars->empty_a[s]), empty_count);
     mbar_init(B(bars->empty_b[s]), 1);
   }
   mbar_init(B(bars->s_full), 1);
@@ -104,8 +110,9 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars) {
   mbar_init(B(bars->p_full), 128);
   mbar_init(B(bars->ds_full), 128);
   mbar_init(B(bars->rows_ready), 128);
-  mbar_init(B(bars->done), 1);
+  mbar_init(B(bars->done), done_count);
   mbar_init(B(bars->mma_final), 1);
+  mbar_init(B(bars->mma_final2), 1);
   bars->ctl.abort = 0;
   fence_barrier_init();
 }
@@ -223,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int last_row = min(q0 + kRows - 1, T - 1);
   const int n_kv = p.causal ? last_row / BN + 1 : (T + BN - 1) / BN;
 
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars);
+  // K_j is released by the dQ_j issuer alone: dQ_j waits for dS_j, formed
+  // after the row warps read S_j, so S_j has completed by then.
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -238,50 +247,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     bwd_producer<C, false, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
                            p.status);
   } else if (warp == 1) {
+    // S_j = Q K_j^T, S_{j+1} once the row warps hold S_j in registers.
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_A0);  // stage-0 descriptor
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j > 0 && !(ok = mbar_wait(B(bars->s_free), (j - 1) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_a[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D,
+                                                kd0 + (uint64_t)(((j % NS) * C::STAGE) >> 4), idS,
+                                                false);
+        umma_commit(B(bars->s_full));
+      }
+      umma_commit(B(bars->mma_final));
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp == kIssuer2Warp) {
+    // dP_j = dO V_j^T and dQ += dS_j K_j.  dP_{j+1} overwrites dS_j only
+    // after dQ_j in this thread's issue order.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idQ = idesc_tf32(128, D, false, true);
-      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_A0);           // stage-0 descriptors
-      const uint64_t kmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      const uint64_t kmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);  // stage-0 descriptors
       const uint64_t vd0 = sdesc_kmajor(tiles + C::OFF_B0);
       auto stg = [&](int j) { return (uint64_t)(((j % NS) * C::STAGE) >> 4); };
-      auto& rk = bars->ready_a;
       auto& rv = bars->ready_b;
-      auto issue_S = [&](int j) {
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D,
-                                                kd0 + stg(j), idS, false);
-        umma_commit(B(bars->s_full));
-      };
       auto issue_dP = [&](int j) {
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D,
                                                 vd0 + stg(j), idS, false);
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full));
       };
-      // Every wait or commit of this thread idles the tensor pipe, so waits
-      // are grouped where their barriers are usually complete already.  K
-      // and V keep separate ready/empty barriers: V_j is released after dP_j,
-      // well before K_j, which keeps the producer ahead with two stages.
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
-                mbar_wait(B(rk[0]), 0, ctl, p.status) && mbar_wait(B(rv[0]), 0, ctl, p.status);
+                mbar_wait(B(rv[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
-        issue_S(0);
         issue_dP(0);
         for (int j = 0; ok && j < n_kv; ++j) {
-          if (j + 1 < n_kv) {  // S_{j+1} once the row warps hold S_j in registers
-            if (!(ok = mbar_wait(B(bars->s_free), j & 1, ctl, p.status))) break;
-            if (!(ok = mbar_wait(B(rk[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
-            tc_fence_after();
-            issue_S(j + 1);
-          }
           if (!(ok = mbar_wait(B(bars->ds_full), j & 1, ctl, p.status))) break;
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL,
                                                   kmd0 + stg(j), idQ, j > 0);
           umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
-          if (j + 1 < n_kv) {  // V_{j+1} often lands late with two stages: wait here,
-                               // not before dQ_j
+          if (j + 1 < n_kv) {
             if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
             issue_dP(j + 1);
@@ -289,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) umma_commit(B(bars->done));
       }
-      umma_commit(B(bars->mma_final));
-      mbar_drain(B(bars->mma_final), 0);
+      umma_commit(B(bars->mma_final2));
+      mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
@@ -414,7 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int j1 = (T + BN - 1) / BN;
   const int n = j1 - j0;
 
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars);
+  // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
+  // by warp 8): the merged stage is free after both have committed.
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -423,41 +436,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
+  auto& rdy = bars->ready_a;  // merged stages: Q_i and dO_i both prepared
+  constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+  constexpr uint32_t idO = idesc_tf32(128, D, false, true);
 
   if (warp == 0) {
     const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
     bwd_producer<C, true, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
                           p.l2, p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
+    //   [P_i ready, tiles i+1 prepared]  dV += P_i^T dO_i;  S^T_{i+1} -> s_full
+    // S^T_{i+1} overwrites P_i after dV_i in this thread's issue order.
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
-      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
-      const uint64_t qd0 = sdesc_kmajor(tiles + C::OFF_A0);           // stage-0 descriptors
-      const uint64_t gd0 = sdesc_kmajor(tiles + C::OFF_B0);
-      const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      const uint64_t qd0 = sdesc_kmajor(tiles + C::OFF_A0);  // stage-0 descriptors
       const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
-      auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
-      auto& rdy = bars->ready_a;  // merged stages: Q_i and dO_i both prepared
       auto issue_S = [&](int i) {
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D,
                                                 qd0 + stg(i), idS, false);
+        umma_commit(B(bars->s_full));
       };
-      auto issue_dP = [&](int i) {
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D,
-                                                gd0 + stg(i), idS, false);
-      };
-      // Two synchronisation points per step with back-to-back MMA groups
-      // between them (every wait or commit of this thread idles the pipe):
-      //   [P_i ready, tiles i+1 split]  dV += P_i^T dO_i;  S_{i+1}     -> s_full
-      //   [dS_i ready]                  dK += dS_i^T Q_i -> empty_i;  dP_{i+1} -> dp_full
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
                 mbar_wait(B(rdy[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
         issue_S(0);
-        umma_commit(B(bars->s_full));
-        issue_dP(0);
-        umma_commit(B(bars->dp_full));
         for (int i = 0; ok && i < n; ++i) {
           if (!(ok = mbar_wait(B(bars->p_full), i & 1, ctl, p.status))) break;
           if (i + 1 < n && !(ok = mbar_wait(B(rdy[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status)))
@@ -465,24 +468,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
               tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, gmd0 + stg(i), idO, i > 0);
-          if (i + 1 < n) {
-            issue_S(i + 1);
-            umma_commit(B(bars->s_full));
-          }
+          if (i + 1 < n) issue_S(i + 1);
+          umma_commit(B(bars->empty_a[i % NS]));
+        }
+        if (ok) umma_commit(B(bars->done));
+      }
+      umma_commit(B(bars->mma_final));
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp == kIssuer2Warp) {
+    //   [dS_i ready]  dK += dS_i^T Q_i -> empty_i;  [tiles i+1 prepared]  dP^T_{i+1} -> dp_full
+    // dP^T_{i+1} overwrites dS_i after dK_i in this thread's issue order.
+    if (lane == 0) {
+      const uint64_t gd0 = sdesc_kmajor(tiles + C::OFF_B0);  // stage-0 descriptors
+      const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      auto issue_dP = [&](int i) {
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D,
+                                                gd0 + stg(i), idS, false);
+        umma_commit(B(bars->dp_full));
+      };
+      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
+                mbar_wait(B(rdy[0]), 0, ctl, p.status);
+      if (ok) {
+        tc_fence_after();
+        issue_dP(0);
+        for (int i = 0; ok && i < n; ++i) {
           if (!(ok = mbar_wait(B(bars->ds_full), i & 1, ctl, p.status))) break;
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
               tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, qmd0 + stg(i), idO, i > 0);
           umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
           if (i + 1 < n) {
+            if (!(ok = mbar_wait(B(rdy[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
             issue_dP(i + 1);
-            umma_commit(B(bars->dp_full));
           }
         }
         if (ok) umma_commit(B(bars->done));
       }
-      umma_commit(B(bars->mma_final));
-      mbar_drain(B(bars->mma_final), 0);
+      umma_commit(B(bars->mma_final2));
+      mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {

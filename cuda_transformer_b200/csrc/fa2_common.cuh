@@ -25,9 +25,15 @@ namespace ct {
 namespace fa2 {
 
 constexpr int kRows = 128;        // stationary rows per CTA
-constexpr int kThreads = 256;     // 8 warps
-constexpr int kRowWarp0 = 4;      // first warp of the row warpgroup
+constexpr int kThreads = 288;     // 9 warps
+constexpr int kRowWarp0 = 4;      // first warp of the row warpgroup (4 warps)
 constexpr int kSplitWarp0 = 2;    // first of the two split warps
+// Warp 1 issues one group of tcgen05.mma chains and warp 8 the other.  An
+// issuing thread waits for each MMA to be accepted, so one thread drives the
+// tensor pipe at ~45 cycles per N <= 64 MMA at best and idles it whenever it
+// waits on a barrier; two threads feeding independent accumulators
+// interleave and reach the pipe's full rate (measured on B200).
+constexpr int kIssuer2Warp = 8;
 constexpr int kSplitThreads = 64;
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kLog2e = 1.44269504088896340736f;

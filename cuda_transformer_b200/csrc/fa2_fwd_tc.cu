@@ -8,11 +8,12 @@
 //
 // Per CTA: one (batch, head) and 128 query rows.  Warp roles:
 //   warp 0      TMA producer of K/V tiles (NS-stage ring)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warp 1      TMEM allocator + issuer of S = Q K^T (one thread)
 //   warps 2-3   TF32 hi/lo split (SPLIT == 3) or rounding (SPLIT == 1) of
 //               each landed K/V tile
 //   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
 //               epilogue (thread r <-> query row r <-> TMEM lane r)
+//   warp 8      issuer of O += P V (one thread)
 // K tiles use the K-major tile layout, V tiles the MN-major one.
 // TMEM columns: Q (hi[,lo]) | O | two S/P buffers (S overwritten by P hi, then
 // P lo).  S_{j+1} = Q K_{j+1}^T runs on the tensor core while the row warps
@@ -51,7 +52,7 @@ struct FwdBars {
   // The row warps learn that S_j is done from empty_k of its stage and that
   // O += P_j V_j is done from empty_v (both complete exactly then); a stage's
   // barrier cannot run a phase ahead of the row warps, whose P feeds it.
-  uint64_t p_full[2], q_ready, mma_final;
+  uint64_t p_full[2], q_ready, mma_final, mma_final_pv;
   CtaCtl ctl;
 };
 
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(B(bars->q_ready), 128);
     mbar_init(B(bars->mma_final), 1);
+    mbar_init(B(bars->mma_final_pv), 1);
     ctl->abort = 0;
     fence_barrier_init();
   }
@@ -152,48 +154,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
+    // ------------------------------------------------------ Q.K^T MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
-      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
-      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);            // stage-0 descriptors
-      const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
-      // One synchronisation point per key tile (every wait or commit of this
-      // thread idles the tensor pipe): once P_jj is in TMEM, V_jj and K_{jj+2}
-      // are prepared, O += P_jj V_jj and S_{jj+2} = Q K_{jj+2}^T go out back
-      // to back.  S_{jj+2} reuses P_jj's buffer; the tensor core executes the
-      // two in order, so P_jj is read first.
-      auto issue_S = [&](int j) {
+      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);  // stage-0 descriptor
+      // S_j = Q K_j^T into S buffer j & 1; before S_j overwrites the buffer of
+      // P_{j-2}, the P.V issuer must have finished O += P_{j-2} V_{j-2}
+      // (empty_v of its stage completes exactly then).  empty_k tells the row
+      // warps that S_j is ready.
+      bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status);
+      for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % NS, bb = j & 1;
+        if (j >= 2) {
+          const int jj = j - 2;
+          if (!(ok = mbar_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status))) break;
+        }
+        if (!(ok = mbar_wait(B(bars->ready_k[s]), (j / NS) & 1, ctl, p.status))) break;
+        tc_fence_after();
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
                                                 tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
                                                 idS, false);
         umma_commit(B(bars->empty_k[s]));  // also tells the row warps S_j is ready
-      };
-      bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status) &&
-                mbar_wait(B(bars->ready_k[0]), 0, ctl, p.status) &&
-                (n_kv < 2 || mbar_wait(B(bars->ready_k[1 % NS]), (1 / NS) & 1, ctl, p.status));
-      if (ok) {
-        tc_fence_after();
-        issue_S(0);
-        if (n_kv > 1) issue_S(1);
-        for (int jj = 0; ok && jj < n_kv; ++jj) {
-          const int s = jj % NS, bb = jj & 1, j2 = jj + 2;
-          if (!(ok = mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status))) break;
-          if (!(ok = mbar_wait(B(bars->ready_v[s]), (jj / NS) & 1, ctl, p.status))) break;
-          if (j2 < n_kv &&
-              !(ok = mbar_wait(B(bars->ready_k[j2 % NS]), (j2 / NS) & 1, ctl, p.status)))
-            break;
-          tc_fence_after();
-          const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
-          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
-                                                  vd0 + (s * C::STAGE >> 4), idO, jj > 0);
-          umma_commit(B(bars->empty_v[s]));  // also: O += P_jj V_jj is done
-          if (j2 < n_kv) issue_S(j2);
-        }
       }
       umma_commit(B(bars->mma_final));  // nothing of ours in flight after this
       mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp == kIssuer2Warp) {
+    // ------------------------------------------------- P.V MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
+      bool ok = true;
+      for (int jj = 0; ok && jj < n_kv; ++jj) {
+        const int s = jj % NS, bb = jj & 1;
+        if (!(ok = mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_v[s]), (jj / NS) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
+        mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
+                                                vd0 + (s * C::STAGE >> 4), idO, jj > 0);
+        umma_commit(B(bars->empty_v[s]));  // also: O += P_jj V_jj is done
+      }
+      umma_commit(B(bars->mma_final_pv));  // nothing of this thread in flight after this
+      mbar_drain(B(bars->mma_final_pv), 0);
     }
     __syncwarp();
   } else if (warp < kRowWarp0) {
