@@ -191,8 +191,8 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
     for (int l = 0; l < C::LA; ++l) {
       const uint32_t t = st + (l ? C::OFF_A1 : C::OFF_A0);
-      if constexpr (C::SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
-      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
+      if constexpr (C::SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
     }
     if (!MERGED) {
       fence_proxy_async_smem();
@@ -201,8 +201,8 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
     for (int l = 0; l < C::LB; ++l) {
       const uint32_t t = st + (l ? C::OFF_B1 : C::OFF_B0);
-      if constexpr (C::SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
-      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
+      if constexpr (C::SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
     }
     fence_proxy_async_smem();
     mbar_arrive(B(MERGED ? bars->ready_a[s] : bars->ready_b[s]));

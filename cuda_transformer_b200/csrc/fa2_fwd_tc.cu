@@ -204,8 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------- split / rounding warps
     const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
     auto prep = [&](uint32_t t) {
-      if constexpr (SPLIT == 3) split_tile_smem(t, t + C::TILE, C::TILE, tid, kSplitThreads);
-      else round_tile_smem(t, C::TILE, tid, kSplitThreads);
+      if constexpr (SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
     };
     for (int j = 0; j < n_kv; ++j) {
       const int s = j % NS, r = j / NS;

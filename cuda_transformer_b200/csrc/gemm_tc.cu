@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             ok = false;
             break;
           }
-          split_tile_smem(st, st + C::LO, C::RAW, tid, kPrepThreads);
+          split_tile_smem<C::RAW, kPrepThreads>(st, st + C::LO, tid);
           fence_proxy_async_smem();
           mbar_arrive(B(bars->ready[s]));
         }

@@ -383,31 +383,59 @@ __device__ __forceinline__ void sts128(uint32_t a, float4 v) {
                : "memory");
 }
 
+// Tile preparation by a group of NTHREADS threads, BYTES bytes per tile.
+// Thread t handles the 16-byte words t, t + NTHREADS, ... (a warp covers 512
+// contiguous bytes: no bank conflicts).  Words go in batches of up to 8: every
+// load of a batch is issued before its first store (the accessors are ordered
+// volatile asm), so the shared-memory latency is paid once per batch rather
+// than once per word.
+template <uint32_t BYTES, uint32_t NTHREADS>
+struct TilePrep {
+  static constexpr uint32_t PER = BYTES / (NTHREADS * 16u);  // words per thread
+  static constexpr uint32_t U = PER < 8u ? PER : 8u;
+  static_assert(PER >= 1 && PER % U == 0 && BYTES % (NTHREADS * 16u) == 0, "tile prep shape");
+};
+
 // 3xTF32 split of a shared-memory tile: lo + i receives x - tf32_trunc(x) for
 // every fp32 word x at raw + i.  The raw tile itself is the "hi" operand,
 // because the tensor core reads it truncated to tf32_trunc(x).  Both buffers
 // share the same swizzled layout, so the element correspondence is positional.
-__device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint32_t bytes,
-                                                uint32_t tid, uint32_t nthreads) {
-#pragma unroll 4
-  for (uint32_t off = tid * 16u; off < bytes; off += nthreads * 16u) {
-    const float4 x = lds128(raw + off);
-    sts128(lo + off, make_float4(x.x - tf32_trunc(x.x), x.y - tf32_trunc(x.y),
-                                 x.z - tf32_trunc(x.z), x.w - tf32_trunc(x.w)));
+template <uint32_t BYTES, uint32_t NTHREADS>
+__device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint32_t tid) {
+  using P = TilePrep<BYTES, NTHREADS>;
+#pragma unroll 1
+  for (uint32_t w0 = 0; w0 < P::PER; w0 += P::U) {
+    float4 x[P::U];
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u) x[u] = lds128(raw + (tid + (w0 + u) * NTHREADS) * 16u);
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u)
+      sts128(lo + (tid + (w0 + u) * NTHREADS) * 16u,
+             make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
+                         x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w)));
   }
 }
 
 // TF32 mode: rounds a shared-memory tile in place to the nearest TF32 value
-// (the tensor core itself truncates the 13 low mantissa bits).
-__device__ __forceinline__ void round_tile_smem(uint32_t raw, uint32_t bytes, uint32_t tid,
-                                                uint32_t nthreads) {
-  for (uint32_t off = tid * 16u; off < bytes; off += nthreads * 16u) {
-    float4 x = lds128(raw + off);
-    x.x = tf32_round(x.x);
-    x.y = tf32_round(x.y);
-    x.z = tf32_round(x.z);
-    x.w = tf32_round(x.w);
-    sts128(raw + off, x);
+// (the tensor core itself truncates the 13 low mantissa bits).  The rounding
+// is the two-integer-operation form of cvt.rna.tf32.f32 (tf32_round_finite),
+// which keeps the conversion pipe free for the exponentials; it differs from
+// cvt.rna only on NaNs whose payload lies entirely in the 13 dropped bits,
+// which become infinities -- exactly what the tensor core's own truncation
+// makes of them.
+template <uint32_t BYTES, uint32_t NTHREADS>
+__device__ __forceinline__ void round_tile_smem(uint32_t raw, uint32_t tid) {
+  using P = TilePrep<BYTES, NTHREADS>;
+#pragma unroll 1
+  for (uint32_t w0 = 0; w0 < P::PER; w0 += P::U) {
+    float4 x[P::U];
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u) x[u] = lds128(raw + (tid + (w0 + u) * NTHREADS) * 16u);
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u)
+      sts128(raw + (tid + (w0 + u) * NTHREADS) * 16u,
+             make_float4(tf32_round_finite(x[u].x), tf32_round_finite(x[u].y),
+                         tf32_round_finite(x[u].z), tf32_round_finite(x[u].w)));
   }
 }
 
