@@ -6,10 +6,10 @@
 // causal diagonal instead of scanning every query tile.
 //
 // Warp roles as in the forward: warp 0 TMA producer, warp 1 TMEM allocator and
-// first MMA issuer, warps 2-3 TF32 hi/lo split or rounding of landed tiles,
-// warps 4-7 row warps (one stationary row per thread / TMEM lane), warp 8 the
-// second MMA issuer.  dQ: warp 1 issues S, warp 8 dP and dQ.  dK/dV: warp 1
-// issues S^T and dV, warp 8 dP^T and dK.
+// first MMA issuer, warps 2, 3, 8, 9 TF32 hi/lo split or rounding of landed
+// tiles, warps 4-7 row warps (one stationary row per thread / TMEM lane), warp
+// 10 the second MMA issuer.  dQ: warp 1 issues S, warp 10 dP and dQ.  dK/dV:
+// warp 1 issues S^T and dV, warp 10 dP^T and dK.
 //
 // dQ kernel, per 128 query rows, per key tile j (BN keys):
 //   S  = Q K_j^T     (A = Q in TMEM, B = K_j K-major)
@@ -62,7 +62,9 @@ struct BwdBars {
   // longer read by the tensor core.  With MERGED stages (dK/dV pass) only the
   // _a barriers are used and cover both tiles.
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
-  uint64_t s_full, dp_full, s_free, p_full, ds_full, rows_ready, done, mma_final, mma_final2;
+  // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
+  uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2];
+  uint64_t s_free, rows_ready, done, mma_final, mma_final2;
   CtaCtl ctl;
 };
 
@@ -91,10 +93,10 @@ constexpr size_t bwd_smem_bytes() {
 }
 
 // empty_count: MMA issuers that read a stage; done_count: issuers whose
-// accumulators the epilogue reads.
+// accumulators the epilogue reads; rows: threads of the row warps.
 template <class C>
 __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_count,
-                                              int done_count) {
+                                              int done_count, int rows) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
@@ -104,12 +106,14 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
     mbar_init(B(bars->empty_a[s]), empty_count);
     mbar_init(B(bars->empty_b[s]), 1);
   }
-  mbar_init(B(bars->s_full), 1);
-  mbar_init(B(bars->dp_full), 1);
-  mbar_init(B(bars->s_free), 128);
-  mbar_init(B(bars->p_full), 128);
-  mbar_init(B(bars->ds_full), 128);
-  mbar_init(B(bars->rows_ready), 128);
+  for (int i = 0; i < 2; ++i) {
+    mbar_init(B(bars->s_full[i]), 1);
+    mbar_init(B(bars->dp_full[i]), 1);
+    mbar_init(B(bars->p_full[i]), rows);
+    mbar_init(B(bars->ds_full[i]), rows);
+  }
+  mbar_init(B(bars->s_free), rows);
+  mbar_init(B(bars->rows_ready), rows);
   mbar_init(B(bars->done), done_count);
   mbar_init(B(bars->mma_final), 1);
   mbar_init(B(bars->mma_final2), 1);
@@ -136,18 +140,33 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       if (maps[m]) tma_prefetch_desc(maps[m]);
   int last_a[NS], last_b[NS];
   for (int s = 0; s < NS; ++s) last_a[s] = last_b[s] = -1;
+  // The vector values of step j + 1 are loaded into registers while step j is
+  // staged, so the global-load latency stays off the stage turnaround.
+  constexpr int NV = VEC ? BN / 32 : 1;
+  float vl[NV], vd[NV];
+  auto load_vec = [&](int j) {
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+      const int q = j * BN + 32 * u + lane;
+      const bool in = VEC && j < j1 && q < T;
+      vl[u] = in ? __ldg(lse_bh + (int64_t)q * lse_t) * kLog2e : 0.0f;
+      vd[u] = in ? __ldg(del_bh + q) : 0.0f;
+    }
+  };
+  if constexpr (VEC) load_vec(j0);
   for (int j = j0; j < j1; ++j) {
     const int i = j - j0, s = i % NS, r = i / NS;
     const uint32_t st = tiles + s * C::STAGE;
     if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
     if constexpr (VEC) {
       float* vs = vec + s * 2 * BN;
-      for (int x = lane; x < BN; x += 32) {
-        const int q = j * BN + x;
-        vs[x] = q < T ? __ldg(lse_bh + (int64_t)q * lse_t) * kLog2e : 0.0f;
-        vs[BN + x] = q < T ? __ldg(del_bh + q) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < NV; ++u) {
+        vs[32 * u + lane] = vl[u];
+        vs[BN + 32 * u + lane] = vd[u];
       }
       __syncwarp();
+      load_vec(j + 1);
     }
     if (lane == 0) {
       mbar_arrive_expect_tx(B(bars->full_a[s]), C::LA * C::TILE);
@@ -184,7 +203,7 @@ template <class C, bool MERGED>
 __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
                                              uint32_t* status) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
-  const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
+  const uint32_t tid = prep_tid();
   for (int i = 0; i < n; ++i) {
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
@@ -209,8 +228,13 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
+// Both backward kernels run two row warpgroups, warps 4-7 and 11-14 (15 warps):
+// warps 0-3 and 8-10 keep the forward's roles.
+constexpr int kBwdThreads = 480;
+constexpr int kBwdRowWarp1 = 11;
+
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmKmn,
                          const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
@@ -232,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // K_j is released by the dQ_j issuer alone: dQ_j waits for dS_j, formed
   // after the row warps read S_j, so S_j has completed by then.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 256);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -259,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D,
                                                 kd0 + (uint64_t)(((j % NS) * C::STAGE) >> 4), idS,
                                                 false);
-        umma_commit(B(bars->s_full));
+        umma_commit(B(bars->s_full[0]));
       }
       umma_commit(B(bars->mma_final));
       mbar_drain(B(bars->mma_final), 0);
@@ -279,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D,
                                                 vd0 + stg(j), idS, false);
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
-        umma_commit(B(bars->dp_full));
+        umma_commit(B(bars->dp_full[0]));
       };
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
                 mbar_wait(B(rv[0]), 0, ctl, p.status);
@@ -287,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_dP(0);
         for (int j = 0; ok && j < n_kv; ++j) {
-          if (!(ok = mbar_wait(B(bars->ds_full), j & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
           tc_fence_after();
           mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL,
                                                   kmd0 + stg(j), idQ, j > 0);
@@ -304,21 +328,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
-  } else if (warp < kRowWarp0) {
+  } else if (is_prep_warp(warp)) {
     bwd_splitter<C, false>(bars, tiles, n_kv, p.status);
   } else {
+    // Row warps 4-7 (group 0) and 11-14 (group 1): thread (quad, lane) owns
+    // query row quad*32 + lane in TMEM lane quarter quad; group g forms P and
+    // dS for the key columns [g*BN/2, (g+1)*BN/2) of every step (both are
+    // elementwise), loads Q (g = 0) or dO (g = 1) into TMEM, and writes dQ
+    // columns [g*D/2, (g+1)*D/2).
+    constexpr int HB = BN / 2, CW = HB < 32 ? HB : 32;
     const int quad = warp & 3;
+    const int grp = warp >= kBwdRowWarp1 ? 1 : 0;
+    const int c0 = grp * HB;
     const int row = q0 + quad * 32 + lane;
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
     float l2 = 0.0f, dl = 0.0f;
     {
-      const float* qr = p.st0.row(b, h, valid ? row : 0);
-      const float* gr = p.st1.row(b, h, valid ? row : 0);
-      const bool vq = p.st0.s3 == 1 && ((reinterpret_cast<uintptr_t>(qr) & 15u) == 0);
-      const bool vg = p.st1.s3 == 1 && ((reinterpret_cast<uintptr_t>(gr) & 15u) == 0);
-      row_to_tmem<D, SPLIT>(p.st0, qr, valid, vq, lb, C::TC_Q);
-      row_to_tmem<D, SPLIT>(p.st1, gr, valid, vg, lb, C::TC_G);
+      const Ptr4& src = grp ? p.st1 : p.st0;
+      const float* r = src.row(b, h, valid ? row : 0);
+      const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0);
+      row_to_tmem<D, SPLIT>(src, r, valid, vr, lb, grp ? C::TC_G : C::TC_Q);
       if (valid) {
         l2 = __ldg(p.lse + b * p.l0 + h * p.l1 + (int64_t)row * p.l2) * kLog2e;
         dl = __ldg(p.delta + (int64_t)bh * T + row);
@@ -329,55 +359,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = warp_wait(B(bars->s_full), j & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->s_full[0]), j & 1, ctl, p.status))) break;
       tc_fence_after();
-      float pv[BN];
+      float pv[HB];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32];
-        tmem_ld32(lb + C::TC_S + 32 * c, t);
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW];
+        tmem_ldn<CW>(lb + C::TC_S + c0 + CW * c, t);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pv[32 * c + i] = t[i];
+        for (int i = 0; i < CW; ++i) pv[CW * c + i] = t[i];
       }
       tc_fence_before();
       mbar_arrive(B(bars->s_free));
-      const int kv0 = j * BN;
-      const bool need_mask = !valid || (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
+      const int kv0 = j * BN + c0;
+      const bool need_mask = !valid || (kv0 + HB > T) || (p.causal && kv0 + HB - 1 > q0);
       // straight-line exponentials, then the mask as a separate pass on the
       // few boundary tiles (a test per column would split the unrolled loop
       // into one basic block per column and serialise it)
 #pragma unroll
-      for (int i = 0; i < BN; ++i) pv[i] = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
+      for (int i = 0; i < HB; ++i) pv[i] = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
       if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
+        for (int i = 0; i < HB; ++i) {
           const int kv = kv0 + i;
           pv[i] = (valid && kv < T && (!p.causal || kv <= row)) ? pv[i] : 0.0f;
         }
       }
-      if (!(ok = warp_wait(B(bars->dp_full), j & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->dp_full[0]), j & 1, ctl, p.status))) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32];
-        tmem_ld32(lb + C::TC_DP + 32 * c, t);
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW], lo[CW];
+        tmem_ldn<CW>(lb + C::TC_DP + c0 + CW * c, t);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float ds = pv[32 * c + i] * (t[i] - dl);
+        for (int i = 0; i < CW; ++i) {
+          const float ds = pv[CW * c + i] * (t[i] - dl);
           if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
           else t[i] = tf32_round_finite(ds);
         }
-        tmem_st32(lb + C::TC_DP + 32 * c, t);
-        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
+        tmem_stn<CW>(lb + C::TC_DP + c0 + CW * c, t);
+        if constexpr (SPLIT == 3) tmem_stn<CW>(lb + C::TC_DSL + c0 + CW * c, lo);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->ds_full));
+      mbar_arrive(B(bars->ds_full[0]));
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_row_to_global<D>(lb, C::TC_DQ, p.scale, p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D,
-                            valid);
+      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale,
+                                 p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2),
+                                 valid);
     }
   }
 
@@ -392,17 +423,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 // -------------------------------------------------------------- dK/dV pass
 // dK/dV pass: A = Q (K-major for S^T, MN-major for dK), B = dO (K-major for
 // dP^T, MN-major for dV).
-template <int D_, int BN_, int SPLIT_, int NS_>
+template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
 struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2> {
   using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2>;
+  // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
+  // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
+  // and dS_i, so the rows go from one step to the next without waiting.
+  static constexpr int NSB = NSB_;
+  static constexpr uint32_t SB = T_::NCOPY * BN_;  // columns of one buffer: hi [| lo]
   static constexpr uint32_t TC_K = 0, TC_V = T_::NCOPY * D_, TC_DK = 2 * T_::NCOPY * D_;
-  static constexpr uint32_t TC_DV = TC_DK + D_, TC_S = TC_DV + D_, TC_PL = TC_S + BN_;
-  static constexpr uint32_t TC_DP = TC_S + T_::NCOPY * BN_, TC_DSL = TC_DP + BN_;
-  static_assert(TC_DP + T_::NCOPY * BN_ <= T_::TMEM_COLS, "TMEM budget");
+  static constexpr uint32_t TC_DV = TC_DK + D_, TC_S = TC_DV + D_, TC_DP = TC_S + NSB * SB;
+  static_assert(NSB == 1 || NSB == 2, "S / dP buffering");
+  static_assert(TC_DP + NSB * SB <= T_::TMEM_COLS, "TMEM budget");
 };
 
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmQmn,
                            const __grid_constant__ CUtensorMap tmG,
@@ -426,8 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n = j1 - j0;
 
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
-  // by warp 8): the merged stage is free after both have committed.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2);
+  // by warp 10): the merged stage is free after both have committed.
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 256);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -446,30 +482,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     bwd_producer<C, true, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
                           p.l2, p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
-    //   [P_i ready, tiles i+1 prepared]  dV += P_i^T dO_i;  S^T_{i+1} -> s_full
-    // S^T_{i+1} overwrites P_i after dV_i in this thread's issue order.
+    // Step i of buffer b = i % NSB:  [P_i ready, tiles i+NSB prepared]
+    //   dV += P_i^T dO_i;  S^T_{i+NSB} -> s_full[b]
+    // S^T_{i+NSB} overwrites P_i after dV_i in this thread's issue order.
     if (lane == 0) {
       const uint64_t qd0 = sdesc_kmajor(tiles + C::OFF_A0);  // stage-0 descriptors
       const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
       auto issue_S = [&](int i) {
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_K, tmem + C::TC_K + D,
-                                                qd0 + stg(i), idS, false);
-        umma_commit(B(bars->s_full));
+        const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
+                                                tmem + C::TC_K + D, qd0 + stg(i), idS, false);
+        umma_commit(B(bars->s_full[i % C::NSB]));
       };
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
                 mbar_wait(B(rdy[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
         issue_S(0);
+        if (C::NSB == 2 && n > 1) {
+          ok = mbar_wait(B(rdy[1 % NS]), (1 / NS) & 1, ctl, p.status);
+          if (ok) {
+            tc_fence_after();
+            issue_S(1);
+          }
+        }
         for (int i = 0; ok && i < n; ++i) {
-          if (!(ok = mbar_wait(B(bars->p_full), i & 1, ctl, p.status))) break;
-          if (i + 1 < n && !(ok = mbar_wait(B(rdy[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status)))
+          const int bi = i % C::NSB, nx = i + C::NSB;
+          if (!(ok = mbar_wait(B(bars->p_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
+          // One buffer: the next S^T is needed by the rows right away, so both
+          // waits are taken together and the MMA groups issue back to back.
+          // Two buffers: stage i is released right after dV_i (the ring holds
+          // steps i .. i+2 at once) and S^T_{i+2} waits for its own tiles.
+          if (C::NSB == 1 && nx < n &&
+              !(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status)))
             break;
           tc_fence_after();
+          const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-              tmem + C::TC_DV, tmem + C::TC_S, tmem + C::TC_PL, gmd0 + stg(i), idO, i > 0);
-          if (i + 1 < n) issue_S(i + 1);
+              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+          if (C::NSB == 1 && nx < n) issue_S(nx);
           umma_commit(B(bars->empty_a[i % NS]));
+          if (C::NSB == 2 && nx < n) {
+            if (!(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_S(nx);
+          }
         }
         if (ok) umma_commit(B(bars->done));
       }
@@ -478,31 +535,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == kIssuer2Warp) {
-    //   [dS_i ready]  dK += dS_i^T Q_i -> empty_i;  [tiles i+1 prepared]  dP^T_{i+1} -> dp_full
-    // dP^T_{i+1} overwrites dS_i after dK_i in this thread's issue order.
+    // Step i of buffer b:  [dS_i ready]  dK += dS_i^T Q_i -> empty_i;
+    //   [tiles i+NSB prepared]  dP^T_{i+NSB} -> dp_full[b]
+    // dP^T_{i+NSB} overwrites dS_i after dK_i in this thread's issue order.
     if (lane == 0) {
       const uint64_t gd0 = sdesc_kmajor(tiles + C::OFF_B0);  // stage-0 descriptors
       const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       auto issue_dP = [&](int i) {
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_V, tmem + C::TC_V + D,
-                                                gd0 + stg(i), idS, false);
-        umma_commit(B(bars->dp_full));
+        const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP + sb, tmem + C::TC_V,
+                                                tmem + C::TC_V + D, gd0 + stg(i), idS, false);
+        umma_commit(B(bars->dp_full[i % C::NSB]));
       };
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
                 mbar_wait(B(rdy[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
         issue_dP(0);
-        for (int i = 0; ok && i < n; ++i) {
-          if (!(ok = mbar_wait(B(bars->ds_full), i & 1, ctl, p.status))) break;
-          tc_fence_after();
-          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
-              tmem + C::TC_DK, tmem + C::TC_DP, tmem + C::TC_DSL, qmd0 + stg(i), idO, i > 0);
-          umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
-          if (i + 1 < n) {
-            if (!(ok = mbar_wait(B(rdy[(i + 1) % NS]), ((i + 1) / NS) & 1, ctl, p.status))) break;
+        if (C::NSB == 2 && n > 1) {
+          ok = mbar_wait(B(rdy[1 % NS]), (1 / NS) & 1, ctl, p.status);
+          if (ok) {
             tc_fence_after();
-            issue_dP(i + 1);
+            issue_dP(1);
+          }
+        }
+        for (int i = 0; ok && i < n; ++i) {
+          const int bi = i % C::NSB, nx = i + C::NSB;
+          if (!(ok = mbar_wait(B(bars->ds_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          const uint32_t db = tmem + C::TC_DP + (uint32_t)bi * C::SB;
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
+              tmem + C::TC_DK, db, db + BN, qmd0 + stg(i), idO, i > 0);
+          umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
+          if (nx < n) {
+            if (!(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_dP(nx);
           }
         }
         if (ok) umma_commit(B(bars->done));
@@ -511,93 +579,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
-  } else if (warp < kRowWarp0) {
+  } else if (is_prep_warp(warp)) {
     bwd_splitter<C, true>(bars, tiles, n, p.status);
   } else {
+    // Row warps 4-7 (group 0) and 11-14 (group 1): thread (quad, lane) owns key
+    // row quad*32 + lane in TMEM lane quarter quad; group g forms P^T and dS^T
+    // for the query columns [g*BN/2, (g+1)*BN/2) of every step (both are
+    // elementwise), loads K (g = 0) or V (g = 1) into TMEM, and writes dK
+    // (g = 0) or dV (g = 1).
+    constexpr int HB = BN / 2, CW = HB < 32 ? HB : 32;
     const int quad = warp & 3;
+    const int grp = warp >= kBwdRowWarp1 ? 1 : 0;
+    const int c0 = grp * HB;
     const int row = k0 + quad * 32 + lane;  // key row
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
     {
-      const float* kr = p.st0.row(b, h, valid ? row : 0);
-      const float* vr = p.st1.row(b, h, valid ? row : 0);
-      const bool vk = p.st0.s3 == 1 && ((reinterpret_cast<uintptr_t>(kr) & 15u) == 0);
-      const bool vv = p.st1.s3 == 1 && ((reinterpret_cast<uintptr_t>(vr) & 15u) == 0);
-      row_to_tmem<D, SPLIT>(p.st0, kr, valid, vk, lb, C::TC_K);
-      row_to_tmem<D, SPLIT>(p.st1, vr, valid, vv, lb, C::TC_V);
+      const Ptr4& src = grp ? p.st1 : p.st0;
+      const float* r = src.row(b, h, valid ? row : 0);
+      const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0);
+      row_to_tmem<D, SPLIT>(src, r, valid, vr, lb, grp ? C::TC_V : C::TC_K);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(B(bars->rows_ready));
     }
     bool ok = n > 0;
     for (int i = 0; ok && i < n; ++i) {
-      const int qs = (j0 + i) * BN;
+      const int qs = (j0 + i) * BN + c0;
+      const int bi = i % C::NSB;
+      const uint32_t par = (uint32_t)(i / C::NSB) & 1u;
+      const uint32_t sc = lb + C::TC_S + (uint32_t)bi * C::SB + c0;
+      const uint32_t dc = lb + C::TC_DP + (uint32_t)bi * C::SB + c0;
       // the step's log-sum-exp * log2(e) and delta, staged by the producer warp
       if (!(ok = warp_wait(B(bars->full_a[i % NS]), (i / NS) & 1, ctl, p.status))) break;
-      const float* vl = vec + (i % NS) * 2 * BN;
-      if (!(ok = warp_wait(B(bars->s_full), i & 1, ctl, p.status))) break;
+      const float* vl = vec + (i % NS) * 2 * BN + c0;
+      if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
-      const bool need_mask = !valid || (qs + BN > T) || (p.causal && qs < k0 + kRows - 1);
-      float pv[BN];
+      const bool need_mask = !valid || (qs + HB > T) || (p.causal && qs < k0 + kRows - 1);
+      float pv[HB];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32], lv[32];
-        tmem_ld32(lb + C::TC_S + 32 * c, t);
-        load_vec32(vl + 32 * c, lv);
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW], lo[CW], lv[CW];
+        tmem_ldn<CW>(sc + CW * c, t);
+        load_vecn<CW>(vl + CW * c, lv);
         // straight-line exponentials; the mask is a separate pass on the few
         // boundary tiles (a test per column would serialise the loop)
 #pragma unroll
-        for (int x = 0; x < 32; ++x) t[x] = ex2_approx(fmaf(t[x], p.scale_log2, -lv[x]));
+        for (int x = 0; x < CW; ++x) t[x] = ex2_approx(fmaf(t[x], p.scale_log2, -lv[x]));
         if (need_mask) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const int q = qs + 32 * c + x;
+          for (int x = 0; x < CW; ++x) {
+            const int q = qs + CW * c + x;
             t[x] = (valid && q < T && (!p.causal || q >= row)) ? t[x] : 0.0f;
           }
         }
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {
+        for (int x = 0; x < CW; ++x) {
           const float e = t[x];
-          pv[32 * c + x] = e;
+          pv[CW * c + x] = e;
           if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
           else t[x] = tf32_round_finite(e);
         }
-        tmem_st32(lb + C::TC_S + 32 * c, t);
-        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_PL + 32 * c, lo);
+        tmem_stn<CW>(sc + CW * c, t);
+        if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->p_full));
-      if (!(ok = warp_wait(B(bars->dp_full), i & 1, ctl, p.status))) break;
+      mbar_arrive(B(bars->p_full[bi]));
+      if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32], dv[32];
-        tmem_ld32(lb + C::TC_DP + 32 * c, t);
-        load_vec32(vl + BN + 32 * c, dv);
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW], lo[CW], dv[CW];
+        tmem_ldn<CW>(dc + CW * c, t);
+        load_vecn<CW>(vl + BN + CW * c, dv);
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {
-          const int cc = 32 * c + x;
-          const float ds = pv[cc] * (t[x] - dv[x]);
+        for (int x = 0; x < CW; ++x) {
+          const float ds = pv[CW * c + x] * (t[x] - dv[x]);
           if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
           else t[x] = tf32_round_finite(ds);
         }
-        tmem_st32(lb + C::TC_DP + 32 * c, t);
-        if constexpr (SPLIT == 3) tmem_st32(lb + C::TC_DSL + 32 * c, lo);
+        tmem_stn<CW>(dc + CW * c, t);
+        if constexpr (SPLIT == 3) tmem_stn<CW>(dc + BN + CW * c, lo);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->ds_full));
+      mbar_arrive(B(bars->ds_full[bi]));
     }
     const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
+    float* out = grp ? p.out1 : p.out0;
     if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
       if (valid) {
-        for (int d = 0; d < D; ++d) p.out0[orow + d] = 0.0f, p.out1[orow + d] = 0.0f;
+        for (int d = 0; d < D; ++d) out[orow + d] = 0.0f;
       }
     } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_row_to_global<D>(lb, C::TC_DK, p.scale, p.out0 + orow, valid);
-      tmem_row_to_global<D>(lb, C::TC_DV, 1.0f, p.out1 + orow, valid);
+      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid);
     }
   }
 
@@ -649,7 +726,7 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, q, g, lse, ls, delta, dq, nullptr, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tk, tkmn, tv, p);
+  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tk, tkmn, tv, p);
   return check_launch();
 }
 
@@ -669,7 +746,7 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tq, tqmn, tg, tgmn, p);
+  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tqmn, tg, tgmn, p);
   return check_launch();
 }
 
@@ -702,7 +779,7 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
   const bool split = pr.precision == CT_PRECISION_3XTF32;
   if (pr.D == 64)
     return split ? run_dkdv<DkvCfg<64, 32, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
-                 : run_dkdv<DkvCfg<64, 64, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+                 : run_dkdv<DkvCfg<64, 64, 1, 3, 2>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
   if (pr.D == 32)
     return split ? run_dkdv<DkvCfg<32, 64, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
                  : run_dkdv<DkvCfg<32, 128, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);

@@ -11,7 +11,7 @@
 //  * Precision: SPLIT == 3 stores every operand as a TF32 hi/lo pair and issues
 //    hi*hi + hi*lo + lo*hi; SPLIT == 1 issues one TF32 MMA per product on
 //    operands rounded to the nearest TF32 (the tensor core truncates raw FP32).
-//  * Warps 2-3 prepare every landed tile before the MMA reads it: the hi/lo
+//  * Warps 2, 3, 8, 9 prepare every landed tile before the MMA reads it: the hi/lo
 //    split (SPLIT == 3) or the in-place rounding (SPLIT == 1).
 #pragma once
 
@@ -25,16 +25,26 @@ namespace ct {
 namespace fa2 {
 
 constexpr int kRows = 128;        // stationary rows per CTA
-constexpr int kThreads = 288;     // 9 warps
+constexpr int kThreads = 352;     // 11 warps
 constexpr int kRowWarp0 = 4;      // first warp of the row warpgroup (4 warps)
-constexpr int kSplitWarp0 = 2;    // first of the two split warps
-// Warp 1 issues one group of tcgen05.mma chains and warp 8 the other.  An
+// Warp w runs on SM sub-partition w % 4.  The four tile-preparation warps
+// (2, 3, 8, 9) sit one per sub-partition, so the split / rounding work of a
+// landed tile spreads over all four schedulers instead of competing with two
+// of the row warps for issue slots.  (ptxas sizes registers for 12 warps
+// whether the block has 9 or 11, so the two extra warps cost no registers.)
+constexpr int kSplitThreads = 128;
+// Warp 1 issues one group of tcgen05.mma chains and warp 10 the other.  An
 // issuing thread waits for each MMA to be accepted, so one thread drives the
 // tensor pipe at ~45 cycles per N <= 64 MMA at best and idles it whenever it
 // waits on a barrier; two threads feeding independent accumulators
 // interleave and reach the pipe's full rate (measured on B200).
-constexpr int kIssuer2Warp = 8;
-constexpr int kSplitThreads = 64;
+constexpr int kIssuer2Warp = 10;
+__device__ __forceinline__ bool is_prep_warp(int w) { return w == 2 || w == 3 || w == 8 || w == 9; }
+// Index 0..127 of this thread among the preparation warps.
+__device__ __forceinline__ uint32_t prep_tid() {
+  const int w = threadIdx.x / 32;
+  return (uint32_t)((((w & 1) + (w >= 8 ? 2 : 0)) * 32) + (threadIdx.x & 31));
+}
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kLog2e = 1.44269504088896340736f;
 
@@ -116,6 +126,30 @@ __device__ __forceinline__ void load_vec32(const float* src, float (&v)[32]) {
   }
 }
 
+// N = 16 or 32 columns of one TMEM lane quarter (load waits, store does not).
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, float (&v)[N]) {
+  static_assert(N == 16 || N == 32, "TMEM access width");
+  if constexpr (N == 32) tmem_ld32(taddr, v);
+  else tmem_ld16(taddr, v);
+}
+template <int N>
+__device__ __forceinline__ void tmem_stn(uint32_t taddr, const float (&v)[N]) {
+  static_assert(N == 16 || N == 32, "TMEM access width");
+  if constexpr (N == 32) tmem_st32(taddr, v);
+  else tmem_st16(taddr, v);
+}
+// N consecutive floats (N % 4 == 0) from 16-byte aligned shared memory (broadcast).
+template <int N>
+__device__ __forceinline__ void load_vecn(const float* src, float (&v)[N]) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 x = s4[i];
+    v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+  }
+}
+
 __device__ __forceinline__ float max32(const float (&t)[32]) {
   float m[8];
 #pragma unroll
@@ -136,6 +170,27 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t 
       float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
+        d4[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
+                            v[4 * i + 3] * scale);
+    }
+  }
+}
+
+// Stores NC (16 or a multiple of 32) TMEM columns [col, col+NC) of this
+// thread's lane times `scale` to dense global memory.
+template <int NC>
+__device__ __forceinline__ void tmem_cols_to_global(uint32_t lane_base, uint32_t col, float scale,
+                                                    float* dst, bool valid) {
+  constexpr int CW = NC < 32 ? NC : 32;
+  static_assert(NC % CW == 0, "column count");
+#pragma unroll
+  for (int c = 0; c < NC / CW; ++c) {
+    float v[CW];
+    tmem_ldn<CW>(lane_base + col + CW * c, v);
+    if (valid) {
+      float4* d4 = reinterpret_cast<float4*>(dst + CW * c);
+#pragma unroll
+      for (int i = 0; i < CW / 4; ++i)
         d4[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
                             v[4 * i + 3] * scale);
     }

@@ -9,11 +9,11 @@
 // Per CTA: one (batch, head) and 128 query rows.  Warp roles:
 //   warp 0      TMA producer of K/V tiles (NS-stage ring)
 //   warp 1      TMEM allocator + issuer of S = Q K^T (one thread)
-//   warps 2-3   TF32 hi/lo split (SPLIT == 3) or rounding (SPLIT == 1) of
+//   warps 2,3,8,9  TF32 hi/lo split (SPLIT == 3) or rounding (SPLIT == 1) of
 //               each landed K/V tile
 //   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
 //               epilogue (thread r <-> query row r <-> TMEM lane r)
-//   warp 8      issuer of O += P V (one thread)
+//   warp 10     issuer of O += P V (one thread)
 // K tiles use the K-major tile layout, V tiles the MN-major one.
 // TMEM columns: Q (hi[,lo]) | O | two S/P buffers (S overwritten by P hi, then
 // P lo).  S_{j+1} = Q K_{j+1}^T runs on the tensor core while the row warps
@@ -200,9 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(B(bars->mma_final_pv), 0);
     }
     __syncwarp();
-  } else if (warp < kRowWarp0) {
+  } else if (is_prep_warp(warp)) {
     // ---------------------------------------- split / rounding warps
-    const uint32_t tid = threadIdx.x - kSplitWarp0 * 32;
+    const uint32_t tid = prep_tid();
     auto prep = [&](uint32_t t) {
       if constexpr (SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
       else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
