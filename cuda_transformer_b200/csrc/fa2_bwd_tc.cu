@@ -48,12 +48,18 @@ struct BwdTiles {
 };
 
 // dQ pass: A = K (K-major for S, MN-major for dQ), B = V (K-major for dP).
-template <int D_, int BN_, int SPLIT_, int NS_>
+// NSB TMEM buffers each for S and dP / dS: with two, S_{j+1} and dP_{j+1} run
+// on the tensor core while the row warps still form dS_j, and dP_{j+1} does
+// not wait for dQ_j to finish reading dS_j.
+template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
 struct DqCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1> {
   using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1>;
+  static constexpr int NSB = NSB_;
+  static constexpr uint32_t SB = T_::NCOPY * BN_;  // one dP / dS buffer: hi [| lo]
   static constexpr uint32_t TC_Q = 0, TC_G = T_::NCOPY * D_, TC_DQ = 2 * T_::NCOPY * D_;
-  static constexpr uint32_t TC_S = TC_DQ + D_, TC_DP = TC_S + BN_, TC_DSL = TC_DP + BN_;
-  static_assert(TC_DP + T_::NCOPY * BN_ <= T_::TMEM_COLS, "TMEM budget");
+  static constexpr uint32_t TC_S = TC_DQ + D_, TC_DP = TC_S + NSB * BN_;
+  static_assert(NSB == 1 || NSB == 2, "S / dP buffering");
+  static_assert(TC_DP + NSB * SB <= T_::TMEM_COLS, "TMEM budget");
 };
 
 template <int NS>
@@ -63,8 +69,8 @@ struct BwdBars {
   // _a barriers are used and cover both tiles.
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
   // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
-  uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2];
-  uint64_t s_free, rows_ready, done, mma_final, mma_final2;
+  uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2], s_free[2];
+  uint64_t rows_ready, done, mma_final, mma_final2;
   CtaCtl ctl;
 };
 
@@ -111,8 +117,8 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
     mbar_init(B(bars->dp_full[i]), 1);
     mbar_init(B(bars->p_full[i]), rows);
     mbar_init(B(bars->ds_full[i]), rows);
+    mbar_init(B(bars->s_free[i]), rows);
   }
-  mbar_init(B(bars->s_free), rows);
   mbar_init(B(bars->rows_ready), rows);
   mbar_init(B(bars->done), done_count);
   mbar_init(B(bars->mma_final), 1);
@@ -271,27 +277,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_producer<C, false, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
                            p.status);
   } else if (warp == 1) {
-    // S_j = Q K_j^T, S_{j+1} once the row warps hold S_j in registers.
+    // S_j = Q K_j^T into S buffer j % NSB once the row warps hold S_{j-NSB}
+    // (the buffer's previous contents) in registers.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_A0);  // stage-0 descriptor
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       for (int j = 0; ok && j < n_kv; ++j) {
-        if (j > 0 && !(ok = mbar_wait(B(bars->s_free), (j - 1) & 1, ctl, p.status))) break;
+        const int bj = j % C::NSB;
+        if (j >= C::NSB &&
+            !(ok = mbar_wait(B(bars->s_free[bj]), ((j - C::NSB) / C::NSB) & 1, ctl, p.status)))
+          break;
         if (!(ok = mbar_wait(B(bars->ready_a[j % NS]), (j / NS) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S, tmem + C::TC_Q, tmem + C::TC_Q + D,
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + (uint32_t)bj * BN, tmem + C::TC_Q,
+                                                tmem + C::TC_Q + D,
                                                 kd0 + (uint64_t)(((j % NS) * C::STAGE) >> 4), idS,
                                                 false);
-        umma_commit(B(bars->s_full[0]));
+        umma_commit(B(bars->s_full[bj]));
       }
       umma_commit(B(bars->mma_final));
       mbar_drain(B(bars->mma_final), 0);
     }
     __syncwarp();
   } else if (warp == kIssuer2Warp) {
-    // dP_j = dO V_j^T and dQ += dS_j K_j.  dP_{j+1} overwrites dS_j only
-    // after dQ_j in this thread's issue order.
+    // dP_j = dO V_j^T into dP buffer j % NSB, and dQ += dS_j K_j.
+    // dP_{j+NSB} overwrites dS_j only after dQ_j in this thread's issue order.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idQ = idesc_tf32(128, D, false, true);
@@ -300,26 +311,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       auto stg = [&](int j) { return (uint64_t)(((j % NS) * C::STAGE) >> 4); };
       auto& rv = bars->ready_b;
       auto issue_dP = [&](int j) {
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP, tmem + C::TC_G, tmem + C::TC_G + D,
+        const uint32_t db = tmem + C::TC_DP + (uint32_t)(j % C::NSB) * C::SB;
+        mma_chain<SPLIT, D, false, BN, C::TILE>(db, tmem + C::TC_G, tmem + C::TC_G + D,
                                                 vd0 + stg(j), idS, false);
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
-        umma_commit(B(bars->dp_full[0]));
+        umma_commit(B(bars->dp_full[j % C::NSB]));
       };
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
                 mbar_wait(B(rv[0]), 0, ctl, p.status);
       if (ok) {
         tc_fence_after();
         issue_dP(0);
-        for (int j = 0; ok && j < n_kv; ++j) {
-          if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
-          tc_fence_after();
-          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, tmem + C::TC_DP, tmem + C::TC_DSL,
-                                                  kmd0 + stg(j), idQ, j > 0);
-          umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
-          if (j + 1 < n_kv) {
-            if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
+        if (C::NSB == 2 && n_kv > 1) {
+          ok = mbar_wait(B(rv[1 % NS]), (1 / NS) & 1, ctl, p.status);
+          if (ok) {
             tc_fence_after();
-            issue_dP(j + 1);
+            issue_dP(1);
+          }
+        }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int bj = j % C::NSB, nx = j + C::NSB;
+          if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j / C::NSB) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          const uint32_t db = tmem + C::TC_DP + (uint32_t)bj * C::SB;
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, db, db + BN, kmd0 + stg(j), idQ,
+                                                  j > 0);
+          umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
+          if (nx < n_kv) {
+            if (!(ok = mbar_wait(B(rv[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_dP(nx);
           }
         }
         if (ok) umma_commit(B(bars->done));
@@ -359,18 +380,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = warp_wait(B(bars->s_full[0]), j & 1, ctl, p.status))) break;
+      const int bj = j % C::NSB;
+      const uint32_t par = (uint32_t)(j / C::NSB) & 1u;
+      const uint32_t dc = lb + C::TC_DP + (uint32_t)bj * C::SB + c0;
+      if (!(ok = warp_wait(B(bars->s_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
       float pv[HB];
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW];
-        tmem_ldn<CW>(lb + C::TC_S + c0 + CW * c, t);
+        tmem_ldn<CW>(lb + C::TC_S + (uint32_t)bj * BN + c0 + CW * c, t);
 #pragma unroll
         for (int i = 0; i < CW; ++i) pv[CW * c + i] = t[i];
       }
       tc_fence_before();
-      mbar_arrive(B(bars->s_free));
+      mbar_arrive(B(bars->s_free[bj]));
       const int kv0 = j * BN + c0;
       const bool need_mask = !valid || (kv0 + HB > T) || (p.causal && kv0 + HB - 1 > q0);
       // straight-line exponentials, then the mask as a separate pass on the
@@ -385,24 +409,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           pv[i] = (valid && kv < T && (!p.causal || kv <= row)) ? pv[i] : 0.0f;
         }
       }
-      if (!(ok = warp_wait(B(bars->dp_full[0]), j & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->dp_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW];
-        tmem_ldn<CW>(lb + C::TC_DP + c0 + CW * c, t);
+        tmem_ldn<CW>(dc + CW * c, t);
 #pragma unroll
         for (int i = 0; i < CW; ++i) {
           const float ds = pv[CW * c + i] * (t[i] - dl);
           if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
           else t[i] = tf32_round_finite(ds);
         }
-        tmem_stn<CW>(lb + C::TC_DP + c0 + CW * c, t);
-        if constexpr (SPLIT == 3) tmem_stn<CW>(lb + C::TC_DSL + c0 + CW * c, lo);
+        tmem_stn<CW>(dc + CW * c, t);
+        if constexpr (SPLIT == 3) tmem_stn<CW>(dc + BN + CW * c, lo);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->ds_full[0]));
+      mbar_arrive(B(bars->ds_full[bj]));
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
@@ -765,7 +789,7 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 
   const bool split = pr.precision == CT_PRECISION_3XTF32;
   if (pr.D == 64)
     return split ? run_dq<DqCfg<64, 64, 3, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
-                 : run_dq<DqCfg<64, 128, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
+                 : run_dq<DqCfg<64, 64, 1, 4, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   if (pr.D == 32)
     return split ? run_dq<DqCfg<32, 64, 3, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<32, 128, 1, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);

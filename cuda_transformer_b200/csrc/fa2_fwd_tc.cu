@@ -15,9 +15,9 @@
 //               epilogue (thread r <-> query row r <-> TMEM lane r)
 //   warp 10     issuer of O += P V (one thread)
 // K tiles use the K-major tile layout, V tiles the MN-major one.
-// TMEM columns: Q (hi[,lo]) | O | two S/P buffers (S overwritten by P hi, then
-// P lo).  S_{j+1} = Q K_{j+1}^T runs on the tensor core while the row warps
-// turn S_j into P_j.  O is rescaled only when a row maximum grows by more
+// TMEM columns: Q (hi[,lo]) | O | two or three S/P buffers (S overwritten by P
+// hi, then P lo).  S_{j+1} (and S_{j+2} with three buffers) runs on the tensor
+// core while the row warps turn S_j into P_j.  O is rescaled only when a row maximum grows by more
 // than 2^8 (exact: l and O always share the stale maximum).
 #include "fa2_common.cuh"
 
@@ -26,9 +26,11 @@ namespace {
 
 using namespace fa2;
 
-template <int D_, int BN_, int SPLIT_, int NS_>
+// NSB S/P buffers in TMEM: S_{j+NSB-1} is computed while the row warps turn
+// S_j into P_j and the tensor core runs O += P_{j-1} V_{j-1}.
+template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 2>
 struct FwdCfg {
-  static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_;
+  static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, NSB = NSB_;
   static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
   static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;  // one K or V tile
   static constexpr uint32_t STAGE = 2u * NCOPY * TILE;
@@ -38,13 +40,14 @@ struct FwdCfg {
   static constexpr uint32_t TC_S = TC_O + D;
   static constexpr uint32_t SBUF = NCOPY * BN;
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(TC_S + 2 * SBUF <= TMEM_COLS, "TMEM budget");
-  static_assert(NS >= 3, "K_{j+2} is needed before V_j is released");
+  static_assert(TC_S + NSB * SBUF <= TMEM_COLS, "TMEM budget");
+  static_assert(NSB == 2 || NSB == 3, "S buffering");
+  static_assert(NS >= 3 && NS >= NSB, "K_{j+NSB} is needed before V_j is released");
   static_assert(D % 32 == 0 && BN % 32 == 0, "tile shape");
 };
 
 template <int NS>
-struct FwdBars {
+struct FwdBars {  // (p_full: one per S/P buffer, at most 3)
   // full_*: TMA landed; ready_*: split or rounded; empty_*: free again.  K and V
   // keep separate barriers: K_j is released when S_j is done, well before V_j,
   // which gives the producer more lead on the next K tiles.
@@ -52,7 +55,7 @@ struct FwdBars {
   // The row warps learn that S_j is done from empty_k of its stage and that
   // O += P_j V_j is done from empty_v (both complete exactly then); a stage's
   // barrier cannot run a phase ahead of the row warps, whose P feeds it.
-  uint64_t p_full[2], q_ready, mma_final, mma_final_pv;
+  uint64_t p_full[3], q_ready, mma_final, mma_final_pv;
   CtaCtl ctl;
 };
 
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(B(bars->empty_k[s]), 1);
       mbar_init(B(bars->empty_v[s]), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(B(bars->p_full[i]), 128);
     }
     mbar_init(B(bars->q_ready), 128);
@@ -158,15 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);  // stage-0 descriptor
-      // S_j = Q K_j^T into S buffer j & 1; before S_j overwrites the buffer of
-      // P_{j-2}, the P.V issuer must have finished O += P_{j-2} V_{j-2}
+      // S_j = Q K_j^T into S buffer j % NSB; before S_j overwrites the buffer
+      // of P_{j-NSB}, the P.V issuer must have finished O += P_{j-NSB} V_{j-NSB}
       // (empty_v of its stage completes exactly then).  empty_k tells the row
       // warps that S_j is ready.
       bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status);
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % NS, bb = j & 1;
-        if (j >= 2) {
-          const int jj = j - 2;
+        const int s = j % NS, bb = j % C::NSB;
+        if (j >= C::NSB) {
+          const int jj = j - C::NSB;
           if (!(ok = mbar_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status))) break;
         }
         if (!(ok = mbar_wait(B(bars->ready_k[s]), (j / NS) & 1, ctl, p.status))) break;
@@ -187,8 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
       bool ok = true;
       for (int jj = 0; ok && jj < n_kv; ++jj) {
-        const int s = jj % NS, bb = jj & 1;
-        if (!(ok = mbar_wait(B(bars->p_full[bb]), (jj >> 1) & 1, ctl, p.status))) break;
+        const int s = jj % NS, bb = jj % C::NSB;
+        if (!(ok = mbar_wait(B(bars->p_full[bb]), (jj / C::NSB) & 1, ctl, p.status))) break;
         if (!(ok = mbar_wait(B(bars->ready_v[s]), (jj / NS) & 1, ctl, p.status))) break;
         tc_fence_after();
         const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
@@ -237,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int bb = j & 1;
+      const int bb = j % C::NSB;
       if (!(ok = warp_wait(B(bars->empty_k[j % NS]), (j / NS) & 1, ctl, p.status))) break;
       tc_fence_after();
       const uint32_t sc = lb + C::TC_S + bb * C::SBUF;
@@ -362,14 +365,14 @@ int launch_fa2_fwd_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, 
   const bool split = pr.precision == CT_PRECISION_3XTF32;
   switch (pr.D) {
     case 32:
-      return split ? run_fwd<FwdCfg<32, 64, 3, 4>>(pr, q, k, v, o, lse, dev, st)
-                   : run_fwd<FwdCfg<32, 128, 1, 4>>(pr, q, k, v, o, lse, dev, st);
+      return split ? run_fwd<FwdCfg<32, 64, 3, 4, 3>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<32, 128, 1, 4, 3>>(pr, q, k, v, o, lse, dev, st);
     case 64:
-      return split ? run_fwd<FwdCfg<64, 64, 3, 3>>(pr, q, k, v, o, lse, dev, st)
-                   : run_fwd<FwdCfg<64, 128, 1, 3>>(pr, q, k, v, o, lse, dev, st);
+      return split ? run_fwd<FwdCfg<64, 64, 3, 3, 2>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<64, 128, 1, 3, 3>>(pr, q, k, v, o, lse, dev, st);
     case 128:
-      return split ? run_fwd<FwdCfg<128, 32, 3, 3>>(pr, q, k, v, o, lse, dev, st)
-                   : run_fwd<FwdCfg<128, 64, 1, 3>>(pr, q, k, v, o, lse, dev, st);
+      return split ? run_fwd<FwdCfg<128, 32, 3, 3, 2>>(pr, q, k, v, o, lse, dev, st)
+                   : run_fwd<FwdCfg<128, 64, 1, 3, 3>>(pr, q, k, v, o, lse, dev, st);
     default:
       return CT_ERR_UNSUPPORTED_HEAD_DIM;
   }
