@@ -155,8 +155,8 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
     for (int u = 0; u < NV; ++u) {
       const int q = j * BN + 32 * u + lane;
       const bool in = VEC && j < j1 && q < T;
-      vl[u] = in ? __ldg(lse_bh + (int64_t)q * lse_t) * kLog2e : 0.0f;
-      vd[u] = in ? __ldg(del_bh + q) : 0.0f;
+      vl[u] = in ? ldg_nc_early(lse_bh + (int64_t)q * lse_t) : 0.0f;
+      vd[u] = in ? ldg_nc_early(del_bh + q) : 0.0f;
     }
   };
   if constexpr (VEC) load_vec(j0);
@@ -168,7 +168,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       float* vs = vec + s * 2 * BN;
 #pragma unroll
       for (int u = 0; u < NV; ++u) {
-        vs[32 * u + lane] = vl[u];
+        vs[32 * u + lane] = vl[u] * kLog2e;
         vs[BN + 32 * u + lane] = vd[u];
       }
       __syncwarp();

@@ -369,6 +369,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Read-only global load issued where it stands: an ordered (volatile) asm
+// statement, so the compiler cannot sink it towards the first use of its
+// result (used to prefetch one pipeline step ahead).
+__device__ __forceinline__ float ldg_nc_early(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
 // 128-bit shared-memory accessors on 32-bit shared addresses.
 __device__ __forceinline__ float4 lds128(uint32_t a) {
   float4 v;
