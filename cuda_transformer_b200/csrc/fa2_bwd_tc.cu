@@ -36,11 +36,15 @@ using namespace fa2;
 // operand layout differs from the K-major one).  Per stage, in order:
 //   A K-major [raw, lo] | A MN-major [raw, lo] (LA == 2) | B K-major [raw, lo] |
 //   B MN-major [raw, lo] (LB == 2), the lo copies present when SPLIT == 3.
-template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_>
+// With KIL (3xTF32 only) the K-major tiles interleave instead: each 32-column
+// chunk of BN raw rows is followed by its BN low-part rows (see mma_chain_kil).
+template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_, bool KIL_ = false>
 struct BwdTiles {
   static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, LA = LA_, LB = LB_;
   static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
+  static constexpr bool KIL = KIL_ && SPLIT == 3;
   static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;
+  static constexpr uint32_t KCH = (KIL ? 2u : 1u) * BN * 128u;  // K-major chunk stride
   static constexpr uint32_t OFF_A0 = 0, OFF_A1 = NCOPY * TILE;
   static constexpr uint32_t OFF_B0 = LA * NCOPY * TILE, OFF_B1 = OFF_B0 + NCOPY * TILE;
   static constexpr uint32_t STAGE = (LA + LB) * NCOPY * TILE;
@@ -180,7 +184,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       for (int l = 0; l < C::LA; ++l)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_A1 : C::OFF_A0) + c * BN * 128, maps[l],
+          tma_load_4d(st + (l ? C::OFF_A1 + c * BN * 128 : C::OFF_A0 + c * C::KCH), maps[l],
                       B(bars->full_a[s]), 32 * c, j * BN, h, b);
     }
     last_a[s] = r;
@@ -191,7 +195,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       for (int l = 0; l < C::LB; ++l)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_B1 : C::OFF_B0) + c * BN * 128, maps[2 + l],
+          tma_load_4d(st + (l ? C::OFF_B1 + c * BN * 128 : C::OFF_B0 + c * C::KCH), maps[2 + l],
                       B(bars->full_b[s]), 32 * c, j * BN, h, b);
     }
     last_b[s] = r;
@@ -205,6 +209,19 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
+// Prepares one landed tile: l = 0 is the K-major copy (interleaved with KIL).
+template <class C>
+__device__ __forceinline__ void prep_tile(uint32_t t, int l, uint32_t tid) {
+  if constexpr (C::SPLIT == 3) {
+    if (C::KIL && l == 0)
+      split_tile_smem_il<C::TILE, kSplitThreads, (uint32_t)C::BN * 128u>(t, tid);
+    else
+      split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+  } else {
+    round_tile_smem<C::TILE, kSplitThreads>(t, tid);
+  }
+}
+
 template <class C, bool MERGED>
 __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
                                              uint32_t* status) {
@@ -214,21 +231,13 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
     if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LA; ++l) {
-      const uint32_t t = st + (l ? C::OFF_A1 : C::OFF_A0);
-      if constexpr (C::SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
-      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
-    }
+    for (int l = 0; l < C::LA; ++l) prep_tile<C>(st + (l ? C::OFF_A1 : C::OFF_A0), l, tid);
     if (!MERGED) {
       fence_proxy_async_smem();
       mbar_arrive(B(bars->ready_a[s]));
     }
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LB; ++l) {
-      const uint32_t t = st + (l ? C::OFF_B1 : C::OFF_B0);
-      if constexpr (C::SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
-      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
-    }
+    for (int l = 0; l < C::LB; ++l) prep_tile<C>(st + (l ? C::OFF_B1 : C::OFF_B0), l, tid);
     fence_proxy_async_smem();
     mbar_arrive(B(MERGED ? bars->ready_a[s] : bars->ready_b[s]));
   }
@@ -447,9 +456,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // -------------------------------------------------------------- dK/dV pass
 // dK/dV pass: A = Q (K-major for S^T, MN-major for dK), B = dO (K-major for
 // dP^T, MN-major for dV).
+// In 3xTF32 mode S^T and dP^T use the interleaved K-major layout: their two
+// hi/lo partial sums land side by side in the buffer's 2*BN columns and the
+// row warps add them (mma_chain_kil).
 template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
-struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2> {
-  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2>;
+struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true>;
   // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
   // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
   // and dS_i, so the rows go from one step to the next without waiting.
@@ -499,6 +511,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
   auto& rdy = bars->ready_a;  // merged stages: Q_i and dO_i both prepared
   constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+  constexpr uint32_t idS2 = idesc_tf32(128, 2 * BN, false, false);  // [hi | lo] rows (KIL)
   constexpr uint32_t idO = idesc_tf32(128, D, false, true);
 
   if (warp == 0) {
@@ -514,8 +527,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
       auto issue_S = [&](int i) {
         const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
-                                                tmem + C::TC_K + D, qd0 + stg(i), idS, false);
+        if constexpr (C::KIL)
+          mma_chain_kil<D, C::KCH>(tmem + C::TC_S + sb, tmem + C::TC_K, tmem + C::TC_K + D,
+                                   qd0 + stg(i), idS2, idS);
+        else
+          mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
+                                                  tmem + C::TC_K + D, qd0 + stg(i), idS, false);
         umma_commit(B(bars->s_full[i % C::NSB]));
       };
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
@@ -567,8 +584,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       auto issue_dP = [&](int i) {
         const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP + sb, tmem + C::TC_V,
-                                                tmem + C::TC_V + D, gd0 + stg(i), idS, false);
+        if constexpr (C::KIL)
+          mma_chain_kil<D, C::KCH>(tmem + C::TC_DP + sb, tmem + C::TC_V, tmem + C::TC_V + D,
+                                   gd0 + stg(i), idS2, idS);
+        else
+          mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP + sb, tmem + C::TC_V,
+                                                  tmem + C::TC_V + D, gd0 + stg(i), idS, false);
         umma_commit(B(bars->dp_full[i % C::NSB]));
       };
       bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
@@ -645,6 +666,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], lv[CW];
         tmem_ldn<CW>(sc + CW * c, t);
+        if constexpr (C::KIL) {  // S^T = [hi-hi + lo-hi part] + [hi-lo part]
+          tmem_ldn<CW>(sc + BN + CW * c, lo);
+#pragma unroll
+          for (int x = 0; x < CW; ++x) t[x] += lo[x];
+        }
         load_vecn<CW>(vl + CW * c, lv);
         // straight-line exponentials; the mask is a separate pass on the few
         // boundary tiles (a test per column would serialise the loop)
@@ -676,6 +702,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], dv[CW];
         tmem_ldn<CW>(dc + CW * c, t);
+        if constexpr (C::KIL) {  // dP^T from its two partial sums
+          tmem_ldn<CW>(dc + BN + CW * c, lo);
+#pragma unroll
+          for (int x = 0; x < CW; ++x) t[x] += lo[x];
+        }
         load_vecn<CW>(vl + BN + CW * c, dv);
 #pragma unroll
         for (int x = 0; x < CW; ++x) {

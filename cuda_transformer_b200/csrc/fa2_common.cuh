@@ -219,6 +219,24 @@ __device__ __forceinline__ void mma_chain(uint32_t d, uint32_t a_hi, uint32_t a_
   }
 }
 
+// 3xTF32 product D = A x B over K = KDIM into 2*BN accumulator columns, B a
+// K-major tile whose 32-column chunks (stride KCH bytes) each hold BN raw rows
+// followed by the BN rows of their low parts.  Per k-step, one MMA of N = 2*BN
+// gives [a_hi*b_hi | a_hi*b_lo] and one of N = BN adds a_lo*b_hi to the first
+// half: the product is the sum of the two halves, and N = 2*BN costs the
+// tensor pipe's issue no more than N = BN does when BN <= 32.
+template <int KDIM, uint32_t KCH>
+__device__ __forceinline__ void mma_chain_kil(uint32_t d, uint32_t a_hi, uint32_t a_lo,
+                                              uint64_t bd, uint32_t id_wide, uint32_t id_narrow) {
+#pragma unroll
+  for (int k = 0; k < KDIM / 8; ++k) {
+    const uint32_t off = (uint32_t)(k / 4) * KCH + (uint32_t)(k % 4) * 32u;
+    const uint64_t bh = bd + (off >> 4);
+    umma_tf32_ts(d, a_hi + 8 * k, bh, id_wide, k > 0 ? 1u : 0u);
+    umma_tf32_ts(d, a_lo + 8 * k, bh, id_narrow, 1u);
+  }
+}
+
 // Maps a linear CTA index to (tile, batch*head).  Heads are taken in groups of
 // `group` (the last group may be smaller): all tiles of a group run before the
 // next group, so resident CTAs share a few heads' streamed operands in L2,

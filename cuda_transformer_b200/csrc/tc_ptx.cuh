@@ -425,6 +425,30 @@ __device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint3
   }
 }
 
+// 3xTF32 split of a tile stored as interleaved chunks: CHUNK raw bytes, then
+// their CHUNK low-part bytes, repeated (BYTES raw bytes in all).  An MMA can
+// then read a raw chunk and its low part as one operand of twice the rows.
+template <uint32_t BYTES, uint32_t NTHREADS, uint32_t CHUNK>
+__device__ __forceinline__ void split_tile_smem_il(uint32_t base, uint32_t tid) {
+  using P = TilePrep<BYTES, NTHREADS>;
+  static_assert(BYTES % CHUNK == 0 && CHUNK % 16u == 0, "chunk shape");
+  auto raw_at = [&](uint32_t w) {
+    const uint32_t byte = w * 16u;
+    return base + (byte / CHUNK) * 2u * CHUNK + byte % CHUNK;
+  };
+#pragma unroll 1
+  for (uint32_t w0 = 0; w0 < P::PER; w0 += P::U) {
+    float4 x[P::U];
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u) x[u] = lds128(raw_at(tid + (w0 + u) * NTHREADS));
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u)
+      sts128(raw_at(tid + (w0 + u) * NTHREADS) + CHUNK,
+             make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
+                         x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w)));
+  }
+}
+
 // TF32 mode: rounds a shared-memory tile in place to the nearest TF32 value
 // (the tensor core itself truncates the 13 low mantissa bits).  The rounding
 // is the two-integer-operation form of cvt.rna.tf32.f32 (tf32_round_finite),
