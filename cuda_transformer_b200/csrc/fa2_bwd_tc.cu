@@ -36,15 +36,18 @@ using namespace fa2;
 // operand layout differs from the K-major one).  Per stage, in order:
 //   A K-major [raw, lo] | A MN-major [raw, lo] (LA == 2) | B K-major [raw, lo] |
 //   B MN-major [raw, lo] (LB == 2), the lo copies present when SPLIT == 3.
-// With KIL (3xTF32 only) the K-major tiles interleave instead: each 32-column
-// chunk of BN raw rows is followed by its BN low-part rows (see mma_chain_kil).
-template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_, bool KIL_ = false>
+// With KILA / KILB (3xTF32 only) the K-major copy of A / B interleaves instead:
+// each 32-column chunk of BN raw rows is followed by its BN low-part rows (see
+// mma_chain_kil).
+template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_, bool KILA_ = false,
+          bool KILB_ = false>
 struct BwdTiles {
   static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, LA = LA_, LB = LB_;
   static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
-  static constexpr bool KIL = KIL_ && SPLIT == 3;
+  static constexpr bool KILA = KILA_ && SPLIT == 3, KILB = KILB_ && SPLIT == 3;
   static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;
-  static constexpr uint32_t KCH = (KIL ? 2u : 1u) * BN * 128u;  // K-major chunk stride
+  // K-major chunk strides of A and B
+  static constexpr uint32_t KCHA = (KILA ? 2u : 1u) * BN * 128u, KCHB = (KILB ? 2u : 1u) * BN * 128u;
   static constexpr uint32_t OFF_A0 = 0, OFF_A1 = NCOPY * TILE;
   static constexpr uint32_t OFF_B0 = LA * NCOPY * TILE, OFF_B1 = OFF_B0 + NCOPY * TILE;
   static constexpr uint32_t STAGE = (LA + LB) * NCOPY * TILE;
@@ -55,9 +58,11 @@ struct BwdTiles {
 // NSB TMEM buffers each for S and dP / dS: with two, S_{j+1} and dP_{j+1} run
 // on the tensor core while the row warps still form dS_j, and dP_{j+1} does
 // not wait for dQ_j to finish reading dS_j.
+// In 3xTF32 mode dP uses the interleaved K-major V tile: its hi/lo partial
+// sums land side by side in the dP / dS buffer's 2*BN columns (mma_chain_kil).
 template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
-struct DqCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1> {
-  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1>;
+struct DqCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1, false, true> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 1, false, true>;
   static constexpr int NSB = NSB_;
   static constexpr uint32_t SB = T_::NCOPY * BN_;  // one dP / dS buffer: hi [| lo]
   static constexpr uint32_t TC_Q = 0, TC_G = T_::NCOPY * D_, TC_DQ = 2 * T_::NCOPY * D_;
@@ -184,7 +189,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       for (int l = 0; l < C::LA; ++l)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_A1 + c * BN * 128 : C::OFF_A0 + c * C::KCH), maps[l],
+          tma_load_4d(st + (l ? C::OFF_A1 + c * BN * 128 : C::OFF_A0 + c * C::KCHA), maps[l],
                       B(bars->full_a[s]), 32 * c, j * BN, h, b);
     }
     last_a[s] = r;
@@ -195,7 +200,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       for (int l = 0; l < C::LB; ++l)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_B1 + c * BN * 128 : C::OFF_B0 + c * C::KCH), maps[2 + l],
+          tma_load_4d(st + (l ? C::OFF_B1 + c * BN * 128 : C::OFF_B0 + c * C::KCHB), maps[2 + l],
                       B(bars->full_b[s]), 32 * c, j * BN, h, b);
     }
     last_b[s] = r;
@@ -209,11 +214,11 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
-// Prepares one landed tile: l = 0 is the K-major copy (interleaved with KIL).
+// Prepares one landed tile: l = 0 is the K-major copy, interleaved when `il`.
 template <class C>
-__device__ __forceinline__ void prep_tile(uint32_t t, int l, uint32_t tid) {
+__device__ __forceinline__ void prep_tile(uint32_t t, int l, bool il, uint32_t tid) {
   if constexpr (C::SPLIT == 3) {
-    if (C::KIL && l == 0)
+    if (il && l == 0)
       split_tile_smem_il<C::TILE, kSplitThreads, (uint32_t)C::BN * 128u>(t, tid);
     else
       split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
@@ -231,13 +236,13 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
     if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LA; ++l) prep_tile<C>(st + (l ? C::OFF_A1 : C::OFF_A0), l, tid);
+    for (int l = 0; l < C::LA; ++l) prep_tile<C>(st + (l ? C::OFF_A1 : C::OFF_A0), l, C::KILA, tid);
     if (!MERGED) {
       fence_proxy_async_smem();
       mbar_arrive(B(bars->ready_a[s]));
     }
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LB; ++l) prep_tile<C>(st + (l ? C::OFF_B1 : C::OFF_B0), l, tid);
+    for (int l = 0; l < C::LB; ++l) prep_tile<C>(st + (l ? C::OFF_B1 : C::OFF_B0), l, C::KILB, tid);
     fence_proxy_async_smem();
     mbar_arrive(B(MERGED ? bars->ready_a[s] : bars->ready_b[s]));
   }
@@ -321,8 +326,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       auto& rv = bars->ready_b;
       auto issue_dP = [&](int j) {
         const uint32_t db = tmem + C::TC_DP + (uint32_t)(j % C::NSB) * C::SB;
-        mma_chain<SPLIT, D, false, BN, C::TILE>(db, tmem + C::TC_G, tmem + C::TC_G + D,
-                                                vd0 + stg(j), idS, false);
+        if constexpr (C::KILB)
+          mma_chain_kil<D, C::KCHB>(db, tmem + C::TC_G, tmem + C::TC_G + D, vd0 + stg(j),
+                                    idesc_tf32(128, 2 * BN, false, false), idS);
+        else
+          mma_chain<SPLIT, D, false, BN, C::TILE>(db, tmem + C::TC_G, tmem + C::TC_G + D,
+                                                  vd0 + stg(j), idS, false);
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full[j % C::NSB]));
       };
@@ -424,6 +433,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW];
         tmem_ldn<CW>(dc + CW * c, t);
+        if constexpr (C::KILB) {  // dP from its two partial sums
+          tmem_ldn<CW>(dc + BN + CW * c, lo);
+#pragma unroll
+          for (int i = 0; i < CW; ++i) t[i] += lo[i];
+        }
 #pragma unroll
         for (int i = 0; i < CW; ++i) {
           const float ds = pv[CW * c + i] * (t[i] - dl);
@@ -460,8 +474,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // hi/lo partial sums land side by side in the buffer's 2*BN columns and the
 // row warps add them (mma_chain_kil).
 template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
-struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true> {
-  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true>;
+struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true>;
   // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
   // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
   // and dS_i, so the rows go from one step to the next without waiting.
@@ -527,8 +541,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
       auto issue_S = [&](int i) {
         const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
-        if constexpr (C::KIL)
-          mma_chain_kil<D, C::KCH>(tmem + C::TC_S + sb, tmem + C::TC_K, tmem + C::TC_K + D,
+        if constexpr (C::KILA)
+          mma_chain_kil<D, C::KCHA>(tmem + C::TC_S + sb, tmem + C::TC_K, tmem + C::TC_K + D,
                                    qd0 + stg(i), idS2, idS);
         else
           mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
@@ -584,8 +598,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       auto issue_dP = [&](int i) {
         const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
-        if constexpr (C::KIL)
-          mma_chain_kil<D, C::KCH>(tmem + C::TC_DP + sb, tmem + C::TC_V, tmem + C::TC_V + D,
+        if constexpr (C::KILB)
+          mma_chain_kil<D, C::KCHB>(tmem + C::TC_DP + sb, tmem + C::TC_V, tmem + C::TC_V + D,
                                    gd0 + stg(i), idS2, idS);
         else
           mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_DP + sb, tmem + C::TC_V,
@@ -666,7 +680,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], lv[CW];
         tmem_ldn<CW>(sc + CW * c, t);
-        if constexpr (C::KIL) {  // S^T = [hi-hi + lo-hi part] + [hi-lo part]
+        if constexpr (C::KILA) {  // S^T = [hi-hi + lo-hi part] + [hi-lo part]
           tmem_ldn<CW>(sc + BN + CW * c, lo);
 #pragma unroll
           for (int x = 0; x < CW; ++x) t[x] += lo[x];
@@ -702,7 +716,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], dv[CW];
         tmem_ldn<CW>(dc + CW * c, t);
-        if constexpr (C::KIL) {  // dP^T from its two partial sums
+        if constexpr (C::KILB) {  // dP^T from its two partial sums
           tmem_ldn<CW>(dc + BN + CW * c, lo);
 #pragma unroll
           for (int x = 0; x < CW; ++x) t[x] += lo[x];

@@ -33,6 +33,11 @@ struct FwdCfg {
   static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, NSB = NSB_;
   static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
   static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;  // one K or V tile
+  // 3xTF32: the K tile interleaves each 32-column chunk of BN raw rows with its
+  // BN low-part rows, so S lands as two partial sums in the S buffer's 2*BN
+  // columns (mma_chain_kil); the row warps add them.
+  static constexpr bool KIL = SPLIT == 3;
+  static constexpr uint32_t KCH = (KIL ? 2u : 1u) * BN * 128u;  // K chunk stride
   static constexpr uint32_t STAGE = 2u * NCOPY * TILE;
   static constexpr uint32_t OFF_K = 0, OFF_V = NCOPY * TILE;  // lo copy at +TILE
   static constexpr uint32_t TC_Q = 0;
@@ -139,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + C::OFF_K + c * BN * 128, &tmK, B(bars->full_k[s]), 32 * c, j * BN, h, b);
+          tma_load_4d(st + C::OFF_K + c * C::KCH, &tmK, B(bars->full_k[s]), 32 * c, j * BN, h, b);
         last_k[s] = r;
         if (r > 0 && !mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status)) break;
         mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ Q.K^T MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      constexpr uint32_t idS2 = idesc_tf32(128, 2 * BN, false, false);  // [hi | lo] rows (KIL)
       const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);  // stage-0 descriptor
       // S_j = Q K_j^T into S buffer j % NSB; before S_j overwrites the buffer
       // of P_{j-NSB}, the P.V issuer must have finished O += P_{j-NSB} V_{j-NSB}
@@ -174,9 +180,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!(ok = mbar_wait(B(bars->ready_k[s]), (j / NS) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
-                                                tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
-                                                idS, false);
+        if constexpr (C::KIL)
+          mma_chain_kil<D, C::KCH>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
+                                   tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4), idS2, idS);
+        else
+          mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + bb * C::SBUF, tmem + C::TC_Q,
+                                                  tmem + C::TC_Q + D, kd0 + (s * C::STAGE >> 4),
+                                                  idS, false);
         umma_commit(B(bars->empty_k[s]));  // also tells the row warps S_j is ready
       }
       umma_commit(B(bars->mma_final));  // nothing of ours in flight after this
@@ -206,19 +216,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (is_prep_warp(warp)) {
     // ---------------------------------------- split / rounding warps
     const uint32_t tid = prep_tid();
-    auto prep = [&](uint32_t t) {
-      if constexpr (SPLIT == 3) split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
-      else round_tile_smem<C::TILE, kSplitThreads>(t, tid);
+    auto prep = [&](uint32_t t, bool is_k) {
+      if constexpr (SPLIT == 3) {
+        if (is_k) split_tile_smem_il<C::TILE, kSplitThreads, (uint32_t)BN * 128u>(t, tid);
+        else split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+      } else {
+        round_tile_smem<C::TILE, kSplitThreads>(t, tid);
+      }
     };
     for (int j = 0; j < n_kv; ++j) {
       const int s = j % NS, r = j / NS;
       const uint32_t st = tiles + s * C::STAGE;
       if (!mbar_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
-      prep(st + C::OFF_K);
+      prep(st + C::OFF_K, true);
       fence_proxy_async_smem();
       mbar_arrive(B(bars->ready_k[s]));
       if (!mbar_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
-      prep(st + C::OFF_V);
+      prep(st + C::OFF_V, false);
       fence_proxy_async_smem();
       mbar_arrive(B(bars->ready_v[s]));
     }
@@ -248,13 +262,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
       // Pass 1: row maximum of the raw scores, 32 columns at a time
       // (scale_log2 > 0, so scaling after the maximum is exact).
+      // With KIL the two partial sums are added here and the masked scores stay
+      // in registers for pass 2.
       float mraw = -INFINITY;
+      [[maybe_unused]] float sv[C::KIL ? BN : 1];
+      if constexpr (C::KIL) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float t[32], t2[32];
+          tmem_ld32(sc + 32 * c, t);
+          tmem_ld32(sc + BN + 32 * c, t2);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] += t2[i];
+          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
+          mraw = fmaxf(mraw, max32(t));
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[32 * c + i] = t[i];
+        }
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32];
-        tmem_ld32(sc + 32 * c, t);
-        if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
-        mraw = fmaxf(mraw, max32(t));
+        for (int c = 0; c < BN / 32; ++c) {
+          float t[32];
+          tmem_ld32(sc + 32 * c, t);
+          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
+          mraw = fmaxf(mraw, max32(t));
+        }
       }
       const float m_new = fmaxf(m_used, mraw * p.scale_log2);
       const bool resc = m_new > m_used + 8.0f;
@@ -279,21 +311,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Pass 2: P = exp2(s * scale_log2 - m), written over S (hi) and next to it (lo).
       const float neg_m = -m_used;
       float ls0 = 0.0f, ls1 = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32], lo[32];
-        tmem_ld32(sc + 32 * c, t);
-        if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
+      if constexpr (C::KIL) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = ex2_approx(fmaf(t[i], p.scale_log2, neg_m));
-          if (i & 1) ls1 += e;
-          else ls0 += e;
-          if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
-          else t[i] = tf32_round_finite(e);
+        for (int c = 0; c < BN / 32; ++c) {
+          float t[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = ex2_approx(fmaf(sv[32 * c + i], p.scale_log2, neg_m));
+            if (i & 1) ls1 += e;
+            else ls0 += e;
+            tf32_split(e, t[i], lo[i]);
+          }
+          tmem_st32(sc + 32 * c, t);
+          tmem_st32(sc + BN + 32 * c, lo);
         }
-        tmem_st32(sc + 32 * c, t);
-        if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, lo);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float t[32], lo[32];
+          tmem_ld32(sc + 32 * c, t);
+          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = ex2_approx(fmaf(t[i], p.scale_log2, neg_m));
+            if (i & 1) ls1 += e;
+            else ls0 += e;
+            if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
+            else t[i] = tf32_round_finite(e);
+          }
+          tmem_st32(sc + 32 * c, t);
+          if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, lo);
+        }
       }
       const float ls = ls0 + ls1;
       l += ls;
