@@ -237,6 +237,23 @@ __device__ __forceinline__ void mma_chain_kil(uint32_t d, uint32_t a_hi, uint32_
   }
 }
 
+// 3xTF32 product D (+)= A x B over K = KDIM with B an MN-major tile of N
+// columns whose low parts follow it at the same chunk stride, i.e. [B_hi | B_lo]
+// is one MN-major operand of 2N columns.  Per k-step, one MMA of N = 2N gives
+// [a_hi*b_hi | a_hi*b_lo] and one of N adds a_lo*b_hi to the first half: the
+// product is the sum of the accumulator's two halves.
+template <int KDIM>
+__device__ __forceinline__ void mma_chain_mn2(uint32_t d, uint32_t a_hi, uint32_t a_lo,
+                                              uint64_t bd, uint32_t id_wide, uint32_t id_narrow,
+                                              bool accumulate) {
+#pragma unroll
+  for (int k = 0; k < KDIM / 8; ++k) {
+    const uint64_t bh = bd + (((uint32_t)k * 1024u) >> 4);
+    umma_tf32_ts(d, a_hi + 8 * k, bh, id_wide, (accumulate || k > 0) ? 1u : 0u);
+    umma_tf32_ts(d, a_lo + 8 * k, bh, id_narrow, 1u);
+  }
+}
+
 // Maps a linear CTA index to (tile, batch*head).  Heads are taken in groups of
 // `group` (the last group may be smaller): all tiles of a group run before the
 // next group, so resident CTAs share a few heads' streamed operands in L2,

@@ -41,8 +41,13 @@ struct FwdCfg {
   static constexpr uint32_t STAGE = 2u * NCOPY * TILE;
   static constexpr uint32_t OFF_K = 0, OFF_V = NCOPY * TILE;  // lo copy at +TILE
   static constexpr uint32_t TC_Q = 0;
+  // 3xTF32 with room in TMEM: O += P V from one N = 2D MMA on [V_hi | V_lo]
+  // and one N = D MMA per k-step (mma_chain_mn2); O then spans 2D columns
+  // whose halves the epilogue adds.
+  static constexpr bool PVM = SPLIT == 3 && NCOPY * D + 2 * D + NSB * NCOPY * BN <= 512;
+  static constexpr uint32_t OW = PVM ? 2 * D : D;  // O accumulator columns
   static constexpr uint32_t TC_O = NCOPY * D;
-  static constexpr uint32_t TC_S = TC_O + D;
+  static constexpr uint32_t TC_S = TC_O + OW;
   static constexpr uint32_t SBUF = NCOPY * BN;
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(TC_S + NSB * SBUF <= TMEM_COLS, "TMEM budget");
@@ -197,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------- P.V MMA issuer
     if (lane == 0) {
       constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      constexpr uint32_t idO2 = idesc_tf32(128, 2 * D, false, true);  // [V_hi | V_lo] (PVM)
       const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
       bool ok = true;
       for (int jj = 0; ok && jj < n_kv; ++jj) {
@@ -205,8 +211,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(B(bars->ready_v[s]), (jj / NS) & 1, ctl, p.status))) break;
         tc_fence_after();
         const uint32_t pA = tmem + C::TC_S + bb * C::SBUF;
-        mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
-                                                vd0 + (s * C::STAGE >> 4), idO, jj > 0);
+        if constexpr (C::PVM)
+          mma_chain_mn2<BN>(tmem + C::TC_O, pA, pA + BN, vd0 + (s * C::STAGE >> 4), idO2, idO,
+                            jj > 0);
+        else
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_O, pA, pA + BN,
+                                                  vd0 + (s * C::STAGE >> 4), idO, jj > 0);
         umma_commit(B(bars->empty_v[s]));  // also: O += P_jj V_jj is done
       }
       umma_commit(B(bars->mma_final_pv));  // nothing of this thread in flight after this
@@ -299,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < (int)C::OW / 32; ++c) {
             float ov[32];
             tmem_ld32(lb + C::TC_O + 32 * c, ov);
 #pragma unroll
@@ -355,7 +365,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float inv_l = 1.0f / l;
         float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;
-        tmem_row_to_global<D>(lb, C::TC_O, inv_l, orow, valid);
+        if constexpr (C::PVM) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float v[32], w[32];
+            tmem_ld32(lb + C::TC_O + 32 * c, v);
+            tmem_ld32(lb + C::TC_O + D + 32 * c, w);
+            if (valid) {
+              float4* d4 = reinterpret_cast<float4*>(orow + 32 * c);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_float4((v[4 * i] + w[4 * i]) * inv_l, (v[4 * i + 1] + w[4 * i + 1]) * inv_l,
+                                    (v[4 * i + 2] + w[4 * i + 2]) * inv_l,
+                                    (v[4 * i + 3] + w[4 * i + 3]) * inv_l);
+            }
+          }
+        } else {
+          tmem_row_to_global<D>(lb, C::TC_O, inv_l, orow, valid);
+        }
         if (valid) p.lse[(int64_t)bh * T + row] = (m_used + log2f(l)) * kLn2;
       }
     }
