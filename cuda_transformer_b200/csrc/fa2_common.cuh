@@ -115,6 +115,23 @@ __device__ __forceinline__ void mask_cols32(float (&t)[32], int kv0, int T, int 
   }
 }
 
+// mask_cols32 and max32 for N (16 or 32) columns.
+template <int N>
+__device__ __forceinline__ void mask_cols(float (&t)[N], int kv0, int T, int causal, int row) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int kv = kv0 + i;
+    if (!(kv < T && (!causal || kv <= row))) t[i] = -INFINITY;
+  }
+}
+template <int N>
+__device__ __forceinline__ float maxn(const float (&t)[N]) {
+  float m = t[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i) m = fmaxf(m, t[i]);
+  return m;
+}
+
 // 32 consecutive floats from 16-byte aligned shared memory (every lane of a
 // warp reads the same address: broadcast).
 __device__ __forceinline__ void load_vec32(const float* src, float (&v)[32]) {

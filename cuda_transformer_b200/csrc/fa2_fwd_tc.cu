@@ -56,6 +56,11 @@ struct FwdCfg {
   static_assert(D % 32 == 0 && BN % 32 == 0, "tile shape");
 };
 
+// Two row warpgroups, warps 4-7 and 11-14 (15 warps); warps 0-3 and 8-10 keep
+// their roles.
+constexpr int kFwdThreads = 480;
+constexpr int kFwdRowWarp1 = 11;
+
 template <int NS>
 struct FwdBars {  // (p_full: one per S/P buffer, at most 3)
   // full_*: TMA landed; ready_*: split or rounded; empty_*: free again.  K and V
@@ -67,6 +72,13 @@ struct FwdBars {  // (p_full: one per S/P buffer, at most 3)
   // barrier cannot run a phase ahead of the row warps, whose P feeds it.
   uint64_t p_full[3], q_ready, mma_final, mma_final_pv;
   CtaCtl ctl;
+  // The two row warps of a TMEM lane quarter (one per row group) exchange each
+  // row's partial maximum (two slots, alternating by step) and, at the end,
+  // its partial sum; xchg / xfin (64 arrivals) tell each warp that its
+  // partner's value is in place (bounded waits, unlike a named barrier).
+  uint64_t xchg[4][2], xfin[4];
+  float xmax[2][2][kRows];
+  float xsum[2][kRows];
 };
 
 struct FwdParams {
@@ -81,12 +93,13 @@ struct FwdParams {
 
 template <class C>
 constexpr size_t fwd_smem_bytes() {
-  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
-  return 1024 + 1024 + (size_t)C::NS * C::STAGE;
+  constexpr size_t head = (sizeof(FwdBars<C::NS>) + 1023) / 1024 * 1024 + 1024;
+  static_assert(head + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
+  return head + (size_t)C::NS * C::STAGE;
 }
 
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fa2_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
@@ -118,9 +131,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(B(bars->empty_v[s]), 1);
     }
     for (int i = 0; i < 3; ++i) {
-      mbar_init(B(bars->p_full[i]), 128);
+      mbar_init(B(bars->p_full[i]), 256);
     }
     mbar_init(B(bars->q_ready), 128);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(B(bars->xchg[i][0]), 64);
+      mbar_init(B(bars->xchg[i][1]), 64);
+      mbar_init(B(bars->xfin[i]), 64);
+    }
     mbar_init(B(bars->mma_final), 1);
     mbar_init(B(bars->mma_final_pv), 1);
     ctl->abort = 0;
@@ -248,12 +266,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------------------------------------- row warps
+    // Warps 4-7 (group 0) and 11-14 (group 1): thread (quad, lane) owns query
+    // row quad*32 + lane (TMEM lane quarter quad); group g takes the score
+    // columns [g*BN/2, (g+1)*BN/2) of every step.  The pair of warps sharing a
+    // quarter exchange partial row maxima through shared memory, so both apply
+    // the same maximum; each keeps its partial row sum and rescales / writes
+    // its half of the O columns.  Group 0 loads Q.
+    constexpr int HB = BN / 2, CW = HB < 32 ? HB : 32;
+    constexpr int OH = (int)C::OW / 2, OCW = OH < 32 ? OH : 32;  // O columns rescaled per group
     const int quad = warp & 3;
+    const int grp = warp >= kFwdRowWarp1 ? 1 : 0;
+    const int c0 = grp * HB;
     const int r = quad * 32 + lane;
     const int row = q0 + r;
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    {
+    if (grp == 0) {
       const float* qrow = p.q.row(b, h, valid ? row : 0);
       const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
       row_to_tmem<D, SPLIT>(p.q, qrow, valid, vec, lb, C::TC_Q);
@@ -267,37 +295,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bb = j % C::NSB;
       if (!(ok = warp_wait(B(bars->empty_k[j % NS]), (j / NS) & 1, ctl, p.status))) break;
       tc_fence_after();
-      const uint32_t sc = lb + C::TC_S + bb * C::SBUF;
-      const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > q0);
-      // Pass 1: row maximum of the raw scores, 32 columns at a time
-      // (scale_log2 > 0, so scaling after the maximum is exact).
-      // With KIL the two partial sums are added here and the masked scores stay
-      // in registers for pass 2.
+      const uint32_t sc = lb + C::TC_S + bb * C::SBUF + c0;
+      const int kv0 = j * BN + c0;
+      const bool need_mask = (kv0 + HB > T) || (p.causal && kv0 + HB - 1 > q0);
+      // This group's masked scores (with KIL the sum of the two partial sums),
+      // kept in registers for the exponentials, and their maximum.
+      float sv[HB];
       float mraw = -INFINITY;
-      [[maybe_unused]] float sv[C::KIL ? BN : 1];
-      if constexpr (C::KIL) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          float t[32], t2[32];
-          tmem_ld32(sc + 32 * c, t);
-          tmem_ld32(sc + BN + 32 * c, t2);
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW];
+        tmem_ldn<CW>(sc + CW * c, t);
+        if constexpr (C::KIL) {
+          float t2[CW];
+          tmem_ldn<CW>(sc + BN + CW * c, t2);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] += t2[i];
-          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
-          mraw = fmaxf(mraw, max32(t));
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[32 * c + i] = t[i];
+          for (int i = 0; i < CW; ++i) t[i] += t2[i];
         }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float t[32];
-          tmem_ld32(sc + 32 * c, t);
-          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
-          mraw = fmaxf(mraw, max32(t));
-        }
+        if (need_mask) mask_cols<CW>(t, kv0 + CW * c, T, p.causal, row);
+        mraw = fmaxf(mraw, maxn<CW>(t));
+#pragma unroll
+        for (int i = 0; i < CW; ++i) sv[CW * c + i] = t[i];
       }
+      bars->xmax[j & 1][grp][r] = mraw;
+      mbar_arrive(B(bars->xchg[quad][j & 1]));
+      if (!(ok = warp_wait(B(bars->xchg[quad][j & 1]), (j >> 1) & 1, ctl, p.status))) break;
+      mraw = fmaxf(mraw, bars->xmax[j & 1][grp ^ 1][r]);
+      // scale_log2 > 0, so scaling after the maximum is exact
       const float m_new = fmaxf(m_used, mraw * p.scale_log2);
       const bool resc = m_new > m_used + 8.0f;
       if (__any_sync(0xffffffffu, resc)) {
@@ -309,81 +333,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < (int)C::OW / 32; ++c) {
-            float ov[32];
-            tmem_ld32(lb + C::TC_O + 32 * c, ov);
+          for (int c = 0; c < OH / OCW; ++c) {
+            float ov[OCW];
+            tmem_ldn<OCW>(lb + C::TC_O + grp * OH + OCW * c, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(lb + C::TC_O + 32 * c, ov);
+            for (int i = 0; i < OCW; ++i) ov[i] *= alpha;
+            tmem_stn<OCW>(lb + C::TC_O + grp * OH + OCW * c, ov);
           }
         }
       }
-      // Pass 2: P = exp2(s * scale_log2 - m), written over S (hi) and next to it (lo).
+      // P = exp2(s * scale_log2 - m), written over S (hi) and next to it (lo).
       const float neg_m = -m_used;
       float ls0 = 0.0f, ls1 = 0.0f;
-      if constexpr (C::KIL) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          float t[32], lo[32];
+      for (int c = 0; c < HB / CW; ++c) {
+        float t[CW], lo[CW];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = ex2_approx(fmaf(sv[32 * c + i], p.scale_log2, neg_m));
-            if (i & 1) ls1 += e;
-            else ls0 += e;
-            tf32_split(e, t[i], lo[i]);
-          }
-          tmem_st32(sc + 32 * c, t);
-          tmem_st32(sc + BN + 32 * c, lo);
+        for (int i = 0; i < CW; ++i) {
+          const float e = ex2_approx(fmaf(sv[CW * c + i], p.scale_log2, neg_m));
+          if (i & 1) ls1 += e;
+          else ls0 += e;
+          if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
+          else t[i] = tf32_round_finite(e);
         }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float t[32], lo[32];
-          tmem_ld32(sc + 32 * c, t);
-          if (need_mask) mask_cols32(t, kv0 + 32 * c, T, p.causal, row);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = ex2_approx(fmaf(t[i], p.scale_log2, neg_m));
-            if (i & 1) ls1 += e;
-            else ls0 += e;
-            if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
-            else t[i] = tf32_round_finite(e);
-          }
-          tmem_st32(sc + 32 * c, t);
-          if constexpr (SPLIT == 3) tmem_st32(sc + BN + 32 * c, lo);
-        }
+        tmem_stn<CW>(sc + CW * c, t);
+        if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);
       }
-      const float ls = ls0 + ls1;
-      l += ls;
+      l += ls0 + ls1;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(B(bars->p_full[bb]));
     }
     if (ok) {
       const int jj = n_kv - 1;
-      if (warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status)) {
+      const bool done = warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status);
+      bars->xsum[grp][r] = l;
+      mbar_arrive(B(bars->xfin[quad]));
+      if (warp_wait(B(bars->xfin[quad]), 0, ctl, p.status) && done) {
         tc_fence_after();
-        const float inv_l = 1.0f / l;
-        float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;
+        const float lt = l + bars->xsum[grp ^ 1][r];
+        const float inv_l = 1.0f / lt;
+        constexpr int DH = D / 2;  // output columns written per group
+        float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * DH;
         if constexpr (C::PVM) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float v[32], w[32];
-            tmem_ld32(lb + C::TC_O + 32 * c, v);
-            tmem_ld32(lb + C::TC_O + D + 32 * c, w);
+          for (int c = 0; c < DH / 16; ++c) {
+            float v[16], w[16];
+            tmem_ld16(lb + C::TC_O + grp * DH + 16 * c, v);
+            tmem_ld16(lb + C::TC_O + D + grp * DH + 16 * c, w);
             if (valid) {
-              float4* d4 = reinterpret_cast<float4*>(orow + 32 * c);
+              float4* d4 = reinterpret_cast<float4*>(orow + 16 * c);
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
+              for (int i = 0; i < 4; ++i)
                 d4[i] = make_float4((v[4 * i] + w[4 * i]) * inv_l, (v[4 * i + 1] + w[4 * i + 1]) * inv_l,
                                     (v[4 * i + 2] + w[4 * i + 2]) * inv_l,
                                     (v[4 * i + 3] + w[4 * i + 3]) * inv_l);
             }
           }
         } else {
-          tmem_row_to_global<D>(lb, C::TC_O, inv_l, orow, valid);
+          tmem_cols_to_global<DH>(lb, C::TC_O + grp * DH, inv_l, orow, valid);
         }
-        if (valid) p.lse[(int64_t)bh * T + row] = (m_used + log2f(l)) * kLn2;
+        if (valid && grp == 0) p.lse[(int64_t)bh * T + row] = (m_used + log2f(lt)) * kLn2;
       }
     }
   }
@@ -421,7 +431,7 @@ int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, 
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
   p.status = dev.status;
   const int64_t grid = (int64_t)p.n_qt * p.bh_total;
-  fa2_fwd_tc_kernel<C><<<(unsigned)grid, kThreads, smem, st>>>(tmK, tmV, p);
+  fa2_fwd_tc_kernel<C><<<(unsigned)grid, kFwdThreads, smem, st>>>(tmK, tmV, p);
   return check_launch();
 }
 
