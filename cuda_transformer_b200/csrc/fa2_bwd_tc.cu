@@ -79,7 +79,8 @@ struct BwdBars {
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
   // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
   uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2], s_free[2];
-  uint64_t rows_ready, done, mma_final, mma_final2;
+  uint64_t dqd[2];  // dQ pass, two buffers: dQ_j has read dS_j from buffer j % 2
+  uint64_t rows_ready, done, mma_final, mma_final2, mma_final3;
   CtaCtl ctl;
 };
 
@@ -132,6 +133,9 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
   mbar_init(B(bars->done), done_count);
   mbar_init(B(bars->mma_final), 1);
   mbar_init(B(bars->mma_final2), 1);
+  mbar_init(B(bars->mma_final3), 1);
+  mbar_init(B(bars->dqd[0]), 1);
+  mbar_init(B(bars->dqd[1]), 1);
   bars->ctl.abort = 0;
   fence_barrier_init();
 }
@@ -248,10 +252,12 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
-// Both backward kernels run two row warpgroups, warps 4-7 and 11-14 (15 warps):
-// warps 0-3 and 8-10 keep the forward's roles.
-constexpr int kBwdThreads = 480;
+// Both backward kernels run two row warpgroups, warps 4-7 and 11-14, and a
+// third MMA issuer, warp 15 (dQ pass with two dP buffers; idle otherwise):
+// 16 warps, warps 0-3 and 8-10 keep the forward's roles.
+constexpr int kBwdThreads = 512;
 constexpr int kBwdRowWarp1 = 11;
+constexpr int kIssuer3Warp = 15;
 
 template <class C>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -314,10 +320,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_drain(B(bars->mma_final), 0);
     }
     __syncwarp();
-  } else if (warp == kIssuer2Warp) {
-    // dP_j = dO V_j^T into dP buffer j % NSB, and dQ += dS_j K_j.
-    // dP_{j+NSB} overwrites dS_j only after dQ_j in this thread's issue order.
-    if (lane == 0) {
+  } else if (warp == kIssuer2Warp || warp == kIssuer3Warp) {
+    // Warp 10 issues dQ += dS_j K_j.  With one dP buffer it also issues
+    // dP_j = dO V_j^T, and dP_{j+1} overwrites dS_j only after dQ_j in its issue
+    // order.  With two buffers warp 15 issues dP_j into buffer j % 2 once dQ_{j-2}
+    // has finished reading dS_{j-2} from it (dqd), so dQ and dP do not queue
+    // behind each other on one issuing thread.
+    const bool dq_here = warp == kIssuer2Warp;
+    const bool dp_here = C::NSB == 1 ? dq_here : warp == kIssuer3Warp;
+    if (lane == 0 && (dq_here || dp_here)) {
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idQ = idesc_tf32(128, D, false, true);
       const uint64_t kmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);  // stage-0 descriptors
@@ -335,36 +346,51 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full[j % C::NSB]));
       };
-      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
-                mbar_wait(B(rv[0]), 0, ctl, p.status);
-      if (ok) {
-        tc_fence_after();
-        issue_dP(0);
-        if (C::NSB == 2 && n_kv > 1) {
-          ok = mbar_wait(B(rv[1 % NS]), (1 / NS) & 1, ctl, p.status);
-          if (ok) {
-            tc_fence_after();
-            issue_dP(1);
-          }
+      auto issue_dQ = [&](int j) {
+        const uint32_t db = tmem + C::TC_DP + (uint32_t)(j % C::NSB) * C::SB;
+        mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, db, db + BN, kmd0 + stg(j), idQ,
+                                                j > 0);
+        umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
+      };
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      if (ok && dq_here && dp_here) {  // one buffer: dP and dQ interleaved
+        if ((ok = mbar_wait(B(rv[0]), 0, ctl, p.status))) {
+          tc_fence_after();
+          issue_dP(0);
         }
         for (int j = 0; ok && j < n_kv; ++j) {
-          const int bj = j % C::NSB, nx = j + C::NSB;
-          if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j / C::NSB) & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
           tc_fence_after();
-          const uint32_t db = tmem + C::TC_DP + (uint32_t)bj * C::SB;
-          mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, db, db + BN, kmd0 + stg(j), idQ,
-                                                  j > 0);
-          umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
-          if (nx < n_kv) {
-            if (!(ok = mbar_wait(B(rv[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
+          issue_dQ(j);
+          if (j + 1 < n_kv) {
+            if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
-            issue_dP(nx);
+            issue_dP(j + 1);
           }
         }
         if (ok) umma_commit(B(bars->done));
+      } else if (ok && dq_here) {  // two buffers, warp 10: dQ only
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int bj = j % C::NSB;
+          if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j / C::NSB) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          issue_dQ(j);
+          umma_commit(B(bars->dqd[bj]));
+        }
+        if (ok) umma_commit(B(bars->done));
+      } else if (ok) {  // two buffers, warp 15: dP only
+        for (int j = 0; ok && j < n_kv; ++j) {
+          if (j >= C::NSB && !(ok = mbar_wait(B(bars->dqd[j % C::NSB]),
+                                              ((j - C::NSB) / C::NSB) & 1, ctl, p.status)))
+            break;
+          if (!(ok = mbar_wait(B(rv[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          issue_dP(j);
+        }
       }
-      umma_commit(B(bars->mma_final2));
-      mbar_drain(B(bars->mma_final2), 0);
+      const uint32_t fin = B(dq_here ? bars->mma_final2 : bars->mma_final3);
+      umma_commit(fin);  // nothing of this thread in flight after this
+      mbar_drain(fin, 0);
     }
     __syncwarp();
   } else if (is_prep_warp(warp)) {
@@ -638,6 +664,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
+  } else if (warp == kIssuer3Warp) {
+    // unused in this pass
   } else if (is_prep_warp(warp)) {
     bwd_splitter<C, true>(bars, tiles, n, p.status);
   } else {
