@@ -77,6 +77,7 @@ struct BwdBars {
   // longer read by the tensor core.  With MERGED stages (dK/dV pass) only the
   // _a barriers are used and cover both tiles.
   uint64_t full_a[NS], full_b[NS], ready_a[NS], ready_b[NS], empty_a[NS], empty_b[NS];
+  uint64_t vec_full[NS];  // dK/dV pass: the step's LSE and delta are in shared memory
   // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
   uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2], s_free[2];
   uint64_t dqd[2];  // dQ pass, two buffers: dQ_j has read dS_j from buffer j % 2
@@ -121,6 +122,7 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
     mbar_init(B(bars->ready_b[s]), kSplitThreads);
     mbar_init(B(bars->empty_a[s]), empty_count);
     mbar_init(B(bars->empty_b[s]), 1);
+    mbar_init(B(bars->vec_full[s]), 1);
   }
   for (int i = 0; i < 2; ++i) {
     mbar_init(B(bars->s_full[i]), 1);
@@ -177,6 +179,25 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
     const int i = j - j0, s = i % NS, r = i / NS;
     const uint32_t st = tiles + s * C::STAGE;
     if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
+    // The tile copies go first: the vector values are needed only by the row
+    // warps, much later, and signal their own barrier.
+    if (lane == 0) {
+      const uint32_t fa = B(bars->full_a[s]);
+      mbar_arrive_expect_tx(fa, C::LA * C::TILE);
+      tma_load_tile<!C::KILA, D>(st + C::OFF_A0, maps[0], fa, j * BN, h, b, C::KCHA);
+      if constexpr (C::LA > 1)
+        tma_load_tile<true, D>(st + C::OFF_A1, maps[1], fa, j * BN, h, b, BN * 128u);
+    }
+    last_a[s] = r;
+    if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
+    if (lane == 0) {
+      const uint32_t fb = B(bars->full_b[s]);
+      mbar_arrive_expect_tx(fb, C::LB * C::TILE);
+      tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[2], fb, j * BN, h, b, C::KCHB);
+      if constexpr (C::LB > 1)
+        tma_load_tile<true, D>(st + C::OFF_B1, maps[3], fb, j * BN, h, b, BN * 128u);
+    }
+    last_b[s] = r;
     if constexpr (VEC) {
       float* vs = vec + s * 2 * BN;
 #pragma unroll
@@ -185,29 +206,9 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
         vs[BN + 32 * u + lane] = vd[u];
       }
       __syncwarp();
+      if (lane == 0) mbar_arrive(B(bars->vec_full[s]));
       load_vec(j + 1);
     }
-    if (lane == 0) {
-      mbar_arrive_expect_tx(B(bars->full_a[s]), C::LA * C::TILE);
-#pragma unroll
-      for (int l = 0; l < C::LA; ++l)
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_A1 + c * BN * 128 : C::OFF_A0 + c * C::KCHA), maps[l],
-                      B(bars->full_a[s]), 32 * c, j * BN, h, b);
-    }
-    last_a[s] = r;
-    if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(B(bars->full_b[s]), C::LB * C::TILE);
-#pragma unroll
-      for (int l = 0; l < C::LB; ++l)
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + (l ? C::OFF_B1 + c * BN * 128 : C::OFF_B0 + c * C::KCHB), maps[2 + l],
-                      B(bars->full_b[s]), 32 * c, j * BN, h, b);
-    }
-    last_b[s] = r;
   }
   __syncwarp();
   if (ctl->abort && lane == 0) {
@@ -698,7 +699,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t sc = lb + C::TC_S + (uint32_t)bi * C::SB + c0;
       const uint32_t dc = lb + C::TC_DP + (uint32_t)bi * C::SB + c0;
       // the step's log-sum-exp * log2(e) and delta, staged by the producer warp
-      if (!(ok = warp_wait(B(bars->full_a[i % NS]), (i / NS) & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->vec_full[i % NS]), (i / NS) & 1, ctl, p.status))) break;
       const float* vl = vec + (i % NS) * 2 * BN + c0;
       if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
@@ -814,9 +815,12 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
            cudaStream_t st) {
   static unsigned long long attr_done = 0;
   CUtensorMap tk, tkmn, tv;
-  int rc = make_tmap_bhtd(&tk, k, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd(&tkmn, k, pr, C::BN, /*mn_major=*/true);
-  if (rc == CT_OK) rc = make_tmap_bhtd(&tv, v, pr, C::BN);
+  // K-major copies of interleaved (KIL) tiles load chunk by chunk, every other
+  // tile in one copy
+  int rc = C::KILA ? make_tmap_bhtd(&tk, k, pr, C::BN) : make_tmap_bhtd_whole(&tk, k, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tkmn, k, pr, C::BN, /*mn_major=*/true);
+  if (rc == CT_OK)
+    rc = C::KILB ? make_tmap_bhtd(&tv, v, pr, C::BN) : make_tmap_bhtd_whole(&tv, v, pr, C::BN);
   if (rc != CT_OK) return rc;
   const size_t smem = bwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_bwd_dq_tc_kernel<C>, smem, dev.device, &attr_done);
@@ -833,10 +837,11 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
              const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
   CUtensorMap tq, tqmn, tg, tgmn;
-  int rc = make_tmap_bhtd(&tq, q, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd(&tqmn, q, pr, C::BN, /*mn_major=*/true);
-  if (rc == CT_OK) rc = make_tmap_bhtd(&tg, g, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd(&tgmn, g, pr, C::BN, /*mn_major=*/true);
+  int rc = C::KILA ? make_tmap_bhtd(&tq, q, pr, C::BN) : make_tmap_bhtd_whole(&tq, q, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tqmn, q, pr, C::BN, /*mn_major=*/true);
+  if (rc == CT_OK)
+    rc = C::KILB ? make_tmap_bhtd(&tg, g, pr, C::BN) : make_tmap_bhtd_whole(&tg, g, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tgmn, g, pr, C::BN, /*mn_major=*/true);
   if (rc != CT_OK) return rc;
   const size_t smem = bwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_bwd_dkdv_tc_kernel<C>, smem, dev.device, &attr_done);

@@ -289,6 +289,20 @@ __device__ __forceinline__ void cta_tile(int n_tiles, int bh_total, int group,
   tile = heavy_first_desc ? n_tiles - 1 - t : t;
 }
 
+// Loads tile row block `r0` of head (h, b) into `dst`: one copy through a
+// whole-tile map (WHOLE), else one copy per 32-column chunk at chunk stride
+// `chunk` bytes (interleaved hi/lo layouts leave room between the chunks).
+template <bool WHOLE, int D>
+__device__ __forceinline__ void tma_load_tile(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                              int r0, int h, int b, uint32_t chunk) {
+  if constexpr (WHOLE) {
+    tma_load_5d(dst, map, bar, 0, r0, 0, h, b);
+  } else {
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) tma_load_4d(dst + c * chunk, map, bar, 32 * c, r0, h, b);
+  }
+}
+
 // Drain-wait used on teardown: ignores the CTA abort flag, bounded by time.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
@@ -318,6 +332,21 @@ inline int make_tmap_bhtd(CUtensorMap* map, const Strided4& t, const Fa2Problem&
   const uint64_t strides[3] = {(uint64_t)t.s[2] * 4u, (uint64_t)t.s[1] * 4u, (uint64_t)t.s[0] * 4u};
   const uint32_t box[4] = {32u, (uint32_t)rows, 1u, 1u};
   return make_tmap_f32(map, t.ptr, 4, dims, strides, box, mn_major);
+}
+
+// Host helper: TMA map that loads a whole `rows` x D tile of an FP32 [B,H,T,D]
+// tensor (unit head-dim stride) with one copy: dims {32, T, D/32, H, B}, the
+// third dimension stepping 128 bytes to the next 32-column chunk.  The box
+// lands as D/32 chunks of `rows` 128-byte rows each -- the same shared-memory
+// tile as D/32 copies of make_tmap_bhtd's box.
+inline int make_tmap_bhtd_whole(CUtensorMap* map, const Strided4& t, const Fa2Problem& p,
+                                int rows, bool mn_major = false) {
+  const uint64_t dims[5] = {32u, (uint64_t)p.T, (uint64_t)(p.D / 32), (uint64_t)p.H,
+                            (uint64_t)p.B};
+  const uint64_t strides[4] = {(uint64_t)t.s[2] * 4u, 128u, (uint64_t)t.s[1] * 4u,
+                               (uint64_t)t.s[0] * 4u};
+  const uint32_t box[5] = {32u, (uint32_t)rows, (uint32_t)(p.D / 32), 1u, 1u};
+  return make_tmap_f32(map, t.ptr, 5, dims, strides, box, mn_major);
 }
 
 // Number of (b,h) heads interleaved per CTA-order group (see fa2::cta_tile).

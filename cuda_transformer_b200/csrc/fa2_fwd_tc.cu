@@ -165,15 +165,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t st = tiles + s * C::STAGE;
         if (r > 0 && !mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status)) break;
         mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + C::OFF_K + c * C::KCH, &tmK, B(bars->full_k[s]), 32 * c, j * BN, h, b);
+        tma_load_tile<!C::KIL, D>(st + C::OFF_K, &tmK, B(bars->full_k[s]), j * BN, h, b, C::KCH);
         last_k[s] = r;
         if (r > 0 && !mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status)) break;
         mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c)
-          tma_load_4d(st + C::OFF_V + c * BN * 128, &tmV, B(bars->full_v[s]), 32 * c, j * BN, h, b);
+        tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_v[s]), j * BN, h, b, BN * 128u);
         last_v[s] = r;
       }
       if (ctl->abort) {  // let every issued copy land before the CTA exits
@@ -411,9 +407,9 @@ int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, 
             const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
   CUtensorMap tmK, tmV;
-  int rc = make_tmap_bhtd(&tmK, k, pr, C::BN);
+  int rc = C::KIL ? make_tmap_bhtd(&tmK, k, pr, C::BN) : make_tmap_bhtd_whole(&tmK, k, pr, C::BN);
   if (rc != CT_OK) return rc;
-  rc = make_tmap_bhtd(&tmV, v, pr, C::BN, /*mn_major=*/true);
+  rc = make_tmap_bhtd_whole(&tmV, v, pr, C::BN, /*mn_major=*/true);
   if (rc != CT_OK) return rc;
   const size_t smem = fwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_fwd_tc_kernel<C>, smem, dev.device, &attr_done);
