@@ -422,11 +422,11 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
   return launch_diag_umma(mode, a, b, d, n, *dev, as_stream(stream));
 }
 
-int ct_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles, void* stream) {
+int ct_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles, void* stream) {
   int err = CT_OK;
   const DeviceInfo* dev = current_device(&err);
   if (err != CT_OK) return err;
-  return launch_diag_mma_rate(n, a_tmem, reps, blocks, cycles, *dev, as_stream(stream));
+  return launch_diag_mma_rate(n, flags, reps, blocks, cycles, *dev, as_stream(stream));
 }
 
 }  // extern "C"

@@ -115,7 +115,7 @@ int launch_layernorm_bwd(const float* x, const float* g, const float* mean, cons
 // -------------------------------------------------------------- diagnostics
 int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
                      const DeviceInfo& dev, cudaStream_t st);
-int launch_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles,
+int launch_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles,
                          const DeviceInfo& dev, cudaStream_t st);
 
 }  // namespace ct

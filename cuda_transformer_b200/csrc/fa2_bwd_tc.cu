@@ -183,19 +183,16 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
     // warps, much later, and signal their own barrier.
     if (lane == 0) {
       const uint32_t fa = B(bars->full_a[s]);
-      mbar_arrive_expect_tx(fa, C::LA * C::TILE);
+      // only the K-major copy: the preparation warps write the MN-major one
+      mbar_arrive_expect_tx(fa, C::TILE);
       tma_load_tile<!C::KILA, D>(st + C::OFF_A0, maps[0], fa, j * BN, h, b, C::KCHA);
-      if constexpr (C::LA > 1)
-        tma_load_tile<true, D>(st + C::OFF_A1, maps[1], fa, j * BN, h, b, BN * 128u);
     }
     last_a[s] = r;
     if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
     if (lane == 0) {
       const uint32_t fb = B(bars->full_b[s]);
-      mbar_arrive_expect_tx(fb, C::LB * C::TILE);
+      mbar_arrive_expect_tx(fb, C::TILE);
       tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[2], fb, j * BN, h, b, C::KCHB);
-      if constexpr (C::LB > 1)
-        tma_load_tile<true, D>(st + C::OFF_B1, maps[3], fb, j * BN, h, b, BN * 128u);
     }
     last_b[s] = r;
     if constexpr (VEC) {
@@ -219,19 +216,33 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   }
 }
 
-// Prepares one landed tile: l = 0 is the K-major copy, interleaved when `il`.
+// Prepares tile A (is_b false) or B of a stage: its K-major copy in place and,
+// for a tile the tensor core also reads MN-major (LA / LB == 2), the MN-major
+// copy derived from it (derive_tile_smem), so TMA loads each tile once.
 template <class C>
-__device__ __forceinline__ void prep_tile(uint32_t t, int l, bool il, uint32_t tid) {
-  if constexpr (C::SPLIT == 3) {
-    if (il && l == 0)
-      split_tile_smem_il<C::TILE, kSplitThreads, (uint32_t)C::BN * 128u>(t, tid);
+__device__ __forceinline__ void prep_tile(uint32_t st, bool is_b, uint32_t tid) {
+  const uint32_t k = st + (is_b ? C::OFF_B0 : C::OFF_A0);
+  const uint32_t mn = st + (is_b ? C::OFF_B1 : C::OFF_A1);
+  const bool il = is_b ? C::KILB : C::KILA;
+  const bool two = (is_b ? C::LB : C::LA) > 1;
+  constexpr uint32_t CH = (uint32_t)C::BN * 128u;
+  if (two) {
+    if (il)
+      derive_tile_smem<C::SPLIT, C::TILE, kSplitThreads, C::BN, 2u * CH, CH, C::TILE>(k, mn, tid);
     else
-      split_tile_smem<C::TILE, kSplitThreads>(t, t + C::TILE, tid);
+      derive_tile_smem<C::SPLIT, C::TILE, kSplitThreads, C::BN, CH, C::TILE, C::TILE>(k, mn, tid);
+  } else if constexpr (C::SPLIT == 3) {
+    if (il) split_tile_smem_il<C::TILE, kSplitThreads, CH>(k, tid);
+    else split_tile_smem<C::TILE, kSplitThreads>(k, k + C::TILE, tid);
   } else {
-    round_tile_smem<C::TILE, kSplitThreads>(t, tid);
+    round_tile_smem<C::TILE, kSplitThreads>(k, tid);
   }
 }
 
+// Per stage: tile A prepared -> ready_a, tile B prepared -> ready_b.  In the
+// dK/dV pass (MERGED) the issuers wait on ready_a for the K-major copies of
+// both tiles (S^T, dP^T) and on ready_b for the MN-major ones (dV, dK); both
+// complete once the two tiles are prepared.
 template <class C, bool MERGED>
 __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
                                              uint32_t* status) {
@@ -241,15 +252,16 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
     if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LA; ++l) prep_tile<C>(st + (l ? C::OFF_A1 : C::OFF_A0), l, C::KILA, tid);
+    prep_tile<C>(st, false, tid);
     if (!MERGED) {
       fence_proxy_async_smem();
       mbar_arrive(B(bars->ready_a[s]));
     }
     if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
-    for (int l = 0; l < C::LB; ++l) prep_tile<C>(st + (l ? C::OFF_B1 : C::OFF_B0), l, C::KILB, tid);
+    prep_tile<C>(st, true, tid);
     fence_proxy_async_smem();
-    mbar_arrive(B(MERGED ? bars->ready_a[s] : bars->ready_b[s]));
+    if (MERGED) mbar_arrive(B(bars->ready_a[s]));
+    mbar_arrive(B(bars->ready_b[s]));
   }
 }
 
@@ -550,7 +562,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
-  auto& rdy = bars->ready_a;  // merged stages: Q_i and dO_i both prepared
+  auto& rdy = bars->ready_a;     // K-major copies of Q_i and dO_i prepared
+  auto& rdy_mn = bars->ready_b;  // MN-major copies prepared
   constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
   constexpr uint32_t idS2 = idesc_tf32(128, 2 * BN, false, false);  // [hi | lo] rows (KIL)
   constexpr uint32_t idO = idesc_tf32(128, D, false, true);
@@ -598,6 +611,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (C::NSB == 1 && nx < n &&
               !(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status)))
             break;
+          // dO_i's MN-major copy (prepared right after the K-major ones)
+          if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
           const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
@@ -648,6 +663,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int i = 0; ok && i < n; ++i) {
           const int bi = i % C::NSB, nx = i + C::NSB;
           if (!(ok = mbar_wait(B(bars->ds_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
           const uint32_t db = tmem + C::TC_DP + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i

@@ -459,6 +459,52 @@ __device__ __forceinline__ void split_tile_smem_il(uint32_t base, uint32_t tid) 
   }
 }
 
+// Prepares a K-major tile landed by TMA -- per 32-column chunk (stride KCH)
+// BN rows of 128 bytes in the 128-byte swizzle (16-byte unit u of row r at
+// u ^ (r % 8)) -- and writes the same data as an MN-major tile at `mn` (chunk
+// stride BN*128, 32-byte-atom swizzle: 32-byte unit a of row r at a ^ (r % 4)).
+// SPLIT == 1 rounds both copies to the nearest TF32 (in place for the K-major
+// one); SPLIT == 3 keeps the raw values and writes the low parts x - trunc(x)
+// at +KLO (K-major) and +MLO (MN-major).  Each word moves within its row, so a
+// warp's stores stay free of bank conflicts.
+template <int SPLIT, uint32_t BYTES, uint32_t NTHREADS, uint32_t BN, uint32_t KCH, uint32_t KLO,
+          uint32_t MLO>
+__device__ __forceinline__ void derive_tile_smem(uint32_t k, uint32_t mn, uint32_t tid) {
+  using P = TilePrep<BYTES, NTHREADS>;
+  constexpr uint32_t CH = BN * 128u;
+  static_assert((CH & (CH - 1)) == 0, "chunk size");
+#pragma unroll 1
+  for (uint32_t w0 = 0; w0 < P::PER; w0 += P::U) {
+    float4 x[P::U];
+    uint32_t ka[P::U], ma[P::U];
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u) {
+      const uint32_t o = (tid + (w0 + u) * NTHREADS) * 16u;
+      const uint32_t c = o / CH, rem = o % CH, r = rem >> 7, pu = (rem >> 4) & 7u;
+      const uint32_t lu = pu ^ (r & 7u);                                // logical 16-byte unit
+      const uint32_t mu = ((((lu >> 1) ^ (r & 3u)) << 1) | (lu & 1u));  // its MN-major place
+      ka[u] = k + c * KCH + rem;
+      ma[u] = mn + c * CH + (r << 7) + (mu << 4);
+      x[u] = lds128(ka[u]);
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < P::U; ++u) {
+      if constexpr (SPLIT == 3) {
+        const float4 lo = make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
+                                      x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w));
+        sts128(ka[u] + KLO, lo);
+        sts128(ma[u], x[u]);
+        sts128(ma[u] + MLO, lo);
+      } else {
+        const float4 y = make_float4(tf32_round_finite(x[u].x), tf32_round_finite(x[u].y),
+                                     tf32_round_finite(x[u].z), tf32_round_finite(x[u].w));
+        sts128(ka[u], y);
+        sts128(ma[u], y);
+      }
+    }
+  }
+}
+
 // TF32 mode: rounds a shared-memory tile in place to the nearest TF32 value
 // (the tensor core itself truncates the 13 low mantissa bits).  The rounding
 // is the two-integer-operation form of cvt.rna.tf32.f32 (tf32_round_finite),

@@ -12,7 +12,7 @@ namespace ct {
 namespace {
 
 struct DiagSmem {
-  uint64_t bar;
+  uint64_t bar, bar2;
   CtaCtl ctl;
 };
 
@@ -115,9 +115,12 @@ __global__ void __launch_bounds__(128, 1)
 // operands (A in TMEM when TS, else shared memory; B K-major in shared
 // memory) and records the clock64 span from the first issue to the commit's
 // completion in cycles[blockIdx.x].
-template <int N, bool TS>
+template <int N, bool TS, bool BMN, bool TWO>
 __global__ void __launch_bounds__(128, 1)
     mma_rate_kernel(int reps, long long* __restrict__ cycles, uint32_t* status) {
+  // One or two issuing threads (thread 0, and thread 32 of the next warp with
+  // TWO), each driving its own accumulator (columns 0 and N); B K-major or
+  // MN-major (BMN); A from shared memory or TMEM columns 256..287.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   DiagSmem* hs = reinterpret_cast<DiagSmem*>(smem_raw);
   const uint32_t base = (smem_u32(smem_raw) + sizeof(DiagSmem) + 1023u) & ~1023u;
@@ -126,6 +129,7 @@ __global__ void __launch_bounds__(128, 1)
   for (int i = threadIdx.x; i < (16384 + N * 128) / 4; i += 128) f[i] = 0.0f;
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&hs->bar), 1);
+    mbar_init(smem_u32(&hs->bar2), 1);
     hs->ctl.abort = 0;
     fence_barrier_init();
   }
@@ -148,20 +152,27 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) {
-    const uint32_t id = idesc_tf32(128, N, false, false);
-    const uint64_t ad = sdesc_kmajor(sa), bd = sdesc_kmajor(sb);
+  const bool issuer = threadIdx.x == 0 || (TWO && threadIdx.x == 32);
+  if (issuer) {
+    const uint32_t d = tmem + (threadIdx.x == 0 ? 0u : (uint32_t)N);
+    const uint32_t bar = smem_u32(threadIdx.x == 0 ? &hs->bar : &hs->bar2);
+    const uint32_t id = idesc_tf32(128, N, false, BMN);
+    // MN-major B: K = 32 rows of 128-byte N chunks (chunk stride 32 * 128),
+    // k-step +1024 bytes; K-major: k-step +32 bytes
+    const uint64_t ad = sdesc_kmajor(sa);
+    const uint64_t bd = BMN ? sdesc_mnmajor(sb, 32u * 128u) : sdesc_kmajor(sb);
+    const uint32_t kstep = BMN ? 1024u : 32u;
     const long long t0 = clock64();
     for (int r = 0; r < reps; ++r) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        if (TS) umma_tf32_ts(tmem, tmem + 256 + 8 * k, bd + (32u * k >> 4), id, (r | k) ? 1u : 0u);
-        else umma_tf32_ss(tmem, ad + (32u * k >> 4), bd + (32u * k >> 4), id, (r | k) ? 1u : 0u);
+        if (TS) umma_tf32_ts(d, tmem + 256 + 8 * k, bd + (kstep * k >> 4), id, (r | k) ? 1u : 0u);
+        else umma_tf32_ss(d, ad + (32u * k >> 4), bd + (kstep * k >> 4), id, (r | k) ? 1u : 0u);
       }
     }
-    umma_commit(smem_u32(&hs->bar));
-    const bool ok = mbar_wait(smem_u32(&hs->bar), 0, &hs->ctl, status);
-    cycles[blockIdx.x] = ok ? clock64() - t0 : -1;
+    umma_commit(bar);
+    const bool ok = mbar_wait(bar, 0, &hs->ctl, status);
+    if (threadIdx.x == 0) cycles[blockIdx.x] = ok ? clock64() - t0 : -1;
   }
   tc_fence_before();
   __syncthreads();
@@ -171,31 +182,46 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
-template <int N, bool TS>
+template <int N, bool TS, bool BMN, bool TWO>
 int run_mma_rate(int reps, int blocks, long long* cycles, const DeviceInfo& dev, cudaStream_t st) {
   const size_t smem = 120 * 1024;  // one CTA per SM: each allocates all 512 TMEM columns
-  if (cudaFuncSetAttribute(mma_rate_kernel<N, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(mma_rate_kernel<N, TS, BMN, TWO>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return CT_ERR_CUDA;
-  mma_rate_kernel<N, TS><<<blocks, 128, smem, st>>>(reps, cycles, dev.status);
+  mma_rate_kernel<N, TS, BMN, TWO><<<blocks, 128, smem, st>>>(reps, cycles, dev.status);
   return check_launch();
+}
+
+template <int N>
+int run_mma_rate_n(int flags, int reps, int blocks, long long* cycles, const DeviceInfo& dev,
+                   cudaStream_t st) {
+  const bool ts = flags & 1, bmn = flags & 2, two = flags & 4;
+  if (two && N > 128) return CT_ERR_INVALID_ARGUMENT;  // two accumulators must fit below A
+  if (two) {
+    if (ts) return bmn ? run_mma_rate<N, true, true, true>(reps, blocks, cycles, dev, st)
+                       : run_mma_rate<N, true, false, true>(reps, blocks, cycles, dev, st);
+    return bmn ? run_mma_rate<N, false, true, true>(reps, blocks, cycles, dev, st)
+               : run_mma_rate<N, false, false, true>(reps, blocks, cycles, dev, st);
+  }
+  if (ts) return bmn ? run_mma_rate<N, true, true, false>(reps, blocks, cycles, dev, st)
+                     : run_mma_rate<N, true, false, false>(reps, blocks, cycles, dev, st);
+  return bmn ? run_mma_rate<N, false, true, false>(reps, blocks, cycles, dev, st)
+             : run_mma_rate<N, false, false, false>(reps, blocks, cycles, dev, st);
 }
 
 }  // namespace
 
-int launch_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles,
+// flags: bit 0 A from TMEM, bit 1 B MN-major, bit 2 two issuing threads.
+int launch_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles,
                          const DeviceInfo& dev, cudaStream_t st) {
-  if (reps <= 0 || reps > (1 << 20) || blocks <= 0 || blocks > dev.sm_count || !cycles)
+  if (reps <= 0 || reps > (1 << 20) || blocks <= 0 || blocks > dev.sm_count || !cycles ||
+      flags < 0 || flags > 7)
     return CT_ERR_INVALID_ARGUMENT;
   switch (n) {
-    case 32: return a_tmem ? run_mma_rate<32, true>(reps, blocks, cycles, dev, st)
-                           : run_mma_rate<32, false>(reps, blocks, cycles, dev, st);
-    case 64: return a_tmem ? run_mma_rate<64, true>(reps, blocks, cycles, dev, st)
-                           : run_mma_rate<64, false>(reps, blocks, cycles, dev, st);
-    case 128: return a_tmem ? run_mma_rate<128, true>(reps, blocks, cycles, dev, st)
-                            : run_mma_rate<128, false>(reps, blocks, cycles, dev, st);
-    case 256: return a_tmem ? run_mma_rate<256, true>(reps, blocks, cycles, dev, st)
-                            : run_mma_rate<256, false>(reps, blocks, cycles, dev, st);
+    case 32: return run_mma_rate_n<32>(flags, reps, blocks, cycles, dev, st);
+    case 64: return run_mma_rate_n<64>(flags, reps, blocks, cycles, dev, st);
+    case 128: return run_mma_rate_n<128>(flags, reps, blocks, cycles, dev, st);
+    case 256: return run_mma_rate_n<256>(flags, reps, blocks, cycles, dev, st);
     default: return CT_ERR_INVALID_ARGUMENT;
   }
 }

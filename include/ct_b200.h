@@ -251,12 +251,14 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
                       void* stream);
 
 /* Diagnostic: tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in
- * {32, 64, 128, 256}, A from TMEM (a_tmem != 0) or shared memory.  `blocks`
- * CTAs (at most one per SM) each issue reps x 4 MMAs back to back and write
- * the clock64 cycles from first issue to completion into the device array
- * cycles[blocks] (-1 if the completion wait timed out).  No reference
- * counterpart. */
-int ct_diag_mma_rate(int n, int a_tmem, int reps, int blocks, long long* cycles, void* stream);
+ * {32, 64, 128, 256}.  `flags`: bit 0 A from TMEM (else shared memory), bit 1
+ * B MN-major (else K-major), bit 2 two issuing threads in different warps,
+ * each with its own accumulator (N <= 128).  `blocks` CTAs (at most one per
+ * SM) each issue reps x 4 MMAs per issuing thread back to back and write the
+ * clock64 cycles from first issue to the first thread's completion into the
+ * device array cycles[blocks] (-1 if the completion wait timed out).  No
+ * reference counterpart. */
+int ct_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles, void* stream);
 
 #ifdef __cplusplus
 }

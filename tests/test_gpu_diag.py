@@ -73,3 +73,12 @@ def test_mma_rate_probe_runs(cuda_device):
         assert bool((cyc > 0).all())
         per[n] = cyc.double().mean().item() / 800
     assert per[128] >= per[32] * 0.95
+    # every operand form and the two-issuer variant complete (flags: A in TMEM,
+    # B MN-major, two issuing threads); out-of-range flags are rejected
+    for flags in (0, 2, 3, 5, 7):
+        H.cb.check(H.cb.lib().ct_diag_mma_rate(64, flags, 50, sms, H._p(cyc), H._stream()),
+                   "rate")
+        torch.cuda.synchronize()
+        assert bool((cyc > 0).all()), flags
+    assert H.cb.lib().ct_diag_mma_rate(256, 4, 50, sms, H._p(cyc), H._stream()) != 0
+    assert H.cb.lib().ct_diag_mma_rate(64, 8, 50, sms, H._p(cyc), H._stream()) != 0
