@@ -32,8 +32,9 @@ using namespace fa2;
 // ------------------------------------------------------------ configuration
 // A stage holds the two streamed tiles of one step (dQ pass: K_j and V_j;
 // dK/dV pass: Q_j and dO_j).  A tile the tensor core reads both K-major and
-// MN-major is loaded twice, once per shared-memory layout (the TF32 MN-major
-// operand layout differs from the K-major one).  Per stage, in order:
+// MN-major is held in both shared-memory layouts (the TF32 MN-major operand
+// layout differs from the K-major one): TMA lands the K-major copy and the
+// preparation warps write the MN-major one from it.  Per stage, in order:
 //   A K-major [raw, lo] | A MN-major [raw, lo] (LA == 2) | B K-major [raw, lo] |
 //   B MN-major [raw, lo] (LB == 2), the lo copies present when SPLIT == 3.
 // With KILA / KILB (3xTF32 only) the K-major copy of A / B interleaves instead:
@@ -143,10 +144,11 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
 }
 
 // Producer warp (all 32 lanes): lane 0 issues the TMA loads of tiles j0..j1-1
-// of two [B,H,T,D] tensors into the stage ring (maps[0..1] = A in the K-major /
-// MN-major layouts, maps[2..3] = B likewise).  With VEC, all lanes first stage
-// the step's per-query log-sum-exp (times log2 e) and delta into the stage's
-// vector slot, so the row warps read them from shared memory.
+// of two [B,H,T,D] tensors into the stage ring (maps[0] = A, maps[1] = B, both
+// as K-major tiles; the preparation warps derive the MN-major copies).  With
+// VEC, all lanes then stage the step's per-query log-sum-exp (times log2 e) and
+// delta into the stage's vector slot, so the row warps read them from shared
+// memory.
 template <class C, bool VEC, bool MERGED>
 __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles, float* vec,
                                              const CUtensorMap* const* maps, int j0, int j1,
@@ -157,8 +159,8 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   CtaCtl* ctl = &bars->ctl;
   const int lane = threadIdx.x & 31;
   if (lane == 0)
-    for (int m = 0; m < 4; ++m)
-      if (maps[m]) tma_prefetch_desc(maps[m]);
+    for (int m = 0; m < 2; ++m)
+      tma_prefetch_desc(maps[m]);
   int last_a[NS], last_b[NS];
   for (int s = 0; s < NS; ++s) last_a[s] = last_b[s] = -1;
   // The vector values of step j + 1 are loaded into registers while step j is
@@ -192,7 +194,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
     if (lane == 0) {
       const uint32_t fb = B(bars->full_b[s]);
       mbar_arrive_expect_tx(fb, C::TILE);
-      tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[2], fb, j * BN, h, b, C::KCHB);
+      tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[1], fb, j * BN, h, b, C::KCHB);
     }
     last_b[s] = r;
     if constexpr (VEC) {
@@ -275,7 +277,6 @@ constexpr int kIssuer3Warp = 15;
 template <class C>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmKmn,
                          const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -306,7 +307,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == 0) {
-    const CUtensorMap* maps[4] = {&tmK, &tmKmn, &tmV, nullptr};
+    const CUtensorMap* maps[2] = {&tmK, &tmV};
     bwd_producer<C, false, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
                            p.status);
   } else if (warp == 1) {
@@ -529,9 +530,8 @@ struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true> {
 template <class C>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
-                           const __grid_constant__ CUtensorMap tmQmn,
                            const __grid_constant__ CUtensorMap tmG,
-                           const __grid_constant__ CUtensorMap tmGmn, const BwdParams p) {
+                           const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t idO = idesc_tf32(128, D, false, true);
 
   if (warp == 0) {
-    const CUtensorMap* maps[4] = {&tmQ, &tmQmn, &tmG, &tmGmn};
+    const CUtensorMap* maps[2] = {&tmQ, &tmG};
     bwd_producer<C, true, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
                           p.l2, p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
@@ -830,11 +830,10 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
            const int64_t ls[3], const float* delta, float* dq, const DeviceInfo& dev,
            cudaStream_t st) {
   static unsigned long long attr_done = 0;
-  CUtensorMap tk, tkmn, tv;
+  CUtensorMap tk, tv;
   // K-major copies of interleaved (KIL) tiles load chunk by chunk, every other
   // tile in one copy
   int rc = C::KILA ? make_tmap_bhtd(&tk, k, pr, C::BN) : make_tmap_bhtd_whole(&tk, k, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tkmn, k, pr, C::BN, /*mn_major=*/true);
   if (rc == CT_OK)
     rc = C::KILB ? make_tmap_bhtd(&tv, v, pr, C::BN) : make_tmap_bhtd_whole(&tv, v, pr, C::BN);
   if (rc != CT_OK) return rc;
@@ -843,7 +842,7 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, q, g, lse, ls, delta, dq, nullptr, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tk, tkmn, tv, p);
+  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tk, tv, p);
   return check_launch();
 }
 
@@ -852,19 +851,17 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
              const float* lse, const int64_t ls[3], const float* delta, float* dk, float* dv,
              const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
-  CUtensorMap tq, tqmn, tg, tgmn;
+  CUtensorMap tq, tg;
   int rc = C::KILA ? make_tmap_bhtd(&tq, q, pr, C::BN) : make_tmap_bhtd_whole(&tq, q, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tqmn, q, pr, C::BN, /*mn_major=*/true);
   if (rc == CT_OK)
     rc = C::KILB ? make_tmap_bhtd(&tg, g, pr, C::BN) : make_tmap_bhtd_whole(&tg, g, pr, C::BN);
-  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tgmn, g, pr, C::BN, /*mn_major=*/true);
   if (rc != CT_OK) return rc;
   const size_t smem = bwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_bwd_dkdv_tc_kernel<C>, smem, dev.device, &attr_done);
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tqmn, tg, tgmn, p);
+  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tg, p);
   return check_launch();
 }
 
