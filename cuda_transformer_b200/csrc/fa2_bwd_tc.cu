@@ -111,7 +111,7 @@ constexpr size_t bwd_smem_bytes() {
 }
 
 // empty_count: MMA issuers that read a stage; done_count: issuers whose
-// accumulators the epilogue reads; rows: threads of the row warps.
+// accumulators the epilogue reads; rows: the row warps (one arrival each).
 template <class C>
 __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_count,
                                               int done_count, int rows) {
@@ -119,8 +119,8 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
     mbar_init(B(bars->full_b[s]), 1);
-    mbar_init(B(bars->ready_a[s]), kSplitThreads);
-    mbar_init(B(bars->ready_b[s]), kSplitThreads);
+    mbar_init(B(bars->ready_a[s]), kPrepWarps);
+    mbar_init(B(bars->ready_b[s]), kPrepWarps);
     mbar_init(B(bars->empty_a[s]), empty_count);
     mbar_init(B(bars->empty_b[s]), 1);
     mbar_init(B(bars->vec_full[s]), 1);
@@ -253,17 +253,17 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
   for (int i = 0; i < n; ++i) {
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
-    if (!mbar_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
+    if (!warp_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
     prep_tile<C>(st, false, tid);
     if (!MERGED) {
       fence_proxy_async_smem();
-      mbar_arrive(B(bars->ready_a[s]));
+      warp_arrive(B(bars->ready_a[s]));
     }
-    if (!mbar_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
+    if (!warp_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
     prep_tile<C>(st, true, tid);
     fence_proxy_async_smem();
-    if (MERGED) mbar_arrive(B(bars->ready_a[s]));
-    mbar_arrive(B(bars->ready_b[s]));
+    if (MERGED) warp_arrive(B(bars->ready_a[s]));
+    warp_arrive(B(bars->ready_b[s]));
   }
 }
 
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   // K_j is released by the dQ_j issuer alone: dQ_j waits for dS_j, formed
   // after the row warps read S_j, so S_j has completed by then.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 256);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->rows_ready));
+      warp_arrive(B(bars->rows_ready));
     }
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int i = 0; i < CW; ++i) pv[CW * c + i] = t[i];
       }
       tc_fence_before();
-      mbar_arrive(B(bars->s_free[bj]));
+      warp_arrive(B(bars->s_free[bj]));
       const int kv0 = j * BN + c0;
       const bool need_mask = !valid || (kv0 + HB > T) || (p.causal && kv0 + HB - 1 > q0);
       // straight-line exponentials, then the mask as a separate pass on the
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->ds_full[bj]));
+      warp_arrive(B(bars->ds_full[bj]));
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
   // by warp 10): the merged stage is free after both have committed.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 256);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -705,7 +705,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       row_to_tmem<D, SPLIT>(src, r, valid, vr, lb, grp ? C::TC_V : C::TC_K);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->rows_ready));
+      warp_arrive(B(bars->rows_ready));
     }
     bool ok = n > 0;
     for (int i = 0; ok && i < n; ++i) {
@@ -754,7 +754,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->p_full[bi]));
+      warp_arrive(B(bars->p_full[bi]));
       if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
 #pragma unroll
@@ -778,7 +778,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->ds_full[bi]));
+      warp_arrive(B(bars->ds_full[bi]));
     }
     const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
     float* out = grp ? p.out1 : p.out0;

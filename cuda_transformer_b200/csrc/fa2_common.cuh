@@ -33,6 +33,7 @@ constexpr int kRowWarp0 = 4;      // first warp of the row warpgroup (4 warps)
 // of the row warps for issue slots.  (ptxas sizes registers for 12 warps
 // whether the block has 9 or 11, so the two extra warps cost no registers.)
 constexpr int kSplitThreads = 128;
+constexpr int kPrepWarps = 4;
 // Warp 1 issues one group of tcgen05.mma chains and warp 10 the other.  An
 // issuing thread waits for each MMA to be accepted, so one thread drives the
 // tensor pipe at ~45 cycles per N <= 64 MMA at best and idles it whenever it
@@ -311,11 +312,21 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Warp-uniform bounded wait (all 32 lanes must call it).
+// Warp-uniform bounded wait (all 32 lanes must call it).  Every lane polls:
+// a warp with only lane 0 suspended in try_wait wakes much later (measured).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, CtaCtl* ctl,
                                           uint32_t* status) {
   const bool ok = mbar_wait(bar, parity, ctl, status);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Warp-uniform arrive (all 32 lanes must call it): the warp synchronises,
+// which orders every lane's earlier writes (and, after
+// tcgen05.fence::before_thread_sync, its tensor-memory stores) before lane 0's
+// single arrival.  Barriers armed with warp_arrive count warps, not threads.
+__device__ __forceinline__ void warp_arrive(uint32_t bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 __device__ __forceinline__ bool status_raised(const uint32_t* status) {

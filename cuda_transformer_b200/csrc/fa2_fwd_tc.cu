@@ -74,7 +74,7 @@ struct FwdBars {  // (p_full: one per S/P buffer, at most 3)
   CtaCtl ctl;
   // The two row warps of a TMEM lane quarter (one per row group) exchange each
   // row's partial maximum (two slots, alternating by step) and, at the end,
-  // its partial sum; xchg / xfin (64 arrivals) tell each warp that its
+  // its partial sum; xchg / xfin (one arrival per warp) tell each warp that its
   // partner's value is in place (bounded waits, unlike a named barrier).
   uint64_t xchg[4][2], xfin[4];
   float xmax[2][2][kRows];
@@ -125,19 +125,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(B(bars->full_k[s]), 1);
       mbar_init(B(bars->full_v[s]), 1);
-      mbar_init(B(bars->ready_k[s]), kSplitThreads);
-      mbar_init(B(bars->ready_v[s]), kSplitThreads);
+      mbar_init(B(bars->ready_k[s]), kPrepWarps);
+      mbar_init(B(bars->ready_v[s]), kPrepWarps);
       mbar_init(B(bars->empty_k[s]), 1);
       mbar_init(B(bars->empty_v[s]), 1);
     }
     for (int i = 0; i < 3; ++i) {
-      mbar_init(B(bars->p_full[i]), 256);
+      mbar_init(B(bars->p_full[i]), 8);  // row warps
     }
-    mbar_init(B(bars->q_ready), 128);
+    mbar_init(B(bars->q_ready), 4);  // row group 0's warps
     for (int i = 0; i < 4; ++i) {
-      mbar_init(B(bars->xchg[i][0]), 64);
-      mbar_init(B(bars->xchg[i][1]), 64);
-      mbar_init(B(bars->xfin[i]), 64);
+      mbar_init(B(bars->xchg[i][0]), 2);  // the two warps of a lane quarter
+      mbar_init(B(bars->xchg[i][1]), 2);
+      mbar_init(B(bars->xfin[i]), 2);
     }
     mbar_init(B(bars->mma_final), 1);
     mbar_init(B(bars->mma_final_pv), 1);
@@ -251,14 +251,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int j = 0; j < n_kv; ++j) {
       const int s = j % NS, r = j / NS;
       const uint32_t st = tiles + s * C::STAGE;
-      if (!mbar_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
+      if (!warp_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
       prep(st + C::OFF_K, true);
       fence_proxy_async_smem();
-      mbar_arrive(B(bars->ready_k[s]));
-      if (!mbar_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
+      warp_arrive(B(bars->ready_k[s]));
+      if (!warp_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
       prep(st + C::OFF_V, false);
       fence_proxy_async_smem();
-      mbar_arrive(B(bars->ready_v[s]));
+      warp_arrive(B(bars->ready_v[s]));
     }
   } else {
     // --------------------------------------------------------- row warps
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       row_to_tmem<D, SPLIT>(p.q, qrow, valid, vec, lb, C::TC_Q);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->q_ready));
+      warp_arrive(B(bars->q_ready));
     }
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i = 0; i < CW; ++i) sv[CW * c + i] = t[i];
       }
       bars->xmax[j & 1][grp][r] = mraw;
-      mbar_arrive(B(bars->xchg[quad][j & 1]));
+      warp_arrive(B(bars->xchg[quad][j & 1]));
       if (!(ok = warp_wait(B(bars->xchg[quad][j & 1]), (j >> 1) & 1, ctl, p.status))) break;
       mraw = fmaxf(mraw, bars->xmax[j & 1][grp ^ 1][r]);
       // scale_log2 > 0, so scaling after the maximum is exact
@@ -358,13 +358,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       l += ls0 + ls1;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B(bars->p_full[bb]));
+      warp_arrive(B(bars->p_full[bb]));
     }
     if (ok) {
       const int jj = n_kv - 1;
       const bool done = warp_wait(B(bars->empty_v[jj % NS]), (jj / NS) & 1, ctl, p.status);
       bars->xsum[grp][r] = l;
-      mbar_arrive(B(bars->xfin[quad]));
+      warp_arrive(B(bars->xfin[quad]));
       if (warp_wait(B(bars->xfin[quad]), 0, ctl, p.status) && done) {
         tc_fence_after();
         const float lt = l + bars->xsum[grp ^ 1][r];
