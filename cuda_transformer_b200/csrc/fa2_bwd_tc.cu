@@ -5,11 +5,13 @@
 // Unlike flash_attention_bwd_dk_dv (:409-411) the dK/dV pass starts at the
 // causal diagonal instead of scanning every query tile.
 //
-// Warp roles as in the forward: warp 0 TMA producer, warp 1 TMEM allocator and
-// first MMA issuer, warps 2, 3, 8, 9 TF32 hi/lo split or rounding of landed
-// tiles, warps 4-7 row warps (one stationary row per thread / TMEM lane), warp
-// 10 the second MMA issuer.  dQ: warp 1 issues S, warp 10 dP and dQ.  dK/dV:
-// warp 1 issues S^T and dV, warp 10 dP^T and dK.
+// Warp roles (16 warps): warp 0 TMA producer, warp 1 TMEM allocator and first
+// MMA issuer, warps 2, 3, 8, 9 TF32 hi/lo split or rounding of landed tiles
+// (and the MN-major copies), warps 4-7 and 11-14 two row warpgroups (one
+// stationary row per thread / TMEM lane, each group half of a step's
+// columns), warp 10 the second MMA issuer, warp 15 a third.  dQ: warp 1 issues
+// S, warp 10 dQ and dP -- dP on warp 15 when S / dP are double-buffered.
+// dK/dV: warp 1 issues S^T and dV, warp 10 dP^T and dK.
 //
 // dQ kernel, per 128 query rows, per key tile j (BN keys):
 //   S  = Q K_j^T     (A = Q in TMEM, B = K_j K-major)
@@ -19,9 +21,12 @@
 // dK/dV kernel, per 128 key rows, per query tile j (BN queries):
 //   S^T  = K Q_j^T,  dP^T = V dO_j^T,  P^T, dS^T in the row warps
 //   dV += P^T dO_j,  dK += dS^T Q_j   (B = Q_j / dO_j read MN-major)
-// The issuers run one phase ahead of the row warps (S_{j+1} while dS_j is
-// formed).  Each single S / dP buffer is written and read by MMAs of one
-// issuer, which order its reuse by issue order.
+// The issuers run one step ahead of the row warps (S_{j+1} while dS_j is
+// formed), two with double-buffered S / dP (TF32).  An S or dP buffer written
+// and read by MMAs of one issuer is reused in that issuer's issue order; the
+// dQ pass's third issuer waits on a barrier (dqd) for dQ_j before dP_{j+2}
+// reuses dS_j's buffer.  3xTF32 interleaves the hi / lo copies of K-major
+// tiles so one MMA forms hi*hi and hi*lo together (mma_chain_kil).
 #include "fa2_common.cuh"
 
 namespace ct {

@@ -6,19 +6,23 @@
 // (:124-141), O = sum P V rescaled (:150), then O /= l and L = m + ln(l)
 // (:163, :167).
 //
-// Per CTA: one (batch, head) and 128 query rows.  Warp roles:
+// Per CTA: one (batch, head) and 128 query rows.  Warp roles (15 warps):
 //   warp 0      TMA producer of K/V tiles (NS-stage ring)
 //   warp 1      TMEM allocator + issuer of S = Q K^T (one thread)
 //   warps 2,3,8,9  TF32 hi/lo split (SPLIT == 3) or rounding (SPLIT == 1) of
 //               each landed K/V tile
-//   warps 4-7   row warps: load Q into TMEM, softmax of S, O correction,
-//               epilogue (thread r <-> query row r <-> TMEM lane r)
+//   warps 4-7, 11-14  two row warpgroups: thread r of a group <-> query row r
+//               <-> TMEM lane r; each group takes half of a step's score
+//               columns (softmax with the pair's maxima exchanged, O
+//               correction and epilogue of half of O); group 0 loads Q
 //   warp 10     issuer of O += P V (one thread)
 // K tiles use the K-major tile layout, V tiles the MN-major one.
 // TMEM columns: Q (hi[,lo]) | O | two or three S/P buffers (S overwritten by P
 // hi, then P lo).  S_{j+1} (and S_{j+2} with three buffers) runs on the tensor
-// core while the row warps turn S_j into P_j.  O is rescaled only when a row maximum grows by more
-// than 2^8 (exact: l and O always share the stale maximum).
+// core while the row warps turn S_j into P_j.  O is rescaled only when a row
+// maximum grows by more than 2^8 (exact: l and O always share the stale
+// maximum).  3xTF32 forms hi*hi and hi*lo of S, and of P V, with one MMA
+// (mma_chain_kil, mma_chain_mn2).
 #include "fa2_common.cuh"
 
 namespace ct {
