@@ -206,7 +206,7 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
       float* vs = vec + s * 2 * BN;
 #pragma unroll
       for (int u = 0; u < NV; ++u) {
-        vs[32 * u + lane] = vl[u] * kLog2e;
+        vs[32 * u + lane] = vl[u] * -kLog2e;  // rows add it in one FMA
         vs[BN + 32 * u + lane] = vd[u];
       }
       __syncwarp();
@@ -463,8 +463,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // straight-line exponentials, then the mask as a separate pass on the
       // few boundary tiles (a test per column would split the unrolled loop
       // into one basic block per column and serialise it)
+      const float nl2 = -l2;
 #pragma unroll
-      for (int i = 0; i < HB; ++i) pv[i] = ex2_approx(fmaf(pv[i], p.scale_log2, -l2));
+      for (int i = 0; i < HB; i += 2) {
+        float a0, a1;
+        ffma2(a0, a1, pv[i], pv[i + 1], p.scale_log2, p.scale_log2, nl2, nl2);
+        pv[i] = ex2_approx(a0);
+        pv[i + 1] = ex2_approx(a1);
+      }
       if (need_mask) {
 #pragma unroll
         for (int i = 0; i < HB; ++i) {
@@ -481,13 +487,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if constexpr (C::KILB) {  // dP from its two partial sums
           tmem_ldn<CW>(dc + BN + CW * c, lo);
 #pragma unroll
-          for (int i = 0; i < CW; ++i) t[i] += lo[i];
+          for (int i = 0; i < CW; i += 2) fadd2(t[i], t[i + 1], t[i], t[i + 1], lo[i], lo[i + 1]);
         }
 #pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const float ds = pv[CW * c + i] * (t[i] - dl);
-          if constexpr (SPLIT == 3) tf32_split(ds, t[i], lo[i]);
-          else t[i] = tf32_round_finite(ds);
+        for (int i = 0; i < CW; i += 2) {
+          float u0, u1, d0, d1;
+          fsub2(u0, u1, t[i], t[i + 1], dl, dl);
+          fmul2(d0, d1, pv[CW * c + i], pv[CW * c + i + 1], u0, u1);  // dS = P (dP - delta)
+          if constexpr (SPLIT == 3) {
+            tf32_split2(d0, d1, t[i], t[i + 1], lo[i], lo[i + 1]);
+          } else {
+            t[i] = tf32_round_finite(d0);
+            t[i + 1] = tf32_round_finite(d1);
+          }
         }
         tmem_stn<CW>(dc + CW * c, t);
         if constexpr (SPLIT == 3) tmem_stn<CW>(dc + BN + CW * c, lo);
@@ -733,13 +745,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if constexpr (C::KILA) {  // S^T = [hi-hi + lo-hi part] + [hi-lo part]
           tmem_ldn<CW>(sc + BN + CW * c, lo);
 #pragma unroll
-          for (int x = 0; x < CW; ++x) t[x] += lo[x];
+          for (int x = 0; x < CW; x += 2) fadd2(t[x], t[x + 1], t[x], t[x + 1], lo[x], lo[x + 1]);
         }
-        load_vecn<CW>(vl + CW * c, lv);
+        load_vecn<CW>(vl + CW * c, lv);  // -LSE * log2(e)
         // straight-line exponentials; the mask is a separate pass on the few
         // boundary tiles (a test per column would serialise the loop)
 #pragma unroll
-        for (int x = 0; x < CW; ++x) t[x] = ex2_approx(fmaf(t[x], p.scale_log2, -lv[x]));
+        for (int x = 0; x < CW; x += 2) {
+          float a0, a1;
+          ffma2(a0, a1, t[x], t[x + 1], p.scale_log2, p.scale_log2, lv[x], lv[x + 1]);
+          t[x] = ex2_approx(a0);
+          t[x + 1] = ex2_approx(a1);
+        }
         if (need_mask) {
 #pragma unroll
           for (int x = 0; x < CW; ++x) {
@@ -748,11 +765,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
 #pragma unroll
-        for (int x = 0; x < CW; ++x) {
-          const float e = t[x];
-          pv[CW * c + x] = e;
-          if constexpr (SPLIT == 3) tf32_split(e, t[x], lo[x]);
-          else t[x] = tf32_round_finite(e);
+        for (int x = 0; x < CW; x += 2) {
+          pv[CW * c + x] = t[x];
+          pv[CW * c + x + 1] = t[x + 1];
+          if constexpr (SPLIT == 3) {
+            tf32_split2(t[x], t[x + 1], t[x], t[x + 1], lo[x], lo[x + 1]);
+          } else {
+            t[x] = tf32_round_finite(t[x]);
+            t[x + 1] = tf32_round_finite(t[x + 1]);
+          }
         }
         tmem_stn<CW>(sc + CW * c, t);
         if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);
@@ -769,14 +790,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if constexpr (C::KILB) {  // dP^T from its two partial sums
           tmem_ldn<CW>(dc + BN + CW * c, lo);
 #pragma unroll
-          for (int x = 0; x < CW; ++x) t[x] += lo[x];
+          for (int x = 0; x < CW; x += 2) fadd2(t[x], t[x + 1], t[x], t[x + 1], lo[x], lo[x + 1]);
         }
         load_vecn<CW>(vl + BN + CW * c, dv);
 #pragma unroll
-        for (int x = 0; x < CW; ++x) {
-          const float ds = pv[CW * c + x] * (t[x] - dv[x]);
-          if constexpr (SPLIT == 3) tf32_split(ds, t[x], lo[x]);
-          else t[x] = tf32_round_finite(ds);
+        for (int x = 0; x < CW; x += 2) {
+          const int cc = CW * c + x;
+          float u0, u1, d0, d1;
+          fsub2(u0, u1, t[x], t[x + 1], dv[x], dv[x + 1]);
+          fmul2(d0, d1, pv[cc], pv[cc + 1], u0, u1);  // dS^T = P^T (dP^T - delta)
+          if constexpr (SPLIT == 3) {
+            tf32_split2(d0, d1, t[x], t[x + 1], lo[x], lo[x + 1]);
+          } else {
+            t[x] = tf32_round_finite(d0);
+            t[x + 1] = tf32_round_finite(d1);
+          }
         }
         tmem_stn<CW>(dc + CW * c, t);
         if constexpr (SPLIT == 3) tmem_stn<CW>(dc + BN + CW * c, lo);

@@ -106,6 +106,15 @@ __device__ __forceinline__ void row_to_tmem(const Ptr4& t, const float* rowp, bo
   }
 }
 
+// 3xTF32 split of two values (tf32_split with the subtraction packed).
+__device__ __forceinline__ void tf32_split2(float x0, float x1, float& h0, float& h1, float& l0,
+                                            float& l1) {
+  const float a = tf32_trunc(x0), b = tf32_trunc(x1);
+  fsub2(l0, l1, x0, x1, a, b);
+  h0 = a;
+  h1 = b;
+}
+
 // Causal / ragged mask of 32 consecutive score columns starting at key kv0:
 // column kv stays iff kv < T and (!causal || kv <= row); others become -inf.
 __device__ __forceinline__ void mask_cols32(float (&t)[32], int kv0, int T, int causal, int row) {

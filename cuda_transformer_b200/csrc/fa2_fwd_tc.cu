@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           float t2[CW];
           tmem_ldn<CW>(sc + BN + CW * c, t2);
 #pragma unroll
-          for (int i = 0; i < CW; ++i) t[i] += t2[i];
+          for (int i = 0; i < CW; i += 2) fadd2(t[i], t[i + 1], t[i], t[i + 1], t2[i], t2[i + 1]);
         }
         if (need_mask) mask_cols<CW>(t, kv0 + CW * c, T, p.causal, row);
         mraw = fmaxf(mraw, maxn<CW>(t));
@@ -349,12 +349,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW];
 #pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const float e = ex2_approx(fmaf(sv[CW * c + i], p.scale_log2, neg_m));
-          if (i & 1) ls1 += e;
-          else ls0 += e;
-          if constexpr (SPLIT == 3) tf32_split(e, t[i], lo[i]);
-          else t[i] = tf32_round_finite(e);
+        for (int i = 0; i < CW; i += 2) {
+          float a0, a1;
+          ffma2(a0, a1, sv[CW * c + i], sv[CW * c + i + 1], p.scale_log2, p.scale_log2, neg_m,
+                neg_m);
+          const float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
+          fadd2(ls0, ls1, ls0, ls1, e0, e1);  // even / odd column sums
+          if constexpr (SPLIT == 3) {
+            tf32_split2(e0, e1, t[i], t[i + 1], lo[i], lo[i + 1]);
+          } else {
+            t[i] = tf32_round_finite(e0);
+            t[i + 1] = tf32_round_finite(e1);
+          }
         }
         tmem_stn<CW>(sc + CW * c, t);
         if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);

@@ -373,6 +373,31 @@ __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
   lo = x - hi;
 }
 
+// Packed pairs of FP32 operations (sm_100 f32x2): one instruction, two
+// independent IEEE round-to-nearest results -- bit-identical to two scalar
+// fmaf / + / - / * -- so row loops spend half the issue slots on them.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+#define CT_F32X2_BINOP(NAME, OP)                                                                 \
+  __device__ __forceinline__ void NAME(float& d0, float& d1, float a0, float a1, float b0,       \
+                                       float b1) {                                               \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"                                                          \
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" OP                                   \
+        " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                              \
+        : "=f"(d0), "=f"(d1)                                                                     \
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));                                                   \
+  }
+CT_F32X2_BINOP(fadd2, "add.rn.f32x2")
+CT_F32X2_BINOP(fsub2, "sub.rn.f32x2")
+CT_F32X2_BINOP(fmul2, "mul.rn.f32x2")
+#undef CT_F32X2_BINOP
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
