@@ -427,6 +427,14 @@ __device__ __forceinline__ void sts128(uint32_t a, float4 v) {
                : "memory");
 }
 
+// Low parts x - tf32_trunc(x) of a float4 (3xTF32 split), subtractions packed.
+__device__ __forceinline__ float4 tf32_lo4(float4 x) {
+  float4 l;
+  fsub2(l.x, l.y, x.x, x.y, tf32_trunc(x.x), tf32_trunc(x.y));
+  fsub2(l.z, l.w, x.z, x.w, tf32_trunc(x.z), tf32_trunc(x.w));
+  return l;
+}
+
 // Tile preparation by a group of NTHREADS threads, BYTES bytes per tile.
 // Thread t handles the 16-byte words t, t + NTHREADS, ... (a warp covers 512
 // contiguous bytes: no bank conflicts).  Words go in batches of up to 8: every
@@ -455,8 +463,7 @@ __device__ __forceinline__ void split_tile_smem(uint32_t raw, uint32_t lo, uint3
 #pragma unroll
     for (uint32_t u = 0; u < P::U; ++u)
       sts128(lo + (tid + (w0 + u) * NTHREADS) * 16u,
-             make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
-                         x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w)));
+             tf32_lo4(x[u]));
   }
 }
 
@@ -479,8 +486,7 @@ __device__ __forceinline__ void split_tile_smem_il(uint32_t base, uint32_t tid) 
 #pragma unroll
     for (uint32_t u = 0; u < P::U; ++u)
       sts128(raw_at(tid + (w0 + u) * NTHREADS) + CHUNK,
-             make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
-                         x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w)));
+             tf32_lo4(x[u]));
   }
 }
 
@@ -515,8 +521,7 @@ __device__ __forceinline__ void derive_tile_smem(uint32_t k, uint32_t mn, uint32
 #pragma unroll
     for (uint32_t u = 0; u < P::U; ++u) {
       if constexpr (SPLIT == 3) {
-        const float4 lo = make_float4(x[u].x - tf32_trunc(x[u].x), x[u].y - tf32_trunc(x[u].y),
-                                      x[u].z - tf32_trunc(x[u].z), x[u].w - tf32_trunc(x[u].w));
+        const float4 lo = tf32_lo4(x[u]);
         sts128(ka[u] + KLO, lo);
         sts128(ma[u], x[u]);
         sts128(ma[u] + MLO, lo);
