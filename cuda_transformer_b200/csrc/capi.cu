@@ -386,7 +386,7 @@ int ct_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, void*
 
 int ct_layernorm_fwd(const float* x, const float* gamma, const float* beta, float* y, float* mean,
                      float* rstd, int64_t rows, int64_t n, float eps, void* stream) {
-  if (rows < 0 || n <= 0 || n > 1024 || ((!x || !gamma || !beta || !y) && rows > 0))
+  if (rows < 0 || n <= 0 || n > kLayerNormMaxCols || ((!x || !gamma || !beta || !y) && rows > 0))
     return CT_ERR_INVALID_ARGUMENT;
   int err = CT_OK;
   current_device(&err);
@@ -402,7 +402,7 @@ size_t ct_layernorm_bwd_workspace_size(int64_t rows, int64_t n) {
 int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean, const float* rstd,
                      const float* dy, float* dx, float* dgamma, float* dbeta, int64_t rows,
                      int64_t n, void* workspace, size_t workspace_bytes, void* stream) {
-  if (rows < 0 || n <= 0 || n > 1024 || !gamma || !dgamma || !dbeta ||
+  if (rows < 0 || n <= 0 || n > kLayerNormMaxCols || !gamma || !dgamma || !dbeta ||
       ((!x || !mean || !rstd || !dy || !dx) && rows > 0))
     return CT_ERR_INVALID_ARGUMENT;
   int err = CT_OK;

@@ -105,6 +105,8 @@ int launch_softmax_bwd(const float* p, const float* dp, float* dx, int64_t rows,
                        cudaStream_t st);
 int launch_gelu_fwd(const float* x, float* y, int64_t numel, cudaStream_t st);
 int launch_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, cudaStream_t st);
+// Widest LayerNorm row: one warp per row up to 1024 columns, one CTA per row above.
+constexpr int64_t kLayerNormMaxCols = 8192;
 int launch_layernorm_fwd(const float* x, const float* g, const float* b, float* y, float* mean,
                          float* rstd, int64_t rows, int64_t n, float eps, cudaStream_t st);
 size_t layernorm_bwd_workspace(int64_t rows, int64_t n);

@@ -417,6 +417,178 @@ __global__ void __launch_bounds__(kLnWarps* kWarp)
   for (int c = threadIdx.x; c < 2 * n; c += blockDim.x) out[c] = lnsm[c];
 }
 
+// ------------------------------------------------- LayerNorm, wide rows
+// Rows of 1025..8192 columns: one 256-thread CTA per row (rows taken in turn
+// by a persistent grid).  Thread t holds J slots of 4 columns: 4*(j*256 + t)
+// .. +3 with float4 access (VEC), else (4j + q)*256 + t.  Same math and, in
+// the backward, the same workspace layout ([CTA][2][n] column partials, each
+// column owned by one thread) as the one-warp-per-row kernels above.
+constexpr int kLnwThreads = 256, kLnwWarps = kLnwThreads / kWarp;
+
+template <int J, bool VEC>
+struct BlockRow {
+  float v[J][4];
+  __device__ __forceinline__ static int col(int t, int j, int q) {
+    return VEC ? 4 * (j * kLnwThreads + t) + q : (4 * j + q) * kLnwThreads + t;
+  }
+  __device__ __forceinline__ void load(const float* __restrict__ p, int n, int t) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      if (VEC) {
+        const int c = col(t, j, 0);
+        if (c < n) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(p + c));
+          v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+        } else {
+          v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.0f;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = col(t, j, q);
+          v[j][q] = c < n ? __ldg(p + c) : 0.0f;
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* __restrict__ p, int n, int t) const {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      if (VEC) {
+        const int c = col(t, j, 0);
+        if (c < n) *reinterpret_cast<float4*>(p + c) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = col(t, j, q);
+          if (c < n) p[c] = v[j][q];
+        }
+      }
+    }
+  }
+};
+
+// Sums of NV values over the CTA, in a fixed order (warp butterflies, then
+// the warps' totals in warp order); every thread gets the results.
+template <int NV>
+__device__ __forceinline__ void block_sums(float (&v)[NV], float (*red)[kLnwWarps]) {
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = warp_sum(v[i]);
+    if (lane == 0) red[i][warp] = v[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kLnwWarps; ++w) s += red[i][w];
+    v[i] = s;
+  }
+  __syncthreads();  // red is reused by the next call
+}
+
+template <int J, bool VEC>
+__global__ void __launch_bounds__(kLnwThreads)
+    layernorm_fwd_wide_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                              const float* __restrict__ beta, float* __restrict__ y,
+                              float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                              int64_t rows, int n, float eps) {
+  __shared__ float red[1][kLnwWarps];
+  const int t = threadIdx.x;
+  BlockRow<J, VEC> g, b;
+  g.load(gamma, n, t);
+  b.load(beta, n, t);
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    BlockRow<J, VEC> r;
+    r.load(x + row * n, n, t);
+    float s[1] = {0.0f};
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) s[0] += r.v[j][q];
+    block_sums<1>(s, red);
+    const float mean = s[0] / (float)n;
+    float ss[1] = {0.0f};
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float d = BlockRow<J, VEC>::col(t, j, q) < n ? r.v[j][q] - mean : 0.0f;
+        ss[0] += d * d;
+      }
+    block_sums<1>(ss, red);
+    const float rstd = 1.0f / sqrtf(ss[0] / (float)n + eps);
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) r.v[j][q] = (r.v[j][q] - mean) * rstd * g.v[j][q] + b.v[j][q];
+    r.store(y + row * n, n, t);
+    if (t == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = rstd;
+    }
+  }
+}
+
+// dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma; the
+// column partials of dy*xhat and dy of this CTA's rows go to ws[blockIdx.x].
+template <int J, bool VEC>
+__global__ void __launch_bounds__(kLnwThreads)
+    layernorm_bwd_wide_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                              const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                              const float* __restrict__ dy, float* __restrict__ dx,
+                              float* __restrict__ ws, int64_t rows, int n) {
+  __shared__ float red[2][kLnwWarps];
+  const int t = threadIdx.x;
+  BlockRow<J, VEC> gam;
+  gam.load(gamma, n, t);
+  float pg[J][4], pb[J][4];
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) pg[j][q] = pb[j][q] = 0.0f;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    BlockRow<J, VEC> xr, g;
+    xr.load(x + row * n, n, t);
+    g.load(dy + row * n, n, t);
+    const float mu = __ldg(mean_in + row), rs = __ldg(rstd_in + row);
+    float s[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float xh = (xr.v[j][q] - mu) * rs;
+        const float gg = g.v[j][q] * gam.v[j][q];
+        pg[j][q] += g.v[j][q] * xh;
+        pb[j][q] += g.v[j][q];
+        xr.v[j][q] = xh;
+        g.v[j][q] = gg;
+        s[0] += gg;
+        s[1] += gg * xh;
+      }
+    block_sums<2>(s, red);
+    const float s1 = s[0] / (float)n, s2 = s[1] / (float)n;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) g.v[j][q] = rs * (g.v[j][q] - s1 - xr.v[j][q] * s2);
+    g.store(dx + row * n, n, t);
+  }
+  float* out = ws + (size_t)blockIdx.x * 2 * n;
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = BlockRow<J, VEC>::col(t, j, q);
+      if (c < n) {
+        out[c] = pg[j][q];
+        out[n + c] = pb[j][q];
+      }
+    }
+}
+
 // Sums `parts` partial rows of length `len` (row stride `len`) column-wise;
 // columns [0, split) go to out_a, the rest to out_b.  A 1024-thread block
 // covers 32 columns: its 32 warps take every 32nd part (eight loads in flight
@@ -663,9 +835,22 @@ int launch_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, c
 int launch_layernorm_fwd(const float* x, const float* g, const float* b, float* y, float* mean,
                          float* rstd, int64_t rows, int64_t n, float eps, cudaStream_t st) {
   if (rows == 0) return CT_OK;
-  if (n <= 0 || n > 1024) return CT_ERR_INVALID_ARGUMENT;
+  if (n <= 0 || n > kLayerNormMaxCols) return CT_ERR_INVALID_ARGUMENT;
   const bool vec = (n % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(b) && aligned16(y);
   const int nn = (int)n;
+  if (n > 1024) {  // one CTA per row
+    const unsigned grid = (unsigned)(rows < 148 * 4 ? rows : 148 * 4);
+#define CT_LNW_FWD(J)                                                                       \
+  (vec ? layernorm_fwd_wide_kernel<J, true><<<grid, kLnwThreads, 0, st>>>(x, g, b, y, mean, \
+                                                                          rstd, rows, nn, eps) \
+       : layernorm_fwd_wide_kernel<J, false><<<grid, kLnwThreads, 0, st>>>(x, g, b, y, mean, \
+                                                                           rstd, rows, nn, eps))
+    if (n <= 2048) CT_LNW_FWD(2);
+    else if (n <= 4096) CT_LNW_FWD(4);
+    else CT_LNW_FWD(8);
+#undef CT_LNW_FWD
+    return check_launch();
+  }
 #define CT_LN_FWD(V) \
   (vec ? ln_fwd_launch<V, true>(x, g, b, y, mean, rstd, rows, nn, eps, st) \
        : ln_fwd_launch<V, false>(x, g, b, y, mean, rstd, rows, nn, eps, st))
@@ -685,7 +870,7 @@ size_t layernorm_bwd_workspace(int64_t rows, int64_t n) {
 int launch_layernorm_bwd(const float* x, const float* g, const float* mean, const float* rstd,
                          const float* dy, float* dx, float* dg, float* db, int64_t rows,
                          int64_t n, float* ws, cudaStream_t st) {
-  if (n <= 0 || n > 1024) return CT_ERR_INVALID_ARGUMENT;
+  if (n <= 0 || n > kLayerNormMaxCols) return CT_ERR_INVALID_ARGUMENT;
   if (rows == 0) {
     if (cudaMemsetAsync(dg, 0, n * sizeof(float), st) != cudaSuccess) return CT_ERR_CUDA;
     if (cudaMemsetAsync(db, 0, n * sizeof(float), st) != cudaSuccess) return CT_ERR_CUDA;
@@ -694,6 +879,21 @@ int launch_layernorm_bwd(const float* x, const float* g, const float* mean, cons
   const bool vec = (n % 4 == 0) && aligned16(x) && aligned16(g) && aligned16(dy) && aligned16(dx);
   const int nn = (int)n, grid = ln_bwd_grid(rows);
   int rc;
+  if (n > 1024) {  // one CTA per row, the same [grid][2][n] partials
+#define CT_LNW_BWD(J)                                                                          \
+  (vec ? layernorm_bwd_wide_kernel<J, true><<<grid, kLnwThreads, 0, st>>>(x, g, mean, rstd, dy, \
+                                                                          dx, ws, rows, nn)   \
+       : layernorm_bwd_wide_kernel<J, false><<<grid, kLnwThreads, 0, st>>>(x, g, mean, rstd, dy, \
+                                                                           dx, ws, rows, nn))
+    if (n <= 2048) CT_LNW_BWD(2);
+    else if (n <= 4096) CT_LNW_BWD(4);
+    else CT_LNW_BWD(8);
+#undef CT_LNW_BWD
+    rc = check_launch();
+    if (rc != CT_OK) return rc;
+    column_sum_parts<<<column_sum_grid(2 * n), kCsCols * kCsGroups, 0, st>>>(ws, grid, 2 * n, dg, db, n);
+    return check_launch();
+  }
 #define CT_LN_BWD(V) \
   rc = vec ? ln_bwd_launch<V, true>(x, g, mean, rstd, dy, dx, ws, rows, nn, grid, st) \
            : ln_bwd_launch<V, false>(x, g, mean, rstd, dy, dx, ws, rows, nn, grid, st)

@@ -4,7 +4,8 @@ measurement shapes and prints one JSON line per kernel with its roofline:
   linear  x[16384,384] @ W[384,1536] + b  and  x[16384,1536] @ W[1536,384] + b,
           plus the backward's dx = dy W^T and dW = x^T dy (2 M N K FLOP each)
   softmax [16384,4096]  fwd (read x, write y), bwd (read p, dp, write dx)
-  layernorm [16384,384] fwd (read x, write y), bwd (read x, dy, write dx)
+  layernorm [16384,384] fwd (read x, write y), bwd (read x, dy, write dx);
+            --ln-cols sets the row width (above 1024: the one-CTA-per-row kernels)
   gelu    [16384,1536]  fwd (read x, write y), bwd (read x, dy, write dx)
   bias grad of dy[16384,1536] (read dy)
 
@@ -131,7 +132,7 @@ def hbm_record(name, shape, ms, nbytes, pk):
             "algorithmic_bytes": nbytes, "peak_source": pk["source"] + " copy bandwidth"}
 
 
-def row_cases(dev, timer, iters, pk, only):
+def row_cases(dev, timer, iters, pk, only, ln_n=384):
     L = lib()
     g = torch.Generator(device=dev).manual_seed(1)
     out = []
@@ -146,7 +147,7 @@ def row_cases(dev, timer, iters, pk, only):
         out.append(hbm_record("softmax_bwd", f"[{rows},{n}]", ms, 3 * rows * n * 4, pk))
         del x, y, dx, dp
     if "layernorm" in only:
-        rows, n = 16384, 384
+        rows, n = 16384, ln_n
         x = torch.randn(rows, n, device=dev, generator=g)
         gam, bet = torch.ones(n, device=dev), torch.zeros(n, device=dev)
         y, dx = torch.empty_like(x), torch.empty_like(x)
@@ -188,6 +189,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", default="linear,softmax,layernorm,gelu,bias_grad")
     ap.add_argument("--precisions", default="3xtf32,tf32,fp32")
+    ap.add_argument("--ln-cols", type=int, default=384, help="LayerNorm row width (<= 8192)")
     a = ap.parse_args()
     only = set(a.only.split(","))
     dev = torch.device("cuda", 0)
@@ -197,7 +199,7 @@ def main() -> None:
     recs = []
     if "linear" in only:
         recs += linear_cases(dev, timer, a.iters, pk, a.precisions.split(","))
-    recs += row_cases(dev, timer, a.iters, pk, only)
+    recs += row_cases(dev, timer, a.iters, pk, only, a.ln_cols)
     for r in recs:
         print(json.dumps(r))
     assert device_status(0, clear=True) == 0, "device watchdog raised"

@@ -217,7 +217,7 @@ int ct_gelu_fwd(const float* x, float* y, int64_t numel, void* stream);
 int ct_gelu_bwd(const float* x, const float* dy, float* dx, int64_t numel, void* stream);
 
 /* LayerNorm over the last dimension of a contiguous [rows, n] tensor:
- * y = (x - mean) / sqrt(var_biased + eps) * gamma + beta (n <= 1024); mean and rstd
+ * y = (x - mean) / sqrt(var_biased + eps) * gamma + beta (n <= 8192); mean and rstd
  * ([rows], may be NULL) are saved for the backward.  The reference has no
  * CUDA LayerNorm: this restates the PyTorch module in gpt/gpt.py:47-59. */
 int ct_layernorm_fwd(const float* x, const float* gamma, const float* beta,

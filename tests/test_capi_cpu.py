@@ -73,6 +73,9 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
     rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, 1, 1, 8, 64, 0, 7, None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
+    # LayerNorm rows are at most 8192 wide
+    rc = lib.ct_layernorm_fwd(None, None, None, None, None, None, 1, 8193, ctypes.c_float(1e-5), None)
+    assert rc == cb.CT_ERR_INVALID_ARGUMENT
 
 
 def test_torch_schemas_match_reference():

@@ -48,7 +48,8 @@ def test_gelu(cuda_device, b, m, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("rows,n", [(5, 384), (37, 512), (16384, 384), (3, 100), (9, 1024)])
+@pytest.mark.parametrize("rows,n", [(5, 384), (37, 512), (16384, 384), (3, 100), (9, 1024),
+                                    (7, 1536), (5, 3001), (700, 2048), (2, 4100), (3, 8192)])
 def test_layernorm(cuda_device, rows, n):
     x = _r((rows, n), n, cuda_device, "randn")
     g = 1.0 + 0.1 * _r((n,), n + 1, cuda_device, "randn")
