@@ -530,18 +530,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // In 3xTF32 mode S^T and dP^T use the interleaved K-major layout: their two
 // hi/lo partial sums land side by side in the buffer's 2*BN columns and the
 // row warps add them (mma_chain_kil).
-template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1>
+//
+// PASS selects what one launch accumulates: kDkvBoth (dK and dV), or, where K,
+// V and both accumulators do not fit TMEM together (D = 128: 4 x 128 columns),
+// kDkvOnlyDv (K, S^T -> P^T, dV; no V, dP^T or dK) followed by kDkvOnlyDk (K,
+// V, S^T, dP^T -> dS^T, dK; no dV), each reading the same streamed tiles.
+constexpr int kDkvBoth = 0, kDkvOnlyDv = 1, kDkvOnlyDk = 2;
+
+template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1, int PASS_ = kDkvBoth>
 struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true> {
   using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true>;
   // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
   // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
   // and dS_i, so the rows go from one step to the next without waiting.
-  static constexpr int NSB = NSB_;
+  static constexpr int NSB = NSB_, PASS = PASS_;
+  static constexpr bool DO_DV = PASS != kDkvOnlyDk, DO_DK = PASS != kDkvOnlyDv;
   static constexpr uint32_t SB = T_::NCOPY * BN_;  // columns of one buffer: hi [| lo]
-  static constexpr uint32_t TC_K = 0, TC_V = T_::NCOPY * D_, TC_DK = 2 * T_::NCOPY * D_;
-  static constexpr uint32_t TC_DV = TC_DK + D_, TC_S = TC_DV + D_, TC_DP = TC_S + NSB * SB;
+  // column map: K [| V] [| dK] [| dV] | S^T buffers [| dP^T buffers]
+  static constexpr uint32_t TC_K = 0, TC_V = T_::NCOPY * D_;
+  static constexpr uint32_t TC_DK = TC_V + (DO_DK ? T_::NCOPY * D_ : 0);
+  static constexpr uint32_t TC_DV = TC_DK + (DO_DK ? D_ : 0);
+  static constexpr uint32_t TC_S = TC_DV + (DO_DV ? D_ : 0), TC_DP = TC_S + NSB * SB;
   static_assert(NSB == 1 || NSB == 2, "S / dP buffering");
-  static_assert(TC_DP + NSB * SB <= T_::TMEM_COLS, "TMEM budget");
+  static_assert((DO_DK ? TC_DP + NSB * SB : TC_S + NSB * SB) <= T_::TMEM_COLS, "TMEM budget");
 };
 
 template <class C>
@@ -568,8 +579,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n = j1 - j0;
 
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
-  // by warp 10): the merged stage is free after both have committed.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8);
+  // by warp 10): the merged stage is free after both have committed.  The dV
+  // pass has no warp-10 work.
+  constexpr int kIssuers = C::DO_DK ? 2 : 1;
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, kIssuers, kIssuers, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -628,12 +641,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (C::NSB == 1 && nx < n &&
               !(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status)))
             break;
-          // dO_i's MN-major copy (prepared right after the K-major ones)
-          if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
-          tc_fence_after();
-          const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
-          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+          if constexpr (C::DO_DV) {
+            // dO_i's MN-major copy (prepared right after the K-major ones)
+            if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
+            mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
+                tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+          }
           if (C::NSB == 1 && nx < n) issue_S(nx);
           umma_commit(B(bars->empty_a[i % NS]));
           if (C::NSB == 2 && nx < n) {
@@ -652,7 +667,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // Step i of buffer b:  [dS_i ready]  dK += dS_i^T Q_i -> empty_i;
     //   [tiles i+NSB prepared]  dP^T_{i+NSB} -> dp_full[b]
     // dP^T_{i+NSB} overwrites dS_i after dK_i in this thread's issue order.
-    if (lane == 0) {
+    if (C::DO_DK && lane == 0) {
       const uint64_t gd0 = sdesc_kmajor(tiles + C::OFF_B0);  // stage-0 descriptors
       const uint64_t qmd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       auto issue_dP = [&](int i) {
@@ -715,15 +730,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = k0 + quad * 32 + lane;  // key row
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    {
+    if (grp == 0 || C::DO_DK) {  // V is read only by dP^T
       const Ptr4& src = grp ? p.st1 : p.st0;
       const float* r = src.row(b, h, valid ? row : 0);
       const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0);
       row_to_tmem<D, SPLIT>(src, r, valid, vr, lb, grp ? C::TC_V : C::TC_K);
       tmem_wait_st();
-      tc_fence_before();
-      warp_arrive(B(bars->rows_ready));
     }
+    tc_fence_before();
+    warp_arrive(B(bars->rows_ready));
     bool ok = n > 0;
     for (int i = 0; ok && i < n; ++i) {
       const int qs = (j0 + i) * BN + c0;
@@ -775,12 +790,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             t[x + 1] = tf32_round_finite(t[x + 1]);
           }
         }
-        tmem_stn<CW>(sc + CW * c, t);
-        if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);
+        if constexpr (C::DO_DV) {  // P^T is the A operand of dV only
+          tmem_stn<CW>(sc + CW * c, t);
+          if constexpr (SPLIT == 3) tmem_stn<CW>(sc + BN + CW * c, lo);
+        }
       }
-      tmem_wait_st();
+      if constexpr (C::DO_DV) tmem_wait_st();
       tc_fence_before();
-      warp_arrive(B(bars->p_full[bi]));
+      warp_arrive(B(bars->p_full[bi]));  // S^T_i read: its buffer may be reused
+      if constexpr (!C::DO_DK) continue;
       if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
 #pragma unroll
@@ -815,7 +833,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
     float* out = grp ? p.out1 : p.out0;
-    if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
+    if (grp == 0 ? !C::DO_DK : !C::DO_DV) {
+      // this pass does not produce the group's gradient
+    } else if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
       if (valid) {
         for (int d = 0; d < D; ++d) out[orow + d] = 0.0f;
       }
@@ -901,7 +921,9 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
 }  // namespace
 
 bool fa2_bwd_tc_supported(const Fa2Problem& p) {
-  return (p.D == 32 || p.D == 64) &&
+  // D = 128 in TF32 only: in 3xTF32 the hi / lo copies of the two stationary
+  // 128-column operands alone fill TMEM.
+  return (p.D == 32 || p.D == 64 || (p.D == 128 && p.precision == CT_PRECISION_TF32)) &&
          (p.precision == CT_PRECISION_3XTF32 || p.precision == CT_PRECISION_TF32) &&
          p.T < (1ll << 31) && ((p.T + kRows - 1) / kRows) * p.B * p.H < (1ll << 31);
 }
@@ -917,6 +939,8 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 
   if (pr.D == 32)
     return split ? run_dq<DqCfg<32, 64, 3, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<32, 128, 1, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
+  if (pr.D == 128 && !split)
+    return run_dq<DqCfg<128, 64, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
 
@@ -931,6 +955,13 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
   if (pr.D == 32)
     return split ? run_dkdv<DkvCfg<32, 64, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
                  : run_dkdv<DkvCfg<32, 128, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+  if (pr.D == 128 && !split) {  // dV, then dK: one pass does not fit TMEM
+    const int rc =
+        run_dkdv<DkvCfg<128, 32, 1, 3, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+    if (rc != CT_OK) return rc;
+    return run_dkdv<DkvCfg<128, 32, 1, 3, 2, kDkvOnlyDk>>(pr, q, k, v, g, lse, ls, delta, dk, dv,
+                                                          dev, st);
+  }
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
 

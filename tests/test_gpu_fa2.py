@@ -75,7 +75,7 @@ def test_baseline_config1(cuda_device, prec, causal):
 @pytest.mark.gpu
 @pytest.mark.parametrize("prec", PRECISIONS)
 @pytest.mark.parametrize("T,D", [(1, 64), (15, 64), (17, 32), (127, 64), (129, 64), (200, 32),
-                                 (300, 128)])
+                                 (300, 128), (1000, 128)])
 def test_ragged_lengths(cuda_device, prec, T, D):
     q, k, v, do = (_rand((1, 3, T, D), 10 + s, cuda_device) for s in range(4))
     for causal in (True, False):
