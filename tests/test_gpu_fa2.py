@@ -111,11 +111,12 @@ def test_golden_vectors(cuda_device):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
-def test_no_out_of_bounds_writes(cuda_device, prec):
+@pytest.mark.parametrize("D", [64, 128])
+def test_no_out_of_bounds_writes(cuda_device, prec, D):
     """Outputs placed inside guard bands of NaN sentinels; ragged T so the last
     tiles are partial.  compute-sanitizer is not available on this pool, so the
     guard bands stand in for it."""
-    B, Hh, T, D = 2, 3, 200, 64
+    B, Hh, T = 2, 3, 200
     q, k, v, do = (_rand((B, Hh, T, D), 30 + s, cuda_device) for s in range(4))
     pad = 4096
     numel = B * Hh * T * D
@@ -147,9 +148,10 @@ def test_no_out_of_bounds_writes(cuda_device, prec):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("prec", PRECISIONS)
-def test_deterministic(cuda_device, prec):
+@pytest.mark.parametrize("D", [64, 128])
+def test_deterministic(cuda_device, prec, D):
     """Atomics-free backward: bit-identical results run to run."""
-    q, k, v, do = (_rand((2, 4, 384, 64), 40 + s, cuda_device) for s in range(4))
+    q, k, v, do = (_rand((2, 4, 384, D), 40 + s, cuda_device) for s in range(4))
     o1, l1 = H.fa2_fwd(q, k, v, True, prec)
     g1 = H.fa2_bwd(q, k, v, o1, do, l1, True, prec)
     o2, l2 = H.fa2_fwd(q, k, v, True, prec)
