@@ -1,14 +1,14 @@
 // fa2_simt.cu -- FlashAttention-2 forward and backward on the CUDA cores in
-// FP32 (FFMA).  Serves head dims the tensor-core backward does not cover yet
-// (D = 128) and the CT_PRECISION_FP32 mode.  Same math as
-// Transformer_kernels/flash_attention.cuh (fwd :27-170, dq :216-354,
+// FP32 (FFMA).  Serves the CT_PRECISION_FP32 mode and the head-dim-128
+// backward in 3xTF32 mode (which the tensor-core kernels do not cover).  Same
+// math as Transformer_kernels/flash_attention.cuh (fwd :27-170, dq :216-354,
 // dk_dv :357-504) including the causal tile skip in all three passes.
 //
-// Layout: a CTA owns a block of stationary rows (forward: 16, one warp per row
-// at a time; backward: 32, eight per warp at once); the streamed K/V (or Q/dO)
-// tile of 32 rows sits in shared memory with a padded row pitch (D + 1) so lane
-// j reading row j hits distinct banks.  Lane j owns column j of the 32-wide
-// score tile; head-dim outputs are spread over lanes (d = lane + 32 * i).
+// Layout: a CTA owns 32 stationary rows, eight per warp taken together; the
+// streamed K/V (or Q/dO) tile of 32 rows sits in shared memory with a padded
+// row pitch (D + 1) so lane j reading row j hits distinct banks.  Lane j owns
+// column j of the 32-wide score tile; head-dim outputs are spread over lanes
+// (d = lane + 32 * i).
 #include <cmath>
 
 #include "ct_internal.h"
@@ -16,7 +16,6 @@
 namespace ct {
 namespace {
 
-constexpr int kSRows = 16;     // stationary rows per CTA (forward)
 constexpr int kSWarps = 4;
 constexpr int kSTile = 32;     // streamed rows per tile
 
@@ -39,82 +38,9 @@ struct P4 {
   }
 };
 
-// Loads rows [t0, t0 + n) of a [B,H,T,D] tensor into smem[n][D + 1].
-template <int D>
-__device__ __forceinline__ void stage_rows(float* sm, const P4& t, int64_t b, int64_t h, int t0,
-                                           int n, int T) {
-  for (int e = threadIdx.x; e < n * D; e += blockDim.x) {
-    const int r = e / D, d = e % D;
-    sm[r * (D + 1) + d] = (t0 + r < T) ? t.at(b, h, t0 + r, d) : 0.0f;
-  }
-}
-
-template <int D>
-__global__ void __launch_bounds__(kSWarps * 32)
-    fa2_fwd_simt_kernel(P4 q, P4 k, P4 v, float* __restrict__ o, float* __restrict__ lse, int H,
-                        int T, int causal, float scale) {
-  constexpr int DL = D / 32;
-  __shared__ float qs[kSRows * (D + 1)];
-  __shared__ float ks[kSTile * (D + 1)];
-  __shared__ float vs[kSTile * (D + 1)];
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.x * kSRows;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  stage_rows<D>(qs, q, b, h, q0, kSRows, T);
-  float acc[kSRows / kSWarps][DL];
-  float m[kSRows / kSWarps], l[kSRows / kSWarps];
-#pragma unroll
-  for (int i = 0; i < kSRows / kSWarps; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.0f;
-#pragma unroll
-    for (int c = 0; c < DL; ++c) acc[i][c] = 0.0f;
-  }
-  const int last = min(q0 + kSRows - 1, T - 1);
-  const int kv_end = causal ? last + 1 : T;
-  for (int kv0 = 0; kv0 < kv_end; kv0 += kSTile) {
-    __syncthreads();
-    stage_rows<D>(ks, k, b, h, kv0, kSTile, T);
-    stage_rows<D>(vs, v, b, h, kv0, kSTile, T);
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kSRows / kSWarps; ++i) {
-      const int r = warp + kSWarps * i, row = q0 + r;
-      const int kv = kv0 + lane;
-      float s = 0.0f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) s += qs[r * (D + 1) + d] * ks[lane * (D + 1) + d];
-      s *= scale;
-      if (!(kv < T && (!causal || kv <= row))) s = -INFINITY;
-      const float mn = fmaxf(m[i], wmax(s));
-      const float p = (mn == -INFINITY) ? 0.0f : expf(s - mn);
-      const float alpha = (m[i] == -INFINITY) ? 0.0f : expf(m[i] - mn);
-      l[i] = l[i] * alpha + wsum(p);
-      m[i] = mn;
-#pragma unroll
-      for (int c = 0; c < DL; ++c) acc[i][c] *= alpha;
-      for (int j = 0; j < kSTile; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-#pragma unroll
-        for (int c = 0; c < DL; ++c) acc[i][c] += pj * vs[j * (D + 1) + lane + 32 * c];
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kSRows / kSWarps; ++i) {
-    const int row = q0 + warp + kSWarps * i;
-    if (row < T) {
-      float* orow = o + ((int64_t)bh * T + row) * D;
-#pragma unroll
-      for (int c = 0; c < DL; ++c) orow[lane + 32 * c] = acc[i][c] / l[i];
-      if (lane == 0) lse[(int64_t)bh * T + row] = m[i] + logf(l[i]);
-    }
-  }
-}
-
 P4 to_p4_(const Strided4& t) { return P4{t.ptr, t.s[0], t.s[1], t.s[2], t.s[3]}; }
 
-// ------------------------------------------------------------------ backward
+// ---------------------------------------------------------- shared layout
 // 32 stationary rows per CTA, 8 per warp computed together: per head-dim step
 // a lane reads its streamed row once (padded pitch, conflict-free) and the
 // warp's 8 stationary rows as float4 broadcasts, so a shared-memory load feeds
@@ -191,6 +117,92 @@ __device__ __forceinline__ void accum8(const float* __restrict__ w, const float*
         acc[i][c] = fmaf(q.z, m[2][c], acc[i][c]);
         acc[i][c] = fmaf(q.w, m[3][c], acc[i][c]);
       }
+    }
+  }
+}
+
+// s[i] += A[i] . x over the head dim (8 stationary rows A, pitch D, broadcast;
+// this lane's streamed row x, pitch D + 1).
+template <int D>
+__device__ __forceinline__ void dot8(const float* __restrict__ A, const float* __restrict__ x,
+                                     float (&s)[kBWarpRows]) {
+#pragma unroll 4
+  for (int d = 0; d < D; d += 4) {
+    const float x0 = x[d], x1 = x[d + 1], x2 = x[d + 2], x3 = x[d + 3];
+#pragma unroll
+    for (int i = 0; i < kBWarpRows; ++i) {
+      const float4 a = *reinterpret_cast<const float4*>(A + i * D + d);
+      s[i] = fmaf(a.x, x0, s[i]); s[i] = fmaf(a.y, x1, s[i]);
+      s[i] = fmaf(a.z, x2, s[i]); s[i] = fmaf(a.w, x3, s[i]);
+    }
+  }
+}
+
+// O, LSE per 32 query rows with the online softmax (reference
+// flash_attention_fwd_kernel, :27-170): the warp's 8 rows take each K/V tile
+// together; P goes through the warp's buffer into the O accumulation.
+template <int D>
+__global__ void __launch_bounds__(kSWarps * 32)
+    fa2_fwd_simt_kernel(P4 q, P4 k, P4 v, float* __restrict__ o, float* __restrict__ lse, int H,
+                        int T, int causal, float scale) {
+  using L = SimtBwdSmem<D>;
+  constexpr int DL = D / 32, R = kBWarpRows;
+  extern __shared__ __align__(16) float sm_simt[];
+  float* qs = sm_simt;
+  float* ks = qs + L::ST;
+  float* vs = ks + L::SM;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float* pw = vs + L::SM + warp * L::WB;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int q0 = blockIdx.x * kBRows;
+  stage_rows_p<D, D>(qs, q, b, h, q0, kBRows, T);
+  const float* qw = qs + warp * R * D;
+  float acc[R][DL], m[R], l[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DL; ++c) acc[i][c] = 0.0f;
+  }
+  const int last = min(q0 + kBRows - 1, T - 1);
+  const int kv_end = causal ? last + 1 : T;
+  for (int kv0 = 0; kv0 < kv_end; kv0 += kSTile) {
+    __syncthreads();
+    stage_rows_p<D, D + 1>(ks, k, b, h, kv0, kSTile, T);
+    stage_rows_p<D, D + 1>(vs, v, b, h, kv0, kSTile, T);
+    __syncthreads();
+    float s[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) s[i] = 0.0f;
+    dot8<D>(qw, ks + lane * (D + 1), s);
+    const int kv = kv0 + lane;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int row = q0 + warp * R + i;
+      float si = s[i] * scale;
+      if (!(kv < T && (!causal || kv <= row))) si = -INFINITY;
+      const float mn = fmaxf(m[i], wmax(si));
+      const float p = (mn == -INFINITY) ? 0.0f : expf(si - mn);
+      const float alpha = (m[i] == -INFINITY) ? 0.0f : expf(m[i] - mn);
+      l[i] = l[i] * alpha + wsum(p);
+      m[i] = mn;
+#pragma unroll
+      for (int c = 0; c < DL; ++c) acc[i][c] *= alpha;
+      pw[i * kSTile + lane] = p;
+    }
+    __syncwarp();
+    accum8<D>(pw, vs, acc, lane);
+    __syncwarp();
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const int row = q0 + warp * R + i;
+    if (row < T) {
+      float* orow = o + ((int64_t)bh * T + row) * D;
+#pragma unroll
+      for (int c = 0; c < DL; ++c) orow[lane + 32 * c] = acc[i][c] / l[i];
+      if (lane == 0) lse[(int64_t)bh * T + row] = m[i] + logf(l[i]);
     }
   }
 }
@@ -353,6 +365,19 @@ int simt_smem_attr(K kernel, size_t bytes, unsigned long long* done) {
 }
 
 template <int D>
+int run_fwd_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, float* o, float* lse,
+                 int c, float scale, dim3 g, cudaStream_t st) {
+  static unsigned long long done = 0;
+  using L = SimtBwdSmem<D>;
+  const size_t smem = (size_t)(L::ST + 2 * L::SM + kSWarps * L::WB) * sizeof(float);
+  const int rc = simt_smem_attr(fa2_fwd_simt_kernel<D>, smem, &done);
+  if (rc != CT_OK) return rc;
+  fa2_fwd_simt_kernel<D><<<g, kSWarps * 32, smem, st>>>(to_p4_(q), to_p4_(k), to_p4_(v), o, lse,
+                                                       (int)p.H, (int)p.T, c, scale);
+  return check_launch();
+}
+
+template <int D>
 int run_dq_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
                 const float* lse, const int64_t ls[3], const float* delta, float* dq, int c,
                 float scale, dim3 g, cudaStream_t st) {
@@ -393,15 +418,14 @@ int launch_fa2_fwd_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v,
                         float* lse, cudaStream_t st) {
   if (p.B * p.H > 65535) return CT_ERR_INVALID_ARGUMENT;
   const float scale = (float)(1.0 / std::sqrt((double)p.D));
-  const dim3 g = simt_grid(p, kSRows);
+  const dim3 g = simt_grid(p, kBRows);
   const int c = p.causal ? 1 : 0;
   switch (p.D) {
-    case 32: fa2_fwd_simt_kernel<32><<<g, kSWarps * 32, 0, st>>>(to_p4(q), to_p4(k), to_p4(v), o, lse, (int)p.H, (int)p.T, c, scale); break;
-    case 64: fa2_fwd_simt_kernel<64><<<g, kSWarps * 32, 0, st>>>(to_p4(q), to_p4(k), to_p4(v), o, lse, (int)p.H, (int)p.T, c, scale); break;
-    case 128: fa2_fwd_simt_kernel<128><<<g, kSWarps * 32, 0, st>>>(to_p4(q), to_p4(k), to_p4(v), o, lse, (int)p.H, (int)p.T, c, scale); break;
+    case 32: return run_fwd_simt<32>(p, q, k, v, o, lse, c, scale, g, st);
+    case 64: return run_fwd_simt<64>(p, q, k, v, o, lse, c, scale, g, st);
+    case 128: return run_fwd_simt<128>(p, q, k, v, o, lse, c, scale, g, st);
     default: return CT_ERR_UNSUPPORTED_HEAD_DIM;
   }
-  return check_launch();
 }
 
 int launch_fa2_bwd_dq_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
