@@ -537,9 +537,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // V, S^T, dP^T -> dS^T, dK; no dV), each reading the same streamed tiles.
 constexpr int kDkvBoth = 0, kDkvOnlyDv = 1, kDkvOnlyDk = 2;
 
+// A single-gradient pass keeps only the layouts it reads: the dV pass no
+// MN-major Q (dK's operand), the dK pass no MN-major dO (dV's operand).
 template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1, int PASS_ = kDkvBoth>
-struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true> {
-  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, 2, 2, true, true>;
+struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, PASS_ == kDkvOnlyDv ? 1 : 2,
+                         PASS_ == kDkvOnlyDk ? 1 : 2, true, true> {
+  using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, PASS_ == kDkvOnlyDv ? 1 : 2,
+                      PASS_ == kDkvOnlyDk ? 1 : 2, true, true>;
   // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
   // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
   // and dS_i, so the rows go from one step to the next without waiting.
@@ -957,9 +961,9 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
                  : run_dkdv<DkvCfg<32, 128, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
   if (pr.D == 128 && !split) {  // dV, then dK: one pass does not fit TMEM
     const int rc =
-        run_dkdv<DkvCfg<128, 32, 1, 3, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+        run_dkdv<DkvCfg<128, 32, 1, 4, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
     if (rc != CT_OK) return rc;
-    return run_dkdv<DkvCfg<128, 32, 1, 3, 2, kDkvOnlyDk>>(pr, q, k, v, g, lse, ls, delta, dk, dv,
+    return run_dkdv<DkvCfg<128, 32, 1, 4, 2, kDkvOnlyDk>>(pr, q, k, v, g, lse, ls, delta, dk, dv,
                                                           dev, st);
   }
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
