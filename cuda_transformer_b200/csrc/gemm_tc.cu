@@ -619,8 +619,9 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
 
 // Tile width: BN = 256 has no TMEM left for a running sum, so K beyond one
 // accumulation chunk is folded in L2 (at most four chunks, TMA-storable
-// output, no split-K); otherwise the choice minimises (waves of tiles) x (tile cost), a 128-wide tile costing a
-// little more than half a 256-wide one (x re-read, per-tile overhead).  The
+// output, no split-K); otherwise the choice minimises (waves of tiles) x (tile
+// cost), a 128-wide tile costing a little more than half a 256-wide one (x
+// re-read, per-tile overhead).  The
 // environment variable CT_GEMM_BN (128 or 256) overrides it (tuning).
 int pick_bn(const GemmProblem& g, int sms) {
   const int64_t kb = (g.k + kBK - 1) / kBK;
@@ -639,7 +640,11 @@ int pick_bn(const GemmProblem& g, int sms) {
     const int64_t waves = (tile_count(g, bn) + sms - 1) / sms;
     return (double)waves * rel;
   };
-  return cost(256, 1.0) <= cost(128, 0.59) ? 256 : 128;
+  // Relative cost of a 128-wide tile, measured on the linear layer's shapes
+  // (M = 16384, K = 384 / 1536): 3xTF32's BN = 256 ring holds only two stages,
+  // so there the narrow tile costs relatively less.
+  const double rel128 = g.precision == CT_PRECISION_3XTF32 ? 0.53 : 0.59;
+  return cost(256, 1.0) <= cost(128, rel128) ? 256 : 128;
 }
 
 }  // namespace
