@@ -76,6 +76,8 @@ def test_invalid_arguments_rejected_before_any_device_work():
     # LayerNorm rows are at most 8192 wide
     rc = lib.ct_layernorm_fwd(None, None, None, None, None, None, 1, 8193, ctypes.c_float(1e-5), None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
+    rc = lib.ct_layernorm_bwd(None, None, None, None, None, None, None, None, 1, 8193, None, 0, None)
+    assert rc == cb.CT_ERR_INVALID_ARGUMENT
 
 
 def test_torch_schemas_match_reference():
