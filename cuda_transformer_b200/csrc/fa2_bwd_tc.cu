@@ -583,10 +583,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n = j1 - j0;
 
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
-  // by warp 10): the merged stage is free after both have committed.  The dV
-  // pass has no warp-10 work.
-  constexpr int kIssuers = C::DO_DK ? 2 : 1;
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, kIssuers, kIssuers, 8);
+  // by warp 10; in the dV pass S^T_i by warp 1, dV_i by warp 10): the merged
+  // stage is free after both have committed.
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -606,6 +605,57 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const CUtensorMap* maps[2] = {&tmQ, &tmG};
     bwd_producer<C, true, true>(bars, tiles, vec, maps, j0, j1, h, b, p.lse + b * p.l0 + h * p.l1,
                           p.l2, p.delta + (int64_t)bh * T, T, p.status);
+  } else if (C::PASS == kDkvOnlyDv && (warp == 1 || warp == kIssuer2Warp)) {
+    // dV pass, two issuing threads.  Warp 1: S^T_{i+NSB} into buffer i % NSB
+    // once dV_i has read P_i from it (dqd[b], committed by warp 10).  Warp 10:
+    // [P_i ready, dO_i MN-major ready]  dV += P_i^T dO_i -> dqd[b].
+    if (lane == 0) {
+      auto issue_S = [&](int i) {
+        const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
+        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
+                                                tmem + C::TC_K + D,
+                                                sdesc_kmajor(tiles + C::OFF_A0) + stg(i), idS,
+                                                false);
+        umma_commit(B(bars->s_full[i % C::NSB]));
+      };
+      const uint32_t fin = B(warp == 1 ? bars->mma_final : bars->mma_final2);
+      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      if (warp == 1) {
+        for (int i = 0; ok && i < C::NSB && i < n; ++i) {
+          if ((ok = mbar_wait(B(rdy[i % NS]), (i / NS) & 1, ctl, p.status))) {
+            tc_fence_after();
+            issue_S(i);
+          }
+        }
+        for (int i = 0; ok && i < n; ++i) {
+          const int bi = i % C::NSB, nx = i + C::NSB;
+          umma_commit(B(bars->empty_a[i % NS]));  // S^T_i, issued earlier, read Q_i
+          if (nx < n) {
+            if (!(ok = mbar_wait(B(bars->dqd[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
+            if (!(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            issue_S(nx);
+          }
+        }
+      } else {
+        const uint64_t gmd0 = sdesc_mnmajor(tiles + C::OFF_B1, BN * 128);
+        for (int i = 0; ok && i < n; ++i) {
+          const int bi = i % C::NSB;
+          if (!(ok = mbar_wait(B(bars->p_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
+          mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
+              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+          umma_commit(B(bars->dqd[bi]));
+          umma_commit(B(bars->empty_a[i % NS]));
+        }
+      }
+      if (ok) umma_commit(B(bars->done));
+      umma_commit(fin);  // nothing of this thread in flight after this
+      mbar_drain(fin, 0);
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // Step i of buffer b = i % NSB:  [P_i ready, tiles i+NSB prepared]
     //   dV += P_i^T dO_i;  S^T_{i+NSB} -> s_full[b]
