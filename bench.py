@@ -20,8 +20,9 @@ TF32-mode run beside the default FP32-accurate (3xTF32) one.
 
 --impl reference times the reference's math path on the host CPU (torch's
 fused CPU attention kernel, forward with log-sum-exp plus autograd backward,
-all host threads) on a bounded sample of the same workload; under torchrun
-only rank 0 runs it.
+all host threads) over the same workload (all 128 pairs): W warm-up steps,
+then exactly K timed steps, median reported; under torchrun only rank 0 runs
+it.
 """
 from __future__ import annotations
 
@@ -46,6 +47,8 @@ METRIC = "FA2 fwd+bwd TFLOPS (B4,H32,N4096,D64) at 1/2/4/8 B200; % of TF32 peak"
 # DRAM bytes of one 3xTF32 dK/dV launch at config 2 (ncu capture at half size, x2) and the
 # kernel's algorithmic bytes: reads Q, K, V, dO (4 x 128 MiB) + LSE, delta, writes dK, dV.
 DKDV_TRAFFIC_BYTES = 2 * 377.0e6
+# the dK/dV kernel instance that capture measured (recaptured whenever it changes)
+DKDV_TRAFFIC_KERNEL = "fa2_bwd_dkdv_tc_kernel<DkvCfg<64, 32, 3, 3>> (3xTF32, D = 64)"
 DKDV_ALGO_BYTES = 4 * 134217728 + 2 * 2097152 + 2 * 134217728
 WORKLOAD = "FA2 fwd+bwd B4 H32 N4096 D64 causal fp32 (BASELINE config 2)"
 
@@ -181,11 +184,13 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- CPU side
-def cpu_reference_throughput(pairs: int, min_seconds: float, max_steps: int | None = None,
-                             threads: int | None = None) -> dict:
+def cpu_reference_throughput(pairs: int, min_seconds: float = 0.0, steps: int | None = None,
+                             warmup: int = 1, threads: int | None = None) -> dict:
     """The reference's FP32 math path on the host: torch's fused CPU attention
-    forward (with log-sum-exp) and autograd backward, one (batch, head) slice
-    of `pairs` pairs at N=4096, D=64, causal, repeated for >= min_seconds."""
+    forward (with log-sum-exp) and autograd backward over one (batch, head)
+    slice of `pairs` pairs at N=4096, D=64, causal.  After `warmup` untimed
+    steps it times exactly `steps` steps when given, else steps until
+    `min_seconds` have passed, and reports the median step."""
     import torch
 
     from oracle.torch_ref import cpu_flash_fwd_bwd
@@ -196,32 +201,40 @@ def cpu_reference_throughput(pairs: int, min_seconds: float, max_steps: int | No
     q, k, v, do = (torch.randn(1, pairs, N, D, generator=g) for _ in range(4))
     for t in (q, k, v):
         t.requires_grad_(True)
-    cpu_flash_fwd_bwd(q, k, v, do, CAUSAL)  # warm-up
-    steps, t0 = 0, time.perf_counter()
-    times = []
-    while True:
+
+    def one():
         for t in (q, k, v):
             t.grad = None
         s0 = time.perf_counter()
         cpu_flash_fwd_bwd(q, k, v, do, CAUSAL)
-        times.append(time.perf_counter() - s0)
-        steps += 1
-        if time.perf_counter() - t0 >= min_seconds or (max_steps and steps >= max_steps):
+        return time.perf_counter() - s0
+
+    for _ in range(max(warmup, 1)):
+        one()
+    times, t0 = [], time.perf_counter()
+    while True:
+        times.append(one())
+        if steps is not None:
+            if len(times) >= steps:
+                break
+        elif time.perf_counter() - t0 >= min_seconds:
             break
     per = statistics.median(times)
     tflops = fa2_flops(pairs, N, D, CAUSAL, "fwd+bwd") / per / 1e12
     return {"value": tflops, "unit": "TFLOPS", "cores": torch.get_num_threads(),
-            "seconds_per_step": per, "steps": steps,
-            "sample": f"{pairs} of 128 (b,h) pairs at N={N}, D={D}, causal, fwd+bwd, "
-                      f"torch CPU fused attention (FP32), median of {steps} steps"}
+            "seconds_per_step": per, "steps": len(times),
+            "sample": f"{pairs} of {PAIRS} (b,h) pairs at N={N}, D={D}, causal, fwd+bwd, "
+                      f"torch CPU fused attention (FP32), median of {len(times)} timed steps"}
 
 
 def run_reference_arm(args) -> None:
+    """The reference's FP32 math path (the CPU implementation its tests use)
+    on all host threads, over the whole workload (all 128 (b,h) pairs): W
+    untimed warm-up steps, then exactly K timed steps, median reported."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    pairs = 8
-    res = cpu_reference_throughput(pairs, min_seconds=0.0, max_steps=args.steps + args.warmup,
+    res = cpu_reference_throughput(PAIRS, steps=args.steps, warmup=args.warmup,
                                    threads=os.cpu_count())
     out = {
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "TFLOPS",
@@ -229,7 +242,7 @@ def run_reference_arm(args) -> None:
         "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,1), seeded",
         "config": {"workload": WORKLOAD, "B": B_FULL, "H": H_FULL, "N": N, "D": D,
-                   "causal": CAUSAL, "sample_pairs": pairs},
+                   "causal": CAUSAL, "sample_pairs": PAIRS},
         "cpu_baseline": {"value": res["value"], "unit": "TFLOPS", "cores": res["cores"],
                          "kind": "port", "sample": res["sample"]},
         "e2e": {"value": res["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 0,
@@ -523,16 +536,16 @@ def main() -> None:
                 "peak_source": f"{pk['source']} bf16 burst {pk['bf16_tflops']} / 2 (dense TF32 = half BF16 rate)",
                 "traffic": DKDV_TRAFFIC_BYTES if (top == "fa2_bwd_dkdv" and prec == cb.PRECISION_3XTF32
                                                   and world == 1) else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one dK/dV "
-                                  "launch at B4 H16 (64 pairs, 377 MB), scaled x2 to the 128 pairs "
-                                  "of a launch here (profiles/fa2_kernels_B4H32N4096D64_causal_3xtf32.md)",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 3xTF32 "
+                                  "dK/dV launch at B4 H16 (64 pairs), scaled x2 to the 128 pairs of "
+                                  "a launch here; captured on " + DKDV_TRAFFIC_KERNEL,
                 "algorithmic_bytes": DKDV_ALGO_BYTES,
                 "algorithmic_flop_per_launch": algo[top], "launch_ms": kern[top]}
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            r = cpu_reference_throughput(8, min_seconds=args.cpu_seconds)
+            r = cpu_reference_throughput(8, min_seconds=args.cpu_seconds, threads=os.cpu_count())
             cpu = {"value": r["value"], "unit": "TFLOPS", "cores": r["cores"], "kind": "port",
                    "sample": r["sample"]}
         out = {

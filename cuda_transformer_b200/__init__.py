@@ -29,6 +29,9 @@ PRECISION_3XTF32 = 0
 PRECISION_TF32 = 1
 PRECISION_FP32 = 2
 CT_FA2_BWD_NOALLOC_MAX_ROWS = 2097152  # batch * heads * seq_len limit of ct_fa2_bwd_noalloc
+CT_DEVSTAT_TIMEOUT = 1  # watchdog word bit: a bounded device-side wait ran out
+CT_WAIT_LIMIT_MIN_NS = 100000
+CT_WAIT_LIMIT_MAX_NS = 60000000000
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _fp = ctypes.c_void_p
@@ -68,8 +71,9 @@ SIGNATURES = {
     "ct_layernorm_bwd_workspace_size": ([_i64, _i64], _sz),
     "ct_layernorm_bwd": ([_fp, _fp, _fp, _fp, _fp, _fp, _fp, _fp, _i64, _i64, _fp, _sz, _fp],
                          _int),
-    "ct_diag_umma_tf32": ([_int, _fp, _fp, _fp, _int, _fp], _int),
-    "ct_diag_mma_rate": ([_int, _int, _int, _int, _fp, _fp], _int),
+    "ct_set_wait_limit_ns": ([_int, ctypes.c_ulonglong], _int),
+    "ct_get_wait_limit_ns": ([_int, ctypes.POINTER(ctypes.c_ulonglong)], _int),
+    "ct_watchdog_selftest": ([_fp], _int),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -102,6 +106,17 @@ def status_string(rc: int) -> str:
 def check(rc: int, what: str = "ct call") -> None:
     if rc != CT_OK:
         raise RuntimeError(f"{what}: {status_string(rc)} (status {rc})")
+
+
+def set_wait_limit_ns(device: int, limit_ns: int) -> None:
+    """Limit of every bounded device-side wait on `device` (default 2 s)."""
+    check(lib().ct_set_wait_limit_ns(device, limit_ns), "ct_set_wait_limit_ns")
+
+
+def wait_limit_ns(device: int = 0) -> int:
+    v = ctypes.c_ulonglong(0)
+    check(lib().ct_get_wait_limit_ns(device, ctypes.byref(v)), "ct_get_wait_limit_ns")
+    return int(v.value)
 
 
 def device_status(device: int = 0, clear: bool = False) -> int:

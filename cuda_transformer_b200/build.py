@@ -5,6 +5,9 @@
   CUDA runtime linked statically, no torch dependency.
 * ``cuda_transformer/_C<ext>`` -- the PyTorch operator registrations
   (``torch.ops.cuda_transformer.*``); a thin C++ shim over the C ABI.
+* ``tests/diag/libct_diag.so`` -- TEST-ONLY diagnostics (operand-layout checks
+  and a tensor-pipe throughput probe, ``tests/diag/ct_diag.h``); not linked
+  into or loaded by the product.
 
 Objects go to ``cuda_transformer_b200/_build``; a translation unit is rebuilt
 when it, or any header next to it, is newer than its object.
@@ -29,6 +32,9 @@ LIB = PKG / "lib" / "libct_b200.so"
 INCLUDE = ROOT / "include"
 TORCH_EXT_SRC = CSRC / "torch_ext" / "ops.cpp"
 TORCH_EXT_OUT = ROOT / "cuda_transformer" / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+DIAG_DIR = ROOT / "tests" / "diag"
+DIAG_SRC = DIAG_DIR / "ct_diag.cu"
+DIAG_LIB = DIAG_DIR / "libct_diag.so"
 
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
@@ -108,9 +114,21 @@ def build_torch_ext(force: bool = False) -> Path:
     return TORCH_EXT_OUT
 
 
+def build_diag(force: bool = False) -> Path | None:
+    """Test-only diagnostics library (absent from a product-only checkout)."""
+    if not DIAG_SRC.exists():
+        return None
+    deps = [DIAG_SRC, DIAG_DIR / "ct_diag.h", *_headers()]
+    if force or _stale(DIAG_LIB, deps):
+        _run([NVCC, *NVCC_FLAGS, "-I", str(DIAG_DIR), "-shared", "-cudart", "static",
+              str(DIAG_SRC), "-o", str(DIAG_LIB)])
+    return DIAG_LIB
+
+
 def build_all(force: bool = False, jobs: int | None = None) -> None:
     build_core(force, jobs)
     build_torch_ext(force)
+    build_diag(force)
 
 
 def main() -> None:

@@ -8,10 +8,12 @@
 #include <mutex>
 
 #include "ct_internal.h"
+#include "tc_ptx.cuh"
 
 namespace {
-// Watchdog word: bounded device-side waits OR CT_DEVSTAT_* bits into it.
-__device__ uint32_t g_ct_device_status;
+// Watchdog block: bounded device-side waits OR CT_DEVSTAT_* bits into its
+// status word and give up after its limit_ns.
+__device__ ct::WatchBlock g_ct_watch = {0u, 0u, CT_WAIT_TIMEOUT_NS};
 }  // namespace
 
 namespace ct {
@@ -57,7 +59,7 @@ const DeviceInfo* current_device(int* err) {
       return nullptr;
     }
     void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, g_ct_device_status) != cudaSuccess) {
+    if (cudaGetSymbolAddress(&addr, g_ct_watch) != cudaSuccess) {
       *err = CT_ERR_CUDA;
       return nullptr;
     }
@@ -103,35 +105,36 @@ int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* 
   return r == CUDA_SUCCESS ? CT_OK : CT_ERR_UNSUPPORTED_LAYOUT;
 }
 
-namespace {
-
-inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
-
 bool fa2_shape_ok(int64_t B, int64_t H, int64_t T, int64_t D) {
-  return B >= 0 && H >= 0 && T >= 0 && D > 0 && T < (1ll << 31) && B * H < (1ll << 31);
+  constexpr int64_t kLim = 1ll << 31;
+  return B >= 0 && H >= 0 && T >= 0 && D > 0 && T < kLim && B < kLim && H < kLim &&
+         B * H < kLim;
 }
 
 bool valid_precision(int p) {
   return p == CT_PRECISION_3XTF32 || p == CT_PRECISION_TF32 || p == CT_PRECISION_FP32;
 }
 
-Strided4 s4(const float* p, const int64_t* s) {
-  Strided4 t;
-  t.ptr = p;
-  for (int i = 0; i < 4; ++i) t.s[i] = s[i];
-  return t;
+int fa2_validate(int64_t B, int64_t H, int64_t T, int64_t D, int precision) {
+  if (!fa2_shape_ok(B, H, T, D) || !valid_precision(precision)) return CT_ERR_INVALID_ARGUMENT;
+  if (!(D == 32 || D == 64 || D == 128)) return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  return CT_OK;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Common preamble of every FA2 entry point.
 int fa2_prelude(int64_t B, int64_t H, int64_t T, int64_t D, int precision, const DeviceInfo** dev) {
-  if (!fa2_shape_ok(B, H, T, D) || !valid_precision(precision)) return CT_ERR_INVALID_ARGUMENT;
-  if (!(D == 32 || D == 64 || D == 128)) return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  const int rc = fa2_validate(B, H, T, D, precision);
+  if (rc != CT_OK) return rc;
   int err = CT_OK;
   *dev = current_device(&err);
   return err;
 }
+
+}  // namespace
 
 int fa2_dq_dispatch(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
                     const float* lse, const int64_t* ls, const float* delta, float* dq,
@@ -149,7 +152,6 @@ int fa2_dkdv_dispatch(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, S
   return launch_fa2_bwd_dkdv_simt(p, q, k, v, g, lse, ls, delta, dk, dv, st);
 }
 
-}  // namespace
 }  // namespace ct
 
 using namespace ct;
@@ -191,6 +193,48 @@ int ct_device_status(int device, int clear, unsigned int* flag_out) {
   cudaSetDevice(prev);
   *flag_out = v;
   return err;
+}
+
+int ct_set_wait_limit_ns(int device, unsigned long long limit_ns) {
+  if (limit_ns < CT_WAIT_LIMIT_MIN_NS || limit_ns > CT_WAIT_LIMIT_MAX_NS)
+    return CT_ERR_INVALID_ARGUMENT;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return CT_ERR_CUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return CT_ERR_CUDA;
+  int err = CT_OK;
+  const DeviceInfo* dev = current_device(&err);
+  if (err == CT_OK) {
+    auto* blk = reinterpret_cast<WatchBlock*>(dev->status);
+    if (cudaMemcpy(&blk->limit_ns, &limit_ns, sizeof(limit_ns), cudaMemcpyHostToDevice) !=
+        cudaSuccess)
+      err = CT_ERR_CUDA;
+  }
+  cudaSetDevice(prev);
+  return err;
+}
+
+int ct_get_wait_limit_ns(int device, unsigned long long* limit_ns) {
+  if (!limit_ns) return CT_ERR_INVALID_ARGUMENT;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return CT_ERR_CUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return CT_ERR_CUDA;
+  int err = CT_OK;
+  const DeviceInfo* dev = current_device(&err);
+  if (err == CT_OK) {
+    const auto* blk = reinterpret_cast<const WatchBlock*>(dev->status);
+    if (cudaMemcpy(limit_ns, &blk->limit_ns, sizeof(*limit_ns), cudaMemcpyDeviceToHost) !=
+        cudaSuccess)
+      err = CT_ERR_CUDA;
+  }
+  cudaSetDevice(prev);
+  return err;
+}
+
+int ct_watchdog_selftest(void* stream) {
+  int err = CT_OK;
+  const DeviceInfo* dev = current_device(&err);
+  if (err != CT_OK) return err;
+  return launch_watchdog_selftest(*dev, as_stream(stream));
 }
 
 int ct_fa2_fwd(const float* q, const int64_t q_stride[4], const float* k, const int64_t k_stride[4],
@@ -412,21 +456,6 @@ int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean, cons
     return CT_ERR_WORKSPACE_TOO_SMALL;
   return launch_layernorm_bwd(x, gamma, mean, rstd, dy, dx, dgamma, dbeta, rows, n,
                               static_cast<float*>(workspace), as_stream(stream));
-}
-
-int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n, void* stream) {
-  if (!a || !b || !d) return CT_ERR_INVALID_ARGUMENT;
-  int err = CT_OK;
-  const DeviceInfo* dev = current_device(&err);
-  if (err != CT_OK) return err;
-  return launch_diag_umma(mode, a, b, d, n, *dev, as_stream(stream));
-}
-
-int ct_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles, void* stream) {
-  int err = CT_OK;
-  const DeviceInfo* dev = current_device(&err);
-  if (err != CT_OK) return err;
-  return launch_diag_mma_rate(n, flags, reps, blocks, cycles, *dev, as_stream(stream));
 }
 
 }  // extern "C"

@@ -53,6 +53,31 @@ struct Strided4 {
   int64_t s[4];  // batch, head, seq, dim (elements)
 };
 
+// ------------------------------------------ FA2 entry-point validation / dispatch
+// Shared by every FA2 entry point of the C ABI (capi.cu, fa2_bwd_noalloc.cu).
+// Shape check without any CUDA call: sizes non-negative, head_dim positive,
+// T < 2^31 and B*H < 2^31 (each factor bounded before the product is formed,
+// so the product cannot overflow).  After it, B*H*T < 2^62.
+bool fa2_shape_ok(int64_t B, int64_t H, int64_t T, int64_t D);
+bool valid_precision(int p);
+// fa2_shape_ok + precision + head dim in {32, 64, 128} (status, no CUDA call).
+int fa2_validate(int64_t B, int64_t H, int64_t T, int64_t D, int precision);
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline Strided4 s4(const float* p, const int64_t* s) {
+  Strided4 t;
+  t.ptr = p;
+  for (int i = 0; i < 4; ++i) t.s[i] = s[i];
+  return t;
+}
+// dQ / dK-dV launch on the tensor cores when they cover the problem, else on
+// the FP32 CUDA-core kernels.
+int fa2_dq_dispatch(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
+                    const float* lse, const int64_t* ls, const float* delta, float* dq,
+                    const DeviceInfo& dev, cudaStream_t st);
+int fa2_dkdv_dispatch(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
+                      const float* lse, const int64_t* ls, const float* delta, float* dk,
+                      float* dv, const DeviceInfo& dev, cudaStream_t st);
+
 // Kernel launchers (one translation unit each).  All return a ct status.
 int launch_fa2_fwd_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, float* o,
                       float* lse, const DeviceInfo& dev, cudaStream_t st);
@@ -114,10 +139,9 @@ int launch_layernorm_bwd(const float* x, const float* g, const float* mean, cons
                          const float* dy, float* dx, float* dg, float* db, int64_t rows,
                          int64_t n, float* ws, cudaStream_t st);
 
-// -------------------------------------------------------------- diagnostics
-int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
-                     const DeviceInfo& dev, cudaStream_t st);
-int launch_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles,
-                         const DeviceInfo& dev, cudaStream_t st);
+// ------------------------------------------------------------ watchdog
+// One CTA whose waits on a barrier phase that nothing completes run out after
+// the device's wait limit, followed by the kernels' abort teardown.
+int launch_watchdog_selftest(const DeviceInfo& dev, cudaStream_t st);
 
 }  // namespace ct

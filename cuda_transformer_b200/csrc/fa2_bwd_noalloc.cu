@@ -11,14 +11,19 @@
 // The array is a file-scope __device__ variable: every GPU that loads the
 // library holds CT_FA2_BWD_NOALLOC_MAX_ROWS floats (8 MiB) for it until the
 // process exits.  Host code cannot use the array's name as a device address,
-// so the first call on each device looks the address up with
-// cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture.  All calls share the one array and it
-// keeps the previous call's contents; every element a call reads is written by
-// the same call first (the delta kernel fills rows [0, B*H*T) before the
+// so the first call on each device (in each CUDA context) looks the address up
+// with cudaGetSymbolAddress, with that device current, and caches it per
+// context; make that first call before any stream capture.  A call from a
+// different context on the same device (a non-primary driver context, or the
+// primary context re-created after cudaDeviceReset) looks the address up again,
+// because the module is loaded anew there.  All calls share the one array and
+// it keeps the previous call's contents; every element a call reads is written
+// by the same call first (the delta kernel fills rows [0, B*H*T) before the
 // gradient kernels read them), so nothing needs clearing.  Two calls whose
 // work overlaps on the GPU (different streams, no ordering between them) race
 // on the array: order such calls on one stream or with events.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "ct_internal.h"
@@ -28,32 +33,43 @@ namespace {
 __device__ __align__(256) float g_fa2_bwd_delta_scratch[CT_FA2_BWD_NOALLOC_MAX_ROWS];
 
 constexpr int kMaxDevices = 64;
+struct ScratchSlot {
+  CUcontext ctx = nullptr;  // context the cached address belongs to
+  float* addr = nullptr;
+};
 std::mutex g_scratch_mu;
-float* g_scratch_addr[kMaxDevices];
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of the scratch array on the current device (looked up once
-// per device and cached).
+PFN_cuCtxGetCurrent_v4000 g_ctx_get = nullptr;
+std::once_flag g_ctx_get_once;
+
+void load_ctx_get() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+}
+
+// Device address of the scratch array in the current device's current context
+// (looked up once per context and cached).
 int scratch_address(int device, float** out) {
   if (device < 0 || device >= kMaxDevices) return CT_ERR_CUDA;
+  std::call_once(g_ctx_get_once, load_ctx_get);
+  CUcontext ctx = nullptr;
+  if (!g_ctx_get || g_ctx_get(&ctx) != CUDA_SUCCESS || ctx == nullptr) return CT_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[device] == nullptr) {
+  ScratchSlot& slot = g_scratch[device];
+  if (slot.addr == nullptr || slot.ctx != ctx) {
     void* addr = nullptr;
     if (cudaGetSymbolAddress(&addr, g_fa2_bwd_delta_scratch) != cudaSuccess || addr == nullptr)
       return CT_ERR_CUDA;
-    g_scratch_addr[device] = static_cast<float*>(addr);
+    slot.ctx = ctx;
+    slot.addr = static_cast<float*>(addr);
   }
-  *out = g_scratch_addr[device];
+  *out = slot.addr;
   return CT_OK;
 }
-
-ct::Strided4 view4(const float* p, const int64_t* s) {
-  ct::Strided4 t;
-  t.ptr = p;
-  for (int i = 0; i < 4; ++i) t.s[i] = s[i];
-  return t;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
@@ -66,11 +82,10 @@ extern "C" int ct_fa2_bwd_noalloc(const float* q, const int64_t q_stride[4], con
                                   int64_t batch, int64_t heads, int64_t seq_len,
                                   int64_t head_dim, int causal, int precision, void* stream) {
   using namespace ct;
-  if (batch < 0 || heads < 0 || seq_len < 0 || seq_len >= (1ll << 31) ||
-      !(precision == CT_PRECISION_3XTF32 || precision == CT_PRECISION_TF32 ||
-        precision == CT_PRECISION_FP32))
-    return CT_ERR_INVALID_ARGUMENT;
-  if (!(head_dim == 32 || head_dim == 64 || head_dim == 128)) return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  // The same validation as ct_fa2_bwd, before any CUDA call: it bounds B*H and
+  // T, so the row count below cannot overflow.
+  int rc = fa2_validate(batch, heads, seq_len, head_dim, precision);
+  if (rc != CT_OK) return rc;
   const int64_t rows = batch * heads * seq_len;
   if (rows == 0) return CT_OK;
   if (rows > CT_FA2_BWD_NOALLOC_MAX_ROWS) return CT_ERR_WORKSPACE_TOO_SMALL;
@@ -87,14 +102,11 @@ extern "C" int ct_fa2_bwd_noalloc(const float* q, const int64_t q_stride[4], con
 
   const Fa2Problem p{batch, heads, seq_len, head_dim, causal != 0, precision};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const Strided4 tq = view4(q, q_stride), tk = view4(k, k_stride), tv = view4(v, v_stride);
-  const Strided4 tg = view4(d_o, do_stride);
-  int rc = launch_fa2_delta(p, view4(o, o_stride), tg, delta, st);
+  const Strided4 tq = s4(q, q_stride), tk = s4(k, k_stride), tv = s4(v, v_stride);
+  const Strided4 tg = s4(d_o, do_stride);
+  rc = launch_fa2_delta(p, s4(o, o_stride), tg, delta, st);
   if (rc != CT_OK) return rc;
-  const bool tc = precision != CT_PRECISION_FP32 && fa2_bwd_tc_supported(p);
-  rc = tc ? launch_fa2_bwd_dq_tc(p, tq, tk, tv, tg, lse, lse_stride, delta, dq, *dev, st)
-          : launch_fa2_bwd_dq_simt(p, tq, tk, tv, tg, lse, lse_stride, delta, dq, st);
+  rc = fa2_dq_dispatch(p, tq, tk, tv, tg, lse, lse_stride, delta, dq, *dev, st);
   if (rc != CT_OK) return rc;
-  return tc ? launch_fa2_bwd_dkdv_tc(p, tq, tk, tv, tg, lse, lse_stride, delta, dk, dv, *dev, st)
-            : launch_fa2_bwd_dkdv_simt(p, tq, tk, tv, tg, lse, lse_stride, delta, dk, dv, st);
+  return fa2_dkdv_dispatch(p, tq, tk, tv, tg, lse, lse_stride, delta, dk, dv, *dev, st);
 }

@@ -145,6 +145,7 @@ __device__ __forceinline__ bool sem_wait(const uint32_t* sem, uint32_t want, Cta
                                          uint32_t* status) {
   if (ld_acquire_gpu(sem) == want) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   for (uint32_t i = 1;; ++i) {
     __nanosleep(128);
     if (ld_acquire_gpu(sem) == want) return true;
@@ -153,7 +154,7 @@ __device__ __forceinline__ bool sem_wait(const uint32_t* sem, uint32_t want, Cta
         ctl->abort = 1u;
         return false;
       }
-      if (globaltimer_ns() - t0 > CT_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > limit) {
         ctl->abort = 1u;
         atomicOr(status, CT_DEVSTAT_TIMEOUT);
         return false;

@@ -713,8 +713,6 @@ __global__ void __launch_bounds__(256)
   if (row < rows && sub == 0) delta[row] = acc;
 }
 
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
 template <int THREADS, int V>
 int softmax_dispatch_fwd(const float* x, float* y, int64_t rows, int64_t n, bool vec,
                          cudaStream_t st) {

@@ -2,7 +2,8 @@
 // waits, TMA tile loads, Tensor Memory (TMEM) allocation / load / store, and
 // tcgen05.mma (kind::tf32) with shared-memory matrix descriptors.
 //
-// Every wait in this file is bounded: after CT_WAIT_TIMEOUT_NS of spinning it
+// Every wait in this file is bounded: after the device's wait limit (the
+// watchdog block's limit_ns, 2 s unless set through ct_set_wait_limit_ns) it
 // records CT_DEVSTAT_TIMEOUT in the device status word, raises the CTA's abort
 // flag and returns false.  Callers then skip the rest of their work and fall
 // through to the kernel teardown (drain in-flight copies, release TMEM).
@@ -12,6 +13,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+// Default wait limit, and the bound of teardown drains (waits for copies and
+// MMAs already in flight, which complete on their own).
 #ifndef CT_WAIT_TIMEOUT_NS
 #define CT_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: legitimate waits are microseconds
 #endif
@@ -20,6 +23,19 @@ namespace ct {
 
 // Device status word bits (see ct_device_status in the C ABI).
 constexpr uint32_t CT_DEVSTAT_TIMEOUT = 1u;
+
+// Per-device watchdog block (one __device__ instance in capi.cu).  Kernels get
+// the address of its first member as `uint32_t* status`: the status word that
+// expired waits OR CT_DEVSTAT_* bits into, followed by the limit of every
+// bounded wait in nanoseconds (set by ct_set_wait_limit_ns).
+struct WatchBlock {
+  uint32_t status;
+  uint32_t reserved;
+  unsigned long long limit_ns;
+};
+__host__ __device__ __forceinline__ unsigned long long wait_limit_ns(const uint32_t* status) {
+  return reinterpret_cast<const volatile WatchBlock*>(status)->limit_ns;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -86,11 +102,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
-// Slow path of mbar_wait: suspend-hinted polls bounded by CT_WAIT_TIMEOUT_NS.
-// Kept out of line so the fast path is one try_wait and a branch.
+// Slow path of mbar_wait: suspend-hinted polls bounded by the device's wait
+// limit.  Kept out of line so the fast path is one try_wait and a branch.
 static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, CtaCtl* ctl,
                                                    uint32_t* status) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if ((i & 15u) == 0u) {
@@ -99,7 +116,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
         ctl->abort = 1u;
         return false;
       }
-      if (globaltimer_ns() - t0 > CT_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > limit) {
         ctl->abort = 1u;
         atomicOr(status, CT_DEVSTAT_TIMEOUT);
         return false;
@@ -110,7 +127,8 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
 
 // Waits until the phase with the given parity of barrier `bar` has completed.
 // Returns false (and raises ctl->abort and the device status word) if the
-// wait exceeds CT_WAIT_TIMEOUT_NS or another wait of this CTA already failed.
+// wait exceeds the device's wait limit or another wait of this CTA already
+// failed.
 // The common case -- the phase has completed -- costs one try_wait: the MMA
 // issuing thread pays for every instruction between two MMA groups, because
 // the tensor pipe idles while that thread is away (measured on B200).

@@ -51,8 +51,35 @@ const char* ct_status_string(int status);
 int ct_version(void);
 
 /* Reads (and optionally clears) the device watchdog word of `device`.
- * *flag_out is 0 when no bounded wait has expired since the last clear. */
+ * *flag_out is 0 when no bounded wait has expired since the last clear.
+ * While the word is non-zero, the tensor-core kernels of this library (FA2
+ * forward, dQ, dK/dV, linear layer) return at entry without writing their
+ * outputs: a failed wait stops the device's queue of tensor-core work until
+ * the caller has seen the failure and cleared the word.  No reference
+ * counterpart: the reference kernels have no failure detection. */
 int ct_device_status(int device, int clear, unsigned int* flag_out);
+
+/* Limit of every bounded device-side wait (barrier phases, split-K ordering)
+ * on `device`, in nanoseconds; 2 s by default.  Legitimate waits last
+ * microseconds, so the limit only decides how long a stuck kernel takes to
+ * give up, report CT_DEVSTAT_TIMEOUT and tear down.  Accepted range
+ * [CT_WAIT_LIMIT_MIN_NS, CT_WAIT_LIMIT_MAX_NS].  The setter copies
+ * synchronously; set it while no kernel of this library runs on the device.
+ * No reference counterpart. */
+#define CT_WAIT_LIMIT_MIN_NS 100000ull         /* 0.1 ms */
+#define CT_WAIT_LIMIT_MAX_NS 60000000000ull    /* 60 s   */
+int ct_set_wait_limit_ns(int device, unsigned long long limit_ns);
+int ct_get_wait_limit_ns(int device, unsigned long long* limit_ns);
+
+/* Failure-detection self-test: launches, on the current device and `stream`,
+ * one CTA whose warps wait on a barrier phase that nothing ever completes.
+ * The waits run out after the device's wait limit and the CTA takes the same
+ * abort teardown as the attention and GEMM kernels (MMA commit and bounded
+ * drain, TMEM release); the kernel then returns, leaving CT_DEVSTAT_TIMEOUT
+ * in the device's status word for ct_device_status to report.  Set a short
+ * limit first (ct_set_wait_limit_ns) and clear the word afterwards.  No
+ * reference counterpart. */
+int ct_watchdog_selftest(void* stream);
 
 /* ======================================================================== */
 /* FlashAttention-2                                                          */
@@ -234,31 +261,6 @@ int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean,
                      float* dx, float* dgamma, float* dbeta,
                      int64_t rows, int64_t n,
                      void* workspace, size_t workspace_bytes, void* stream);
-
-/* ======================================================================== */
-/* Diagnostics                                                               */
-/* ======================================================================== */
-
-/* One 128 x n x 32 TF32 tensor-core product on a single CTA, used by the
- * test-suite to check operand layouts and rounding on the device:
- *   mode 0: A smem K-major,  B smem K-major      (b is [n,32])
- *   mode 1: A smem K-major,  B smem MN-major     (b is [32,n])
- *   mode 2: A TMEM,          B smem K-major      (b is [n,32])
- *   mode 3: A TMEM,          B smem MN-major     (b is [32,n])
- *   mode 4: A smem MN-major, B smem MN-major     (a is [32,128], b is [32,n])
- * a is [128,32] row-major for modes 0-3; d is [128,n] row-major.  n in {32,64,128}. */
-int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
-                      void* stream);
-
-/* Diagnostic: tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in
- * {32, 64, 128, 256}.  `flags`: bit 0 A from TMEM (else shared memory), bit 1
- * B MN-major (else K-major), bit 2 two issuing threads in different warps,
- * each with its own accumulator (N <= 128).  `blocks` CTAs (at most one per
- * SM) each issue reps x 4 MMAs per issuing thread back to back and write the
- * clock64 cycles from first issue to the first thread's completion into the
- * device array cycles[blocks] (-1 if the completion wait timed out).  No
- * reference counterpart. */
-int ct_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles, void* stream);
 
 #ifdef __cplusplus
 }

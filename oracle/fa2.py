@@ -94,6 +94,45 @@ def attention_bwd(q, k, v, o, do, lse, causal: bool):
     return dq, dk, dv
 
 
+def attention_fwd_bwd_chunked(q, k, v, do, causal: bool, chunk: int = 1024):
+    """The closed forms of attention_fwd and attention_bwd (same reference
+    lines) evaluated for one (b,h) pair at a time over `chunk` query rows at a
+    time, so host memory stays O(chunk * T) at long sequence lengths: per chunk
+    S = Q_c K^T / sqrt(D) (masked), L = rowmax + ln(rowsum), O_c = P V,
+    delta_c = rowsum(O_c * dO_c), dS = P * (dO_c V^T - delta_c),
+    dQ_c = dS K / sqrt(D); dK += dS^T Q_c / sqrt(D), dV += P^T dO_c.
+    Returns O, LSE, dQ, dK, dV in float64."""
+    q, k, v, do = (np.asarray(t, dtype=np.float64) for t in (q, k, v, do))
+    B, H, T, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    o = np.empty_like(q)
+    lse = np.empty((B, H, T))
+    dq, dk, dv = np.empty_like(q), np.zeros_like(q), np.zeros_like(q)
+    cols = np.arange(T)
+    for b in range(B):
+        for h in range(H):
+            kk, vv = k[b, h], v[b, h]
+            for r0 in range(0, T, chunk):
+                r1 = min(r0 + chunk, T)
+                qc, dc = q[b, h, r0:r1], do[b, h, r0:r1]
+                s = (qc @ kk.T) * scale
+                if causal:
+                    s = np.where(cols[None, :] <= np.arange(r0, r1)[:, None], s, -np.inf)
+                m = s.max(axis=1, keepdims=True)
+                e = np.exp(s - m)
+                l = e.sum(axis=1, keepdims=True)
+                p = e / l
+                oc = p @ vv
+                o[b, h, r0:r1] = oc
+                lse[b, h, r0:r1] = (m + np.log(l))[:, 0]
+                delta = (oc * dc).sum(axis=1, keepdims=True)
+                ds = p * (dc @ vv.T - delta)
+                dq[b, h, r0:r1] = (ds @ kk) * scale
+                dk[b, h] += (ds.T @ qc) * scale
+                dv[b, h] += p.T @ dc
+    return o, lse, dq, dk, dv
+
+
 # ------------------------------------------------------------- row kernels
 def softmax_fwd(x):
     """naive_softmax (Transformer_kernels/softmax.cuh:25-106): exp(x - max) / sum."""

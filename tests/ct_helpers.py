@@ -133,8 +133,14 @@ def layernorm_bwd(x, g, mean, rstd, dy):
 
 
 def diag_umma(mode, a, b, n):
+    """One TF32 tensor-core product through the test-only diagnostics library."""
+    from tests import diag
+
     d = torch.empty(128, n, device=a.device, dtype=torch.float32)
-    cb.check(cb.lib().ct_diag_umma_tf32(mode, _p(a), _p(b), _p(d), n, _stream()), "ct_diag_umma")
+    diag.check(diag.lib().ct_diag_umma_tf32(mode, _p(a), _p(b), _p(d), n, _stream()),
+               "ct_diag_umma")
+    torch.cuda.synchronize()
+    assert diag.status() == 0, "diagnostic kernel's bounded wait ran out"
     return d
 
 

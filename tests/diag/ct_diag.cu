@@ -1,15 +1,36 @@
-// umma_diag.cu -- a single-CTA 128 x n x 32 TF32 tensor-core product used by
-// the test-suite to check, on the device, the operand layouts that the
-// FlashAttention and GEMM kernels rely on: K-major and MN-major shared-memory
-// operands in the 128-byte swizzle, A read from Tensor Memory, and how the
-// tensor core treats the 13 low mantissa bits of an FP32 operand.  Also a
-// throughput probe: back-to-back kind::tf32 MMAs of one shape, timed in SM
-// cycles on every SM (the tensor-pipe ceiling the roofline figures use).
-#include "ct_internal.h"
+// ct_diag.cu -- TEST-ONLY diagnostics library (tests/diag/libct_diag.so), not
+// part of the product library.
+//
+// * ct_diag_umma_tf32: a single-CTA 128 x n x 32 TF32 tensor-core product used
+//   by the test-suite to check, on the device, the operand layouts that the
+//   FlashAttention and GEMM kernels rely on: K-major and MN-major shared-memory
+//   operands in the 128-byte swizzle, A read from Tensor Memory, and how the
+//   tensor core treats the 13 low mantissa bits of an FP32 operand.
+// * ct_diag_mma_rate: a throughput probe -- back-to-back kind::tf32 MMAs of one
+//   shape, timed in SM cycles on every SM (the tensor-pipe ceiling the tile
+//   shapes of the product kernels are chosen against).
+//
+// Built from the product's PTX layer (cuda_transformer_b200/csrc/tc_ptx.cuh)
+// with its own watchdog block; declared in tests/diag/ct_diag.h.
+#include <cuda_runtime.h>
+
+#include "ct_diag.h"
 #include "tc_ptx.cuh"
+
+namespace {
+__device__ ct::WatchBlock g_diag_watch = {0u, 0u, CT_WAIT_TIMEOUT_NS};
+}  // namespace
 
 namespace ct {
 namespace {
+
+int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : 4; }
+
+uint32_t* diag_status() {
+  void* addr = nullptr;
+  return cudaGetSymbolAddress(&addr, g_diag_watch) == cudaSuccess ? static_cast<uint32_t*>(addr)
+                                                                   : nullptr;
+}
 
 struct DiagSmem {
   uint64_t bar, bar2;
@@ -183,58 +204,78 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 template <int N, bool TS, bool BMN, bool TWO>
-int run_mma_rate(int reps, int blocks, long long* cycles, const DeviceInfo& dev, cudaStream_t st) {
+int run_mma_rate(int reps, int blocks, long long* cycles, uint32_t* status, cudaStream_t st) {
   const size_t smem = 120 * 1024;  // one CTA per SM: each allocates all 512 TMEM columns
   if (cudaFuncSetAttribute(mma_rate_kernel<N, TS, BMN, TWO>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return CT_ERR_CUDA;
-  mma_rate_kernel<N, TS, BMN, TWO><<<blocks, 128, smem, st>>>(reps, cycles, dev.status);
-  return check_launch();
+    return 6;
+  mma_rate_kernel<N, TS, BMN, TWO><<<blocks, 128, smem, st>>>(reps, cycles, status);
+  return launch_ok();
 }
 
 template <int N>
-int run_mma_rate_n(int flags, int reps, int blocks, long long* cycles, const DeviceInfo& dev,
+int run_mma_rate_n(int flags, int reps, int blocks, long long* cycles, uint32_t* status,
                    cudaStream_t st) {
   const bool ts = flags & 1, bmn = flags & 2, two = flags & 4;
-  if (two && N > 128) return CT_ERR_INVALID_ARGUMENT;  // two accumulators must fit below A
+  if (two && N > 128) return 1;  // two accumulators must fit below A
   if (two) {
-    if (ts) return bmn ? run_mma_rate<N, true, true, true>(reps, blocks, cycles, dev, st)
-                       : run_mma_rate<N, true, false, true>(reps, blocks, cycles, dev, st);
-    return bmn ? run_mma_rate<N, false, true, true>(reps, blocks, cycles, dev, st)
-               : run_mma_rate<N, false, false, true>(reps, blocks, cycles, dev, st);
+    if (ts) return bmn ? run_mma_rate<N, true, true, true>(reps, blocks, cycles, status, st)
+                       : run_mma_rate<N, true, false, true>(reps, blocks, cycles, status, st);
+    return bmn ? run_mma_rate<N, false, true, true>(reps, blocks, cycles, status, st)
+               : run_mma_rate<N, false, false, true>(reps, blocks, cycles, status, st);
   }
-  if (ts) return bmn ? run_mma_rate<N, true, true, false>(reps, blocks, cycles, dev, st)
-                     : run_mma_rate<N, true, false, false>(reps, blocks, cycles, dev, st);
-  return bmn ? run_mma_rate<N, false, true, false>(reps, blocks, cycles, dev, st)
-             : run_mma_rate<N, false, false, false>(reps, blocks, cycles, dev, st);
+  if (ts) return bmn ? run_mma_rate<N, true, true, false>(reps, blocks, cycles, status, st)
+                     : run_mma_rate<N, true, false, false>(reps, blocks, cycles, status, st);
+  return bmn ? run_mma_rate<N, false, true, false>(reps, blocks, cycles, status, st)
+             : run_mma_rate<N, false, false, false>(reps, blocks, cycles, status, st);
 }
 
 }  // namespace
+}  // namespace ct
+
+extern "C" {
 
 // flags: bit 0 A from TMEM, bit 1 B MN-major, bit 2 two issuing threads.
-int launch_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles,
-                         const DeviceInfo& dev, cudaStream_t st) {
-  if (reps <= 0 || reps > (1 << 20) || blocks <= 0 || blocks > dev.sm_count || !cycles ||
-      flags < 0 || flags > 7)
-    return CT_ERR_INVALID_ARGUMENT;
+int ct_diag_mma_rate(int n, int flags, int reps, int blocks, long long* cycles, void* stream) {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 6;
+  if (reps <= 0 || reps > (1 << 20) || blocks <= 0 || blocks > sms || !cycles || flags < 0 ||
+      flags > 7)
+    return 1;
+  uint32_t* status = ct::diag_status();
+  if (!status) return 6;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (n) {
-    case 32: return run_mma_rate_n<32>(flags, reps, blocks, cycles, dev, st);
-    case 64: return run_mma_rate_n<64>(flags, reps, blocks, cycles, dev, st);
-    case 128: return run_mma_rate_n<128>(flags, reps, blocks, cycles, dev, st);
-    case 256: return run_mma_rate_n<256>(flags, reps, blocks, cycles, dev, st);
-    default: return CT_ERR_INVALID_ARGUMENT;
+    case 32: return ct::run_mma_rate_n<32>(flags, reps, blocks, cycles, status, st);
+    case 64: return ct::run_mma_rate_n<64>(flags, reps, blocks, cycles, status, st);
+    case 128: return ct::run_mma_rate_n<128>(flags, reps, blocks, cycles, status, st);
+    case 256: return ct::run_mma_rate_n<256>(flags, reps, blocks, cycles, status, st);
+    default: return 1;
   }
 }
 
-int launch_diag_umma(int mode, const float* a, const float* b, float* d, int n,
-                     const DeviceInfo& dev, cudaStream_t st) {
-  if (mode < 0 || mode > 4 || !(n == 32 || n == 64 || n == 128)) return CT_ERR_INVALID_ARGUMENT;
+int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n, void* stream) {
+  if (!a || !b || !d || mode < 0 || mode > 4 || !(n == 32 || n == 64 || n == 128)) return 1;
+  uint32_t* status = ct::diag_status();
+  if (!status) return 6;
   const size_t smem = 1024 + 1024 + 128 * 128 + (size_t)n * 128;
-  cudaError_t e = cudaFuncSetAttribute(umma_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return CT_ERR_CUDA;
-  umma_diag_kernel<<<1, 128, smem, st>>>(mode, a, b, d, n, dev.status);
-  return check_launch();
+  if (cudaFuncSetAttribute(ct::umma_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return 6;
+  ct::umma_diag_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mode, a, b, d,
+                                                                                 n, status);
+  return ct::launch_ok();
 }
 
-}  // namespace ct
+int ct_diag_status(unsigned int* flag_out) {
+  if (!flag_out) return 1;
+  uint32_t* status = ct::diag_status();
+  if (!status) return 6;
+  return cudaMemcpy(flag_out, status, sizeof(*flag_out), cudaMemcpyDeviceToHost) == cudaSuccess
+             ? 0
+             : 6;
+}
+
+}  // extern "C"

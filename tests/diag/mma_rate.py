@@ -1,9 +1,9 @@
-"""Measures the tcgen05 kind::tf32 tensor-pipe rate (M = 128) on every SM
-through ct_diag_mma_rate and prints cycles per MMA and FLOP per cycle per SM
+"""TEST-ONLY probe.  Measures the tcgen05 kind::tf32 tensor-pipe rate (M = 128)
+on every SM through ct_diag_mma_rate (tests/diag/libct_diag.so) and prints cycles per MMA and FLOP per cycle per SM
 for each N, A-operand source, B-operand layout and number of issuing threads,
 plus the chip rate at the maximum SM clock.
 
-  python -m cuda_transformer_b200.mma_rate [--reps 2000]
+  python -m tests.diag.mma_rate [--reps 2000]
 
 With two issuing threads the cycles per MMA count the MMAs of both, i.e. the
 SM's combined rate.
@@ -16,7 +16,7 @@ import json
 
 import torch
 
-from . import check, lib
+from tests.diag import check, lib
 
 
 def main() -> None:

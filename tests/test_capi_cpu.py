@@ -48,6 +48,21 @@ def test_library_exports_every_declared_symbol():
     assert set(syms) == set(cb.SIGNATURES), "ctypes signature table out of sync with the header"
 
 
+def test_test_only_diagnostics_stay_out_of_the_product():
+    """Layout checks and the throughput probe live in tests/diag/libct_diag.so,
+    which exports what its header declares; the product library exports none
+    of them."""
+    from tests import diag
+
+    text = re.sub(r"/\*.*?\*/", "", diag.HEADER_PATH.read_text(), flags=re.S)
+    syms = sorted(set(re.findall(r"\b(ct_[a-z0-9_]+)\s*\(", text)))
+    assert syms == sorted(diag.SIGNATURES)
+    dl = diag.lib()
+    for s in syms:
+        assert hasattr(dl, s), s
+        assert not hasattr(cb.lib(), s), f"{s} is exported by the product library"
+
+
 def test_status_strings_and_version():
     lib = cb.lib()
     assert lib.ct_version() >= 10000
@@ -73,6 +88,10 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
     rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, 1, 1, 8, 64, 0, 7, None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
+    # B*H is bounded factor by factor, so a product that would wrap is rejected
+    for B, Hh in ((2 ** 62 + 1, 4), (2 ** 40, 2 ** 40), (2 ** 31, 1)):
+        rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, B, Hh, 1, 64, 0, 0, None)
+        assert rc == cb.CT_ERR_INVALID_ARGUMENT, (B, Hh)
     # LayerNorm rows are at most 8192 wide
     rc = lib.ct_layernorm_fwd(None, None, None, None, None, None, 1, 8193, ctypes.c_float(1e-5), None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT

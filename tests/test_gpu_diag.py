@@ -59,16 +59,18 @@ def test_tf32_operand_rounding_rule(cuda_device, record_property):
     H.assert_device_clean()
 
 
-
 @pytest.mark.gpu
 def test_mma_rate_probe_runs(cuda_device):
-    """The tensor-pipe probe completes on every SM and wider N never costs
-    fewer cycles per MMA than narrower N."""
+    """The test-only tensor-pipe probe completes on every SM and wider N never
+    costs fewer cycles per MMA than narrower N."""
+    from tests import diag
+
+    L = diag.lib()
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
     cyc = torch.zeros(sms, dtype=torch.int64, device=cuda_device)
     per = {}
     for n in (32, 128):
-        H.cb.check(H.cb.lib().ct_diag_mma_rate(n, 1, 200, sms, H._p(cyc), H._stream()), "rate")
+        diag.check(L.ct_diag_mma_rate(n, 1, 200, sms, H._p(cyc), H._stream()), "rate")
         torch.cuda.synchronize()
         assert bool((cyc > 0).all())
         per[n] = cyc.double().mean().item() / 800
@@ -76,9 +78,9 @@ def test_mma_rate_probe_runs(cuda_device):
     # every operand form and the two-issuer variant complete (flags: A in TMEM,
     # B MN-major, two issuing threads); out-of-range flags are rejected
     for flags in (0, 2, 3, 5, 7):
-        H.cb.check(H.cb.lib().ct_diag_mma_rate(64, flags, 50, sms, H._p(cyc), H._stream()),
-                   "rate")
+        diag.check(L.ct_diag_mma_rate(64, flags, 50, sms, H._p(cyc), H._stream()), "rate")
         torch.cuda.synchronize()
         assert bool((cyc > 0).all()), flags
-    assert H.cb.lib().ct_diag_mma_rate(256, 4, 50, sms, H._p(cyc), H._stream()) != 0
-    assert H.cb.lib().ct_diag_mma_rate(64, 8, 50, sms, H._p(cyc), H._stream()) != 0
+    assert L.ct_diag_mma_rate(256, 4, 50, sms, H._p(cyc), H._stream()) != 0
+    assert L.ct_diag_mma_rate(64, 8, 50, sms, H._p(cyc), H._stream()) != 0
+    assert diag.status() == 0

@@ -182,3 +182,54 @@ def test_delta_kernel(cuda_device):
     ot = o.transpose(2, 3).contiguous().transpose(2, 3)
     d2 = H.fa2_delta(ot, do)
     assert H.rel_err(d2, ref) < 1e-6
+
+
+_LONG_CACHE = {}
+
+
+def _long_case(key, shape, seed, causal, dev):
+    """Seeded inputs of `shape` and the row-chunked FP64 oracle's outputs for
+    them (computed once per case, shared by the precision modes)."""
+    if key not in _LONG_CACHE:
+        g = torch.Generator().manual_seed(seed)
+        host = [torch.randn(*shape, generator=g) for _ in range(4)]
+        ref = orc.attention_fwd_bwd_chunked(*(t.double().numpy() for t in host), causal)
+        _LONG_CACHE.clear()  # one case at a time in host memory
+        _LONG_CACHE[key] = (host, ref)
+    host, ref = _LONG_CACHE[key]
+    return [t.to(dev) for t in host], ref
+
+
+def _check_against(got, ref, tol):
+    for name, a, r in zip(("O", "LSE", "dQ", "dK", "dV"), got, ref):
+        assert torch.isfinite(a).all(), name
+        assert H.rel_err(a, r) < tol, (name, H.rel_err(a, r))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
+@pytest.mark.parametrize("N,pairs", [(8192, 2), (16384, 1)])
+def test_config3_long_sequences(cuda_device, prec, N, pairs):
+    """BASELINE config 3's longest lengths (non-causal, D = 64) on 1-2 (b,h)
+    pairs against the row-chunked FP64 oracle: accumulation error grows with
+    N, and the tile counts at these lengths are the ones the sweep runs."""
+    (q, k, v, do), ref = _long_case(("c3", N), (1, pairs, N, 64), 70 + N // 1024, False,
+                                    cuda_device)
+    o, lse = H.fa2_fwd(q, k, v, False, prec)
+    dq, dk, dv = H.fa2_bwd(q, k, v, o, do, lse, False, prec)
+    torch.cuda.synchronize()
+    _check_against((o, lse, dq, dk, dv), ref, TOL[prec])
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
+def test_head_dim_128_at_length(cuda_device, prec):
+    """D = 128 (gpt/gpt.py's head size) at N = 4096, causal, 2 (b,h) pairs:
+    the head-dim-128 backward paths at length."""
+    (q, k, v, do), ref = _long_case(("d128", 4096), (1, 2, 4096, 128), 88, True, cuda_device)
+    o, lse = H.fa2_fwd(q, k, v, True, prec)
+    dq, dk, dv = H.fa2_bwd(q, k, v, o, do, lse, True, prec)
+    torch.cuda.synchronize()
+    _check_against((o, lse, dq, dk, dv), ref, TOL[prec])
+    H.assert_device_clean()

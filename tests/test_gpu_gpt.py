@@ -15,7 +15,7 @@ def _ln(x, a, b):
     return (x - x.mean(-1, keepdim=True)) / torch.sqrt(var + 1e-5) * a + b  # gpt/gpt.py:55-58
 
 
-def reference_loss(p, idx, tgt, layers, heads):
+def reference_loss(p, idx, tgt, layers, heads, tied=True):
     B, T = idx.shape
     x = p["tok.weight"][idx] + p["pos.weight"][:T]
     C = x.shape[-1]
@@ -30,7 +30,8 @@ def reference_loss(p, idx, tgt, layers, heads):
         h = F.gelu(h @ p[q_ + "mlp.fc1_weights"] + p[q_ + "mlp.fc1_bias"])
         x = x + h @ p[q_ + "mlp.fc2_weights"] + p[q_ + "mlp.fc2_bias"]
     x = _ln(x, p["ln.alpha"], p["ln.beta"])
-    logits = x @ p["tok.weight"].t() + p["lm_head_bias"]
+    w = p["tok.weight"].t() if tied else p["lm_head_weights"]
+    logits = x @ w + p["lm_head_bias"]
     return F.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1))
 
 
@@ -48,6 +49,32 @@ def test_gpt_step_matches_fp64_torch(cuda_device, layers, d, heads, ctx, batch):
     loss.backward()
     ref_p = {k: v.detach().double().requires_grad_() for k, v in model.named_parameters()}
     ref = reference_loss(ref_p, idx, tgt, layers, heads)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 1e-5 * abs(ref.item())
+    for name, prm in model.named_parameters():
+        assert H.rel_err(prm.grad, ref_p[name].grad) < 1e-4, name
+    H.assert_device_clean()
+
+
+@pytest.mark.gpu
+def test_gpt_at_reference_model_shape(cuda_device):
+    """gpt/gpt.py's own model shape (:16-22, :149-175): one block, d_model 512,
+    4 heads of 128 -- the head size the reference launcher special-cases
+    (flash_attn_launcher.cu:123-133) -- context 256, vocabulary 100256 with an
+    untied lm_head and bias, here at 2 sequences, in the default
+    (FP32-accurate) precision, against the same network in FP64 torch."""
+    from cuda_transformer_b200.gpt_case import GPT
+
+    layers, d, heads, ctx, vocab, batch = 1, 512, 4, 256, 100256, 2
+    torch.manual_seed(117)
+    model = GPT(layers, d, heads, ctx, vocab, tied=False).to(cuda_device)
+    g = torch.Generator().manual_seed(3)
+    t = torch.randint(0, vocab, (batch, ctx + 1), generator=g).to(cuda_device)
+    idx, tgt = t[:, :-1], t[:, 1:]
+    _, loss = model(idx, tgt)
+    loss.backward()
+    ref_p = {k: v.detach().double().requires_grad_() for k, v in model.named_parameters()}
+    ref = reference_loss(ref_p, idx, tgt, layers, heads, tied=False)
     ref.backward()
     assert abs(loss.item() - ref.item()) < 1e-5 * abs(ref.item())
     for name, prm in model.named_parameters():
