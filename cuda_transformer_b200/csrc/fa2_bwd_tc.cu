@@ -87,6 +87,10 @@ struct BwdBars {
   // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
   uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2], s_free[2];
   uint64_t dqd[2];  // dQ pass, two buffers: dQ_j has read dS_j from buffer j % 2
+  // Accumulator folds (kFoldLen): acc_chunk[g] -- the last MMA of a chunk of
+  // gradient g (0: dQ or dK, 1: dV) has completed; acc_free[g] -- the row
+  // warps have added that chunk into the output, the next MMA may restart it.
+  uint64_t acc_chunk[2], acc_free[2];
   uint64_t rows_ready, done, mma_final, mma_final2, mma_final3;
   CtaCtl ctl;
 };
@@ -116,10 +120,11 @@ constexpr size_t bwd_smem_bytes() {
 }
 
 // empty_count: MMA issuers that read a stage; done_count: issuers whose
-// accumulators the epilogue reads; rows: the row warps (one arrival each).
+// accumulators the epilogue reads; rows: the row warps (one arrival each);
+// fold0 / fold1: row warps that fold gradient 0 / 1.
 template <class C>
 __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_count,
-                                              int done_count, int rows) {
+                                              int done_count, int rows, int fold0, int fold1) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
@@ -144,6 +149,10 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
   mbar_init(B(bars->mma_final3), 1);
   mbar_init(B(bars->dqd[0]), 1);
   mbar_init(B(bars->dqd[1]), 1);
+  mbar_init(B(bars->acc_chunk[0]), 1);
+  mbar_init(B(bars->acc_chunk[1]), 1);
+  mbar_init(B(bars->acc_free[0]), fold0);
+  mbar_init(B(bars->acc_free[1]), fold1);
   bars->ctl.abort = 0;
   fence_barrier_init();
 }
@@ -284,6 +293,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  constexpr int FOLD = kFoldLen / BN;  // key steps per dQ accumulator chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   // K_j is released by the dQ_j issuer alone: dQ_j waits for dS_j, formed
   // after the row warps read S_j, so S_j has completed by then.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8, 8, 1);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -365,11 +375,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full[j % C::NSB]));
       };
-      auto issue_dQ = [&](int j) {
+      // dQ_j; the first step of a chunk restarts the accumulator once the rows
+      // have folded the previous chunk out of it, the last one signals its end
+      auto issue_dQ = [&](int j) -> bool {
+        if (j > 0 && j % FOLD == 0) {
+          if (!mbar_wait(B(bars->acc_free[0]), (uint32_t)(j / FOLD - 1) & 1u, ctl, p.status))
+            return false;
+          tc_fence_after();
+        }
         const uint32_t db = tmem + C::TC_DP + (uint32_t)(j % C::NSB) * C::SB;
         mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, db, db + BN, kmd0 + stg(j), idQ,
-                                                j > 0);
+                                                j % FOLD != 0);
         umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
+        if ((j + 1) % FOLD == 0 && j + 1 < n_kv) umma_commit(B(bars->acc_chunk[0]));
+        return true;
       };
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       if (ok && dq_here && dp_here) {  // one buffer: dP and dQ interleaved
@@ -380,7 +399,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int j = 0; ok && j < n_kv; ++j) {
           if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
           tc_fence_after();
-          issue_dQ(j);
+          if (!(ok = issue_dQ(j))) break;
           if (j + 1 < n_kv) {
             if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
@@ -393,7 +412,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int bj = j % C::NSB;
           if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j / C::NSB) & 1, ctl, p.status))) break;
           tc_fence_after();
-          issue_dQ(j);
+          if (!(ok = issue_dQ(j))) break;
           umma_commit(B(bars->dqd[bj]));
         }
         if (ok) umma_commit(B(bars->done));
@@ -427,6 +446,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = q0 + quad * 32 + lane;
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    float* const dq_row = p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2);
     float l2 = 0.0f, dl = 0.0f;
     {
       const Ptr4& src = grp ? p.st1 : p.st0;
@@ -480,6 +500,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (!(ok = warp_wait(B(bars->dp_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
+      if (j > 0 && j % FOLD == 0) {  // fold the finished dQ chunk into this row's output
+        const int ch = j / FOLD - 1;
+        if (!(ok = warp_wait(B(bars->acc_chunk[0]), (uint32_t)ch & 1u, ctl, p.status))) break;
+        tc_fence_after();
+        tmem_cols_fold<D / 2>(lb, C::TC_DQ + grp * (D / 2), dq_row, valid, ch == 0);
+        tc_fence_before();
+        warp_arrive(B(bars->acc_free[0]));
+      }
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW];
@@ -510,9 +538,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale,
-                                 p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2),
-                                 valid);
+      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale, dq_row, valid,
+                                 n_kv > FOLD);
     }
   }
 
@@ -565,6 +592,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                            const __grid_constant__ CUtensorMap tmG,
                            const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
+  constexpr int FOLD = kFoldLen / BN;  // query steps per dK / dV accumulator chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
@@ -585,7 +613,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
   // by warp 10; in the dV pass S^T_i by warp 1, dV_i by warp 10): the merged
   // stage is free after both have committed.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8, 4, 4);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -600,6 +628,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
   constexpr uint32_t idS2 = idesc_tf32(128, 2 * BN, false, false);  // [hi | lo] rows (KIL)
   constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+  // Gradient g's accumulator (0: dK, 1: dV) restarts every FOLD steps: before
+  // the first MMA of a chunk, wait until the rows have folded the previous
+  // chunk out of TMEM; after the last MMA of a chunk, signal its end.
+  auto fold_wait = [&](int g, int i) -> bool {
+    if (i == 0 || i % FOLD != 0) return true;
+    if (!mbar_wait(B(bars->acc_free[g]), (uint32_t)(i / FOLD - 1) & 1u, ctl, p.status))
+      return false;
+    tc_fence_after();
+    return true;
+  };
+  auto fold_signal = [&](int g, int i) {
+    if ((i + 1) % FOLD == 0 && i + 1 < n) umma_commit(B(bars->acc_chunk[g]));
+  };
 
   if (warp == 0) {
     const CUtensorMap* maps[2] = {&tmQ, &tmG};
@@ -644,11 +685,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = mbar_wait(B(bars->p_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
           if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
+          if (!(ok = fold_wait(1, i))) break;
           const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i % FOLD != 0);
           umma_commit(B(bars->dqd[bi]));
           umma_commit(B(bars->empty_a[i % NS]));
+          fold_signal(1, i);
         }
       }
       if (ok) umma_commit(B(bars->done));
@@ -699,9 +742,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             // dO_i's MN-major copy (prepared right after the K-major ones)
             if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
+            if (!(ok = fold_wait(1, i))) break;
             const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
             mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-                tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
+                tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i % FOLD != 0);
+            fold_signal(1, i);
           }
           if (C::NSB == 1 && nx < n) issue_S(nx);
           umma_commit(B(bars->empty_a[i % NS]));
@@ -751,10 +796,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = mbar_wait(B(bars->ds_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
           if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
+          if (!(ok = fold_wait(0, i))) break;
           const uint32_t db = tmem + C::TC_DP + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
-              tmem + C::TC_DK, db, db + BN, qmd0 + stg(i), idO, i > 0);
+              tmem + C::TC_DK, db, db + BN, qmd0 + stg(i), idO, i % FOLD != 0);
           umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
+          fold_signal(0, i);
           if (nx < n) {
             if (!(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
@@ -784,6 +831,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = k0 + quad * 32 + lane;  // key row
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
+    float* const out = grp ? p.out1 : p.out0;  // dV (group 1) or dK (group 0) rows
     if (grp == 0 || C::DO_DK) {  // V is read only by dP^T
       const Ptr4& src = grp ? p.st1 : p.st0;
       const float* r = src.row(b, h, valid ? row : 0);
@@ -805,6 +854,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float* vl = vec + (i % NS) * 2 * BN + c0;
       if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
+      // Fold the finished dV chunk here (group 1), and the dK chunk (group 0)
+      // here too when the P phase's registers are many (HB > 32); otherwise
+      // group 0 folds in the dS phase, when dK_{i-1} has surely completed.
+      constexpr bool kDkFoldEarly = HB > 32;
+      if (i > 0 && i % FOLD == 0 &&
+          ((C::DO_DV && grp == 1) || (C::DO_DK && kDkFoldEarly && grp == 0))) {
+        const int g = grp == 1 ? 1 : 0, ch = i / FOLD - 1;
+        if (!(ok = warp_wait(B(bars->acc_chunk[g]), (uint32_t)ch & 1u, ctl, p.status))) break;
+        tc_fence_after();
+        tmem_cols_fold<D>(lb, g ? C::TC_DV : C::TC_DK, out + orow, valid, ch == 0);
+        tc_fence_before();
+        warp_arrive(B(bars->acc_free[g]));
+      }
       const bool need_mask = !valid || (qs + HB > T) || (p.causal && qs < k0 + kRows - 1);
       float pv[HB];
 #pragma unroll
@@ -855,6 +917,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if constexpr (!C::DO_DK) continue;
       if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
+      if (!kDkFoldEarly && grp == 0 && i > 0 && i % FOLD == 0) {  // fold the finished dK chunk
+        const int ch = i / FOLD - 1;
+        if (!(ok = warp_wait(B(bars->acc_chunk[0]), (uint32_t)ch & 1u, ctl, p.status))) break;
+        tc_fence_after();
+        tmem_cols_fold<D>(lb, C::TC_DK, out + orow, valid, ch == 0);
+        tc_fence_before();
+        warp_arrive(B(bars->acc_free[0]));
+      }
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], dv[CW];
@@ -885,8 +955,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       warp_arrive(B(bars->ds_full[bi]));
     }
-    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
-    float* out = grp ? p.out1 : p.out0;
     if (grp == 0 ? !C::DO_DK : !C::DO_DV) {
       // this pass does not produce the group's gradient
     } else if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
@@ -895,7 +963,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid);
+      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid,
+                            n > FOLD);
     }
   }
 

@@ -184,30 +184,14 @@ __device__ __forceinline__ float max32(const float (&t)[32]) {
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
-// Stores a D-wide row of TMEM columns [col, col+D) times `scale` to a dense
-// global row.
-template <int D>
-__device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t col, float scale,
-                                                   float* dst, bool valid) {
-#pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    float v[32];
-    tmem_ld32(lane_base + col + 32 * c, v);
-    if (valid) {
-      float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        d4[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
-                            v[4 * i + 3] * scale);
-    }
-  }
-}
-
 // Stores NC (16 or a multiple of 32) TMEM columns [col, col+NC) of this
-// thread's lane times `scale` to dense global memory.
+// thread's lane times `scale` to dense global memory.  With `add_partial`,
+// dst already holds the partial sums folded out of TMEM earlier
+// (tmem_cols_fold): the result is (dst + TMEM) * scale.
 template <int NC>
 __device__ __forceinline__ void tmem_cols_to_global(uint32_t lane_base, uint32_t col, float scale,
-                                                    float* dst, bool valid) {
+                                                    float* dst, bool valid,
+                                                    bool add_partial = false) {
   constexpr int CW = NC < 32 ? NC : 32;
   static_assert(NC % CW == 0, "column count");
 #pragma unroll
@@ -217,9 +201,53 @@ __device__ __forceinline__ void tmem_cols_to_global(uint32_t lane_base, uint32_t
     if (valid) {
       float4* d4 = reinterpret_cast<float4*>(dst + CW * c);
 #pragma unroll
-      for (int i = 0; i < CW / 4; ++i)
-        d4[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
-                            v[4 * i + 3] * scale);
+      for (int i = 0; i < CW / 4; ++i) {
+        float4 a = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        if (add_partial) {
+          const float4 o = d4[i];
+          a = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
+        }
+        d4[i] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+      }
+    }
+  }
+}
+// A D-wide row: tmem_cols_to_global over D columns.
+template <int D>
+__device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t col, float scale,
+                                                   float* dst, bool valid,
+                                                   bool add_partial = false) {
+  tmem_cols_to_global<D>(lane_base, col, scale, dst, valid, add_partial);
+}
+
+// Long reductions.  The tensor core adds each MMA's products into its FP32
+// accumulator with a rounding biased toward zero (measured: over 16384-long
+// reductions in 3xTF32 the gradients came out ~1.5e-4 relatively small), so
+// the gradient accumulators are restarted every kFoldLen keys / queries and
+// the chunk sums are added in FP32 with round-to-nearest: the row thread adds
+// its lane's NC accumulator columns into its own row of the output (stored
+// unscaled, in L2), `first` storing instead.  Fixed order: deterministic.
+constexpr int kFoldLen = 1024;
+template <int NC>
+__device__ __forceinline__ void tmem_cols_fold(uint32_t lane_base, uint32_t col, float* dst,
+                                               bool valid, bool first) {
+  constexpr int CW = NC < 32 ? NC : 32;
+  static_assert(NC % CW == 0, "column count");
+#pragma unroll
+  for (int c = 0; c < NC / CW; ++c) {
+    float v[CW];
+    tmem_ldn<CW>(lane_base + col + CW * c, v);
+    if (valid) {
+      float4* d4 = reinterpret_cast<float4*>(dst + CW * c);
+#pragma unroll
+      for (int i = 0; i < CW / 4; ++i) {
+        float4 a = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        if (!first) {
+          const float4 o = d4[i];
+          a = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
+        }
+        d4[i] = a;
+      }
     }
   }
 }

@@ -18,10 +18,14 @@ reference's Generate_Batch does, gpt/gpt.py:39-45).
 One process per GPU (torchrun); with more than one, gradients are averaged by
 torch DistributedDataParallel over NCCL: bucketed all-reduces that start
 while the backward is still running.  The step time is the maximum over ranks
-of the CUDA-event time of the timed steps.
+of the CUDA-event time of the timed steps.  With N > 1 the line also reports
+the communication the step exposes: the same steps timed again with DDP's
+gradient synchronisation switched off (``no_sync``: compute only), the
+difference to the synchronised step, and one stand-alone all-reduce of all
+gradients (a bound on the communication if none of it overlapped).
 
   python -m cuda_transformer_b200.gpt_case [--steps 20 --warmup 5]
-  torchrun --nproc-per-node N -m cuda_transformer_b200.gpt_case ...
+  torchrun --nproc-per-node N -m cuda_transformer_b200.gpt_case --gpus N ...
 """
 from __future__ import annotations
 
@@ -141,6 +145,32 @@ def rank_batches(seed: int, n: int, batch: int, ctx: int, vocab: int) -> list:
     return out
 
 
+def max_over_ranks(ms: float, dist, world: int, device) -> float:
+    """The job's time: the maximum over ranks of a per-rank time."""
+    if world == 1:
+        return ms
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def tokens_per_step(world: int, batch_per_gpu: int, ctx: int) -> int:
+    """Weak scaling: every rank trains batch_per_gpu sequences of ctx tokens."""
+    return world * batch_per_gpu * ctx
+
+
+def timed_ms(fn, steps: int) -> float:
+    """CUDA-event time of `steps` calls of fn() on the current stream."""
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=20)
@@ -152,12 +182,17 @@ def main() -> None:
     ap.add_argument("--vocab", type=int, default=65)
     ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
     ap.add_argument("--lr", type=float, default=3e-4)
+    ap.add_argument("--gpus", type=int, default=None,
+                    help="expected number of ranks (launch N > 1 with torchrun)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
     import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if a.gpus is not None and a.gpus != world:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}: launch one process per GPU "
+                         "with torchrun --nproc-per-node N")
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -191,36 +226,53 @@ def main() -> None:
         losses.append(step(i).item())
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    last = None
-    for i in range(a.steps):
-        last = step(a.warmup + i)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    losses.append(last.item())
+    last = [None]
+
+    def timed_step(i):
+        last[0] = step(a.warmup + i)
+
+    ms = timed_ms(timed_step, a.steps)
+    losses.append(last[0].item())
+    ms = max_over_ranks(ms, dist, world, dev)
+    comm = None
     if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        # the same steps without DDP's gradient all-reduces (compute only), and
+        # one stand-alone all-reduce of every gradient (fp32, flattened)
         dist.barrier()
-    tokens = world * a.batch * a.ctx
+
+        def unsynced(i):
+            with net.no_sync():
+                step(a.warmup + a.steps + i)
+
+        ms_nosync = max_over_ranks(timed_ms(unsynced, a.steps), dist, world, dev)
+        flat = torch.zeros(params, device=dev)
+        dist.all_reduce(flat)  # warm-up
+        dist.barrier()
+        ar_ms = max_over_ranks(timed_ms(lambda i: dist.all_reduce(flat), 5) / 5, dist, world, dev)
+        dist.barrier()
+        step_ms, comp_ms = ms / a.steps, ms_nosync / a.steps
+        comm = {"allreduce_bytes": params * 4, "allreduce_ms_standalone": ar_ms,
+                "allreduce_share_if_unoverlapped": ar_ms / step_ms,
+                "step_ms_without_sync": comp_ms,
+                "exposed_comm_ms": step_ms - comp_ms,
+                "exposed_comm_share": (step_ms - comp_ms) / step_ms,
+                "allreduce_busbw_gbs": 2.0 * (world - 1) / world * params * 4 / (ar_ms * 1e-3) / 1e9}
+    tokens = tokens_per_step(world, a.batch, a.ctx)
     if rank == 0:
         flops = step_flops(params, a.layers, a.d, a.ctx, tokens)
         print(json.dumps({
             "metric": "GPT DP training tokens/s", "value": tokens * a.steps / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms / a.steps, "steps": a.steps,
             "warmup": a.warmup, "tflops": flops * a.steps / (ms * 1e-3) / 1e12,
-            "params": params, "loss_first": losses[0], "loss_last": losses[-1],
-            "loss_uniform": math.log(a.vocab),
+            "scaling": "weak", "params": params, "loss_first": losses[0], "loss_last": losses[-1],
+            "loss_uniform": math.log(a.vocab), "communication": comm,
             "config": {"layers": a.layers, "d_model": a.d, "heads": a.heads, "ctx": a.ctx,
-                       "vocab": a.vocab, "batch_per_gpu": a.batch, "tied": True,
-                       "optimizer": "AdamW(fused) lr %g" % a.lr,
+                       "vocab": a.vocab, "batch_per_gpu": a.batch, "global_batch": a.batch * world,
+                       "tied": True, "optimizer": "AdamW(fused) lr %g" % a.lr,
                        "grad_sync": "DDP bucketed NCCL all-reduce" if world > 1 else "none"},
-            "data": "synthetic uniform tokens, pinned host -> device each step"}))
+            "data": "synthetic uniform tokens, pinned host -> device each step"}), flush=True)
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

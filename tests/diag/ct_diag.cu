@@ -136,6 +136,109 @@ __global__ void __launch_bounds__(128, 1)
 // operands (A in TMEM when TS, else shared memory; B K-major in shared
 // memory) and records the clock64 span from the first issue to the commit's
 // completion in cycles[blockIdx.x].
+// tcgen05.ld of 16 lanes x 32-bit, two halves: threads 0-15 read lanes
+// base..base+15 at columns [col, col + N), threads 16-31 the same lanes at
+// columns [col + N, col + 2N) (immediate half-split offset N).
+__device__ __forceinline__ void tmem_ld_16x32bx2_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16], 16;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// M = 64 product D[64 x n] = A[64 x 32] B[n x 32]^T, B K-major in shared
+// memory, checking the M = 64 data-path layout of TMEM: row r of D (and of a
+// TMEM A operand) sits in lane 32 * (r / 16) + r % 16 + L.  mode bit 0: A from
+// TMEM (columns 128..159), else shared memory K-major; bit 1: L = 16 (the
+// upper half of each warp's lane quadrant), else 0; bit 2: D read with the
+// 16-lane 16x32bx2 shape (n = 32: threads 0-15 columns 0-15, threads 16-31
+// columns 16-31 of the same rows), else with 32x32b.
+__global__ void __launch_bounds__(128, 1)
+    umma_m64_kernel(int mode, const float* __restrict__ a, const float* __restrict__ b,
+                    float* __restrict__ d, int n, uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DiagSmem* hs = reinterpret_cast<DiagSmem*>(smem_raw);
+  const uint32_t base = (smem_u32(smem_raw) + sizeof(DiagSmem) + 1023u) & ~1023u;
+  uint8_t* gen = smem_raw + (base - smem_u32(smem_raw));
+  const uint32_t sa = base, sb = base + 64u * 128u;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const bool a_tmem = (mode & 1) != 0, x2 = (mode & 4) != 0;
+  const uint32_t L = (mode & 2) ? 16u : 0u;
+  if (tid == 0) {
+    mbar_init(smem_u32(&hs->bar), 1);
+    hs->ctl.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&hs->ctl.tmem_base), 256);
+    tmem_relinquish();
+  }
+  for (int e = tid; e < 64 * 32; e += 128)
+    *reinterpret_cast<float*>(gen + sw128_offset(e / 32, e % 32, 64)) = a[e];
+  for (int e = tid; e < n * 32; e += 128)
+    *reinterpret_cast<float*>(gen + (sb - sa) + sw128_offset(e / 32, e % 32, n)) = b[e];
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = hs->ctl.tmem_base;
+  const bool mine = (uint32_t)lane >= L && (uint32_t)lane < L + 16u;  // this lane holds a row
+  const int r = 16 * warp + lane - (int)L;
+  if (a_tmem) {
+    float row[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) row[i] = mine ? a[r * 32 + i] : 0.0f;
+    tmem_st32(tmem_addr(tmem, 32u * warp, 128), row);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_tf32(64, n, false, false);
+    const uint32_t dt = tmem + (L << 16);
+    for (int k = 0; k < 4; ++k) {
+      const uint64_t bd = sdesc_kmajor(sb + k * 32u);
+      if (a_tmem) umma_tf32_ts(dt, tmem + (L << 16) + 128u + 8u * k, bd, idesc, k > 0);
+      else umma_tf32_ss(dt, sdesc_kmajor(sa + k * 32u), bd, idesc, k > 0);
+    }
+    umma_commit(smem_u32(&hs->bar));
+  }
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&hs->bar), 0, &hs->ctl, status));
+  if (ok) {
+    tc_fence_after();
+    if (x2) {  // n == 32
+      float v[16];
+      tmem_ld_16x32bx2_x16(tmem + ((32u * warp + L) << 16), v);
+      const int rr = 16 * warp + (lane & 15), c0 = (lane >> 4) * 16;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d[rr * n + c0 + i] = v[i];
+    } else {
+      for (int c = 0; c < n; c += 32) {
+        float v[32];
+        tmem_ld32(tmem_addr(tmem, 32u * warp, c), v);
+        if (mine) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) d[r * n + c + i] = v[i];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 template <int N, bool TS, bool BMN, bool TWO>
 __global__ void __launch_bounds__(128, 1)
     mma_rate_kernel(int reps, long long* __restrict__ cycles, uint32_t* status) {
@@ -266,6 +369,20 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
     return 6;
   ct::umma_diag_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mode, a, b, d,
                                                                                  n, status);
+  return ct::launch_ok();
+}
+
+int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, void* stream) {
+  if (!a || !b || !d || mode < 0 || mode > 7 || !(n == 32 || n == 64) || ((mode & 4) && n != 32))
+    return 1;
+  uint32_t* status = ct::diag_status();
+  if (!status) return 6;
+  const size_t smem = 1024 + 1024 + 64 * 128 + (size_t)n * 128;
+  if (cudaFuncSetAttribute(ct::umma_m64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return 6;
+  ct::umma_m64_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mode, a, b, d, n,
+                                                                                status);
   return ct::launch_ok();
 }
 

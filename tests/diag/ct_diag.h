@@ -20,6 +20,13 @@ extern "C" {
  * a is [128,32] row-major for modes 0-3; d is [128,n] row-major.  n in {32,64,128}. */
 int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n, void* stream);
 
+/* One M = 64 TF32 product D[64 x n] = A[64 x 32] B[n x 32]^T on a single CTA,
+ * checking the M = 64 data-path layout of Tensor Memory (row r of D in lane
+ * 32 * (r / 16) + r % 16 + L).  mode bit 0: A from TMEM (else shared memory);
+ * bit 1: L = 16 (else 0); bit 2: D read with the 16-lane 16x32bx2 shape
+ * (n = 32 only).  a is [64,32] row-major, b [n,32], d [64,n]; n in {32, 64}. */
+int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, void* stream);
+
 /* Tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in {32, 64, 128, 256}.
  * `flags`: bit 0 A from TMEM (else shared memory), bit 1 B MN-major (else
  * K-major), bit 2 two issuing threads in different warps, each with its own

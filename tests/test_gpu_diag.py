@@ -84,3 +84,26 @@ def test_mma_rate_probe_runs(cuda_device):
     assert L.ct_diag_mma_rate(256, 4, 50, sms, H._p(cyc), H._stream()) != 0
     assert L.ct_diag_mma_rate(64, 8, 50, sms, H._p(cyc), H._stream()) != 0
     assert diag.status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", range(8))
+@pytest.mark.parametrize("n", [32, 64])
+def test_umma_m64_layouts(cuda_device, mode, n):
+    """M = 64 MMAs: rows in lanes 32*(r//16) + r%16 (+16 for the upper half of
+    each lane quadrant), A from shared memory or TMEM, D read with the 32x32b
+    or the 16-lane 16x32bx2 shape."""
+    from tests import diag
+
+    if (mode & 4) and n != 32:
+        pytest.skip("16x32bx2 read covers n = 32")
+    g = torch.Generator().manual_seed(300 + 10 * mode + n)
+    a = _tf32_exact((64, 32), g, cuda_device)
+    b = _tf32_exact((n, 32), g, cuda_device)
+    d = torch.full((64, n), float("nan"), device=cuda_device)
+    diag.check(diag.lib().ct_diag_umma_m64(mode, H._p(a), H._p(b), H._p(d), n, H._stream()),
+               "ct_diag_umma_m64")
+    torch.cuda.synchronize()
+    assert diag.status() == 0
+    ref = a.double() @ b.double().t()
+    assert H.rel_err(d, ref) < 1e-6, mode

@@ -55,3 +55,38 @@ def test_max_over_ranks_gloo():
     res = sorted(q.get(timeout=10) for _ in range(world))
     assert [r[1] for r in res] == [15.0, 15.0]
     assert all(r[2] == bench.PAIRS for r in res)
+
+
+def _gpt_worker(rank, world, port, q):
+    """One gloo rank of the data-parallel GPT driver's host logic: per-rank
+    token streams, the weak-scaling token count and the max-over-ranks time."""
+    from cuda_transformer_b200 import gpt_case
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, y = gpt_case.rank_batches(1000 + rank, 1, 4, 32, 65)[0]
+        got = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(got, x)
+        distinct = all(not torch.equal(got[i], got[j])
+                       for i in range(world) for j in range(i + 1, world))
+        ms = gpt_case.max_over_ranks(20.0 + rank, dist, world, torch.device("cpu"))
+        q.put((rank, distinct, ms, gpt_case.tokens_per_step(world, 64, 256)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gpt_case_host_logic_gloo():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gpt_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    assert all(r[1] for r in res)                      # every rank trains on its own tokens
+    assert [r[2] for r in res] == [21.0, 21.0]         # the job time is the slowest rank's
+    assert all(r[3] == 2 * 64 * 256 for r in res)      # global batch = ranks x 64 sequences
