@@ -27,6 +27,10 @@
 // dQ pass's third issuer waits on a barrier (dqd) for dQ_j before dP_{j+2}
 // reuses dS_j's buffer.  3xTF32 interleaves the hi / lo copies of K-major
 // tiles so one MMA forms hi*hi and hi*lo together (mma_chain_kil).
+// Sequences longer than kSegLen run one launch per segment of the reduced
+// dimension, each adding into the previous one's output (fa2_common.cuh).
+#include <algorithm>
+
 #include "fa2_common.cuh"
 
 namespace ct {
@@ -87,10 +91,6 @@ struct BwdBars {
   // Indexed by S / dP TMEM buffer (the dQ pass and single-buffered dK/dV use [0]).
   uint64_t s_full[2], dp_full[2], p_full[2], ds_full[2], s_free[2];
   uint64_t dqd[2];  // dQ pass, two buffers: dQ_j has read dS_j from buffer j % 2
-  // Accumulator folds (kFoldLen): acc_chunk[g] -- the last MMA of a chunk of
-  // gradient g (0: dQ or dK, 1: dV) has completed; acc_free[g] -- the row
-  // warps have added that chunk into the output, the next MMA may restart it.
-  uint64_t acc_chunk[2], acc_free[2];
   uint64_t rows_ready, done, mma_final, mma_final2, mma_final3;
   CtaCtl ctl;
 };
@@ -103,6 +103,10 @@ struct BwdParams {
   float* out0;         // dQ | dK
   float* out1;         // -  | dV
   int H, T, n_tiles, bh_total, head_group, causal;
+  // This launch reduces over streamed rows [seg_lo, seg_hi) (keys in the dQ
+  // pass, queries in the dK/dV pass; kSegLen long); accumulate_out: add into
+  // the output written by the previous segment's launch instead of storing.
+  int seg_lo, seg_hi, accumulate_out;
   float scale_log2, scale;
   uint32_t* status;
 };
@@ -120,11 +124,10 @@ constexpr size_t bwd_smem_bytes() {
 }
 
 // empty_count: MMA issuers that read a stage; done_count: issuers whose
-// accumulators the epilogue reads; rows: the row warps (one arrival each);
-// fold0 / fold1: row warps that fold gradient 0 / 1.
+// accumulators the epilogue reads; rows: the row warps (one arrival each).
 template <class C>
 __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_count,
-                                              int done_count, int rows, int fold0, int fold1) {
+                                              int done_count, int rows) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
@@ -149,10 +152,6 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
   mbar_init(B(bars->mma_final3), 1);
   mbar_init(B(bars->dqd[0]), 1);
   mbar_init(B(bars->dqd[1]), 1);
-  mbar_init(B(bars->acc_chunk[0]), 1);
-  mbar_init(B(bars->acc_chunk[1]), 1);
-  mbar_init(B(bars->acc_free[0]), fold0);
-  mbar_init(B(bars->acc_free[1]), fold1);
   bars->ctl.abort = 0;
   fence_barrier_init();
 }
@@ -293,7 +292,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
-  constexpr int FOLD = kFoldLen / BN;  // key steps per dQ accumulator chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
@@ -307,11 +305,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int b = bh / p.H, h = bh % p.H;
   const int q0 = qt * kRows, T = p.T;
   const int last_row = min(q0 + kRows - 1, T - 1);
-  const int n_kv = p.causal ? last_row / BN + 1 : (T + BN - 1) / BN;
+  // key tiles [jb, jb + n_kv) of this launch's segment
+  const int jb = p.seg_lo / BN;
+  const int n_kv = max(0, min(p.causal ? last_row / BN + 1 : (T + BN - 1) / BN,
+                              (p.seg_hi + BN - 1) / BN) - jb);
+  if (n_kv == 0) {  // no key of the segment reaches these queries (uniform exit)
+    if (!p.accumulate_out && threadIdx.x < kRows && q0 + (int)threadIdx.x < T) {
+      float* o = p.out0 + ((int64_t)bh * T + q0 + threadIdx.x) * D;
+      for (int d = 0; d < D; ++d) o[d] = 0.0f;
+    }
+    return;
+  }
 
   // K_j is released by the dQ_j issuer alone: dQ_j waits for dS_j, formed
   // after the row warps read S_j, so S_j has completed by then.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8, 8, 1);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -323,8 +331,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (warp == 0) {
     const CUtensorMap* maps[2] = {&tmK, &tmV};
-    bwd_producer<C, false, false>(bars, tiles, nullptr, maps, 0, n_kv, h, b, nullptr, 0, nullptr, T,
-                           p.status);
+    bwd_producer<C, false, false>(bars, tiles, nullptr, maps, jb, jb + n_kv, h, b, nullptr, 0,
+                                  nullptr, T, p.status);
   } else if (warp == 1) {
     // S_j = Q K_j^T into S buffer j % NSB once the row warps hold S_{j-NSB}
     // (the buffer's previous contents) in registers.
@@ -375,20 +383,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(B(bars->empty_b[j % NS]));  // V_j read for the last time
         umma_commit(B(bars->dp_full[j % C::NSB]));
       };
-      // dQ_j; the first step of a chunk restarts the accumulator once the rows
-      // have folded the previous chunk out of it, the last one signals its end
-      auto issue_dQ = [&](int j) -> bool {
-        if (j > 0 && j % FOLD == 0) {
-          if (!mbar_wait(B(bars->acc_free[0]), (uint32_t)(j / FOLD - 1) & 1u, ctl, p.status))
-            return false;
-          tc_fence_after();
-        }
+      auto issue_dQ = [&](int j) {
         const uint32_t db = tmem + C::TC_DP + (uint32_t)(j % C::NSB) * C::SB;
         mma_chain<SPLIT, BN, true, BN, C::TILE>(tmem + C::TC_DQ, db, db + BN, kmd0 + stg(j), idQ,
-                                                j % FOLD != 0);
+                                                j > 0);
         umma_commit(B(bars->empty_a[j % NS]));  // K_j read for the last time
-        if ((j + 1) % FOLD == 0 && j + 1 < n_kv) umma_commit(B(bars->acc_chunk[0]));
-        return true;
       };
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       if (ok && dq_here && dp_here) {  // one buffer: dP and dQ interleaved
@@ -399,7 +398,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int j = 0; ok && j < n_kv; ++j) {
           if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
           tc_fence_after();
-          if (!(ok = issue_dQ(j))) break;
+          issue_dQ(j);
           if (j + 1 < n_kv) {
             if (!(ok = mbar_wait(B(rv[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
@@ -412,7 +411,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int bj = j % C::NSB;
           if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j / C::NSB) & 1, ctl, p.status))) break;
           tc_fence_after();
-          if (!(ok = issue_dQ(j))) break;
+          issue_dQ(j);
           umma_commit(B(bars->dqd[bj]));
         }
         if (ok) umma_commit(B(bars->done));
@@ -446,7 +445,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = q0 + quad * 32 + lane;
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    float* const dq_row = p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2);
     float l2 = 0.0f, dl = 0.0f;
     {
       const Ptr4& src = grp ? p.st1 : p.st0;
@@ -478,7 +476,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_before();
       warp_arrive(B(bars->s_free[bj]));
-      const int kv0 = j * BN + c0;
+      const int kv0 = (jb + j) * BN + c0;
       const bool need_mask = !valid || (kv0 + HB > T) || (p.causal && kv0 + HB - 1 > q0);
       // straight-line exponentials, then the mask as a separate pass on the
       // few boundary tiles (a test per column would split the unrolled loop
@@ -500,14 +498,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (!(ok = warp_wait(B(bars->dp_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
-      if (j > 0 && j % FOLD == 0) {  // fold the finished dQ chunk into this row's output
-        const int ch = j / FOLD - 1;
-        if (!(ok = warp_wait(B(bars->acc_chunk[0]), (uint32_t)ch & 1u, ctl, p.status))) break;
-        tc_fence_after();
-        tmem_cols_fold<D / 2>(lb, C::TC_DQ + grp * (D / 2), dq_row, valid, ch == 0);
-        tc_fence_before();
-        warp_arrive(B(bars->acc_free[0]));
-      }
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW];
@@ -538,8 +528,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale, dq_row, valid,
-                                 n_kv > FOLD);
+      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale,
+                                 p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2),
+                                 valid, p.accumulate_out != 0);
     }
   }
 
@@ -592,7 +583,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                            const __grid_constant__ CUtensorMap tmG,
                            const BwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
-  constexpr int FOLD = kFoldLen / BN;  // query steps per dK / dV accumulator chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
@@ -606,14 +596,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   cta_tile(p.n_tiles, p.bh_total, p.head_group, false, kt_, bh);
   const int b = bh / p.H, h = bh % p.H;
   const int k0 = kt_ * kRows, T = p.T;
-  const int j0 = p.causal ? k0 / BN : 0;
-  const int j1 = (T + BN - 1) / BN;
-  const int n = j1 - j0;
+  // query tiles [j0, j1) of this launch's segment
+  const int j0 = max(p.causal ? k0 / BN : 0, p.seg_lo / BN);
+  const int j1 = min((T + BN - 1) / BN, (p.seg_hi + BN - 1) / BN);
+  const int n = max(0, j1 - j0);
+  if (n == 0 && p.accumulate_out) return;  // nothing to add (uniform exit)
 
   // Q_i / dO_i are read by both issuers (S^T_i, dV_i by warp 1; dP^T_i, dK_i
   // by warp 10; in the dV pass S^T_i by warp 1, dV_i by warp 10): the merged
   // stage is free after both have committed.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8, 4, 4);
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 2, 2, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -628,19 +620,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
   constexpr uint32_t idS2 = idesc_tf32(128, 2 * BN, false, false);  // [hi | lo] rows (KIL)
   constexpr uint32_t idO = idesc_tf32(128, D, false, true);
-  // Gradient g's accumulator (0: dK, 1: dV) restarts every FOLD steps: before
-  // the first MMA of a chunk, wait until the rows have folded the previous
-  // chunk out of TMEM; after the last MMA of a chunk, signal its end.
-  auto fold_wait = [&](int g, int i) -> bool {
-    if (i == 0 || i % FOLD != 0) return true;
-    if (!mbar_wait(B(bars->acc_free[g]), (uint32_t)(i / FOLD - 1) & 1u, ctl, p.status))
-      return false;
-    tc_fence_after();
-    return true;
-  };
-  auto fold_signal = [&](int g, int i) {
-    if ((i + 1) % FOLD == 0 && i + 1 < n) umma_commit(B(bars->acc_chunk[g]));
-  };
 
   if (warp == 0) {
     const CUtensorMap* maps[2] = {&tmQ, &tmG};
@@ -685,13 +664,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = mbar_wait(B(bars->p_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
           if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
-          if (!(ok = fold_wait(1, i))) break;
           const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i % FOLD != 0);
+              tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
           umma_commit(B(bars->dqd[bi]));
           umma_commit(B(bars->empty_a[i % NS]));
-          fold_signal(1, i);
         }
       }
       if (ok) umma_commit(B(bars->done));
@@ -742,11 +719,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             // dO_i's MN-major copy (prepared right after the K-major ones)
             if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
-            if (!(ok = fold_wait(1, i))) break;
             const uint32_t pb = tmem + C::TC_S + (uint32_t)bi * C::SB;
             mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dV += P^T dO_i
-                tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i % FOLD != 0);
-            fold_signal(1, i);
+                tmem + C::TC_DV, pb, pb + BN, gmd0 + stg(i), idO, i > 0);
           }
           if (C::NSB == 1 && nx < n) issue_S(nx);
           umma_commit(B(bars->empty_a[i % NS]));
@@ -796,12 +771,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = mbar_wait(B(bars->ds_full[bi]), (i / C::NSB) & 1, ctl, p.status))) break;
           if (!(ok = mbar_wait(B(rdy_mn[i % NS]), (i / NS) & 1, ctl, p.status))) break;
           tc_fence_after();
-          if (!(ok = fold_wait(0, i))) break;
           const uint32_t db = tmem + C::TC_DP + (uint32_t)bi * C::SB;
           mma_chain<SPLIT, BN, true, BN, C::TILE>(  // dK += dS^T Q_i
-              tmem + C::TC_DK, db, db + BN, qmd0 + stg(i), idO, i % FOLD != 0);
+              tmem + C::TC_DK, db, db + BN, qmd0 + stg(i), idO, i > 0);
           umma_commit(B(bars->empty_a[i % NS]));  // Q_i, dO_i read for the last time
-          fold_signal(0, i);
           if (nx < n) {
             if (!(ok = mbar_wait(B(rdy[nx % NS]), (nx / NS) & 1, ctl, p.status))) break;
             tc_fence_after();
@@ -831,8 +804,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int row = k0 + quad * 32 + lane;  // key row
     const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
-    float* const out = grp ? p.out1 : p.out0;  // dV (group 1) or dK (group 0) rows
     if (grp == 0 || C::DO_DK) {  // V is read only by dP^T
       const Ptr4& src = grp ? p.st1 : p.st0;
       const float* r = src.row(b, h, valid ? row : 0);
@@ -854,19 +825,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float* vl = vec + (i % NS) * 2 * BN + c0;
       if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
-      // Fold the finished dV chunk here (group 1), and the dK chunk (group 0)
-      // here too when the P phase's registers are many (HB > 32); otherwise
-      // group 0 folds in the dS phase, when dK_{i-1} has surely completed.
-      constexpr bool kDkFoldEarly = HB > 32;
-      if (i > 0 && i % FOLD == 0 &&
-          ((C::DO_DV && grp == 1) || (C::DO_DK && kDkFoldEarly && grp == 0))) {
-        const int g = grp == 1 ? 1 : 0, ch = i / FOLD - 1;
-        if (!(ok = warp_wait(B(bars->acc_chunk[g]), (uint32_t)ch & 1u, ctl, p.status))) break;
-        tc_fence_after();
-        tmem_cols_fold<D>(lb, g ? C::TC_DV : C::TC_DK, out + orow, valid, ch == 0);
-        tc_fence_before();
-        warp_arrive(B(bars->acc_free[g]));
-      }
       const bool need_mask = !valid || (qs + HB > T) || (p.causal && qs < k0 + kRows - 1);
       float pv[HB];
 #pragma unroll
@@ -917,14 +875,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if constexpr (!C::DO_DK) continue;
       if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
       tc_fence_after();
-      if (!kDkFoldEarly && grp == 0 && i > 0 && i % FOLD == 0) {  // fold the finished dK chunk
-        const int ch = i / FOLD - 1;
-        if (!(ok = warp_wait(B(bars->acc_chunk[0]), (uint32_t)ch & 1u, ctl, p.status))) break;
-        tc_fence_after();
-        tmem_cols_fold<D>(lb, C::TC_DK, out + orow, valid, ch == 0);
-        tc_fence_before();
-        warp_arrive(B(bars->acc_free[0]));
-      }
 #pragma unroll
       for (int c = 0; c < HB / CW; ++c) {
         float t[CW], lo[CW], dv[CW];
@@ -955,16 +905,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       warp_arrive(B(bars->ds_full[bi]));
     }
+    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
+    float* out = grp ? p.out1 : p.out0;
     if (grp == 0 ? !C::DO_DK : !C::DO_DV) {
       // this pass does not produce the group's gradient
-    } else if (n == 0) {  // no query reaches these keys (cannot happen for k0 < T)
+    } else if (n == 0) {  // no query of the first segment reaches these keys
       if (valid) {
         for (int d = 0; d < D; ++d) out[orow + d] = 0.0f;
       }
     } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
       tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid,
-                            n > FOLD);
+                            p.accumulate_out != 0);
     }
   }
 
@@ -995,6 +947,9 @@ BwdParams make_params(const Fa2Problem& pr, Strided4 a, Strided4 b, const float*
   p.bh_total = (int)(pr.B * pr.H);
   p.head_group = fa2_head_group(p.bh_total);
   p.causal = pr.causal ? 1 : 0;
+  p.seg_lo = 0;
+  p.seg_hi = (int)pr.T;
+  p.accumulate_out = 0;
   p.scale = (float)(1.0 / std::sqrt((double)pr.D));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
   p.status = dev.status;
@@ -1018,8 +973,15 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, q, g, lse, ls, delta, dq, nullptr, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tk, tv, p);
-  return check_launch();
+  for (int64_t s0 = 0; s0 < pr.T; s0 += kSegLen) {  // one launch per key segment
+    p.seg_lo = (int)s0;
+    p.seg_hi = (int)std::min<int64_t>(s0 + kSegLen, pr.T);
+    p.accumulate_out = s0 > 0;
+    fa2_bwd_dq_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tk, tv, p);
+    rc = check_launch();
+    if (rc != CT_OK) return rc;
+  }
+  return CT_OK;
 }
 
 template <class C>
@@ -1037,8 +999,15 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
   const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
-  fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tg, p);
-  return check_launch();
+  for (int64_t s0 = 0; s0 < pr.T; s0 += kSegLen) {  // one launch per query segment
+    p.seg_lo = (int)s0;
+    p.seg_hi = (int)std::min<int64_t>(s0 + kSegLen, pr.T);
+    p.accumulate_out = s0 > 0;
+    fa2_bwd_dkdv_tc_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tg, p);
+    rc = check_launch();
+    if (rc != CT_OK) return rc;
+  }
+  return CT_OK;
 }
 
 }  // namespace

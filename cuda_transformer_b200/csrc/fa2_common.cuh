@@ -186,8 +186,8 @@ __device__ __forceinline__ float max32(const float (&t)[32]) {
 
 // Stores NC (16 or a multiple of 32) TMEM columns [col, col+NC) of this
 // thread's lane times `scale` to dense global memory.  With `add_partial`,
-// dst already holds the partial sums folded out of TMEM earlier
-// (tmem_cols_fold): the result is (dst + TMEM) * scale.
+// dst already holds the previous segments' sum (kSegLen): the result is
+// dst + TMEM * scale.
 template <int NC>
 __device__ __forceinline__ void tmem_cols_to_global(uint32_t lane_base, uint32_t col, float scale,
                                                     float* dst, bool valid,
@@ -202,12 +202,13 @@ __device__ __forceinline__ void tmem_cols_to_global(uint32_t lane_base, uint32_t
       float4* d4 = reinterpret_cast<float4*>(dst + CW * c);
 #pragma unroll
       for (int i = 0; i < CW / 4; ++i) {
-        float4 a = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        float4 a = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale,
+                               v[4 * i + 3] * scale);
         if (add_partial) {
           const float4 o = d4[i];
           a = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
         }
-        d4[i] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+        d4[i] = a;
       }
     }
   }
@@ -221,36 +222,15 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t 
 }
 
 // Long reductions.  The tensor core adds each MMA's products into its FP32
-// accumulator with a rounding biased toward zero (measured: over 16384-long
-// reductions in 3xTF32 the gradients came out ~1.5e-4 relatively small), so
-// the gradient accumulators are restarted every kFoldLen keys / queries and
-// the chunk sums are added in FP32 with round-to-nearest: the row thread adds
-// its lane's NC accumulator columns into its own row of the output (stored
-// unscaled, in L2), `first` storing instead.  Fixed order: deterministic.
-constexpr int kFoldLen = 1024;
-template <int NC>
-__device__ __forceinline__ void tmem_cols_fold(uint32_t lane_base, uint32_t col, float* dst,
-                                               bool valid, bool first) {
-  constexpr int CW = NC < 32 ? NC : 32;
-  static_assert(NC % CW == 0, "column count");
-#pragma unroll
-  for (int c = 0; c < NC / CW; ++c) {
-    float v[CW];
-    tmem_ldn<CW>(lane_base + col + CW * c, v);
-    if (valid) {
-      float4* d4 = reinterpret_cast<float4*>(dst + CW * c);
-#pragma unroll
-      for (int i = 0; i < CW / 4; ++i) {
-        float4 a = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        if (!first) {
-          const float4 o = d4[i];
-          a = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
-        }
-        d4[i] = a;
-      }
-    }
-  }
-}
+// accumulator with a rounding biased toward zero: the relative error of a
+// gradient grows with the reduction length (measured in 3xTF32: ~4e-5 at
+// 4096 keys, 1.5e-4 at 16384).  The backward therefore reduces over at most
+// kSegLen keys (dQ) or queries (dK, dV) per launch: longer sequences run one
+// launch per segment, each adding its FP32 partial gradient into the output
+// written by the previous one (round-to-nearest adds, fixed order:
+// deterministic), which keeps the error at the one-segment level at any
+// length.  The step loops are the same for every segment.
+constexpr int kSegLen = 4096;
 
 // D (+)= A x B over K = KDIM in steps of 8: A from TMEM columns a_hi (+ a_lo
 // for the 3xTF32 low part), B from a shared-memory tile whose k-step-0

@@ -233,3 +233,22 @@ def test_head_dim_128_at_length(cuda_device, prec):
     torch.cuda.synchronize()
     _check_against((o, lse, dq, dk, dv), ref, TOL[prec])
     H.assert_device_clean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", [cb.PRECISION_3XTF32, cb.PRECISION_TF32])
+@pytest.mark.parametrize("T,causal", [(4097, True), (4296, False), (8256, True)])
+def test_segment_boundaries(cuda_device, prec, T, causal):
+    """Backward reductions longer than one segment (4096 keys / queries) run
+    as several launches that add into the previous one's output: ragged last
+    segments, causal tiles with no work in a segment, and bit determinism."""
+    (q, k, v, do), ref = _long_case(("seg", T, causal), (1, 1, T, 64), 90 + T % 97, causal,
+                                    cuda_device)
+    o, lse = H.fa2_fwd(q, k, v, causal, prec)
+    g1 = H.fa2_bwd(q, k, v, o, do, lse, causal, prec)
+    g2 = H.fa2_bwd(q, k, v, o, do, lse, causal, prec)
+    torch.cuda.synchronize()
+    _check_against((o, lse, *g1), ref, TOL[prec])
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+    H.assert_device_clean()
