@@ -632,10 +632,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       auto issue_S = [&](int i) {
         const uint32_t sb = (uint32_t)(i % C::NSB) * C::SB;
-        mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
-                                                tmem + C::TC_K + D,
-                                                sdesc_kmajor(tiles + C::OFF_A0) + stg(i), idS,
-                                                false);
+        if constexpr (C::KILA)
+          mma_chain_kil<D, C::KCHA>(tmem + C::TC_S + sb, tmem + C::TC_K, tmem + C::TC_K + D,
+                                   sdesc_kmajor(tiles + C::OFF_A0) + stg(i), idS2, idS);
+        else
+          mma_chain<SPLIT, D, false, BN, C::TILE>(tmem + C::TC_S + sb, tmem + C::TC_K,
+                                                  tmem + C::TC_K + D,
+                                                  sdesc_kmajor(tiles + C::OFF_A0) + stg(i), idS,
+                                                  false);
         umma_commit(B(bars->s_full[i % C::NSB]));
       };
       const uint32_t fin = B(warp == 1 ? bars->mma_final : bars->mma_final2);
@@ -928,6 +932,303 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+
+// ------------------------------------------------------- 64-row (M = 64) pass
+// Head dim 128 in 3xTF32: the hi / lo copies of two stationary 128-column
+// operands alone fill the 512 TMEM columns of a 128-row tile.  An M = 64 MMA
+// keeps its rows in 16 lanes of each warp's lane quadrant (row r in lane
+// 32 * (r / 16) + r % 16, plus 16 in the quadrant's upper half; the A operand
+// read from TMEM sits in the same lanes as the accumulator), so a 64-row tile
+// gives each stationary operand its own half of the lanes:
+//   lower halves: X hi | X lo | S (two partial sums)
+//   upper halves: Y hi | Y lo | dP (two partial sums, then dS hi | lo) | gradient
+//   S = X A_j^T,  dP = Y B_j^T,  dS = P * (dP - delta),  grad += dS A_j
+// QSTAT (dQ pass): X = Q, Y = dO, A = K, B = V, grad = dQ, P and delta per row.
+// !QSTAT (dK pass): X = K, Y = V, A = Q, B = dO, grad = dK, P and delta per
+// column (staged in shared memory by the producer warp).
+// P = exp2(S * log2e / sqrt(D) - LSE * log2e) and delta = rowsum(O * dO) are
+// per query (flash_attention.cuh:318-326 for dQ, :452-476 for dK).  The row
+// warps read both halves with the 16-lane 16x32bx2 shape, so one thread sees
+// S and dP of the same element: row 16 * quad + lane % 16, a quarter of the
+// step's columns (lane half x row warpgroup).
+// Warps: 0 TMA producer, 1 TMEM allocator and S issuer, 2, 3, 8, 9 tile
+// preparation (3xTF32 split; MN-major copy of A), 10 dP and gradient issuer,
+// 4-7 and 11-14 row warps, 15 idle.
+constexpr int kRows64 = 64;
+constexpr uint32_t kUpperLanes = 16u << 16;  // TMEM lane offset of a quadrant's upper half
+
+template <int D_, int BN_, int NS_>
+struct Half64Cfg : BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true> {
+  using T_ = BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true>;
+  static constexpr uint32_t SB = 2u * BN_;  // one S / dP buffer
+  static constexpr uint32_t TC_X = 0, TC_S = 2u * D_;                     // lower halves
+  static constexpr uint32_t TC_Y = 0, TC_DP = 2u * D_, TC_G = 2u * D_ + SB;  // upper halves
+  static constexpr int CT = BN_ / 4;  // score columns per row thread per step
+  static_assert(D_ == 128, "the 64-row pass is the head-dim-128 3xTF32 path");
+  static_assert(CT == 8 || CT == 16, "16x32bx2 access width");
+  static_assert(TC_G + D_ <= T_::TMEM_COLS && TC_S + SB <= T_::TMEM_COLS, "TMEM budget");
+};
+
+template <class C, bool QSTAT>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    fa2_bwd_m64_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB, const BwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS = C::NS, CT = C::CT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(BwdBars<NS>) + 1023u) & ~1023u;
+  float* vec = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) + NS * C::STAGE);
+  CtaCtl* ctl = &bars->ctl;
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  int tile, bh;  // head-major; dQ: late (heavy) query tiles first
+  cta_tile(p.n_tiles, p.bh_total, p.head_group, QSTAT, tile, bh);
+  const int b = bh / p.H, h = bh % p.H;
+  const int r0 = tile * kRows64, T = p.T;
+  // streamed tiles [j0, j0 + n) of this launch's segment
+  int j0, n;
+  if constexpr (QSTAT) {
+    const int last_row = min(r0 + kRows64 - 1, T - 1);
+    j0 = p.seg_lo / BN;
+    n = max(0, min(p.causal ? last_row / BN + 1 : (T + BN - 1) / BN, (p.seg_hi + BN - 1) / BN) -
+                   j0);
+  } else {
+    j0 = max(p.causal ? r0 / BN : 0, p.seg_lo / BN);
+    n = max(0, min((T + BN - 1) / BN, (p.seg_hi + BN - 1) / BN) - j0);
+  }
+  if (n == 0) {  // nothing of the segment reaches these rows (uniform exit)
+    if (!p.accumulate_out && threadIdx.x < kRows64 && r0 + (int)threadIdx.x < T) {
+      float* o = p.out0 + ((int64_t)bh * T + r0 + threadIdx.x) * D;
+      for (int d = 0; d < D; ++d) o[d] = 0.0f;
+    }
+    return;
+  }
+
+  // A_j is released by the gradient MMA (issued after dS_j, i.e. after S_j
+  // was read), B_j by dP_j.
+  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
+  constexpr uint32_t idS2 = idesc_tf32(64, 2 * BN, false, false);  // [hi | lo] rows (kil)
+  constexpr uint32_t idS = idesc_tf32(64, BN, false, false);
+  constexpr uint32_t idG = idesc_tf32(64, D, false, true);
+
+  if (warp == 0) {
+    const CUtensorMap* maps[2] = {&tmA, &tmB};
+    if constexpr (QSTAT)
+      bwd_producer<C, false, false>(bars, tiles, nullptr, maps, j0, j0 + n, h, b, nullptr, 0,
+                                    nullptr, T, p.status);
+    else
+      bwd_producer<C, true, false>(bars, tiles, vec, maps, j0, j0 + n, h, b,
+                                   p.lse + b * p.l0 + h * p.l1, p.l2, p.delta + (int64_t)bh * T,
+                                   T, p.status);
+  } else if (warp == 1) {
+    // S_j = X A_j^T (lower halves) once the rows hold S_{j-1} in registers.
+    if (lane == 0) {
+      const uint64_t ad0 = sdesc_kmajor(tiles + C::OFF_A0);
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j > 0 && !(ok = mbar_wait(B(bars->s_free[0]), (j - 1) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_a[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        mma_chain_kil<D, C::KCHA>(tmem + C::TC_S, tmem + C::TC_X, tmem + C::TC_X + D,
+                                  ad0 + stg(j), idS2, idS);
+        umma_commit(B(bars->s_full[0]));
+      }
+      umma_commit(B(bars->mma_final));
+      mbar_drain(B(bars->mma_final), 0);
+    }
+    __syncwarp();
+  } else if (warp == kIssuer2Warp) {
+    // dP_j = Y B_j^T and grad += dS_j A_j (upper halves); dP_{j+1} overwrites
+    // dS_j after grad_j in this thread's issue order.
+    if (lane == 0) {
+      const uint64_t bd0 = sdesc_kmajor(tiles + C::OFF_B0);
+      const uint64_t amd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
+      const uint32_t up = tmem + kUpperLanes;
+      auto issue_dP = [&](int j) {
+        mma_chain_kil<D, C::KCHB>(up + C::TC_DP, up + C::TC_Y, up + C::TC_Y + D, bd0 + stg(j),
+                                  idS2, idS);
+        umma_commit(B(bars->empty_b[j % NS]));  // B_j read for the last time
+        umma_commit(B(bars->dp_full[0]));
+      };
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
+                mbar_wait(B(bars->ready_b[0]), 0, ctl, p.status);
+      if (ok) {
+        tc_fence_after();
+        issue_dP(0);
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
+        tc_fence_after();
+        mma_chain<3, BN, true, BN, C::TILE>(up + C::TC_G, up + C::TC_DP, up + C::TC_DP + BN,
+                                            amd0 + stg(j), idG, j > 0);
+        umma_commit(B(bars->empty_a[j % NS]));  // A_j read for the last time
+        if (j + 1 < n) {
+          if (!(ok = mbar_wait(B(bars->ready_b[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl,
+                               p.status)))
+            break;
+          tc_fence_after();
+          issue_dP(j + 1);
+        }
+      }
+      if (ok) umma_commit(B(bars->done));
+      umma_commit(B(bars->mma_final2));
+      mbar_drain(B(bars->mma_final2), 0);
+    }
+    __syncwarp();
+  } else if (is_prep_warp(warp)) {
+    bwd_splitter<C, false>(bars, tiles, n, p.status);
+  } else if (warp != kIssuer3Warp) {
+    // Row warps 4-7 (group 0) and 11-14 (group 1) of lane quadrant q = warp % 4.
+    const int quad = warp & 3;
+    const int grp = warp >= kBwdRowWarp1 ? 1 : 0;
+    const int hl = lane >> 4;                 // lane half: which columns of a 16x32bx2 access
+    const int row = r0 + 16 * quad + (lane & 15);
+    const bool valid = row < T;
+    const uint32_t qlo = tmem + ((32u * quad) << 16);  // the quadrant's lower half
+    const uint32_t qup = qlo + kUpperLanes;            // and upper half
+    // Stationary rows into TMEM (32x32b: each thread its own lane): lanes
+    // 0-15 X's row into the lower half, lanes 16-31 Y's row into the upper
+    // half; group g writes head-dim columns [g D/2, (g + 1) D/2), hi and lo.
+    {
+      const int srow = r0 + 16 * quad + (lane & 15);
+      const bool sval = srow < T;
+      const Ptr4& src = hl ? p.st1 : p.st0;
+      const float* rp = src.row(b, h, sval ? srow : 0);
+      const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(rp) & 15u) == 0);
+      const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        const int col = grp * (D / 2) + 32 * c;
+        float x[32], lo[32];
+        load_row32(src, rp, col, sval, vr, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float hi;
+          tf32_split(x[i], hi, lo[i]);
+          x[i] = hi;
+        }
+        tmem_st32(lb + C::TC_X + col, x);  // TC_X == TC_Y: the lane picks the operand
+        tmem_st32(lb + C::TC_X + D + col, lo);
+      }
+      tmem_wait_st();
+    }
+    float l2 = 0.0f, dl = 0.0f;  // per-row LSE * log2e and delta (dQ pass)
+    if constexpr (QSTAT) {
+      if (valid) {
+        l2 = __ldg(p.lse + b * p.l0 + h * p.l1 + (int64_t)row * p.l2) * kLog2e;
+        dl = __ldg(p.delta + (int64_t)bh * T + row);
+      }
+    }
+    tc_fence_before();
+    warp_arrive(B(bars->rows_ready));
+    const int cs = grp * (BN / 2) + hl * CT;  // this thread's first column of a step
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int col0 = (j0 + j) * BN + cs;  // its key (dQ) or query (dK) index
+      float lv[CT], dv[CT];
+      if constexpr (!QSTAT) {  // the step's -LSE * log2e and delta, per column
+        if (!(ok = warp_wait(B(bars->vec_full[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        const float* vs = vec + (j % NS) * 2 * BN + cs;
+        load_vecn<CT>(vs, lv);
+        load_vecn<CT>(vs + BN, dv);
+      } else {
+#pragma unroll
+        for (int x = 0; x < CT; ++x) {
+          lv[x] = -l2;
+          dv[x] = dl;
+        }
+      }
+      if (!(ok = warp_wait(B(bars->s_full[0]), j & 1, ctl, p.status))) break;
+      tc_fence_after();
+      float pv[CT];
+      {
+        float t1[CT];
+        tmem_ld_16x32bx2<CT>(qlo + C::TC_S + grp * (BN / 2), pv);
+        tmem_ld_16x32bx2<CT>(qlo + C::TC_S + BN + grp * (BN / 2), t1);
+#pragma unroll
+        for (int x = 0; x < CT; x += 2) fadd2(pv[x], pv[x + 1], pv[x], pv[x + 1], t1[x], t1[x + 1]);
+      }
+      tc_fence_before();
+      warp_arrive(B(bars->s_free[0]));  // S_j read: S_{j+1} may overwrite it
+#pragma unroll
+      for (int x = 0; x < CT; x += 2) {
+        float a0, a1;
+        ffma2(a0, a1, pv[x], pv[x + 1], p.scale_log2, p.scale_log2, lv[x], lv[x + 1]);
+        pv[x] = ex2_approx(a0);
+        pv[x + 1] = ex2_approx(a1);
+      }
+      const bool need_mask =
+          !valid || (col0 + CT > T) ||
+          (p.causal && (QSTAT ? (col0 + CT - 1 > row) : (col0 < row)));
+      if (need_mask) {
+#pragma unroll
+        for (int x = 0; x < CT; ++x) {
+          const int c = col0 + x;
+          const bool keep = valid && c < T && (!p.causal || (QSTAT ? c <= row : c >= row));
+          pv[x] = keep ? pv[x] : 0.0f;
+        }
+      }
+      if (!(ok = warp_wait(B(bars->dp_full[0]), j & 1, ctl, p.status))) break;
+      tc_fence_after();
+      const uint32_t dpb = qup + C::TC_DP + grp * (BN / 2);
+      float d0[CT], d1[CT];
+      tmem_ld_16x32bx2<CT>(dpb, d0);
+      tmem_ld_16x32bx2<CT>(dpb + BN, d1);
+#pragma unroll
+      for (int x = 0; x < CT; x += 2) {
+        float u0, u1, s0, s1;
+        fadd2(u0, u1, d0[x], d0[x + 1], d1[x], d1[x + 1]);        // dP from its partial sums
+        fsub2(u0, u1, u0, u1, dv[x], dv[x + 1]);
+        fmul2(s0, s1, pv[x], pv[x + 1], u0, u1);                  // dS = P (dP - delta)
+        tf32_split2(s0, s1, d0[x], d0[x + 1], d1[x], d1[x + 1]);  // hi | lo
+      }
+      tmem_st_16x32bx2<CT>(dpb, d0);
+      tmem_st_16x32bx2<CT>(dpb + BN, d1);
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive(B(bars->ds_full[0]));
+    }
+    if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
+      tc_fence_after();
+      // gradient rows (upper halves): group g, lane half -> columns [g D/2 + 32 hl, +32)
+      float v[32];
+      tmem_ld_16x32bx2<32>(qup + C::TC_G + grp * (D / 2), v);
+      if (valid) {
+        float4* d4 =
+            reinterpret_cast<float4*>(p.out0 + ((int64_t)bh * T + row) * D + grp * (D / 2) + 32 * hl);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 a = make_float4(v[4 * i] * p.scale, v[4 * i + 1] * p.scale,
+                                 v[4 * i + 2] * p.scale, v[4 * i + 3] * p.scale);
+          if (p.accumulate_out) {
+            const float4 o = d4[i];
+            a = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
+          }
+          d4[i] = a;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 BwdParams make_params(const Fa2Problem& pr, Strided4 a, Strided4 b, const float* lse,
                       const int64_t ls[3], const float* delta, float* out0, float* out1,
                       const DeviceInfo& dev) {
@@ -1010,12 +1311,40 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
   return CT_OK;
 }
 
+// The 64-row pass: streamed tiles a (A: S and the gradient) and bb (B: dP),
+// stationary x (X) and y (Y); the gradient into grad.
+template <class C, bool QSTAT>
+int run_m64(const Fa2Problem& pr, Strided4 a, Strided4 bb, Strided4 x, Strided4 y,
+            const float* lse, const int64_t ls[3], const float* delta, float* grad,
+            const DeviceInfo& dev, cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap ta, tb;  // interleaved hi / lo tiles load chunk by chunk
+  int rc = make_tmap_bhtd(&ta, a, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd(&tb, bb, pr, C::BN);
+  if (rc != CT_OK) return rc;
+  const size_t smem = bwd_smem_bytes<C>();
+  rc = ensure_smem_attr(fa2_bwd_m64_tc_kernel<C, QSTAT>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  BwdParams p = make_params(pr, x, y, lse, ls, delta, grad, nullptr, dev);
+  p.n_tiles = (int)((pr.T + kRows64 - 1) / kRows64);
+  const int64_t grid = (int64_t)p.n_tiles * p.bh_total;
+  for (int64_t s0 = 0; s0 < pr.T; s0 += kSegLen) {  // one launch per segment
+    p.seg_lo = (int)s0;
+    p.seg_hi = (int)std::min<int64_t>(s0 + kSegLen, pr.T);
+    p.accumulate_out = s0 > 0;
+    fa2_bwd_m64_tc_kernel<C, QSTAT><<<(unsigned)grid, kBwdThreads, smem, st>>>(ta, tb, p);
+    rc = check_launch();
+    if (rc != CT_OK) return rc;
+  }
+  return CT_OK;
+}
+
 }  // namespace
 
 bool fa2_bwd_tc_supported(const Fa2Problem& p) {
-  // D = 128 in TF32 only: in 3xTF32 the hi / lo copies of the two stationary
-  // 128-column operands alone fill TMEM.
-  return (p.D == 32 || p.D == 64 || (p.D == 128 && p.precision == CT_PRECISION_TF32)) &&
+  // D = 128 in 3xTF32 runs the 64-row pass (the hi / lo copies of two
+  // stationary 128-column operands fill the TMEM of a 128-row tile).
+  return (p.D == 32 || p.D == 64 || p.D == 128) &&
          (p.precision == CT_PRECISION_3XTF32 || p.precision == CT_PRECISION_TF32) &&
          p.T < (1ll << 31) && ((p.T + kRows - 1) / kRows) * p.B * p.H < (1ll << 31);
 }
@@ -1031,8 +1360,9 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 
   if (pr.D == 32)
     return split ? run_dq<DqCfg<32, 64, 3, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<32, 128, 1, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
-  if (pr.D == 128 && !split)
-    return run_dq<DqCfg<128, 64, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
+  if (pr.D == 128)
+    return split ? run_m64<Half64Cfg<128, 32, 2>, true>(pr, k, v, q, g, lse, ls, delta, dq, dev, st)
+                 : run_dq<DqCfg<128, 64, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
 
@@ -1053,6 +1383,12 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
     if (rc != CT_OK) return rc;
     return run_dkdv<DkvCfg<128, 32, 1, 4, 2, kDkvOnlyDk>>(pr, q, k, v, g, lse, ls, delta, dk, dv,
                                                           dev, st);
+  }
+  if (pr.D == 128) {  // 3xTF32: dV on 128-row tiles, then dK on 64-row tiles (K, V in lane halves)
+    const int rc =
+        run_dkdv<DkvCfg<128, 32, 3, 2, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+    if (rc != CT_OK) return rc;
+    return run_m64<Half64Cfg<128, 32, 2>, false>(pr, q, g, k, v, lse, ls, delta, dk, dev, st);
   }
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }

@@ -287,6 +287,60 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       CT_W8(0), CT_W8(8)
       : "memory");
 }
+// 16 lanes x 32-bit, two halves (M = 64 accumulators, whose rows occupy 16
+// lanes of each warp's quadrant): threads 0-15 access lanes base .. base + 15
+// at columns [col, col + N), threads 16-31 the same lanes at [col + N,
+// col + 2N) (half-split offset N).  The address's lane field selects the
+// quadrant's lower (+0) or upper (+16) half.  N in {8, 16, 32}.
+template <int N>
+__device__ __forceinline__ void tmem_ld_16x32bx2(uint32_t taddr, float (&v)[N]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  static_assert(N == 8 || N == 16 || N == 32, "16x32bx2 width");
+  if constexpr (N == 8) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], 8;\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : CT_R8(0)
+        : "r"(taddr)
+        : "memory");
+  } else if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15}, [%16], 16;\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : CT_R8(0), CT_R8(8)
+        : "r"(taddr)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], "
+        "32;\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : CT_R8(0), CT_R8(8), CT_R8(16), CT_R8(24)
+        : "r"(taddr)
+        : "memory");
+  }
+}
+// Store counterpart of tmem_ld_16x32bx2 (does not wait; tmem_wait_st before
+// publishing).
+template <int N>
+__device__ __forceinline__ void tmem_st_16x32bx2(uint32_t taddr, const float (&v)[N]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  static_assert(N == 8 || N == 16, "16x32bx2 width");
+  if constexpr (N == 8) {
+    asm volatile("tcgen05.st.sync.aligned.16x32bx2.x8.b32 [%0], 8, {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                     taddr),
+                 CT_W8(0)
+                 : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 16, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+        "%12,%13,%14,%15,%16};" ::"r"(taddr),
+        CT_W8(0), CT_W8(8)
+        : "memory");
+  }
+}
 #undef CT_R8
 #undef CT_W8
 
