@@ -162,7 +162,7 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars<C::NS>* bars, int empty_co
 // VEC, all lanes then stage the step's per-query log-sum-exp (times log2 e) and
 // delta into the stage's vector slot, so the row warps read them from shared
 // memory.
-template <class C, bool VEC, bool MERGED>
+template <class C, bool VEC, bool MERGED, bool B_FIRST = false>
 __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tiles, float* vec,
                                              const CUtensorMap* const* maps, int j0, int j1,
                                              int h, int b, const float* lse_bh, int64_t lse_t,
@@ -193,23 +193,36 @@ __device__ __forceinline__ void bwd_producer(BwdBars<C::NS>* bars, uint32_t tile
   for (int j = j0; j < j1; ++j) {
     const int i = j - j0, s = i % NS, r = i / NS;
     const uint32_t st = tiles + s * C::STAGE;
-    if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) break;
     // The tile copies go first: the vector values are needed only by the row
-    // warps, much later, and signal their own barrier.
-    if (lane == 0) {
-      const uint32_t fa = B(bars->full_a[s]);
-      // only the K-major copy: the preparation warps write the MN-major one
-      mbar_arrive_expect_tx(fa, C::TILE);
-      tma_load_tile<!C::KILA, D>(st + C::OFF_A0, maps[0], fa, j * BN, h, b, C::KCHA);
+    // warps, much later, and signal their own barrier.  B_FIRST (separate
+    // stage releases): B's copy, freed earlier by its single reader, first.
+    auto load_a = [&]() -> bool {
+      if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, status)) return false;
+      if (lane == 0) {
+        const uint32_t fa = B(bars->full_a[s]);
+        // only the K-major copy: the preparation warps write the MN-major one
+        mbar_arrive_expect_tx(fa, C::TILE);
+        tma_load_tile<!C::KILA, D>(st + C::OFF_A0, maps[0], fa, j * BN, h, b, C::KCHA);
+      }
+      last_a[s] = r;
+      return true;
+    };
+    auto load_b = [&]() -> bool {
+      if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status))
+        return false;
+      if (lane == 0) {
+        const uint32_t fb = B(bars->full_b[s]);
+        mbar_arrive_expect_tx(fb, C::TILE);
+        tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[1], fb, j * BN, h, b, C::KCHB);
+      }
+      last_b[s] = r;
+      return true;
+    };
+    if (B_FIRST) {
+      if (!load_b() || !load_a()) break;
+    } else {
+      if (!load_a() || !load_b()) break;
     }
-    last_a[s] = r;
-    if (!MERGED && r > 0 && !warp_wait(B(bars->empty_b[s]), (r - 1) & 1, ctl, status)) break;
-    if (lane == 0) {
-      const uint32_t fb = B(bars->full_b[s]);
-      mbar_arrive_expect_tx(fb, C::TILE);
-      tma_load_tile<!C::KILB, D>(st + C::OFF_B0, maps[1], fb, j * BN, h, b, C::KCHB);
-    }
-    last_b[s] = r;
     if constexpr (VEC) {
       float* vs = vec + s * 2 * BN;
 #pragma unroll
@@ -258,7 +271,7 @@ __device__ __forceinline__ void prep_tile(uint32_t st, bool is_b, uint32_t tid) 
 // dK/dV pass (MERGED) the issuers wait on ready_a for the K-major copies of
 // both tiles (S^T, dP^T) and on ready_b for the MN-major ones (dV, dK); both
 // complete once the two tiles are prepared.
-template <class C, bool MERGED>
+template <class C, bool MERGED, bool B_FIRST = false>
 __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tiles, int n,
                                              uint32_t* status) {
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
@@ -266,6 +279,17 @@ __device__ __forceinline__ void bwd_splitter(BwdBars<C::NS>* bars, uint32_t tile
   for (int i = 0; i < n; ++i) {
     const int s = i % C::NS, r = i / C::NS;
     const uint32_t st = tiles + s * C::STAGE;
+    if constexpr (B_FIRST) {  // separate stages: B, then A, each released as prepared
+      if (!warp_wait(B(bars->full_b[s]), r & 1, &bars->ctl, status)) break;
+      prep_tile<C>(st, true, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_b[s]));
+      if (!warp_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
+      prep_tile<C>(st, false, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_a[s]));
+      continue;
+    }
     if (!warp_wait(B(bars->full_a[s]), r & 1, &bars->ctl, status)) break;
     prep_tile<C>(st, false, tid);
     if (!MERGED) {
@@ -940,8 +964,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // 32 * (r / 16) + r % 16, plus 16 in the quadrant's upper half; the A operand
 // read from TMEM sits in the same lanes as the accumulator), so a 64-row tile
 // gives each stationary operand its own half of the lanes:
-//   lower halves: X hi | X lo | S (two partial sums)
-//   upper halves: Y hi | Y lo | dP (two partial sums, then dS hi | lo) | gradient
+//   lower halves: X hi | X lo | 2 x S (two partial sums)
+//   upper halves: Y hi | Y lo | 2 x dP (two partial sums, then dS hi | lo) | gradient
 //   S = X A_j^T,  dP = Y B_j^T,  dS = P * (dP - delta),  grad += dS A_j
 // QSTAT (dQ pass): X = Q, Y = dO, A = K, B = V, grad = dQ, P and delta per row.
 // !QSTAT (dK pass): X = K, Y = V, A = Q, B = dO, grad = dK, P and delta per
@@ -951,22 +975,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // warps read both halves with the 16-lane 16x32bx2 shape, so one thread sees
 // S and dP of the same element: row 16 * quad + lane % 16, a quarter of the
 // step's columns (lane half x row warpgroup).
-// Warps: 0 TMA producer, 1 TMEM allocator and S issuer, 2, 3, 8, 9 tile
-// preparation (3xTF32 split; MN-major copy of A), 10 dP and gradient issuer,
-// 4-7 and 11-14 row warps, 15 idle.
+// S and dP are double-buffered (step j in buffer j % 2), so S_{j+1} and
+// dP_{j+1} run on the tensor core while the rows form dS_j.  Warps: 0 TMA
+// producer (B tiles before A tiles: a B stage is freed by dP alone, early),
+// 1 TMEM allocator and S issuer, 2, 3, 8, 9 tile preparation (3xTF32 split;
+// MN-major copy of A), 10 gradient issuer, 15 dP issuer, 4-7 and 11-14 row
+// warps.
 constexpr int kRows64 = 64;
 constexpr uint32_t kUpperLanes = 16u << 16;  // TMEM lane offset of a quadrant's upper half
 
 template <int D_, int BN_, int NS_>
 struct Half64Cfg : BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true> {
   using T_ = BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true>;
+  static constexpr int NSB = 2;
   static constexpr uint32_t SB = 2u * BN_;  // one S / dP buffer
-  static constexpr uint32_t TC_X = 0, TC_S = 2u * D_;                     // lower halves
-  static constexpr uint32_t TC_Y = 0, TC_DP = 2u * D_, TC_G = 2u * D_ + SB;  // upper halves
+  static constexpr uint32_t TC_X = 0, TC_S = 2u * D_;                           // lower halves
+  static constexpr uint32_t TC_Y = 0, TC_DP = 2u * D_, TC_G = 2u * D_ + NSB * SB;  // upper halves
   static constexpr int CT = BN_ / 4;  // score columns per row thread per step
   static_assert(D_ == 128, "the 64-row pass is the head-dim-128 3xTF32 path");
   static_assert(CT == 8 || CT == 16, "16x32bx2 access width");
-  static_assert(TC_G + D_ <= T_::TMEM_COLS && TC_S + SB <= T_::TMEM_COLS, "TMEM budget");
+  static_assert(TC_G + D_ <= T_::TMEM_COLS && TC_S + NSB * SB <= T_::TMEM_COLS, "TMEM budget");
 };
 
 template <class C, bool QSTAT>
@@ -1007,7 +1035,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 
   // A_j is released by the gradient MMA (issued after dS_j, i.e. after S_j
-  // was read), B_j by dP_j.
+  // was read), B_j by dP_j; dqd[b]: grad_j has read dS_j from dP buffer b.
   if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
@@ -1025,70 +1053,77 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 0) {
     const CUtensorMap* maps[2] = {&tmA, &tmB};
     if constexpr (QSTAT)
-      bwd_producer<C, false, false>(bars, tiles, nullptr, maps, j0, j0 + n, h, b, nullptr, 0,
-                                    nullptr, T, p.status);
+      bwd_producer<C, false, false, true>(bars, tiles, nullptr, maps, j0, j0 + n, h, b, nullptr,
+                                          0, nullptr, T, p.status);
     else
-      bwd_producer<C, true, false>(bars, tiles, vec, maps, j0, j0 + n, h, b,
-                                   p.lse + b * p.l0 + h * p.l1, p.l2, p.delta + (int64_t)bh * T,
-                                   T, p.status);
+      bwd_producer<C, true, false, true>(bars, tiles, vec, maps, j0, j0 + n, h, b,
+                                         p.lse + b * p.l0 + h * p.l1, p.l2,
+                                         p.delta + (int64_t)bh * T, T, p.status);
   } else if (warp == 1) {
-    // S_j = X A_j^T (lower halves) once the rows hold S_{j-1} in registers.
+    // S_j = X A_j^T (lower halves) into buffer j % 2 once the rows hold
+    // S_{j-2} in registers.
     if (lane == 0) {
       const uint64_t ad0 = sdesc_kmajor(tiles + C::OFF_A0);
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       for (int j = 0; ok && j < n; ++j) {
-        if (j > 0 && !(ok = mbar_wait(B(bars->s_free[0]), (j - 1) & 1, ctl, p.status))) break;
+        const int bj = j & 1;
+        if (j >= 2 && !(ok = mbar_wait(B(bars->s_free[bj]), ((j - 2) >> 1) & 1, ctl, p.status)))
+          break;
         if (!(ok = mbar_wait(B(bars->ready_a[j % NS]), (j / NS) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain_kil<D, C::KCHA>(tmem + C::TC_S, tmem + C::TC_X, tmem + C::TC_X + D,
+        mma_chain_kil<D, C::KCHA>(tmem + C::TC_S + bj * C::SB, tmem + C::TC_X, tmem + C::TC_X + D,
                                   ad0 + stg(j), idS2, idS);
-        umma_commit(B(bars->s_full[0]));
+        umma_commit(B(bars->s_full[bj]));
       }
       umma_commit(B(bars->mma_final));
       mbar_drain(B(bars->mma_final), 0);
     }
     __syncwarp();
   } else if (warp == kIssuer2Warp) {
-    // dP_j = Y B_j^T and grad += dS_j A_j (upper halves); dP_{j+1} overwrites
-    // dS_j after grad_j in this thread's issue order.
+    // grad += dS_j A_j (upper halves) once the rows formed dS_j in buffer j % 2.
     if (lane == 0) {
-      const uint64_t bd0 = sdesc_kmajor(tiles + C::OFF_B0);
       const uint64_t amd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       const uint32_t up = tmem + kUpperLanes;
-      auto issue_dP = [&](int j) {
-        mma_chain_kil<D, C::KCHB>(up + C::TC_DP, up + C::TC_Y, up + C::TC_Y + D, bd0 + stg(j),
-                                  idS2, idS);
-        umma_commit(B(bars->empty_b[j % NS]));  // B_j read for the last time
-        umma_commit(B(bars->dp_full[0]));
-      };
-      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
-                mbar_wait(B(bars->ready_b[0]), 0, ctl, p.status);
-      if (ok) {
-        tc_fence_after();
-        issue_dP(0);
-      }
+      bool ok = true;
       for (int j = 0; ok && j < n; ++j) {
-        if (!(ok = mbar_wait(B(bars->ds_full[0]), j & 1, ctl, p.status))) break;
+        const int bj = j & 1;
+        if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j >> 1) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain<3, BN, true, BN, C::TILE>(up + C::TC_G, up + C::TC_DP, up + C::TC_DP + BN,
-                                            amd0 + stg(j), idG, j > 0);
+        const uint32_t db = up + C::TC_DP + bj * C::SB;
+        mma_chain<3, BN, true, BN, C::TILE>(up + C::TC_G, db, db + BN, amd0 + stg(j), idG, j > 0);
         umma_commit(B(bars->empty_a[j % NS]));  // A_j read for the last time
-        if (j + 1 < n) {
-          if (!(ok = mbar_wait(B(bars->ready_b[(j + 1) % NS]), ((j + 1) / NS) & 1, ctl,
-                               p.status)))
-            break;
-          tc_fence_after();
-          issue_dP(j + 1);
-        }
+        umma_commit(B(bars->dqd[bj]));          // dS_j read: dP_{j+2} may overwrite it
       }
       if (ok) umma_commit(B(bars->done));
       umma_commit(B(bars->mma_final2));
       mbar_drain(B(bars->mma_final2), 0);
     }
     __syncwarp();
+  } else if (warp == kIssuer3Warp) {
+    // dP_j = Y B_j^T (upper halves) into buffer j % 2 once grad_{j-2} has read
+    // dS_{j-2} from it.
+    if (lane == 0) {
+      const uint64_t bd0 = sdesc_kmajor(tiles + C::OFF_B0);
+      const uint32_t up = tmem + kUpperLanes;
+      bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
+      for (int j = 0; ok && j < n; ++j) {
+        const int bj = j & 1;
+        if (j >= 2 && !(ok = mbar_wait(B(bars->dqd[bj]), ((j - 2) >> 1) & 1, ctl, p.status)))
+          break;
+        if (!(ok = mbar_wait(B(bars->ready_b[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        mma_chain_kil<D, C::KCHB>(up + C::TC_DP + bj * C::SB, up + C::TC_Y, up + C::TC_Y + D,
+                                  bd0 + stg(j), idS2, idS);
+        umma_commit(B(bars->empty_b[j % NS]));  // B_j read for the last time
+        umma_commit(B(bars->dp_full[bj]));
+      }
+      umma_commit(B(bars->mma_final3));
+      mbar_drain(B(bars->mma_final3), 0);
+    }
+    __syncwarp();
   } else if (is_prep_warp(warp)) {
-    bwd_splitter<C, false>(bars, tiles, n, p.status);
-  } else if (warp != kIssuer3Warp) {
+    bwd_splitter<C, false, true>(bars, tiles, n, p.status);
+  } else {
     // Row warps 4-7 (group 0) and 11-14 (group 1) of lane quadrant q = warp % 4.
     const int quad = warp & 3;
     const int grp = warp >= kBwdRowWarp1 ? 1 : 0;
@@ -1149,18 +1184,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           dv[x] = dl;
         }
       }
-      if (!(ok = warp_wait(B(bars->s_full[0]), j & 1, ctl, p.status))) break;
+      const int bj = j & 1;
+      const uint32_t par = (uint32_t)(j >> 1) & 1u;
+      if (!(ok = warp_wait(B(bars->s_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
       float pv[CT];
       {
+        const uint32_t sb = qlo + C::TC_S + bj * C::SB + grp * (BN / 2);
         float t1[CT];
-        tmem_ld_16x32bx2<CT>(qlo + C::TC_S + grp * (BN / 2), pv);
-        tmem_ld_16x32bx2<CT>(qlo + C::TC_S + BN + grp * (BN / 2), t1);
+        tmem_ld_16x32bx2<CT>(sb, pv);
+        tmem_ld_16x32bx2<CT>(sb + BN, t1);
 #pragma unroll
         for (int x = 0; x < CT; x += 2) fadd2(pv[x], pv[x + 1], pv[x], pv[x + 1], t1[x], t1[x + 1]);
       }
       tc_fence_before();
-      warp_arrive(B(bars->s_free[0]));  // S_j read: S_{j+1} may overwrite it
+      warp_arrive(B(bars->s_free[bj]));  // S_j read: S_{j+2} may overwrite it
 #pragma unroll
       for (int x = 0; x < CT; x += 2) {
         float a0, a1;
@@ -1179,9 +1217,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           pv[x] = keep ? pv[x] : 0.0f;
         }
       }
-      if (!(ok = warp_wait(B(bars->dp_full[0]), j & 1, ctl, p.status))) break;
+      if (!(ok = warp_wait(B(bars->dp_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
-      const uint32_t dpb = qup + C::TC_DP + grp * (BN / 2);
+      const uint32_t dpb = qup + C::TC_DP + bj * C::SB + grp * (BN / 2);
       float d0[CT], d1[CT];
       tmem_ld_16x32bx2<CT>(dpb, d0);
       tmem_ld_16x32bx2<CT>(dpb + BN, d1);
@@ -1197,7 +1235,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_st_16x32bx2<CT>(dpb + BN, d1);
       tmem_wait_st();
       tc_fence_before();
-      warp_arrive(B(bars->ds_full[0]));
+      warp_arrive(B(bars->ds_full[bj]));
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
