@@ -48,18 +48,22 @@ using namespace fa2;
 //   B MN-major [raw, lo] (LB == 2), the lo copies present when SPLIT == 3.
 // With KILA / KILB (3xTF32 only) the K-major copy of A / B interleaves instead:
 // each 32-column chunk of BN raw rows is followed by its BN low-part rows (see
-// mma_chain_kil).
+// mma_chain_kil).  With BMN, B is read only MN-major: TMA lands it in that
+// layout and the preparation splits (or rounds) it in place -- no K-major copy.
 template <int D_, int BN_, int SPLIT_, int NS_, int LA_, int LB_, bool KILA_ = false,
-          bool KILB_ = false>
+          bool KILB_ = false, bool BMN_ = false>
 struct BwdTiles {
   static constexpr int D = D_, BN = BN_, SPLIT = SPLIT_, NS = NS_, LA = LA_, LB = LB_;
   static constexpr int NCOPY = SPLIT == 3 ? 2 : 1;
-  static constexpr bool KILA = KILA_ && SPLIT == 3, KILB = KILB_ && SPLIT == 3;
+  static constexpr bool BMN = BMN_;
+  static constexpr bool KILA = KILA_ && SPLIT == 3, KILB = KILB_ && SPLIT == 3 && !BMN_;
+  static_assert(!BMN_ || LB_ == 1, "an MN-only B tile has one layout");
   static constexpr uint32_t TILE = (uint32_t)BN * D * 4u;
   // K-major chunk strides of A and B
   static constexpr uint32_t KCHA = (KILA ? 2u : 1u) * BN * 128u, KCHB = (KILB ? 2u : 1u) * BN * 128u;
   static constexpr uint32_t OFF_A0 = 0, OFF_A1 = NCOPY * TILE;
-  static constexpr uint32_t OFF_B0 = LA * NCOPY * TILE, OFF_B1 = OFF_B0 + NCOPY * TILE;
+  static constexpr uint32_t OFF_B0 = LA * NCOPY * TILE,
+                            OFF_B1 = BMN_ ? OFF_B0 : OFF_B0 + NCOPY * TILE;
   static constexpr uint32_t STAGE = (LA + LB) * NCOPY * TILE;
   static constexpr uint32_t TMEM_COLS = 512;
 };
@@ -580,12 +584,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 constexpr int kDkvBoth = 0, kDkvOnlyDv = 1, kDkvOnlyDk = 2;
 
 // A single-gradient pass keeps only the layouts it reads: the dV pass no
-// MN-major Q (dK's operand), the dK pass no MN-major dO (dV's operand).
+// MN-major Q (dK's operand) and dO only MN-major (landed so by TMA), the dK
+// pass no MN-major dO (dV's operand).
 template <int D_, int BN_, int SPLIT_, int NS_, int NSB_ = 1, int PASS_ = kDkvBoth>
 struct DkvCfg : BwdTiles<D_, BN_, SPLIT_, NS_, PASS_ == kDkvOnlyDv ? 1 : 2,
-                         PASS_ == kDkvOnlyDk ? 1 : 2, true, true> {
+                         PASS_ == kDkvBoth ? 2 : 1, true, true, PASS_ == kDkvOnlyDv> {
   using T_ = BwdTiles<D_, BN_, SPLIT_, NS_, PASS_ == kDkvOnlyDv ? 1 : 2,
-                      PASS_ == kDkvOnlyDk ? 1 : 2, true, true>;
+                      PASS_ == kDkvBoth ? 2 : 1, true, true, PASS_ == kDkvOnlyDv>;
   // NSB TMEM buffers each for S^T / P^T and dP^T / dS^T.  With two, S^T_{i+1}
   // and dP^T_{i+1} run on the tensor core while the row warps still form P_i
   // and dS_i, so the rows go from one step to the next without waiting.
@@ -1331,7 +1336,8 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
   CUtensorMap tq, tg;
   int rc = C::KILA ? make_tmap_bhtd(&tq, q, pr, C::BN) : make_tmap_bhtd_whole(&tq, q, pr, C::BN);
   if (rc == CT_OK)
-    rc = C::KILB ? make_tmap_bhtd(&tg, g, pr, C::BN) : make_tmap_bhtd_whole(&tg, g, pr, C::BN);
+    rc = C::KILB ? make_tmap_bhtd(&tg, g, pr, C::BN)
+                 : make_tmap_bhtd_whole(&tg, g, pr, C::BN, C::BMN);
   if (rc != CT_OK) return rc;
   const size_t smem = bwd_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_bwd_dkdv_tc_kernel<C>, smem, dev.device, &attr_done);
@@ -1417,14 +1423,14 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
                  : run_dkdv<DkvCfg<32, 128, 1, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
   if (pr.D == 128 && !split) {  // dV, then dK: one pass does not fit TMEM
     const int rc =
-        run_dkdv<DkvCfg<128, 32, 1, 4, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+        run_dkdv<DkvCfg<128, 32, 1, 6, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
     if (rc != CT_OK) return rc;
     return run_dkdv<DkvCfg<128, 32, 1, 4, 2, kDkvOnlyDk>>(pr, q, k, v, g, lse, ls, delta, dk, dv,
                                                           dev, st);
   }
   if (pr.D == 128) {  // 3xTF32: dV on 128-row tiles, then dK on 64-row tiles (K, V in lane halves)
     const int rc =
-        run_dkdv<DkvCfg<128, 32, 3, 2, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
+        run_dkdv<DkvCfg<128, 32, 3, 3, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
     if (rc != CT_OK) return rc;
     return run_m64<Half64Cfg<128, 32, 2>, false>(pr, q, g, k, v, lse, ls, delta, dk, dev, st);
   }
