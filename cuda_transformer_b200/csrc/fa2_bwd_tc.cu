@@ -981,37 +981,67 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // S and dP of the same element: row 16 * quad + lane % 16, a quarter of the
 // step's columns (lane half x row warpgroup).
 // S and dP are double-buffered (step j in buffer j % 2), so S_{j+1} and
-// dP_{j+1} run on the tensor core while the rows form dS_j.  Warps: 0 TMA
-// producer (B tiles before A tiles: a B stage is freed by dP alone, early),
-// 1 TMEM allocator and S issuer, 2, 3, 8, 9 tile preparation (3xTF32 split;
-// MN-major copy of A), 10 gradient issuer, 15 dP issuer, 4-7 and 11-14 row
-// warps.
+// dP_{j+1} run on the tensor core while the rows form dS_j.
+// Staging in two rings, so the early readers of a step do not wait for its
+// late one: ring 1 holds the K-major tiles A_j and B_j (read by S_j and dP_j,
+// hi / lo interleaved) and is released as soon as both MMAs complete; ring 2
+// holds A_j MN-major (read by grad_j), landed in that layout by TMA and split
+// in place, released by grad_j.  In the dK pass every row thread loads the
+// LSE and delta of its step's columns itself, one step ahead (the same
+// addresses across half a warp: broadcast L2 hits).
+// Warps: 0 TMA producer (lane 0 ring 1, lane 1 ring 2), 1 TMEM allocator and
+// S issuer, 2, 3, 8, 9 tile preparation (3xTF32 split), 10 gradient issuer,
+// 15 dP issuer, 4-7 and 11-14 row warps.
 constexpr int kRows64 = 64;
 constexpr uint32_t kUpperLanes = 16u << 16;  // TMEM lane offset of a quadrant's upper half
 
-template <int D_, int BN_, int NS_>
-struct Half64Cfg : BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true> {
-  using T_ = BwdTiles<D_, BN_, 3, NS_, 2, 1, true, true>;
-  static constexpr int NSB = 2;
+template <int D_, int BN_, int NS1_, int NS2_>
+struct Half64Cfg {
+  static constexpr int D = D_, BN = BN_, NS1 = NS1_, NS2 = NS2_, NSB = 2;
+  static constexpr uint32_t TILE = (uint32_t)BN_ * D_ * 4u;
+  static constexpr uint32_t CH = (uint32_t)BN_ * 128u;  // one 32-column chunk of BN rows
+  static constexpr uint32_t KCH = 2u * CH;              // interleaved hi | lo chunk stride
+  // ring 1 slot: A K-major (hi | lo interleaved) | B K-major (the same)
+  static constexpr uint32_t OFF_A = 0, OFF_B = 2u * TILE, SLOT1 = 4u * TILE;
+  // ring 2 slot: A MN-major raw | its low parts
+  static constexpr uint32_t SLOT2 = 2u * TILE, RING2 = NS1 * SLOT1, TILE_BYTES = RING2 + NS2 * SLOT2;
+  static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t SB = 2u * BN_;  // one S / dP buffer
   static constexpr uint32_t TC_X = 0, TC_S = 2u * D_;                           // lower halves
   static constexpr uint32_t TC_Y = 0, TC_DP = 2u * D_, TC_G = 2u * D_ + NSB * SB;  // upper halves
   static constexpr int CT = BN_ / 4;  // score columns per row thread per step
   static_assert(D_ == 128, "the 64-row pass is the head-dim-128 3xTF32 path");
   static_assert(CT == 8 || CT == 16, "16x32bx2 access width");
-  static_assert(TC_G + D_ <= T_::TMEM_COLS && TC_S + NSB * SB <= T_::TMEM_COLS, "TMEM budget");
+  static_assert(TC_G + D_ <= TMEM_COLS && TC_S + NSB * SB <= TMEM_COLS, "TMEM budget");
 };
+
+template <int NS1, int NS2>
+struct M64Bars {
+  uint64_t full_a[NS1], full_b[NS1], ready_a[NS1], ready_b[NS1], empty1[NS1];
+  uint64_t full_c[NS2], ready_c[NS2], empty2[NS2];
+  uint64_t s_full[2], s_free[2], dp_full[2], ds_full[2], dqd[2];
+  uint64_t rows_ready, done, mma_final, mma_final2, mma_final3;
+  CtaCtl ctl;
+};
+
+template <class C>
+constexpr size_t m64_smem_bytes() {
+  constexpr size_t b = 1024 + 1024 + (size_t)C::TILE_BYTES;
+  static_assert(sizeof(M64Bars<C::NS1, C::NS2>) <= 1024, "barrier block");
+  static_assert(b <= 227 * 1024, "shared memory budget");
+  return b;
+}
 
 template <class C, bool QSTAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_m64_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                          const __grid_constant__ CUtensorMap tmB, const BwdParams p) {
-  constexpr int D = C::D, BN = C::BN, NS = C::NS, CT = C::CT;
+                          const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmAm, const BwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS1 = C::NS1, NS2 = C::NS2, CT = C::CT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
-  auto* bars = reinterpret_cast<BwdBars<NS>*>(smem_raw);
-  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(BwdBars<NS>) + 1023u) & ~1023u;
-  float* vec = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) + NS * C::STAGE);
+  auto* bars = reinterpret_cast<M64Bars<NS1, NS2>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(M64Bars<NS1, NS2>) + 1023u) & ~1023u;
   CtaCtl* ctl = &bars->ctl;
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -1039,9 +1069,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     return;
   }
 
-  // A_j is released by the gradient MMA (issued after dS_j, i.e. after S_j
-  // was read), B_j by dP_j; dqd[b]: grad_j has read dS_j from dP buffer b.
-  if (threadIdx.x == 0) init_bwd_bars<C>(bars, 1, 1, 8);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS1; ++s) {
+      mbar_init(B(bars->full_a[s]), 1);
+      mbar_init(B(bars->full_b[s]), 1);
+      mbar_init(B(bars->ready_a[s]), kPrepWarps);
+      mbar_init(B(bars->ready_b[s]), kPrepWarps);
+      mbar_init(B(bars->empty1[s]), 2);  // S_j and dP_j
+    }
+    for (int s = 0; s < NS2; ++s) {
+      mbar_init(B(bars->full_c[s]), 1);
+      mbar_init(B(bars->ready_c[s]), kPrepWarps);
+      mbar_init(B(bars->empty2[s]), 1);  // grad_j
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(B(bars->s_full[i]), 1);
+      mbar_init(B(bars->s_free[i]), 8);
+      mbar_init(B(bars->dp_full[i]), 1);
+      mbar_init(B(bars->ds_full[i]), 8);
+      mbar_init(B(bars->dqd[i]), 1);
+    }
+    mbar_init(B(bars->rows_ready), 8);
+    mbar_init(B(bars->done), 1);
+    mbar_init(B(bars->mma_final), 1);
+    mbar_init(B(bars->mma_final2), 1);
+    mbar_init(B(bars->mma_final3), 1);
+    bars->ctl.abort = 0;
+    fence_barrier_init();
+  }
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
     tmem_relinquish();
@@ -1050,35 +1105,65 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
+  auto slot1 = [&](int i) { return tiles + (uint32_t)(i % NS1) * C::SLOT1; };
+  auto slot2 = [&](int i) { return tiles + C::RING2 + (uint32_t)(i % NS2) * C::SLOT2; };
   constexpr uint32_t idS2 = idesc_tf32(64, 2 * BN, false, false);  // [hi | lo] rows (kil)
   constexpr uint32_t idS = idesc_tf32(64, BN, false, false);
   constexpr uint32_t idG = idesc_tf32(64, D, false, true);
 
   if (warp == 0) {
-    const CUtensorMap* maps[2] = {&tmA, &tmB};
-    if constexpr (QSTAT)
-      bwd_producer<C, false, false, true>(bars, tiles, nullptr, maps, j0, j0 + n, h, b, nullptr,
-                                          0, nullptr, T, p.status);
-    else
-      bwd_producer<C, true, false, true>(bars, tiles, vec, maps, j0, j0 + n, h, b,
-                                         p.lse + b * p.l0 + h * p.l1, p.l2,
-                                         p.delta + (int64_t)bh * T, T, p.status);
+    // Lane 0: ring 1 (K-major A_j, B_j; B first); lane 1: ring 2 (MN-major A_j).
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int last = -1;
+      for (int i = 0; i < n; ++i) {
+        const int j = j0 + i, s = i % NS1, r = i / NS1;
+        if (r > 0 && !mbar_wait(B(bars->empty1[s]), (r - 1) & 1, ctl, p.status)) break;
+        const uint32_t st = slot1(i);
+        mbar_arrive_expect_tx(B(bars->full_b[s]), C::TILE);
+        tma_load_tile<false, D>(st + C::OFF_B, &tmB, B(bars->full_b[s]), j * BN, h, b, C::KCH);
+        mbar_arrive_expect_tx(B(bars->full_a[s]), C::TILE);
+        tma_load_tile<false, D>(st + C::OFF_A, &tmA, B(bars->full_a[s]), j * BN, h, b, C::KCH);
+        last = i;
+      }
+      if (ctl->abort) {  // drain this lane's copies in flight
+        for (int i = max(0, last - NS1 + 1); i <= last; ++i) {
+          mbar_drain(B(bars->full_b[i % NS1]), (i / NS1) & 1);
+          mbar_drain(B(bars->full_a[i % NS1]), (i / NS1) & 1);
+        }
+      }
+    } else if (lane == 1) {
+      tma_prefetch_desc(&tmAm);
+      int last = -1;
+      for (int i = 0; i < n; ++i) {
+        const int j = j0 + i, s = i % NS2, r = i / NS2;
+        if (r > 0 && !mbar_wait(B(bars->empty2[s]), (r - 1) & 1, ctl, p.status)) break;
+        mbar_arrive_expect_tx(B(bars->full_c[s]), C::TILE);
+        tma_load_5d(slot2(i), &tmAm, B(bars->full_c[s]), 0, j * BN, 0, h, b);
+        last = i;
+      }
+      if (ctl->abort) {
+        for (int i = max(0, last - NS2 + 1); i <= last; ++i)
+          mbar_drain(B(bars->full_c[i % NS2]), (i / NS2) & 1);
+      }
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // S_j = X A_j^T (lower halves) into buffer j % 2 once the rows hold
     // S_{j-2} in registers.
     if (lane == 0) {
-      const uint64_t ad0 = sdesc_kmajor(tiles + C::OFF_A0);
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       for (int j = 0; ok && j < n; ++j) {
         const int bj = j & 1;
         if (j >= 2 && !(ok = mbar_wait(B(bars->s_free[bj]), ((j - 2) >> 1) & 1, ctl, p.status)))
           break;
-        if (!(ok = mbar_wait(B(bars->ready_a[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_a[j % NS1]), (j / NS1) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain_kil<D, C::KCHA>(tmem + C::TC_S + bj * C::SB, tmem + C::TC_X, tmem + C::TC_X + D,
-                                  ad0 + stg(j), idS2, idS);
+        mma_chain_kil<D, C::KCH>(tmem + C::TC_S + bj * C::SB, tmem + C::TC_X, tmem + C::TC_X + D,
+                                 sdesc_kmajor(slot1(j) + C::OFF_A), idS2, idS);
         umma_commit(B(bars->s_full[bj]));
+        umma_commit(B(bars->empty1[j % NS1]));  // A_j K-major read
       }
       umma_commit(B(bars->mma_final));
       mbar_drain(B(bars->mma_final), 0);
@@ -1087,16 +1172,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == kIssuer2Warp) {
     // grad += dS_j A_j (upper halves) once the rows formed dS_j in buffer j % 2.
     if (lane == 0) {
-      const uint64_t amd0 = sdesc_mnmajor(tiles + C::OFF_A1, BN * 128);
       const uint32_t up = tmem + kUpperLanes;
       bool ok = true;
       for (int j = 0; ok && j < n; ++j) {
         const int bj = j & 1;
         if (!(ok = mbar_wait(B(bars->ds_full[bj]), (j >> 1) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_c[j % NS2]), (j / NS2) & 1, ctl, p.status))) break;
         tc_fence_after();
         const uint32_t db = up + C::TC_DP + bj * C::SB;
-        mma_chain<3, BN, true, BN, C::TILE>(up + C::TC_G, db, db + BN, amd0 + stg(j), idG, j > 0);
-        umma_commit(B(bars->empty_a[j % NS]));  // A_j read for the last time
+        mma_chain<3, BN, true, BN, C::TILE>(up + C::TC_G, db, db + BN,
+                                            sdesc_mnmajor(slot2(j), BN * 128), idG, j > 0);
+        umma_commit(B(bars->empty2[j % NS2]));  // A_j MN-major read
         umma_commit(B(bars->dqd[bj]));          // dS_j read: dP_{j+2} may overwrite it
       }
       if (ok) umma_commit(B(bars->done));
@@ -1108,26 +1194,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // dP_j = Y B_j^T (upper halves) into buffer j % 2 once grad_{j-2} has read
     // dS_{j-2} from it.
     if (lane == 0) {
-      const uint64_t bd0 = sdesc_kmajor(tiles + C::OFF_B0);
       const uint32_t up = tmem + kUpperLanes;
       bool ok = mbar_wait(B(bars->rows_ready), 0, ctl, p.status);
       for (int j = 0; ok && j < n; ++j) {
         const int bj = j & 1;
         if (j >= 2 && !(ok = mbar_wait(B(bars->dqd[bj]), ((j - 2) >> 1) & 1, ctl, p.status)))
           break;
-        if (!(ok = mbar_wait(B(bars->ready_b[j % NS]), (j / NS) & 1, ctl, p.status))) break;
+        if (!(ok = mbar_wait(B(bars->ready_b[j % NS1]), (j / NS1) & 1, ctl, p.status))) break;
         tc_fence_after();
-        mma_chain_kil<D, C::KCHB>(up + C::TC_DP + bj * C::SB, up + C::TC_Y, up + C::TC_Y + D,
-                                  bd0 + stg(j), idS2, idS);
-        umma_commit(B(bars->empty_b[j % NS]));  // B_j read for the last time
+        mma_chain_kil<D, C::KCH>(up + C::TC_DP + bj * C::SB, up + C::TC_Y, up + C::TC_Y + D,
+                                 sdesc_kmajor(slot1(j) + C::OFF_B), idS2, idS);
         umma_commit(B(bars->dp_full[bj]));
+        umma_commit(B(bars->empty1[j % NS1]));  // B_j read
       }
       umma_commit(B(bars->mma_final3));
       mbar_drain(B(bars->mma_final3), 0);
     }
     __syncwarp();
   } else if (is_prep_warp(warp)) {
-    bwd_splitter<C, false, true>(bars, tiles, n, p.status);
+    // Per step: B_j, then A_j K-major (both interleaved hi | lo), then A_j
+    // MN-major (split in place), each released to its readers when done.
+    const uint32_t tid = prep_tid();
+    for (int i = 0; i < n; ++i) {
+      const int s = i % NS1, r = i / NS1, s2 = i % NS2, r2 = i / NS2;
+      if (!warp_wait(B(bars->full_b[s]), r & 1, ctl, p.status)) break;
+      split_tile_smem_il<C::TILE, kSplitThreads, C::CH>(slot1(i) + C::OFF_B, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_b[s]));
+      if (!warp_wait(B(bars->full_a[s]), r & 1, ctl, p.status)) break;
+      split_tile_smem_il<C::TILE, kSplitThreads, C::CH>(slot1(i) + C::OFF_A, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_a[s]));
+      if (!warp_wait(B(bars->full_c[s2]), r2 & 1, ctl, p.status)) break;
+      split_tile_smem<C::TILE, kSplitThreads>(slot2(i), slot2(i) + C::TILE, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_c[s2]));
+    }
   } else {
     // Row warps 4-7 (group 0) and 11-14 (group 1) of lane quadrant q = warp % 4.
     const int quad = warp & 3;
@@ -1141,17 +1243,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // 0-15 X's row into the lower half, lanes 16-31 Y's row into the upper
     // half; group g writes head-dim columns [g D/2, (g + 1) D/2), hi and lo.
     {
-      const int srow = r0 + 16 * quad + (lane & 15);
-      const bool sval = srow < T;
       const Ptr4& src = hl ? p.st1 : p.st0;
-      const float* rp = src.row(b, h, sval ? srow : 0);
+      const float* rp = src.row(b, h, valid ? row : 0);
       const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(rp) & 15u) == 0);
       const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
         const int col = grp * (D / 2) + 32 * c;
         float x[32], lo[32];
-        load_row32(src, rp, col, sval, vr, x);
+        load_row32(src, rp, col, valid, vr, x);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float hi;
@@ -1173,15 +1273,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_fence_before();
     warp_arrive(B(bars->rows_ready));
     const int cs = grp * (BN / 2) + hl * CT;  // this thread's first column of a step
+    // dK pass: LSE and delta of this thread's columns, loaded one step ahead
+    const float* lse_bh = p.lse + b * p.l0 + h * p.l1;
+    const float* del_bh = p.delta + (int64_t)bh * T;
+    float nl[CT], nd[CT];
+    auto fetch_cols = [&](int j) {
+#pragma unroll
+      for (int x = 0; x < CT; ++x) {
+        const int q = (j0 + j) * BN + cs + x;
+        const bool in = !QSTAT && j < n && q < T;
+        nl[x] = in ? ldg_nc_early(lse_bh + (int64_t)q * p.l2) : 0.0f;
+        nd[x] = in ? ldg_nc_early(del_bh + q) : 0.0f;
+      }
+    };
+    if constexpr (!QSTAT) fetch_cols(0);
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       const int col0 = (j0 + j) * BN + cs;  // its key (dQ) or query (dK) index
+      const int bj = j & 1;
+      const uint32_t par = (uint32_t)(j >> 1) & 1u;
       float lv[CT], dv[CT];
-      if constexpr (!QSTAT) {  // the step's -LSE * log2e and delta, per column
-        if (!(ok = warp_wait(B(bars->vec_full[j % NS]), (j / NS) & 1, ctl, p.status))) break;
-        const float* vs = vec + (j % NS) * 2 * BN + cs;
-        load_vecn<CT>(vs, lv);
-        load_vecn<CT>(vs + BN, dv);
+      if constexpr (!QSTAT) {  // this step's -LSE * log2e and delta, per column
+#pragma unroll
+        for (int x = 0; x < CT; ++x) {
+          lv[x] = nl[x] * -kLog2e;
+          dv[x] = nd[x];
+        }
+        fetch_cols(j + 1);
       } else {
 #pragma unroll
         for (int x = 0; x < CT; ++x) {
@@ -1189,8 +1307,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           dv[x] = dl;
         }
       }
-      const int bj = j & 1;
-      const uint32_t par = (uint32_t)(j >> 1) & 1u;
       if (!(ok = warp_wait(B(bars->s_full[bj]), par, ctl, p.status))) break;
       tc_fence_after();
       float pv[CT];
@@ -1362,11 +1478,14 @@ int run_m64(const Fa2Problem& pr, Strided4 a, Strided4 bb, Strided4 x, Strided4 
             const float* lse, const int64_t ls[3], const float* delta, float* grad,
             const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
-  CUtensorMap ta, tb;  // interleaved hi / lo tiles load chunk by chunk
+  // K-major tiles interleave hi / lo and load chunk by chunk; A's MN-major
+  // copy loads whole
+  CUtensorMap ta, tb, tam;
   int rc = make_tmap_bhtd(&ta, a, pr, C::BN);
   if (rc == CT_OK) rc = make_tmap_bhtd(&tb, bb, pr, C::BN);
+  if (rc == CT_OK) rc = make_tmap_bhtd_whole(&tam, a, pr, C::BN, true);
   if (rc != CT_OK) return rc;
-  const size_t smem = bwd_smem_bytes<C>();
+  const size_t smem = m64_smem_bytes<C>();
   rc = ensure_smem_attr(fa2_bwd_m64_tc_kernel<C, QSTAT>, smem, dev.device, &attr_done);
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, x, y, lse, ls, delta, grad, nullptr, dev);
@@ -1376,7 +1495,7 @@ int run_m64(const Fa2Problem& pr, Strided4 a, Strided4 bb, Strided4 x, Strided4 
     p.seg_lo = (int)s0;
     p.seg_hi = (int)std::min<int64_t>(s0 + kSegLen, pr.T);
     p.accumulate_out = s0 > 0;
-    fa2_bwd_m64_tc_kernel<C, QSTAT><<<(unsigned)grid, kBwdThreads, smem, st>>>(ta, tb, p);
+    fa2_bwd_m64_tc_kernel<C, QSTAT><<<(unsigned)grid, kBwdThreads, smem, st>>>(ta, tb, tam, p);
     rc = check_launch();
     if (rc != CT_OK) return rc;
   }
@@ -1405,7 +1524,7 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 
     return split ? run_dq<DqCfg<32, 64, 3, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<32, 128, 1, 4>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   if (pr.D == 128)
-    return split ? run_m64<Half64Cfg<128, 32, 2>, true>(pr, k, v, q, g, lse, ls, delta, dq, dev, st)
+    return split ? run_m64<Half64Cfg<128, 32, 2, 2>, true>(pr, k, v, q, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<128, 64, 1, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
@@ -1432,7 +1551,7 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
     const int rc =
         run_dkdv<DkvCfg<128, 32, 3, 3, 2, kDkvOnlyDv>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
     if (rc != CT_OK) return rc;
-    return run_m64<Half64Cfg<128, 32, 2>, false>(pr, q, g, k, v, lse, ls, delta, dk, dev, st);
+    return run_m64<Half64Cfg<128, 32, 2, 2>, false>(pr, q, g, k, v, lse, ls, delta, dk, dev, st);
   }
   return CT_ERR_UNSUPPORTED_HEAD_DIM;
 }
