@@ -3,11 +3,15 @@
 Forward: out = x @ W + b with W stored (in, out).  Backward: dx = dy @ W^T;
 dW is one GEMM with the (batch, seq) dimensions folded into the reduction
 (x^T @ dy over batch*seq rows) instead of a per-batch product followed by a
-torch sum; db is the bias-gradient column sum.  The zero biases of the two
-backward products are cached per device and length (the operator only reads
-them)."""
+torch sum, and db -- the column sums of dy -- is formed inside that same GEMM
+from the dy tiles it stages (no separate pass over dy).  The zero biases of
+the two backward products are cached per device and length (the operator only
+reads them)."""
+import functools
+import os
+
 import torch
-from cuda_transformer.ops import cuda_fma, db_calculation
+from cuda_transformer.ops import cuda_fma, db_calculation, linear_fused
 
 _ZEROS = {}
 
@@ -19,6 +23,24 @@ def _zeros(n, device):
     if z is None:
         z = _ZEROS[key] = torch.zeros(n, dtype=torch.float32, device=device)
     return z
+
+
+@functools.lru_cache(maxsize=1)
+def _precision():
+    """The operators' default precision (CUDA_TRANSFORMER_PRECISION, read once
+    like the operator library does)."""
+    return {"tf32": 1, "fp32": 2, "simt": 2}.get(os.environ.get("CUDA_TRANSFORMER_PRECISION", ""), 0)
+
+
+def weight_and_bias_grad(x, dy, precision=None):
+    """dW = x^T dy and db = colsum(dy) over all leading dimensions, in one GEMM
+    (x (..., k), dy (..., n))."""
+    rows = x.numel() // x.shape[-1]
+    x2 = x.reshape(1, rows, x.shape[-1])
+    dy2 = dy.reshape(1, rows, dy.shape[-1])
+    dw, _, db = linear_fused(x2.transpose(1, 2), dy2, _zeros(dy.shape[-1], dy.device),
+                             _precision() if precision is None else precision, 0, None, True)
+    return dw[0], db
 
 
 class CudaLinearLayer(torch.autograd.Function):
@@ -34,13 +56,9 @@ class CudaLinearLayer(torch.autograd.Function):
         dy = grad_output
         w = weights.unsqueeze(0) if weights.dim() == 2 else weights
         dx = cuda_fma(dy, w.transpose(1, 2), _zeros(x.shape[-1], x.device))
-        zero_n = _zeros(dy.shape[-1], dy.device)
         if weights.dim() == 2:
-            rows = x.shape[0] * x.shape[1]
-            x2 = x.reshape(1, rows, x.shape[-1])
-            dy2 = dy.reshape(1, rows, dy.shape[-1])
-            dw = cuda_fma(x2.transpose(1, 2), dy2, zero_n)[0]
+            dw, db = weight_and_bias_grad(x, dy)
         else:
-            dw = cuda_fma(x.transpose(1, 2), dy, zero_n)
-        db = db_calculation(dy)
+            dw = cuda_fma(x.transpose(1, 2), dy, _zeros(dy.shape[-1], dy.device))
+            db = db_calculation(dy)
         return dx, dw, db

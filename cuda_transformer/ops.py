@@ -18,11 +18,15 @@ __all__ = [
     "flash_attention_fwd", "flash_attention_bwd",
     "flash_attention_fwd_ex", "flash_attention_bwd_ex", "cuda_fma_ex",
     "layernorm_fwd", "layernorm_bwd",
+    "linear_fused", "linear_accumulate_", "cross_entropy_fwd_bwd_",
 ]
 
 PRECISION_3XTF32 = 0
 PRECISION_TF32 = 1
 PRECISION_FP32 = 2
+EPILOGUE_NONE = 0
+EPILOGUE_GELU = 1
+EPILOGUE_GELU_GRAD = 2
 
 
 def _f32(*ts):
@@ -234,3 +238,46 @@ def layernorm_bwd(x: Tensor, gamma: Tensor, mean: Tensor, rstd: Tensor, dy: Tens
 def _(x, gamma, mean, rstd, dy):
     _f32(x, gamma, mean, rstd, dy)
     return torch.empty_like(x), torch.empty_like(gamma), torch.empty_like(gamma)
+
+
+# ------------------------------------------------- linear layer, fused options
+def linear_fused(x: Tensor, weights: Tensor, bias: Tensor, precision: int = PRECISION_3XTF32,
+                 epilogue: int = EPILOGUE_NONE, act_in: Tensor | None = None,
+                 want_colsum: bool = False):
+    """out = x @ weights + bias with GELU (EPILOGUE_GELU: also returns
+    gelu(out)) or the GELU gradient (EPILOGUE_GELU_GRAD: out * gelu'(act_in))
+    applied in the GEMM's epilogue, and optionally the column sums of
+    `weights` over its reduction index (the bias gradient when weights is dY,
+    batch 1).  Returns (out, act, colsum); unused ones are empty."""
+    return torch.ops.cuda_transformer.linear_fused.default(x, weights, bias, precision, epilogue,
+                                                           act_in, want_colsum)
+
+
+@torch.library.register_fake("cuda_transformer::linear_fused")
+def _(x, weights, bias, precision, epilogue, act_in, want_colsum):
+    out = _fma_meta(x, weights, bias)
+    act = torch.empty_like(out) if epilogue == EPILOGUE_GELU else out.new_empty(0)
+    cs = out.new_empty(out.size(2)) if want_colsum else out.new_empty(0)
+    return out, act, cs
+
+
+def linear_accumulate_(out: Tensor, colsum: Tensor | None, x: Tensor, weights: Tensor,
+                       bias: Tensor, precision: int = PRECISION_3XTF32) -> None:
+    """out += x @ weights + bias, and colsum += the column sums of weights."""
+    torch.ops.cuda_transformer.linear_accumulate_.default(out, colsum, x, weights, bias, precision)
+
+
+@torch.library.register_fake("cuda_transformer::linear_accumulate_")
+def _(out, colsum, x, weights, bias, precision):
+    return None
+
+
+def cross_entropy_fwd_bwd_(logits: Tensor, targets: Tensor, ignore_index: int = -100) -> Tensor:
+    """Per-row cross entropy of (rows, vocab) logits; the logits are
+    overwritten with softmax - onehot(targets) (unscaled gradient)."""
+    return torch.ops.cuda_transformer.cross_entropy_fwd_bwd_.default(logits, targets, ignore_index)
+
+
+@torch.library.register_fake("cuda_transformer::cross_entropy_fwd_bwd_")
+def _(logits, targets, ignore_index):
+    return logits.new_empty(logits.size(0))

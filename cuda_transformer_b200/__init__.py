@@ -28,6 +28,9 @@ CT_ERR_WORKSPACE_TOO_SMALL = 8
 PRECISION_3XTF32 = 0
 PRECISION_TF32 = 1
 PRECISION_FP32 = 2
+EPILOGUE_NONE = 0
+EPILOGUE_GELU = 1
+EPILOGUE_GELU_GRAD = 2
 CT_FA2_BWD_NOALLOC_MAX_ROWS = 2097152  # batch * heads * seq_len limit of ct_fa2_bwd_noalloc
 CT_DEVSTAT_TIMEOUT = 1  # watchdog word bit: a bounded device-side wait ran out
 CT_WAIT_LIMIT_MIN_NS = 100000
@@ -59,6 +62,8 @@ SIGNATURES = {
     "ct_linear_fwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64, _int,
                        _fp], _int),
     "ct_linear_workspace_size": ([_i64, _i64, _i64, _i64], _sz),
+    "ct_linear_fwd_ex": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64,
+                          _int, _int, _fp, _fp, _fp, _int, _fp, _sz, _fp], _int),
     "ct_linear_fwd_ws": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64,
                           _int, _fp, _sz, _fp], _int),
     "ct_bias_grad_workspace_size": ([_i64, _i64, _i64], _sz),
@@ -71,6 +76,7 @@ SIGNATURES = {
     "ct_layernorm_bwd_workspace_size": ([_i64, _i64], _sz),
     "ct_layernorm_bwd": ([_fp, _fp, _fp, _fp, _fp, _fp, _fp, _fp, _i64, _i64, _fp, _sz, _fp],
                          _int),
+    "ct_cross_entropy_fwd_bwd": ([_fp, _i64, _i64, _i64, _fp, _i64, _fp, _fp], _int),
     "ct_set_wait_limit_ns": ([_int, ctypes.c_ulonglong], _int),
     "ct_get_wait_limit_ns": ([_int, ctypes.POINTER(ctypes.c_ulonglong)], _int),
     "ct_watchdog_selftest": ([_fp], _int),

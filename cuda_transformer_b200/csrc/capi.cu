@@ -367,6 +367,49 @@ int ct_linear_fwd_ws(const float* x, const int64_t x_stride[3], const float* w,
   return launch_linear_simt(g, as_stream(stream));
 }
 
+int ct_linear_fwd_ex(const float* x, const int64_t x_stride[3], const float* w,
+                     const int64_t w_stride[3], const float* bias, int64_t bias_stride, float* out,
+                     int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
+                     int precision, int epilogue, float* act_out, const float* act_in,
+                     float* w_colsum, int accumulate, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (batch < 0 || m < 0 || k < 0 || n < 0 || !valid_precision(precision) ||
+      !(w_batch == 1 || w_batch == batch) ||
+      !(epilogue == CT_EPILOGUE_NONE || epilogue == CT_EPILOGUE_GELU ||
+        epilogue == CT_EPILOGUE_GELU_GRAD) ||
+      (epilogue == CT_EPILOGUE_GELU && !act_out) ||
+      (epilogue == CT_EPILOGUE_GELU_GRAD && !act_in) ||
+      (accumulate && epilogue != CT_EPILOGUE_NONE) || (w_colsum && batch != 1))
+    return CT_ERR_INVALID_ARGUMENT;
+  if (batch * n == 0) return CT_OK;
+  if (!x_stride || !w_stride || (m > 0 && (!x || !bias || !out)) || (k > 0 && !w))
+    return CT_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes > 0 && !workspace) return CT_ERR_INVALID_ARGUMENT;
+  int err = CT_OK;
+  const DeviceInfo* dev = current_device(&err);
+  if (err != CT_OK) return err;
+  GemmProblem g;
+  g.batch = batch; g.m = m; g.k = k; g.n = n;
+  g.x = x; g.w = w; g.bias = bias; g.bias_s = bias_stride; g.out = out;
+  for (int i = 0; i < 3; ++i) { g.xs[i] = x_stride[i]; g.ws[i] = w_stride[i]; }
+  if (w_batch == 1) g.ws[0] = 0;
+  g.precision = precision;
+  g.epilogue = epilogue;
+  g.out_act = act_out;
+  g.act_in = act_in;
+  g.w_colsum = w_colsum;
+  g.accumulate = accumulate != 0;
+  if (m > 0 && precision != CT_PRECISION_FP32 && linear_tc_supported(g)) {
+    const int rc = launch_linear_tc(g, workspace, workspace_bytes, *dev, as_stream(stream));
+    if (rc != CT_ERR_UNSUPPORTED_LAYOUT) return rc;  // else: TMA cannot address it
+  }
+  if (m > 0) {
+    const int rc = launch_linear_simt(g, as_stream(stream));
+    if (rc != CT_OK) return rc;
+  }
+  return launch_w_colsum_simt(g, as_stream(stream));
+}
+
 int ct_linear_fwd(const float* x, const int64_t x_stride[3], const float* w,
                   const int64_t w_stride[3], const float* bias, int64_t bias_stride, float* out,
                   int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch, int precision,
@@ -456,6 +499,18 @@ int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean, cons
     return CT_ERR_WORKSPACE_TOO_SMALL;
   return launch_layernorm_bwd(x, gamma, mean, rstd, dy, dx, dgamma, dbeta, rows, n,
                               static_cast<float*>(workspace), as_stream(stream));
+}
+
+int ct_cross_entropy_fwd_bwd(float* logits, int64_t ld, int64_t rows, int64_t vocab,
+                             const int64_t* targets, int64_t ignore_index, float* loss_rows,
+                             void* stream) {
+  if (rows < 0 || vocab <= 0 || ld < vocab || ((!logits || !targets || !loss_rows) && rows > 0))
+    return CT_ERR_INVALID_ARGUMENT;
+  int err = CT_OK;
+  current_device(&err);
+  if (err != CT_OK) return err;
+  return launch_cross_entropy(logits, ld, rows, vocab, targets, ignore_index, loss_rows,
+                              as_stream(stream));
 }
 
 }  // extern "C"

@@ -113,6 +113,15 @@ struct GemmProblem {
   int64_t bias_s;
   float* out;     // contiguous [batch, m, n]
   int precision;
+  // Fused epilogues (CT_EPILOGUE_*): GELU writes gelu(out) to out_act as well;
+  // GELU_GRAD multiplies out by gelu'(act_in) (act_in dense [batch, m, n]).
+  int epilogue = CT_EPILOGUE_NONE;
+  float* out_act = nullptr;
+  const float* act_in = nullptr;
+  // Column sums of the W operand over the batch and reduction indices, [n]
+  // (the bias gradient when W is dY); batch == 1.
+  float* w_colsum = nullptr;
+  bool accumulate = false;  // out (and w_colsum) += instead of =
 };
 // ws / ws_bytes: optional per-tile counters that enable the split-K schedule.
 int launch_linear_tc(const GemmProblem& g, void* ws, size_t ws_bytes, const DeviceInfo& dev,
@@ -120,6 +129,8 @@ int launch_linear_tc(const GemmProblem& g, void* ws, size_t ws_bytes, const Devi
 size_t linear_workspace_bytes(int64_t batch, int64_t m, int64_t n);
 bool linear_tc_supported(const GemmProblem& g);
 int launch_linear_simt(const GemmProblem& g, cudaStream_t st);
+// w_colsum of a GemmProblem on the CUDA cores (fallback path).
+int launch_w_colsum_simt(const GemmProblem& g, cudaStream_t st);
 
 // -------------------------------------------------------- row-wise kernels
 size_t bias_grad_workspace(int64_t rows, int64_t n);
@@ -138,6 +149,10 @@ size_t layernorm_bwd_workspace(int64_t rows, int64_t n);
 int launch_layernorm_bwd(const float* x, const float* g, const float* mean, const float* rstd,
                          const float* dy, float* dx, float* dg, float* db, int64_t rows,
                          int64_t n, float* ws, cudaStream_t st);
+
+// Cross entropy of logit rows (loss per row; gradient written over the logits).
+int launch_cross_entropy(float* x, int64_t ld, int64_t rows, int64_t vocab, const int64_t* targets,
+                         int64_t ignore, float* loss_rows, cudaStream_t st);
 
 // ------------------------------------------------------------ watchdog
 // One CTA whose waits on a barrier phase that nothing completes run out after

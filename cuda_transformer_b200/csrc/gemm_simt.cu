@@ -6,7 +6,10 @@
 // [batch, m, n] output.
 //
 // 64 x 64 output tile per CTA, 256 threads each owning a 4 x 4 block, K
-// staged through shared memory 16 at a time.
+// staged through shared memory 16 at a time.  The fused options of
+// ct_linear_fwd_ex (GELU epilogues, accumulate) apply in the store; the W
+// column sums run as a separate kernel.
+#include "act.cuh"
 #include "ct_internal.h"
 
 namespace ct {
@@ -18,7 +21,8 @@ __global__ void __launch_bounds__(256)
     gemm_bias_simt_kernel(const float* __restrict__ x, int64_t xs0, int64_t xs1, int64_t xs2,
                           const float* __restrict__ w, int64_t ws0, int64_t ws1, int64_t ws2,
                           const float* __restrict__ bias, int64_t bs, float* __restrict__ out,
-                          int64_t m, int64_t k, int64_t n) {
+                          int64_t m, int64_t k, int64_t n, int epi, float* __restrict__ out_act,
+                          const float* __restrict__ act_in, int accumulate) {
   __shared__ float As[kTK][kTM + 4];
   __shared__ float Bs[kTK][kTN + 4];
   const int64_t b = blockIdx.z;
@@ -60,12 +64,49 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t gn = n0 + tx * 4 + j;
-      if (gn < n) out[(b * m + gm) * n + gn] = acc[i][j] + __ldg(bias + gn * bs);
+      if (gn >= n) continue;
+      const int64_t o = (b * m + gm) * n + gn;
+      float v = acc[i][j] + __ldg(bias + gn * bs);
+      if (epi == CT_EPILOGUE_GELU_GRAD) v *= gelu_d(__ldg(act_in + o));
+      if (accumulate) v += out[o];
+      out[o] = v;
+      if (epi == CT_EPILOGUE_GELU) out_act[o] = gelu_f(v);
     }
   }
 }
 
+// cs[j] (+)= sum over (b, kk) of W[b | 0][kk][j]: 32 columns per CTA, eight
+// row groups summed in parallel and combined in a fixed order.
+__global__ void __launch_bounds__(256)
+    w_colsum_simt_kernel(const float* __restrict__ w, int64_t ws0, int64_t ws1, int64_t ws2,
+                         int64_t batch, int64_t k, int64_t n, float* __restrict__ cs,
+                         int accumulate) {
+  __shared__ float part[8][32];
+  const int c = threadIdx.x % 32, g = threadIdx.x / 32;
+  const int64_t j = (int64_t)blockIdx.x * 32 + c;
+  float acc = 0.0f;
+  if (j < n) {
+    for (int64_t b = 0; b < batch; ++b)
+      for (int64_t kk = g; kk < k; kk += 8) acc += __ldg(w + b * ws0 + kk * ws1 + j * ws2);
+  }
+  part[g][c] = acc;
+  __syncthreads();
+  if (g == 0 && j < n) {
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += part[i][c];
+    cs[j] = accumulate ? cs[j] + t : t;
+  }
+}
+
 }  // namespace
+
+int launch_w_colsum_simt(const GemmProblem& g, cudaStream_t st) {
+  if (!g.w_colsum || g.n <= 0) return CT_OK;
+  w_colsum_simt_kernel<<<(unsigned)((g.n + 31) / 32), 256, 0, st>>>(
+      g.w, g.ws[0], g.ws[1], g.ws[2], g.batch, g.k, g.n, g.w_colsum, g.accumulate ? 1 : 0);
+  return check_launch();
+}
 
 int launch_linear_simt(const GemmProblem& g, cudaStream_t st) {
   if (g.batch > 65535 || (g.m + kTM - 1) / kTM > 65535) return CT_ERR_INVALID_ARGUMENT;
@@ -73,7 +114,8 @@ int launch_linear_simt(const GemmProblem& g, cudaStream_t st) {
             (unsigned)g.batch);
   gemm_bias_simt_kernel<<<grid, 256, 0, st>>>(g.x, g.xs[0], g.xs[1], g.xs[2], g.w, g.ws[0],
                                               g.ws[1], g.ws[2], g.bias, g.bias_s, g.out, g.m, g.k,
-                                              g.n);
+                                              g.n, g.epilogue, g.out_act, g.act_in,
+                                              g.accumulate ? 1 : 0);
   return check_launch();
 }
 

@@ -44,8 +44,17 @@
 // tile sits in the same round of the persistent loop (the grid is a multiple
 // of `slices`), on CTAs of increasing index, so each wait is on a CTA that is
 // already running; all waits are bounded.
+//
+// Fused neighbours (ct_linear_fwd_ex).  The epilogue can apply the MLP's GELU
+// to the tile (writing the pre-activation and gelu of it) or multiply by the
+// GELU derivative at a given pre-activation (the input gradient through the
+// activation), and can add into the output.  The column sums of the W
+// operand (the bias gradient when W is dY) are formed by the preparation
+// warps from the W tiles the units of the first tile row stage anyway, and
+// added into the result by the epilogue in slice order.
 #include <cstring>
 
+#include "act.cuh"
 #include "fa2_common.cuh"
 
 namespace ct {
@@ -83,6 +92,7 @@ struct GemmCfg {
 struct GemmBars {
   uint64_t full[8], ready[8], empty[8];
   uint64_t acc_full[2], acc_empty[2], stored, mma_final;
+  uint64_t db_ready[2], db_free[2];  // column-sum partials (w_colsum)
   CtaCtl ctl;
 };
 
@@ -97,19 +107,27 @@ struct GemmParams {
   float* out;
   uint32_t* sem;  // one counter per tile (slices > 1)
   uint32_t* status;
-  int tma_out;    // epilogue stores through TMA (tmO) instead of per-thread rows
+  int tma_out;    // epilogue stores through TMA (tmO, tmO2) instead of per-thread rows
+  int epi;        // CT_EPILOGUE_*
+  float* out_act;        // CT_EPILOGUE_GELU: gelu(out)
+  const float* act_in;   // CT_EPILOGUE_GELU_GRAD: pre-activation [batch, m, n]
+  float* colsum;         // column sums of the W operand (batch == 1, BN == 128), or null
+  int accumulate;        // out (and colsum) += instead of =
 };
 
 // Epilogue staging: two 32 x 32 FP32 tiles (4 KB each, 128-byte swizzle) per
-// epilogue warp, after the stage ring.
+// epilogue warp, after the stage ring; then (BN = 128) two BN-float buffers
+// of column-sum partials.
 constexpr uint32_t kStageOut = 4u * 2u * 4096u;
+template <class C>
+constexpr uint32_t db_bytes() { return C::BN == 128 ? 2u * 128u * 4u : 0u; }
 
 template <class C>
 constexpr size_t gemm_smem_bytes() {
   static_assert(sizeof(GemmBars) <= 1024, "barrier block");
-  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut <= 227 * 1024,
+  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut + db_bytes<C>() <= 227 * 1024,
                 "shared memory budget");
-  return 1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut;
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE + kStageOut + db_bytes<C>();
 }
 
 struct Unit {
@@ -181,14 +199,14 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const GemmParams& p, 
 }
 
 // Per-thread epilogue of one 32-column slice of a tile row (outputs TMA
-// cannot address): adds the bias (first slice) or the partial sum the earlier
-// slices stored (later slices), then stores the row.
+// cannot address): adds what the output holds (later split-K slices, or
+// accumulate), then stores the row.
 __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p, float* orow,
-                                            int col0, bool vec_ok, bool first_slice) {
+                                            int col0, bool vec_ok, bool add_existing) {
   const int n = p.n;
   if (col0 >= n) return;
   const bool full = col0 + 32 <= n;
-  if (!first_slice) {
+  if (add_existing) {
     if (full && vec_ok) {
       const float4* o4 = reinterpret_cast<const float4*>(orow + col0);
 #pragma unroll
@@ -201,8 +219,6 @@ __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p,
       for (int i = 0; i < 32; ++i)
         if (col0 + i < n) v[i] += __ldcg(orow + col0 + i);
     }
-  } else {
-    add_bias32(v, p, col0);
   }
   if (full && vec_ok) {
     float4* d4 = reinterpret_cast<float4*>(orow + col0);
@@ -216,10 +232,65 @@ __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p,
   }
 }
 
+// v[i] *= gelu'(act_in[row][col0 + i]) for the columns inside the output.
+__device__ __forceinline__ void mul_gelu_grad32(float (&v)[32], const GemmParams& p,
+                                                const float* arow, int col0, bool vec_ok) {
+  const int n = p.n;
+  if (col0 + 32 <= n && vec_ok) {
+    const float4* a4 = reinterpret_cast<const float4*>(arow + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 a = __ldg(a4 + i);
+      v[4 * i] *= gelu_d(a.x);
+      v[4 * i + 1] *= gelu_d(a.y);
+      v[4 * i + 2] *= gelu_d(a.z);
+      v[4 * i + 3] *= gelu_d(a.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < n) v[i] *= gelu_d(__ldg(arow + col0 + i));
+  }
+}
+
+__device__ __forceinline__ float lds32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+
+// Adds the column sums of one staged W tile (32 K rows) into cs: thread t of
+// the 64 preparation threads owns columns t + 64 i.  MN-major tiles are 32-
+// column chunks of 32 rows x 128 bytes with 32-byte units XORed with row % 4;
+// K-major tiles are BN rows (one per column) of 32 values, 16-byte units
+// XORed with row % 8 (summed in stored order).
+template <int BN>
+__device__ __forceinline__ void colsum_tile(uint32_t b, bool b_mn, uint32_t tid,
+                                            float (&cs)[BN / 64]) {
+#pragma unroll
+  for (int i = 0; i < BN / 64; ++i) {
+    const uint32_t col = tid + 64u * i;
+    float acc = 0.0f;
+    if (b_mn) {
+      const uint32_t base = b + (col >> 5) * 4096u + (col & 7u) * 4u, u = (col & 31u) >> 3;
+#pragma unroll 8
+      for (uint32_t kr = 0; kr < 32; ++kr) acc += lds32(base + kr * 128u + ((u ^ (kr & 3u)) << 5));
+    } else {
+#pragma unroll
+      for (uint32_t u = 0; u < 8; ++u) {
+        const float4 x = lds128(b + col * 128u + u * 16u);
+        acc += (x.x + x.y) + (x.z + x.w);
+      }
+    }
+    cs[i] += acc;
+  }
+}
+
 template <class C>
 __global__ void __launch_bounds__(kThreadsG, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmO,
+                     const __grid_constant__ CUtensorMap tmO2, const GemmParams p) {
   constexpr int BN = C::BN, NS = C::NS, SPLIT = C::SPLIT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (status_raised(p.status)) return;
@@ -246,6 +317,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
     mbar_init(B(bars->stored), 128);
     mbar_init(B(bars->mma_final), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(B(bars->db_ready[i]), kPrepThreads);
+      mbar_init(B(bars->db_free[i]), 128);
+    }
     ctl->abort = 0;
     fence_barrier_init();
   }
@@ -312,6 +387,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const uint64_t bd0 = p.b_mn ? sdesc_mnmajor(tiles + C::OFF_B, 4096u) : sdesc_kmajor(tiles + C::OFF_B);
       const uint32_t astep = p.a_mn ? 1024u >> 4 : 32u >> 4;  // per 8-deep k step
       const uint32_t bstep = p.b_mn ? 1024u >> 4 : 32u >> 4;
+      // the preparation warps release a stage (3xTF32 split, column sums)
+      const bool use_ready = SPLIT == 3 || p.colsum != nullptr;
       uint32_t it = 0, ci = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
@@ -327,7 +404,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           const int kce = min(w.kb1, kc + chunk_kb(SPLIT));
           for (int kb = kc; kb < kce; ++kb, ++it) {
             const int s = (int)(it % NS), r = (int)(it / NS);
-            const uint32_t rbar = SPLIT == 3 ? B(bars->ready[s]) : B(bars->full[s]);
+            const uint32_t rbar = use_ready ? B(bars->ready[s]) : B(bars->full[s]);
             if (!mbar_wait(rbar, r & 1, ctl, p.status)) {
               ok = false;
               break;
@@ -354,13 +431,19 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
     __syncwarp();
   } else if (warp < kEpiWarp0) {
-    // ------------------------------------------------ 3xTF32 split warps
-    if constexpr (SPLIT == 3) {
+    // ---------------------------- 3xTF32 split warps, W column sums
+    if (SPLIT == 3 || p.colsum != nullptr) {
       const uint32_t tid = threadIdx.x - kPrepWarp0 * 32;
-      uint32_t it = 0;
+      float* dbs = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
+                                            NS * C::STAGE + kStageOut);
+      uint32_t it = 0, n_db = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
         const Unit w = decode_unit(u, p, BN);
+        const bool sums = BN == 128 && p.colsum != nullptr && w.m0 == 0;
+        float cs[BN / 64];
+#pragma unroll
+        for (int i = 0; i < BN / 64; ++i) cs[i] = 0.0f;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = (int)(it % NS), r = (int)(it / NS);
           const uint32_t st = tiles + s * C::STAGE;
@@ -368,9 +451,19 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             ok = false;
             break;
           }
-          split_tile_smem<C::RAW, kPrepThreads>(st, st + C::LO, tid);
+          if (sums) colsum_tile<BN>(st + C::OFF_B, p.b_mn != 0, tid, cs);
+          if constexpr (SPLIT == 3) split_tile_smem<C::RAW, kPrepThreads>(st, st + C::LO, tid);
           fence_proxy_async_smem();
           mbar_arrive(B(bars->ready[s]));
+        }
+        if (ok && sums) {  // hand the unit's partial column sums to the epilogue
+          const uint32_t buf = n_db & 1u;
+          if (n_db >= 2 && !mbar_wait(B(bars->db_free[buf]), ((n_db >> 1) - 1) & 1, ctl, p.status))
+            break;
+#pragma unroll
+          for (int i = 0; i < BN / 64; ++i) dbs[buf * 128u + tid + 64u * i] = cs[i];
+          mbar_arrive(B(bars->db_ready[buf]));
+          ++n_db;
         }
       }
     }
@@ -384,15 +477,21 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
     const bool vec_ok = (p.n & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0);
     const uint32_t stg = tiles + NS * C::STAGE + (uint32_t)quad * 2u * 4096u;
-    if (p.tma_out && lane == 0) tma_prefetch_desc(&tmO);
-    uint32_t ci = 0, n_split = 0, n_out = 0;
+    const float* dbs = reinterpret_cast<const float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
+                                                      NS * C::STAGE + kStageOut);
+    if (p.tma_out && lane == 0) {
+      tma_prefetch_desc(&tmO);
+      if (p.epi == CT_EPILOGUE_GELU) tma_prefetch_desc(&tmO2);
+    }
+    uint32_t ci = 0, n_split = 0, n_out = 0, n_db = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const Unit w = decode_unit(u, p, BN);
       const int row = w.m0 + r;
       const bool valid = row < p.m;
       const bool rows_in = w.m0 + 32 * quad < p.m;  // warp-uniform
-      float* orow = p.out + ((int64_t)w.b * p.m + (valid ? row : 0)) * p.n;
+      const int64_t row_off = ((int64_t)w.b * p.m + (valid ? row : 0)) * p.n;
+      float* orow = p.out + row_off;
       const int nch = n_chunks(w.kb1 - w.kb0, chunk_kb(SPLIT));
       for (int c = 0; c < nch; ++c, ++ci) {
         const int acc = (int)(ci & 1);
@@ -403,7 +502,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         // this warp's previous writes have completed (fixed order).
         const bool writes = last || !C::FOLD;
         const bool first_write = C::FOLD ? last : c == 0;
-        const bool add_mode = w.slice > 0 || (!C::FOLD && c > 0);
+        const bool add_mode = p.accumulate || w.slice > 0 || (!C::FOLD && c > 0);
         const bool with_bias = w.slice == 0 && first_write;
         if (!warp_wait(B(bars->acc_full[acc]), (ci >> 1) & 1, ctl, p.status)) {
           ok = false;
@@ -441,24 +540,44 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           } else if (p.tma_out) {
             if (rows_in && col0 < p.n) {
               if (with_bias) add_bias32(v, p, col0);
-              const uint32_t buf = stg + (n_out & 1u) * 4096u;
-              if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
-              __syncwarp();
+              if (p.epi == CT_EPILOGUE_GELU_GRAD && valid)
+                mul_gelu_grad32(v, p, p.act_in + row_off, col0, vec_ok);
+              // one 32 x 32 piece: stage it, then one TMA store (or add)
+              auto put = [&](const CUtensorMap* map, bool add) {
+                const uint32_t buf = stg + (n_out & 1u) * 4096u;
+                if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
+                __syncwarp();
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                sts128(buf + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4),
-                       make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                if (!add_mode) tma_store_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
-                else tma_reduce_add_3d(&tmO, buf, col0, w.m0 + 32 * quad, w.b);
-                bulk_commit_group();
+                for (int j = 0; j < 8; ++j)
+                  sts128(buf + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4),
+                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  if (!add) tma_store_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
+                  else tma_reduce_add_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
+                  bulk_commit_group();
+                }
+                ++n_out;
+              };
+              put(&tmO, add_mode);
+              if (p.epi == CT_EPILOGUE_GELU) {  // then the activation of the same piece
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
+                put(&tmO2, false);
               }
-              ++n_out;
             }
           } else if (valid) {
-            store_row32(v, p, orow, col0, vec_ok, w.slice == 0);
+            if (w.slice == 0) add_bias32(v, p, col0);
+            if (p.epi == CT_EPILOGUE_GELU_GRAD)
+              mul_gelu_grad32(v, p, p.act_in + row_off, col0, vec_ok);
+            store_row32(v, p, orow, col0, vec_ok, p.accumulate || w.slice > 0);
+            if (p.epi == CT_EPILOGUE_GELU) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
+              store_row32(v, p, p.out_act + row_off, col0,
+                          vec_ok && ((reinterpret_cast<uintptr_t>(p.out_act) & 15u) == 0), false);
+            }
           }
         }
         if (!last) tmem_wait_st();
@@ -466,6 +585,20 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         mbar_arrive(B(bars->acc_empty[acc]));
       }
       if (!__all_sync(0xffffffffu, ok)) break;
+      if (BN == 128 && p.colsum != nullptr && w.m0 == 0) {
+        // the unit's W column sums, added in slice order (the tile's counter
+        // is held by this slice here) or stored by slice 0
+        const uint32_t buf = n_db & 1u;
+        if (!warp_wait(B(bars->db_ready[buf]), (n_db >> 1) & 1, ctl, p.status)) break;
+        const int col = r, j = w.n0 + col;
+        if (col < BN && j < p.n) {
+          float val = dbs[buf * 128u + col];
+          if (p.accumulate || w.slice > 0) val += __ldcg(p.colsum + j);
+          p.colsum[j] = val;
+        }
+        mbar_arrive(B(bars->db_free[buf]));
+        ++n_db;
+      }
       if (p.slices > 1) {  // publish this slice: counter = slice + 1
         if (p.tma_out && lane == 0) {
           bulk_wait_group<0>();  // this warp's TMA writes are done
@@ -553,7 +686,8 @@ void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int ckb, in
   *slices = 1;
   *kbps = kb_total;
   const int64_t tiles = tile_count(g, bn);
-  if (!have_ws || tiles * 2 > sms) return;
+  // a GELU epilogue needs the whole sum of a tile at once
+  if (!have_ws || tiles * 2 > sms || g.epilogue != CT_EPILOGUE_NONE) return;
   int s = (int)(sms / tiles);
   const int max_s = kb_total / (2 * ckb);
   if (s > max_s) s = max_s;
@@ -564,25 +698,27 @@ void pick_split(const GemmProblem& g, int bn, int sms, bool have_ws, int ckb, in
   *slices = (kb_total + per - 1) / per;
 }
 
-// TMA map of the dense output [batch, m, n] with 32 x 32 boxes (epilogue);
+// TMA map of a dense [batch, m, n] output with 32 x 32 boxes (epilogue);
 // false when TMA cannot address it (n not a multiple of 4, unaligned base).
-bool make_out_map(const GemmProblem& g, CUtensorMap* to) {
-  if ((g.n & 3) != 0 || (reinterpret_cast<uintptr_t>(g.out) & 15u) != 0) return false;
+bool make_out_map(const GemmProblem& g, float* out, CUtensorMap* to) {
+  if ((g.n & 3) != 0 || (reinterpret_cast<uintptr_t>(out) & 15u) != 0) return false;
   const uint64_t s1 = (uint64_t)g.n * 4u;
   const uint64_t dims[3] = {(uint64_t)g.n, (uint64_t)g.m, (uint64_t)g.batch};
   const uint64_t strides[2] = {s1, s1 * (uint64_t)g.m};
   const uint32_t box[3] = {32u, 32u, 1u};
-  return make_tmap_f32(to, g.out, 3, dims, strides, box, false) == CT_OK;
+  return make_tmap_f32(to, out, 3, dims, strides, box, false) == CT_OK;
 }
 
 template <class C>
 int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_bytes,
                const DeviceInfo& dev, cudaStream_t st) {
   static unsigned long long attr_done = 0;
-  CUtensorMap ta, tb, to;
+  CUtensorMap ta, tb, to, to2;
   int rc = make_maps(g, a_mn, b_mn, C::BN, &ta, &tb);
   if (rc != CT_OK) return rc;
-  const bool tma_out = make_out_map(g, &to);
+  std::memset(&to2, 0, sizeof(to2));
+  bool tma_out = make_out_map(g, g.out, &to);
+  if (tma_out && g.epilogue == CT_EPILOGUE_GELU) tma_out = make_out_map(g, g.out_act, &to2);
   if (!tma_out) std::memset(&to, 0, sizeof(to));
   const size_t smem = gemm_smem_bytes<C>();
   rc = ensure_smem_attr(linear_tc_kernel<C>, smem, dev.device, &attr_done);
@@ -609,12 +745,19 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   p.sem = static_cast<uint32_t*>(ws);
   p.status = dev.status;
   p.tma_out = tma_out ? 1 : 0;
+  p.epi = g.epilogue;
+  p.out_act = g.out_act;
+  p.act_in = g.act_in;
+  p.colsum = g.w_colsum;
+  p.accumulate = g.accumulate ? 1 : 0;
+  if ((p.epi != CT_EPILOGUE_NONE || p.colsum) && (!C::FOLD || C::BN != 128))
+    return CT_ERR_UNSUPPORTED_LAYOUT;  // (pick_bn picks 128-wide tiles for these)
   int grid = p.units < dev.sm_count ? p.units : dev.sm_count;
   if (p.slices > 1) {
     grid = grid / p.slices * p.slices;  // whole tiles per round of the persistent loop
     if (cudaMemsetAsync(ws, 0, (size_t)tiles * 4u, st) != cudaSuccess) return CT_ERR_CUDA;
   }
-  linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, to, p);
+  linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, to, to2, p);
   return check_launch();
 }
 
@@ -627,10 +770,12 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
 int pick_bn(const GemmProblem& g, int sms) {
   const int64_t kb = (g.k + kBK - 1) / kBK;
   const int ckb = chunk_kb(g.precision == CT_PRECISION_3XTF32 ? 3 : 1);
-  if (g.n <= 128) return 128;
+  // fused epilogues and W column sums run on 128-wide tiles (the TMEM running
+  // sum holds the whole K before the epilogue; room for the sum buffers)
+  if (g.n <= 128 || g.epilogue != CT_EPILOGUE_NONE || g.w_colsum) return 128;
   if (kb > ckb) {  // several chunks: BN = 256 folds them in L2 (TMA stores, no split-K)
     const bool tma_out = (g.n & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15u) == 0;
-    if (!tma_out || kb > 4 * ckb || tile_count(g, 256) * 2 <= sms) return 128;
+    if (!tma_out || g.accumulate || kb > 4 * ckb || tile_count(g, 256) * 2 <= sms) return 128;
   }
   static const int env = [] {
     const char* e = std::getenv("CT_GEMM_BN");

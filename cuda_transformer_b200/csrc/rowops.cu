@@ -8,6 +8,7 @@
 #include <cfloat>
 #include <cmath>
 
+#include "act.cuh"
 #include "ct_internal.h"
 
 namespace ct {
@@ -192,20 +193,7 @@ __global__ void __launch_bounds__(THREADS) softmax_bwd_long_kernel(const float* 
 }
 
 // ------------------------------------------------------------------ GELU
-// gelu / gelu_bwd (Transformer_kernels/GeLU.cuh:7-29): y = x * Phi(x) and
-// dx = dy * (Phi(x) + x * phi(x)), phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
-// Phi(x) = (1 + erf(x / sqrt 2)) / 2, the form torch's exact GELU uses; erff
-// costs fewer instructions than normcdff, which keeps these element-wise
-// kernels at the memory bound (normcdff's extra accuracy is in the far
-// negative tail, where the products are below 1e-6 in absolute value).
-__device__ __forceinline__ float phi_cdf(float x) {
-  return fmaf(0.5f, erff(x * 0.7071067811865476f), 0.5f);
-}
-__device__ __forceinline__ float gelu_f(float x) { return x * phi_cdf(x); }
-__device__ __forceinline__ float gelu_g(float x, float dy) {
-  const float inv_sqrt_2pi = 0.3989422804014327f;
-  return dy * (phi_cdf(x) + x * inv_sqrt_2pi * expf(-0.5f * x * x));
-}
+// gelu / gelu_bwd (Transformer_kernels/GeLU.cuh:7-29), math in act.cuh.
 
 __global__ void gelu_fwd_vec(const float4* __restrict__ x, float4* __restrict__ y, int64_t n4) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
@@ -958,6 +946,134 @@ int launch_fa2_delta(const Fa2Problem& p, Strided4 o, Strided4 dO, float* delta,
     default: return CT_ERR_UNSUPPORTED_HEAD_DIM;
   }
 #undef CT_DELTA
+  return check_launch();
+}
+
+
+// ----------------------------------------------------------- cross entropy
+// F.cross_entropy over the lm_head logits (gpt/gpt.py:170-175; the reference
+// calls torch for it), forward and backward of one row together:
+//   loss_row = logsumexp(x) - x[t],   dx = softmax(x) - onehot(t)
+// written over x in place (the caller scales by 1 / rows afterwards).  A
+// target equal to `ignore` gives loss 0 and a zero gradient row; a target
+// outside [0, vocab) gives NaN (the row is poisoned, not silently wrong).
+// TPR threads per row: a warp (8 rows per CTA) for short rows, the CTA for
+// long ones.  Pass 1 keeps a running (max, sum of exp) per thread, combined
+// across threads in a fixed order; pass 2 writes the gradient.
+__device__ __forceinline__ void online_combine(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;  // both empty
+  s = s * expf(m - mn) + s2 * expf(m2 - mn);
+  m = mn;
+}
+
+template <int TPR, bool VEC>
+__global__ void __launch_bounds__(256)
+    ce_fwd_bwd_kernel(float* __restrict__ x, int64_t ld, int64_t rows, int64_t vocab,
+                      const int64_t* __restrict__ targets, int64_t ignore,
+                      float* __restrict__ loss_rows) {
+  constexpr int RPB = 256 / TPR;  // rows per CTA
+  __shared__ float red_m[256 / 32], red_s[256 / 32];
+  __shared__ float sh_lse[RPB];
+  const int sub = threadIdx.x / TPR, t_in = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * RPB + sub;
+  const bool live = row < rows;
+  float* xr = x + (live ? row : 0) * ld;
+  const int64_t tgt = live ? targets[row] : ignore;
+  // pass 1: running max and sum of exp
+  float m = -INFINITY, sum = 0.0f;
+  if (live) {
+    if constexpr (VEC) {
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      for (int64_t i = t_in; i < vocab / 4; i += TPR) {
+        const float4 v = x4[i];
+        const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+        if (mx > m) {
+          sum *= expf(m - mx);
+          m = mx;
+        }
+        sum += expf(v.x - m) + expf(v.y - m) + expf(v.z - m) + expf(v.w - m);
+      }
+    } else {
+      for (int64_t i = t_in; i < vocab; i += TPR) {
+        const float v = xr[i];
+        if (v > m) {
+          sum *= expf(m - v);
+          m = v;
+        }
+        sum += expf(v - m);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+    const float s2 = __shfl_xor_sync(0xffffffffu, sum, off);
+    online_combine(m, sum, m2, s2);
+  }
+  if constexpr (TPR > 32) {
+    const int w = threadIdx.x / 32;
+    if ((threadIdx.x & 31) == 0) {
+      red_m[w] = m;
+      red_s[w] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float mm = red_m[0], ss = red_s[0];
+      for (int i = 1; i < TPR / 32; ++i) online_combine(mm, ss, red_m[i], red_s[i]);
+      sh_lse[0] = mm + logf(ss);
+    }
+  } else if (t_in == 0) {
+    sh_lse[sub] = m + logf(sum);
+  }
+  __syncthreads();
+  const float lse = sh_lse[sub];
+  const bool ignored = tgt == ignore;
+  const bool bad = !ignored && (tgt < 0 || tgt >= vocab);
+  if (live && t_in == 0)
+    loss_rows[row] = ignored ? 0.0f : (bad ? NAN : lse - xr[tgt]);
+  if constexpr (TPR > 32) __syncthreads();  // x[t] read before the row is overwritten
+  else __syncwarp();
+  if (!live) return;
+  // pass 2: dx = softmax - onehot, in place
+  if constexpr (VEC) {
+    float4* x4 = reinterpret_cast<float4*>(xr);
+    for (int64_t i = t_in; i < vocab / 4; i += TPR) {
+      float4 v = x4[i];
+      if (ignored) {
+        v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      } else {
+        v = make_float4(expf(v.x - lse), expf(v.y - lse), expf(v.z - lse), expf(v.w - lse));
+        if (bad) v = make_float4(NAN, NAN, NAN, NAN);
+        if (tgt / 4 == i) {
+          const int c = (int)(tgt % 4);
+          if (c == 0) v.x -= 1.0f; else if (c == 1) v.y -= 1.0f; else if (c == 2) v.z -= 1.0f; else v.w -= 1.0f;
+        }
+      }
+      x4[i] = v;
+    }
+  } else {
+    for (int64_t i = t_in; i < vocab; i += TPR) {
+      float v = ignored ? 0.0f : (bad ? NAN : expf(xr[i] - lse) - (i == tgt ? 1.0f : 0.0f));
+      xr[i] = v;
+    }
+  }
+}
+
+int launch_cross_entropy(float* x, int64_t ld, int64_t rows, int64_t vocab, const int64_t* targets,
+                         int64_t ignore, float* loss_rows, cudaStream_t st) {
+  if (rows == 0) return CT_OK;
+  const bool vec = (vocab % 4) == 0 && (ld % 4) == 0 && aligned16(x);
+  if (vocab <= 2048) {
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    if (vec) ce_fwd_bwd_kernel<32, true><<<grid, 256, 0, st>>>(x, ld, rows, vocab, targets, ignore, loss_rows);
+    else ce_fwd_bwd_kernel<32, false><<<grid, 256, 0, st>>>(x, ld, rows, vocab, targets, ignore, loss_rows);
+  } else {
+    if (rows > 0x7fffffffll) return CT_ERR_INVALID_ARGUMENT;
+    const unsigned grid = (unsigned)rows;
+    if (vec) ce_fwd_bwd_kernel<256, true><<<grid, 256, 0, st>>>(x, ld, rows, vocab, targets, ignore, loss_rows);
+    else ce_fwd_bwd_kernel<256, false><<<grid, 256, 0, st>>>(x, ld, rows, vocab, targets, ignore, loss_rows);
+  }
   return check_launch();
 }
 

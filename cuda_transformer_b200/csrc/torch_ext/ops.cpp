@@ -21,6 +21,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <optional>
 #include <string>
 #include <tuple>
 
@@ -208,6 +209,107 @@ Tensor cuda_fma(Tensor x, Tensor weights, Tensor bias) {
 }
 Tensor cuda_fma_ex(Tensor x, Tensor weights, Tensor bias, int64_t precision) {
   return fma_impl(x, weights, bias, precision);
+}
+
+// The linear layer with its neighbours fused in (ct_linear_fwd_ex): epilogue
+// 0 none, 1 GELU (returns out = x W + b and act = gelu(out)), 2 GELU gradient
+// (out = (x W + b) * gelu'(act_in)); want_colsum also returns the column sums
+// of `weights` over its reduction index (db when weights is dY; batch 1).
+// Returns (out, act or an empty tensor, colsum or an empty tensor).
+std::tuple<Tensor, Tensor, Tensor> linear_fused(Tensor x0, Tensor weights0, Tensor bias,
+                                                int64_t precision, int64_t epilogue,
+                                                std::optional<Tensor> act_in0, bool want_colsum) {
+  if (weights0.dim() == 2) weights0 = weights0.unsqueeze(0);
+  TORCH_CHECK(x0.dim() == 3, "x must be a 3D tensor (batch, m, k)");
+  check_cuda_f32(x0, "x");
+  check_cuda_f32(weights0, "weights");
+  check_cuda_f32(bias, "bias");
+  c10::cuda::CUDAGuard guard0(x0.device());
+  const bool tc = precision != (int64_t)CT_PRECISION_FP32;
+  const Tensor x = tc && x0.numel() > 0 ? linear_operand(x0) : x0;
+  const Tensor weights = tc && weights0.numel() > 0 ? linear_operand(weights0) : weights0;
+  const int64_t batch = x.size(0), m = x.size(1), k = x.size(2), n = weights.size(2);
+  TORCH_CHECK(weights.size(1) == k, "weights.size(1) must match x.size(2)");
+  TORCH_CHECK(bias.size(0) == n, "bias.size(0) must match weights.size(2)");
+  TORCH_CHECK(weights.size(0) == 1 || weights.size(0) == batch, "weights batch must be 1 or match x");
+  TORCH_CHECK(!want_colsum || batch == 1, "column sums need batch 1");
+  Tensor out = at::empty({batch, m, n}, x.options());
+  Tensor act = epilogue == CT_EPILOGUE_GELU ? at::empty({batch, m, n}, x.options())
+                                            : at::empty({0}, x.options());
+  Tensor cs = want_colsum ? at::empty({n}, x.options()) : at::empty({0}, x.options());
+  Tensor act_in;
+  if (epilogue == CT_EPILOGUE_GELU_GRAD) {
+    TORCH_CHECK(act_in0.has_value(), "the GELU-gradient epilogue needs act_in");
+    act_in = act_in0->contiguous();
+    check_cuda_f32(act_in, "act_in");
+    TORCH_CHECK(act_in.numel() == batch * m * n, "act_in must have batch*m*n elements");
+  }
+  const int64_t xs[3] = {x.stride(0), x.stride(1), x.stride(2)};
+  const int64_t wsd[3] = {weights.stride(0), weights.stride(1), weights.stride(2)};
+  const size_t wsb = ct_linear_workspace_size(batch, m, k, n);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(wsb, 16)}, x.options().dtype(at::kByte));
+  check_rc(ct_linear_fwd_ex(x.data_ptr<float>(), xs, weights.data_ptr<float>(), wsd,
+                            bias.data_ptr<float>(), bias.stride(0), out.data_ptr<float>(), batch, m,
+                            k, n, weights.size(0), (int)precision, (int)epilogue,
+                            epilogue == CT_EPILOGUE_GELU ? act.data_ptr<float>() : nullptr,
+                            epilogue == CT_EPILOGUE_GELU_GRAD ? act_in.data_ptr<float>() : nullptr,
+                            want_colsum ? cs.data_ptr<float>() : nullptr, 0, ws.data_ptr(), wsb,
+                            cur_stream()),
+           "linear_fused");
+  return {out, act, cs};
+}
+
+// out += x W + bias (and colsum += column sums of weights, when given); out
+// dense (batch, m, n).
+void linear_accumulate_(Tensor out, std::optional<Tensor> colsum, Tensor x0, Tensor weights0,
+                        Tensor bias, int64_t precision) {
+  if (weights0.dim() == 2) weights0 = weights0.unsqueeze(0);
+  TORCH_CHECK(x0.dim() == 3, "x must be a 3D tensor (batch, m, k)");
+  check_cuda_f32(x0, "x");
+  check_cuda_f32(weights0, "weights");
+  check_cuda_f32(bias, "bias");
+  check_cuda_f32(out, "out");
+  c10::cuda::CUDAGuard guard0(x0.device());
+  const bool tc = precision != (int64_t)CT_PRECISION_FP32;
+  const Tensor x = tc && x0.numel() > 0 ? linear_operand(x0) : x0;
+  const Tensor weights = tc && weights0.numel() > 0 ? linear_operand(weights0) : weights0;
+  const int64_t batch = x.size(0), m = x.size(1), k = x.size(2), n = weights.size(2);
+  TORCH_CHECK(weights.size(1) == k && bias.size(0) == n, "linear_accumulate_: shape mismatch");
+  TORCH_CHECK(out.is_contiguous() && out.numel() == batch * m * n, "out must be dense (batch, m, n)");
+  float* csp = nullptr;
+  if (colsum.has_value()) {
+    check_cuda_f32(*colsum, "colsum");
+    TORCH_CHECK(colsum->is_contiguous() && colsum->numel() == n && batch == 1,
+                "colsum must be a dense (n,) tensor, batch 1");
+    csp = colsum->data_ptr<float>();
+  }
+  const int64_t xs[3] = {x.stride(0), x.stride(1), x.stride(2)};
+  const int64_t wsd[3] = {weights.stride(0), weights.stride(1), weights.stride(2)};
+  const size_t wsb = ct_linear_workspace_size(batch, m, k, n);
+  Tensor ws = at::empty({(int64_t)std::max<size_t>(wsb, 16)}, x.options().dtype(at::kByte));
+  check_rc(ct_linear_fwd_ex(x.data_ptr<float>(), xs, weights.data_ptr<float>(), wsd,
+                            bias.data_ptr<float>(), bias.stride(0), out.data_ptr<float>(), batch, m,
+                            k, n, weights.size(0), (int)precision, CT_EPILOGUE_NONE, nullptr,
+                            nullptr, csp, 1, ws.data_ptr(), wsb, cur_stream()),
+           "linear_accumulate_");
+}
+
+// ------------------------------------------------------------ cross entropy
+// loss per row; logits (rows, vocab), row stride free, overwritten with
+// softmax - onehot(targets).  targets int64 (rows,).
+Tensor cross_entropy_fwd_bwd_(Tensor logits, Tensor targets, int64_t ignore_index) {
+  check_cuda_f32(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be (rows, vocab), unit column stride");
+  TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == at::kLong, "targets must be int64 on the GPU");
+  TORCH_CHECK(targets.numel() == logits.size(0), "one target per row");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const Tensor t = targets.contiguous();
+  Tensor loss = at::empty({logits.size(0)}, logits.options());
+  check_rc(ct_cross_entropy_fwd_bwd(logits.data_ptr<float>(), logits.stride(0), logits.size(0),
+                                    logits.size(1), t.data_ptr<int64_t>(), ignore_index,
+                                    loss.data_ptr<float>(), cur_stream()),
+           "cross_entropy_fwd_bwd_");
+  return loss;
 }
 
 // dy: (batch, m, n) -> db: (n,)  -- linear_layer.cu:72-97.
@@ -398,6 +500,9 @@ TORCH_LIBRARY(cuda_transformer, m) {
   m.def("cuda_fma_ex(Tensor x, Tensor weights, Tensor bias, int precision) -> Tensor");
   m.def("layernorm_fwd(Tensor x, Tensor gamma, Tensor beta, float eps) -> (Tensor, Tensor, Tensor)");
   m.def("layernorm_bwd(Tensor x, Tensor gamma, Tensor mean, Tensor rstd, Tensor dy) -> (Tensor, Tensor, Tensor)");
+  m.def("linear_fused(Tensor x, Tensor weights, Tensor bias, int precision, int epilogue, Tensor? act_in, bool want_colsum) -> (Tensor, Tensor, Tensor)");
+  m.def("linear_accumulate_(Tensor(a!) out, Tensor(b!)? colsum, Tensor x, Tensor weights, Tensor bias, int precision) -> ()");
+  m.def("cross_entropy_fwd_bwd_(Tensor(a!) logits, Tensor targets, int ignore_index) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(cuda_transformer, CUDA, m) {
@@ -416,6 +521,9 @@ TORCH_LIBRARY_IMPL(cuda_transformer, CUDA, m) {
   m.impl("cuda_fma_ex", &cuda_fma_ex);
   m.impl("layernorm_fwd", &layernorm_fwd);
   m.impl("layernorm_bwd", &layernorm_bwd);
+  m.impl("linear_fused", &linear_fused);
+  m.impl("linear_accumulate_", &linear_accumulate_);
+  m.impl("cross_entropy_fwd_bwd_", &cross_entropy_fwd_bwd_);
 }
 
 }  // namespace cuda_transformer

@@ -4,9 +4,11 @@ The model follows the reference GPT (gpt/gpt.py:47-175): token + position
 embedding, pre-LayerNorm decoder blocks (x + attn(ln1(x)), x + mlp(ln2(x))),
 causal FlashAttention-2 on the (B, nh, T, hs) views of the fused QKV
 projection, an exact-GELU 4x MLP, a final LayerNorm and the lm_head, with the
-cross-entropy loss.  Every linear layer, LayerNorm, GELU and attention runs on
-this package's kernels (CudaLinearLayer, CudaLayerNorm, CudaGeluLayer,
-CudaFlashAttention); the embeddings, the loss and AdamW are torch's.
+cross-entropy loss.  Every linear layer, LayerNorm, GELU, attention and the
+loss run on this package's kernels (CudaLinearLayer, CudaLayerNorm,
+CudaFlashAttention; CudaMLP with the GELU in the GEMM epilogues;
+CudaLinearCrossEntropy for the lm_head and loss, chunked so the logits of
+every row are never held at once); the embeddings and AdamW are torch's.
 
 Default shape (the data-parallel benchmark configuration): 6 blocks,
 d_model 384, 6 heads of 64, context 256, vocabulary 65 with the lm_head tied to
@@ -36,9 +38,9 @@ import os
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
-from cuda_autograd_fns import CudaFlashAttention, CudaGeluLayer, CudaLayerNorm, CudaLinearLayer
+from cuda_autograd_fns import (CudaFlashAttention, CudaLayerNorm, CudaLinearCrossEntropy,
+                               CudaLinearLayer, CudaMLP)
 
 
 class LayerNorm(nn.Module):
@@ -78,10 +80,8 @@ class MLP(nn.Module):
         self.fc2_weights = nn.Parameter(torch.empty(4 * d, d).normal_(0.0, 0.02))
         self.fc2_bias = nn.Parameter(torch.zeros(d))
 
-    def forward(self, x):
-        x = CudaLinearLayer.apply(x, self.fc1_weights, self.fc1_bias)
-        x = CudaGeluLayer.apply(x)
-        return CudaLinearLayer.apply(x, self.fc2_weights, self.fc2_bias)
+    def forward(self, x):  # fc1 -> GELU -> fc2, the activation in the GEMM epilogues
+        return CudaMLP.apply(x, self.fc1_weights, self.fc1_bias, self.fc2_weights, self.fc2_bias)
 
 
 class Block(nn.Module):
@@ -109,17 +109,17 @@ class GPT(nn.Module):
         self.lm_head_bias = nn.Parameter(torch.zeros(vocab))
 
     def forward(self, idx, targets=None):
+        """(logits, None) without targets; (None, mean cross-entropy loss) with
+        them -- the lm_head and the loss then run fused, chunk by chunk."""
         T = idx.shape[1]
         x = self.tok(idx) + self.pos(torch.arange(T, device=idx.device))
         for blk in self.blocks:
             x = blk(x)
         x = self.ln(x)
         w = self.tok.weight.t() if self.tied else self.lm_head_weights
-        logits = CudaLinearLayer.apply(x, w, self.lm_head_bias)
-        loss = None
         if targets is not None:
-            loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), targets.reshape(-1))
-        return logits, loss
+            return None, CudaLinearCrossEntropy.apply(x, w, self.lm_head_bias, targets)
+        return CudaLinearLayer.apply(x, w, self.lm_head_bias), None
 
 
 def n_params(model: nn.Module) -> int:

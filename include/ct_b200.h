@@ -209,6 +209,38 @@ int ct_linear_fwd_ws(const float* x, const int64_t x_stride[3],
                      int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
                      int precision, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Fused epilogues of ct_linear_fwd_ex. */
+enum {
+  CT_EPILOGUE_NONE = 0,      /* out = x W + bias                                        */
+  CT_EPILOGUE_GELU = 1,      /* out = x W + bias and act_out = gelu(out) (erf form)     */
+  CT_EPILOGUE_GELU_GRAD = 2  /* out = (x W + bias) * gelu'(act_in), act_in [batch,m,n]  */
+};
+
+/* ct_linear_fwd_ws with the linear layer's neighbours fused in:
+ *  - `epilogue` applies GELU (gelu/gelu_bwd of Transformer_kernels/GeLU.cuh:7-29)
+ *    to the GEMM's output tile before it leaves the chip: CT_EPILOGUE_GELU
+ *    also writes act_out = gelu(out) (the MLP's fc1 and activation,
+ *    gpt/gpt.py:134-135), CT_EPILOGUE_GELU_GRAD multiplies by the GELU
+ *    derivative at act_in (the fc2 input gradient times gelu', the same
+ *    MLP's backward);
+ *  - `w_colsum` (batch == 1), when not NULL, receives the column sums of the
+ *    W operand over the reduction index: with W = dY this is the bias
+ *    gradient db, formed from the dY tiles the weight-gradient GEMM
+ *    dW = x^T dY already stages (cuda_autograd_fns/cuda_linear_layer.py:25-27,
+ *    Transformer_kernels/warp_sum_kernel.cuh:13-51);
+ *  - `accumulate` != 0 adds into out (and w_colsum) instead of storing
+ *    (CT_EPILOGUE_NONE only).
+ * Deterministic: split-K slices and the column sums add in a fixed order.
+ * Same reference counterpart as ct_linear_fwd (linear_layer.cu:28-70). */
+int ct_linear_fwd_ex(const float* x, const int64_t x_stride[3],
+                     const float* w, const int64_t w_stride[3],
+                     const float* bias, int64_t bias_stride,
+                     float* out,
+                     int64_t batch, int64_t m, int64_t k, int64_t n, int64_t w_batch,
+                     int precision, int epilogue, float* act_out, const float* act_in,
+                     float* w_colsum, int accumulate,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of workspace ct_bias_grad needs. */
 size_t ct_bias_grad_workspace_size(int64_t batch, int64_t m, int64_t n);
 
@@ -261,6 +293,20 @@ int ct_layernorm_bwd(const float* x, const float* gamma, const float* mean,
                      float* dx, float* dgamma, float* dbeta,
                      int64_t rows, int64_t n,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Cross entropy of `rows` logit rows of length `vocab` (row stride ld),
+ * forward and backward together:
+ *   loss_rows[r] = logsumexp(logits[r]) - logits[r][targets[r]]
+ *   logits[r][:] <- softmax(logits[r]) - onehot(targets[r])   (in place)
+ * A target equal to ignore_index gives loss 0 and a zero gradient row; one
+ * outside [0, vocab) gives NaN for that row.  With mean reduction the caller
+ * divides the summed loss and the gradient by the number of counted rows.
+ * The reference applies torch's F.cross_entropy to the lm_head logits
+ * (gpt/gpt.py:167-175); this lets the lm_head GEMM and the loss run chunk by
+ * chunk without materialising every row of logits. */
+int ct_cross_entropy_fwd_bwd(float* logits, int64_t ld, int64_t rows, int64_t vocab,
+                             const int64_t* targets, int64_t ignore_index, float* loss_rows,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -92,6 +92,21 @@ def test_invalid_arguments_rejected_before_any_device_work():
     for B, Hh in ((2 ** 62 + 1, 4), (2 ** 40, 2 ** 40), (2 ** 31, 1)):
         rc = lib.ct_fa2_fwd(None, s, None, s, None, s, None, None, B, Hh, 1, 64, 0, 0, None)
         assert rc == cb.CT_ERR_INVALID_ARGUMENT, (B, Hh)
+    # fused linear options: a GELU epilogue needs its output, accumulate goes
+    # with no epilogue, column sums need batch 1
+    s3 = (ctypes.c_int64 * 3)(1, 1, 1)
+    p = ctypes.c_void_p(256)
+    assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 1, 4, 4, 4, 1, 0, 1, None, None, None, 0,
+                                None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
+    assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 1, 4, 4, 4, 1, 0, 2, None, None, None, 0,
+                                None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
+    assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 1, 4, 4, 4, 1, 0, 1, p, None, None, 1,
+                                None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
+    assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 2, 4, 4, 4, 1, 0, 0, None, None, p, 0,
+                                None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
+    assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 1, 4, 4, 4, 1, 0, 3, None, None, None, 0,
+                                None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
+    assert lib.ct_cross_entropy_fwd_bwd(p, 4, 2, 8, p, -100, p, None) == cb.CT_ERR_INVALID_ARGUMENT
     # LayerNorm rows are at most 8192 wide
     rc = lib.ct_layernorm_fwd(None, None, None, None, None, None, 1, 8193, ctypes.c_float(1e-5), None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT
@@ -133,6 +148,11 @@ def test_fake_kernels_give_reference_shapes():
         assert ops.db_calculation(torch.empty(3, 5, 11)).shape == (11,)
         y, m, r = ops.layernorm_fwd(torch.empty(6, 384), torch.empty(384), torch.empty(384))
         assert y.shape == (6, 384) and m.shape == (6,) and r.shape == (6,)
+        o, a, cs = ops.linear_fused(x, w, torch.empty(11), 0, ops.EPILOGUE_GELU, None, False)
+        assert o.shape == (3, 5, 11) and a.shape == (3, 5, 11) and cs.numel() == 0
+        o, a, cs = ops.linear_fused(x[:1], w, torch.empty(11), 0, 0, None, True)
+        assert cs.shape == (11,) and a.numel() == 0
+        assert ops.cross_entropy_fwd_bwd_(torch.empty(4, 9), torch.empty(4, dtype=torch.long)).shape == (4,)
 
 
 def test_product_path_does_not_import_oracle():
