@@ -48,10 +48,16 @@
 // Fused neighbours (ct_linear_fwd_ex).  The epilogue can apply the MLP's GELU
 // to the tile (writing the pre-activation and gelu of it) or multiply by the
 // GELU derivative at a given pre-activation (the input gradient through the
-// activation), and can add into the output.  The column sums of the W
-// operand (the bias gradient when W is dY) are formed by the preparation
-// warps from the W tiles the units of the first tile row stage anyway, and
-// added into the result by the epilogue in slice order.
+// activation; the pre-activation of the next 32 columns is loaded while the
+// current ones are finished), and can add into the output.  The column sums
+// of the W operand (the bias gradient when W is dY) are formed by the
+// preparation warps from the W tiles the units stage anyway: the units of a
+// tile column share the K blocks between them (unit of tile row tm: blocks
+// kb % tiles_m == tm).  A unit adds its partial sums into its tile row's slot
+// of the workspace (the slices of a tile in slice order, like the output);
+// the last tile of a column to finish (an atomic counter per tile column)
+// adds the slots in tile-row order into the result -- deterministic, and no
+// unit waits for another tile.
 #include <cstring>
 
 #include "act.cuh"
@@ -71,9 +77,12 @@ __host__ __device__ constexpr int chunk_kb(int split) { return split == 3 ? 8 : 
 constexpr int kThreadsG = 256;
 constexpr int kPrepWarp0 = 2, kPrepThreads = 64, kEpiWarp0 = 4;
 
-template <int BN_, int SPLIT_, int NS_>
+// EPI_: the epilogue (CT_EPILOGUE_*) compiled into this instance, so the plain
+// GEMM carries none of the activation code and each variant gets its own
+// register allocation.
+template <int BN_, int SPLIT_, int NS_, int EPI_ = CT_EPILOGUE_NONE>
 struct GemmCfg {
-  static constexpr int BN = BN_, SPLIT = SPLIT_, NS = NS_;
+  static constexpr int BN = BN_, SPLIT = SPLIT_, NS = NS_, EPI = EPI_;
   static constexpr uint32_t A_TILE = kBM * kBK * 4u;      // 16 KB
   static constexpr uint32_t B_TILE = (uint32_t)BN * kBK * 4u;
   static constexpr uint32_t RAW = A_TILE + B_TILE;         // bytes TMA writes per stage
@@ -92,7 +101,8 @@ struct GemmCfg {
 struct GemmBars {
   uint64_t full[8], ready[8], empty[8];
   uint64_t acc_full[2], acc_empty[2], stored, mma_final;
-  uint64_t db_ready[2], db_free[2];  // column-sum partials (w_colsum)
+  uint64_t db_ready[2], db_free[2], db_stored;  // column-sum partials (w_colsum)
+  uint32_t cs_last;
   CtaCtl ctl;
 };
 
@@ -105,7 +115,9 @@ struct GemmParams {
   const float* bias;
   int64_t bias_s;
   float* out;
-  uint32_t* sem;  // one counter per tile (slices > 1)
+  uint32_t* sem;     // one counter per tile (slices > 1)
+  uint32_t* cs_cnt;  // one counter per tile column (colsum: finished tiles)
+  float* cs_part;    // [tiles_m][n] partial column sums (colsum)
   uint32_t* status;
   int tma_out;    // epilogue stores through TMA (tmO, tmO2) instead of per-thread rows
   int epi;        // CT_EPILOGUE_*
@@ -232,27 +244,6 @@ __device__ __forceinline__ void store_row32(float (&v)[32], const GemmParams& p,
   }
 }
 
-// v[i] *= gelu'(act_in[row][col0 + i]) for the columns inside the output.
-__device__ __forceinline__ void mul_gelu_grad32(float (&v)[32], const GemmParams& p,
-                                                const float* arow, int col0, bool vec_ok) {
-  const int n = p.n;
-  if (col0 + 32 <= n && vec_ok) {
-    const float4* a4 = reinterpret_cast<const float4*>(arow + col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 a = __ldg(a4 + i);
-      v[4 * i] *= gelu_d(a.x);
-      v[4 * i + 1] *= gelu_d(a.y);
-      v[4 * i + 2] *= gelu_d(a.z);
-      v[4 * i + 3] *= gelu_d(a.w);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (col0 + i < n) v[i] *= gelu_d(__ldg(arow + col0 + i));
-  }
-}
-
 __device__ __forceinline__ float lds32(uint32_t a) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
@@ -321,6 +312,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       mbar_init(B(bars->db_ready[i]), kPrepThreads);
       mbar_init(B(bars->db_free[i]), 128);
     }
+    mbar_init(B(bars->db_stored), 128);
     ctl->abort = 0;
     fence_barrier_init();
   }
@@ -440,7 +432,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
         const Unit w = decode_unit(u, p, BN);
-        const bool sums = BN == 128 && p.colsum != nullptr && w.m0 == 0;
+        const bool sums = BN == 128 && p.colsum != nullptr;
+        const int tm = w.m0 / kBM;  // this unit sums the K blocks kb % tiles_m == tm
         float cs[BN / 64];
 #pragma unroll
         for (int i = 0; i < BN / 64; ++i) cs[i] = 0.0f;
@@ -451,7 +444,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             ok = false;
             break;
           }
-          if (sums) colsum_tile<BN>(st + C::OFF_B, p.b_mn != 0, tid, cs);
+          if (sums && kb % p.tiles_m == tm) colsum_tile<BN>(st + C::OFF_B, p.b_mn != 0, tid, cs);
           if constexpr (SPLIT == 3) split_tile_smem<C::RAW, kPrepThreads>(st, st + C::LO, tid);
           fence_proxy_async_smem();
           mbar_arrive(B(bars->ready[s]));
@@ -479,9 +472,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     const uint32_t stg = tiles + NS * C::STAGE + (uint32_t)quad * 2u * 4096u;
     const float* dbs = reinterpret_cast<const float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
                                                       NS * C::STAGE + kStageOut);
+    volatile uint32_t* ctl_last = &bars->cs_last;  // "this was the column's last tile"
     if (p.tma_out && lane == 0) {
       tma_prefetch_desc(&tmO);
-      if (p.epi == CT_EPILOGUE_GELU) tma_prefetch_desc(&tmO2);
+      if (C::EPI == CT_EPILOGUE_GELU) tma_prefetch_desc(&tmO2);
     }
     uint32_t ci = 0, n_split = 0, n_out = 0, n_db = 0;
     bool ok = true;
@@ -522,6 +516,28 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           }
           __syncwarp();
         }
+        // GELU-gradient epilogue: the pre-activation of column slice q + 1 is
+        // loaded as soon as slice q has used its own (the latency overlaps
+        // slice q's staging and store)
+        float hnext[32];
+        auto load_act = [&](int q) {
+          const int col0 = w.n0 + 32 * q;
+          const float* arow = p.act_in + row_off;
+          if (valid && col0 + 32 <= p.n && vec_ok) {
+            const float4* a4 = reinterpret_cast<const float4*>(arow + col0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 a = __ldg(a4 + i);
+              hnext[4 * i] = a.x; hnext[4 * i + 1] = a.y; hnext[4 * i + 2] = a.z; hnext[4 * i + 3] = a.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              hnext[i] = (valid && col0 + i < p.n) ? __ldg(arow + col0 + i) : 0.0f;
+          }
+        };
+        const bool gelu_grad = C::EPI == CT_EPILOGUE_GELU_GRAD && writes;
+        if (gelu_grad) load_act(0);
 #pragma unroll 1
         for (int q = 0; q < BN / 32; ++q) {
           float v[32];
@@ -537,46 +553,49 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             tmem_st32(lb + C::TC_SUM + 32 * q, v);
           } else if (!__all_sync(0xffffffffu, ok)) {
             // a wait of this unit failed: nothing is written
-          } else if (p.tma_out) {
-            if (rows_in && col0 < p.n) {
-              if (with_bias) add_bias32(v, p, col0);
-              if (p.epi == CT_EPILOGUE_GELU_GRAD && valid)
-                mul_gelu_grad32(v, p, p.act_in + row_off, col0, vec_ok);
-              // one 32 x 32 piece: stage it, then one TMA store (or add)
-              auto put = [&](const CUtensorMap* map, bool add) {
-                const uint32_t buf = stg + (n_out & 1u) * 4096u;
-                if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
-                __syncwarp();
+          } else {
+            const bool live = p.tma_out ? (rows_in && col0 < p.n) : valid;
+            if (live && with_bias) add_bias32(v, p, col0);
+            if (gelu_grad) {  // times gelu'(pre-activation), then fetch the next slice's
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                  sts128(buf + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4),
-                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                  if (!add) tma_store_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
-                  else tma_reduce_add_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
-                  bulk_commit_group();
+              for (int i = 0; i < 32; ++i) v[i] *= gelu_d(hnext[i]);
+              if (q + 1 < BN / 32) load_act(q + 1);
+            }
+            if (p.tma_out) {
+              if (live) {
+                // one 32 x 32 piece: stage it, then one TMA store (or add)
+                auto put = [&](const CUtensorMap* map, bool add) {
+                  const uint32_t buf = stg + (n_out & 1u) * 4096u;
+                  if (lane == 0) bulk_wait_group_read<1>();  // the store two pieces back has read buf
+                  __syncwarp();
+#pragma unroll
+                  for (int j = 0; j < 8; ++j)
+                    sts128(buf + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4),
+                           make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                  fence_proxy_async_smem();
+                  __syncwarp();
+                  if (lane == 0) {
+                    if (!add) tma_store_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
+                    else tma_reduce_add_3d(map, buf, col0, w.m0 + 32 * quad, w.b);
+                    bulk_commit_group();
+                  }
+                  ++n_out;
+                };
+                put(&tmO, add_mode);
+                if (C::EPI == CT_EPILOGUE_GELU) {  // then the activation of the same piece
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
+                  put(&tmO2, false);
                 }
-                ++n_out;
-              };
-              put(&tmO, add_mode);
-              if (p.epi == CT_EPILOGUE_GELU) {  // then the activation of the same piece
+              }
+            } else if (valid) {
+              store_row32(v, p, orow, col0, vec_ok, p.accumulate || w.slice > 0);
+              if (C::EPI == CT_EPILOGUE_GELU) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
-                put(&tmO2, false);
+                store_row32(v, p, p.out_act + row_off, col0,
+                            vec_ok && ((reinterpret_cast<uintptr_t>(p.out_act) & 15u) == 0), false);
               }
-            }
-          } else if (valid) {
-            if (w.slice == 0) add_bias32(v, p, col0);
-            if (p.epi == CT_EPILOGUE_GELU_GRAD)
-              mul_gelu_grad32(v, p, p.act_in + row_off, col0, vec_ok);
-            store_row32(v, p, orow, col0, vec_ok, p.accumulate || w.slice > 0);
-            if (p.epi == CT_EPILOGUE_GELU) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
-              store_row32(v, p, p.out_act + row_off, col0,
-                          vec_ok && ((reinterpret_cast<uintptr_t>(p.out_act) & 15u) == 0), false);
             }
           }
         }
@@ -585,18 +604,35 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         mbar_arrive(B(bars->acc_empty[acc]));
       }
       if (!__all_sync(0xffffffffu, ok)) break;
-      if (BN == 128 && p.colsum != nullptr && w.m0 == 0) {
-        // the unit's W column sums, added in slice order (the tile's counter
-        // is held by this slice here) or stored by slice 0
+      if (BN == 128 && p.colsum != nullptr) {
+        // the unit's partial W column sums into its tile row's slot (the
+        // slices of this tile add in slice order: this slice holds the tile's
+        // counter here); the tile column's last tile adds the slots up
         const uint32_t buf = n_db & 1u;
+        const int tn = w.n0 / BN, tm = w.m0 / kBM;
         if (!warp_wait(B(bars->db_ready[buf]), (n_db >> 1) & 1, ctl, p.status)) break;
         const int col = r, j = w.n0 + col;
-        if (col < BN && j < p.n) {
-          float val = dbs[buf * 128u + col];
-          if (p.accumulate || w.slice > 0) val += __ldcg(p.colsum + j);
-          p.colsum[j] = val;
-        }
+        const bool in = col < BN && j < p.n;
+        float* slot = p.cs_part + (int64_t)tm * p.n;
+        if (in) slot[j] = w.slice > 0 ? __ldcg(slot + j) + dbs[buf * 128u + col] : dbs[buf * 128u + col];
         mbar_arrive(B(bars->db_free[buf]));
+        if (w.slice == p.slices - 1) {  // this tile's column sums are complete
+          __threadfence();
+          mbar_arrive(B(bars->db_stored));
+          if (!mbar_wait(B(bars->db_stored), n_db & 1, ctl, p.status)) {
+            ok = false;
+          } else if (r == 0) {
+            *ctl_last = atomicAdd(p.cs_cnt + tn, 1u) == (uint32_t)(p.tiles_m - 1) ? 1u : 0u;
+          }
+          // every epilogue thread learns whether this was the column's last tile
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (ok && *ctl_last && in) {
+            __threadfence();
+            float sum = p.accumulate ? p.colsum[j] : 0.0f;
+            for (int t = 0; t < p.tiles_m; ++t) sum += __ldcg(p.cs_part + (int64_t)t * p.n + j);
+            p.colsum[j] = sum;
+          }
+        }
         ++n_db;
       }
       if (p.slices > 1) {  // publish this slice: counter = slice + 1
@@ -731,7 +767,14 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   p.tiles_n = (int)((g.n + C::BN - 1) / C::BN);
   p.kb_total = (int)((g.k + kBK - 1) / kBK);
   const int64_t tiles = tile_count(g, C::BN);
-  const bool have_ws = ws != nullptr && ws_bytes >= (size_t)tiles * 4u;
+  // counters: one per tile (split-K order), then one per tile column (column
+  // sums); then the column sums' [tiles_m][n] partial slots
+  const size_t sem_bytes = (size_t)(tiles + (g.n + C::BN - 1) / C::BN) * 4u;
+  const size_t cs_part_off = (sem_bytes + 255) / 256 * 256;
+  const size_t need = g.w_colsum ? cs_part_off + (size_t)((g.m + kBM - 1) / kBM) * g.n * 4u
+                                 : sem_bytes;
+  const bool have_ws = ws != nullptr && ws_bytes >= need;
+  if (g.w_colsum && !have_ws) return CT_ERR_WORKSPACE_TOO_SMALL;
   pick_split(g, C::BN, dev.sm_count, have_ws, chunk_kb(C::SPLIT), &p.slices, &p.kb_per_slice);
   if (!C::FOLD && p.kb_per_slice > chunk_kb(C::SPLIT) && (!tma_out || p.slices > 1))
     return CT_ERR_UNSUPPORTED_LAYOUT;  // the L2 fold needs TMA stores (caller falls back)
@@ -743,20 +786,21 @@ int run_linear(const GemmProblem& g, bool a_mn, bool b_mn, void* ws, size_t ws_b
   p.bias_s = g.bias_s;
   p.out = g.out;
   p.sem = static_cast<uint32_t*>(ws);
+  p.cs_cnt = p.sem + tiles;
+  p.cs_part = reinterpret_cast<float*>(static_cast<char*>(ws) + cs_part_off);
   p.status = dev.status;
   p.tma_out = tma_out ? 1 : 0;
-  p.epi = g.epilogue;
+  p.epi = C::EPI;
   p.out_act = g.out_act;
   p.act_in = g.act_in;
   p.colsum = g.w_colsum;
   p.accumulate = g.accumulate ? 1 : 0;
-  if ((p.epi != CT_EPILOGUE_NONE || p.colsum) && (!C::FOLD || C::BN != 128))
+  if ((g.epilogue != C::EPI) || ((C::EPI != CT_EPILOGUE_NONE || p.colsum) && (!C::FOLD || C::BN != 128)))
     return CT_ERR_UNSUPPORTED_LAYOUT;  // (pick_bn picks 128-wide tiles for these)
   int grid = p.units < dev.sm_count ? p.units : dev.sm_count;
-  if (p.slices > 1) {
-    grid = grid / p.slices * p.slices;  // whole tiles per round of the persistent loop
-    if (cudaMemsetAsync(ws, 0, (size_t)tiles * 4u, st) != cudaSuccess) return CT_ERR_CUDA;
-  }
+  if (p.slices > 1) grid = grid / p.slices * p.slices;  // whole tiles per round
+  if ((p.slices > 1 || p.colsum) && cudaMemsetAsync(ws, 0, sem_bytes, st) != cudaSuccess)
+    return CT_ERR_CUDA;
   linear_tc_kernel<C><<<grid, kThreadsG, smem, st>>>(ta, tb, to, to2, p);
   return check_launch();
 }
@@ -797,8 +841,10 @@ int pick_bn(const GemmProblem& g, int sms) {
 
 size_t linear_workspace_bytes(int64_t batch, int64_t m, int64_t n) {
   if (batch <= 0 || m <= 0 || n <= 0) return 0;
-  const int64_t tiles = batch * ((m + kBM - 1) / kBM) * ((n + 127) / 128);
-  return (size_t)((tiles * 4 + 255) / 256 * 256);
+  // counters (split-K, column sums), then (batch 1) the column sums' partial slots
+  const int64_t tiles = batch * ((m + kBM - 1) / kBM) * ((n + 127) / 128) + (n + 127) / 128;
+  const int64_t slots = batch == 1 ? ((m + kBM - 1) / kBM) * n : 0;
+  return (size_t)((tiles * 4 + 255) / 256 * 256 + slots * 4);
 }
 
 bool linear_tc_supported(const GemmProblem& g) {
@@ -828,6 +874,14 @@ int launch_linear_tc(const GemmProblem& g, void* ws, size_t ws_bytes, const Devi
   a_layout(g, &amn);
   b_layout(g, &bmn);
   const bool split = g.precision == CT_PRECISION_3XTF32;
+  if (g.epilogue == CT_EPILOGUE_GELU)
+    return split ? run_linear<GemmCfg<128, 3, 3, CT_EPILOGUE_GELU>>(g, amn, bmn, ws, ws_bytes, dev, st)
+                 : run_linear<GemmCfg<128, 1, 6, CT_EPILOGUE_GELU>>(g, amn, bmn, ws, ws_bytes, dev, st);
+  if (g.epilogue == CT_EPILOGUE_GELU_GRAD)
+    return split ? run_linear<GemmCfg<128, 3, 3, CT_EPILOGUE_GELU_GRAD>>(g, amn, bmn, ws, ws_bytes,
+                                                                          dev, st)
+                 : run_linear<GemmCfg<128, 1, 6, CT_EPILOGUE_GELU_GRAD>>(g, amn, bmn, ws, ws_bytes,
+                                                                          dev, st);
   if (pick_bn(g, dev.sm_count) == 256)
     return split ? run_linear<GemmCfg<256, 3, 2>>(g, amn, bmn, ws, ws_bytes, dev, st)
                  : run_linear<GemmCfg<256, 1, 4>>(g, amn, bmn, ws, ws_bytes, dev, st);

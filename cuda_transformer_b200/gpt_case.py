@@ -5,10 +5,12 @@ embedding, pre-LayerNorm decoder blocks (x + attn(ln1(x)), x + mlp(ln2(x))),
 causal FlashAttention-2 on the (B, nh, T, hs) views of the fused QKV
 projection, an exact-GELU 4x MLP, a final LayerNorm and the lm_head, with the
 cross-entropy loss.  Every linear layer, LayerNorm, GELU, attention and the
-loss run on this package's kernels (CudaLinearLayer, CudaLayerNorm,
-CudaFlashAttention; CudaMLP with the GELU in the GEMM epilogues;
-CudaLinearCrossEntropy for the lm_head and loss, chunked so the logits of
-every row are never held at once); the embeddings and AdamW are torch's.
+large-vocabulary loss run on this package's kernels (CudaLinearLayer,
+CudaLayerNorm, CudaFlashAttention, CudaMLP; the weight gradients form the bias
+gradients in the same GEMM; with a vocabulary of FUSED_CE_MIN_VOCAB or more,
+CudaLinearCrossEntropy runs the lm_head and the loss chunk by chunk so the
+logits of every row are never held at once); the embeddings, AdamW and the
+small-vocabulary loss are torch's.
 
 Default shape (the data-parallel benchmark configuration): 6 blocks,
 d_model 384, 6 heads of 64, context 256, vocabulary 65 with the lm_head tied to
@@ -39,8 +41,15 @@ import os
 import torch
 import torch.nn as nn
 
+import torch.nn.functional as F
+
 from cuda_autograd_fns import (CudaFlashAttention, CudaLayerNorm, CudaLinearCrossEntropy,
                                CudaLinearLayer, CudaMLP)
+
+# The fused lm_head + loss pays where the logits are large (gpt/gpt.py's
+# 100256-token vocabulary); for 65 characters torch's loss on the full logits
+# is cheaper than chunking.
+FUSED_CE_MIN_VOCAB = 4096
 
 
 class LayerNorm(nn.Module):
@@ -80,7 +89,7 @@ class MLP(nn.Module):
         self.fc2_weights = nn.Parameter(torch.empty(4 * d, d).normal_(0.0, 0.02))
         self.fc2_bias = nn.Parameter(torch.zeros(d))
 
-    def forward(self, x):  # fc1 -> GELU -> fc2, the activation in the GEMM epilogues
+    def forward(self, x):  # fc1 -> GELU -> fc2
         return CudaMLP.apply(x, self.fc1_weights, self.fc1_bias, self.fc2_weights, self.fc2_bias)
 
 
@@ -109,17 +118,21 @@ class GPT(nn.Module):
         self.lm_head_bias = nn.Parameter(torch.zeros(vocab))
 
     def forward(self, idx, targets=None):
-        """(logits, None) without targets; (None, mean cross-entropy loss) with
-        them -- the lm_head and the loss then run fused, chunk by chunk."""
+        """(logits, None) without targets; with them the mean cross-entropy
+        loss, as (None, loss) when the lm_head and the loss run fused (large
+        vocabularies), else (logits, loss)."""
         T = idx.shape[1]
         x = self.tok(idx) + self.pos(torch.arange(T, device=idx.device))
         for blk in self.blocks:
             x = blk(x)
         x = self.ln(x)
         w = self.tok.weight.t() if self.tied else self.lm_head_weights
-        if targets is not None:
+        if targets is not None and w.shape[1] >= FUSED_CE_MIN_VOCAB:
             return None, CudaLinearCrossEntropy.apply(x, w, self.lm_head_bias, targets)
-        return CudaLinearLayer.apply(x, w, self.lm_head_bias), None
+        logits = CudaLinearLayer.apply(x, w, self.lm_head_bias)
+        if targets is None:
+            return logits, None
+        return logits, F.cross_entropy(logits.reshape(-1, logits.shape[-1]), targets.reshape(-1))
 
 
 def n_params(model: nn.Module) -> int:

@@ -230,6 +230,9 @@ enum {
  *    Transformer_kernels/warp_sum_kernel.cuh:13-51);
  *  - `accumulate` != 0 adds into out (and w_colsum) instead of storing
  *    (CT_EPILOGUE_NONE only).
+ * On the tensor cores w_colsum needs workspace_bytes >= ct_linear_workspace_size
+ * (CT_ERR_WORKSPACE_TOO_SMALL otherwise): the units that share a tile column
+ * add their partial sums in a fixed order through counters kept there.
  * Deterministic: split-K slices and the column sums add in a fixed order.
  * Same reference counterpart as ct_linear_fwd (linear_layer.cu:28-70). */
 int ct_linear_fwd_ex(const float* x, const int64_t x_stride[3],
