@@ -274,7 +274,15 @@ class Fa2Runner:
         self.delta = torch.empty(1, pairs, n, device=dev)
         self.s4 = (ctypes.c_int64 * 4)(*self.q.stride())
         self.s3 = (ctypes.c_int64 * 3)(*self.lse.stride())
-        self.launches_per_step = 4
+        self.ws_bytes = self.lib.ct_fa2_bwd_workspace_size(1, pairs, n, D)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+
+    @property
+    def launches_per_step(self) -> int:
+        """This library's kernels per step: fwd, delta, then the dQ and dK/dV
+        kernels (one launch each per 4096-long segment of a longer sequence)."""
+        segs = (self.n + 4095) // 4096
+        return 2 + 2 * segs
 
     def _p(self, t):
         return ctypes.c_void_p(t.data_ptr())
@@ -308,13 +316,21 @@ class Fa2Runner:
                                                self.n, D, self.causal, self.prec, self._st()),
                       "dkdv")
 
+    def bwd(self):
+        """The whole backward through ct_fa2_bwd (delta, dQ, dK/dV)."""
+        p, s4 = self._p, self.s4
+        self.cb.check(self.lib.ct_fa2_bwd(p(self.q), s4, p(self.k), s4, p(self.v), s4, p(self.o),
+                                          s4, p(self.do), s4, p(self.lse), self.s3, p(self.dq),
+                                          p(self.dk), p(self.dv), p(self.ws), self.ws_bytes, 1,
+                                          self.P, self.n, D, self.causal, self.prec, self._st()),
+                      "bwd")
+
     def step(self):
         self.fwd()
-        self.delta_k()
-        self.dq_k()
-        self.dkdv_k()
+        self.bwd()
 
     def kernel_times_ms(self, reps: int = 3) -> dict:
+        """Per-kernel CUDA-event times through the per-kernel entry points."""
         torch = self.torch
         out = {}
         for name, fn in (("fa2_fwd", self.fwd), ("fa2_bwd_delta", self.delta_k),
@@ -498,6 +514,7 @@ def main() -> None:
     alt = cb.PRECISION_TF32 if prec == cb.PRECISION_3XTF32 else cb.PRECISION_3XTF32
 
     runner = Fa2Runner(pairs, dev, prec, seed=1000 + s0)
+    launches = runner.launches_per_step * args.steps
     with ClockSampler(local) as clk:
         ms = timed_steps(runner, args.steps, args.warmup, dist, world)
     clocks = clk.summary()
@@ -561,7 +578,7 @@ def main() -> None:
                        "l2": "inputs larger than L2 (Q, K, V, dO = 512 MiB per step at N=1)",
                        "parallelism": f"bh-shard{world}"},
             "kernel_ms": kern,
-            "gpu_launches": runner_launches(args.steps) * world,
+            "gpu_launches": launches * world,
             "roofline": roofline,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "steps": e2e_k,
@@ -580,12 +597,6 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def runner_launches(steps: int) -> int:
-    """This library's kernel launches per rank in the timed region: fwd,
-    delta, dq and dkdv per step."""
-    return 4 * steps
 
 
 if __name__ == "__main__":

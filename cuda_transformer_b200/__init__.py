@@ -57,6 +57,8 @@ SIGNATURES = {
     "ct_fa2_bwd_workspace_size": ([_i64, _i64, _i64, _i64], _sz),
     "ct_fa2_bwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp,
                     _fp, _fp, _fp, _sz, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
+    "ct_fa2_bwd_fused": ([_fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p,
+                          _fp, _fp, _fp, _fp, _sz, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
     "ct_fa2_bwd_noalloc": ([_fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp, _i64p, _fp,
                             _i64p, _fp, _fp, _fp, _i64, _i64, _i64, _i64, _int, _int, _fp], _int),
     "ct_linear_fwd": ([_fp, _i64p, _fp, _i64p, _fp, _i64, _fp, _i64, _i64, _i64, _i64, _i64, _int,

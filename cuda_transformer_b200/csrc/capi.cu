@@ -303,10 +303,19 @@ int ct_fa2_bwd_dkdv(const float* q, const int64_t q_stride[4], const float* k,
                            as_stream(stream));
 }
 
+namespace {
+// ct_fa2_bwd's workspace: delta (B*H*T floats), then at a 256-byte boundary
+// the one-kernel backward's ordering counters and tickets.
+size_t fa2_bwd_delta_bytes(int64_t B, int64_t H, int64_t T) {
+  return ((size_t)(B * H * T) * sizeof(float) + 255u) & ~(size_t)255u;
+}
+}  // namespace
+
 size_t ct_fa2_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim) {
   (void)head_dim;
-  if (batch < 0 || heads < 0 || seq_len < 0) return 0;
-  return (size_t)(batch * heads * seq_len) * sizeof(float);
+  if (!fa2_shape_ok(batch, heads, seq_len, 1)) return 0;
+  return fa2_bwd_delta_bytes(batch, heads, seq_len) +
+         fa2_bwd_fused_sync_words(batch, heads, seq_len) * sizeof(uint32_t);
 }
 
 int ct_fa2_bwd(const float* q, const int64_t q_stride[4], const float* k, const int64_t k_stride[4],
@@ -334,6 +343,39 @@ int ct_fa2_bwd(const float* q, const int64_t q_stride[4], const float* k, const 
   if (rc != CT_OK) return rc;
   return fa2_dkdv_dispatch(p, s4(q, q_stride), s4(k, k_stride), s4(v, v_stride),
                            s4(d_o, do_stride), lse, lse_stride, delta, dk, dv, *dev, st);
+}
+
+int ct_fa2_bwd_fused(const float* q, const int64_t q_stride[4], const float* k,
+                     const int64_t k_stride[4], const float* v, const int64_t v_stride[4],
+                     const float* o, const int64_t o_stride[4], const float* d_o,
+                     const int64_t do_stride[4], const float* lse, const int64_t lse_stride[3],
+                     float* dq, float* dk, float* dv, void* workspace, size_t workspace_bytes,
+                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, int causal,
+                     int precision, void* stream) {
+  const DeviceInfo* dev = nullptr;
+  int rc = fa2_validate(batch, heads, seq_len, head_dim, precision);
+  if (rc != CT_OK) return rc;
+  if (head_dim != 64) return CT_ERR_UNSUPPORTED_HEAD_DIM;
+  if (precision != CT_PRECISION_TF32) return CT_ERR_INVALID_ARGUMENT;
+  if (batch * heads * seq_len == 0) return CT_OK;
+  if (!q || !k || !v || !o || !d_o || !lse || !dq || !dk || !dv || !lse_stride ||
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    return CT_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < ct_fa2_bwd_workspace_size(batch, heads, seq_len, head_dim))
+    return CT_ERR_WORKSPACE_TOO_SMALL;
+  rc = fa2_prelude(batch, heads, seq_len, head_dim, precision, &dev);
+  if (rc != CT_OK) return rc;
+  Fa2Problem p{batch, heads, seq_len, head_dim, causal != 0, precision};
+  if (!fa2_bwd_fused_supported(p)) return CT_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = as_stream(stream);
+  float* delta = static_cast<float*>(workspace);
+  rc = launch_fa2_delta(p, s4(o, o_stride), s4(d_o, do_stride), delta, st);
+  if (rc != CT_OK) return rc;
+  uint32_t* sync_words = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) +
+                                                     fa2_bwd_delta_bytes(batch, heads, seq_len));
+  return launch_fa2_bwd_fused_tc(p, s4(q, q_stride), s4(k, k_stride), s4(v, v_stride),
+                                 s4(d_o, do_stride), lse, lse_stride, delta, dq, dk, dv,
+                                 sync_words, *dev, st);
 }
 
 size_t ct_linear_workspace_size(int64_t batch, int64_t m, int64_t k, int64_t n) {

@@ -87,9 +87,19 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v
 int launch_fa2_bwd_dkdv_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
                            const float* lse, const int64_t lse_s[3], const float* delta,
                            float* dk, float* dv, const DeviceInfo& dev, cudaStream_t st);
+// The one-kernel backward (TF32, head dim 64): dQ, dK and dV from one
+// key/value-stationary pass, dQ added in a fixed key-tile order.  sync_words:
+// fa2_bwd_fused_sync_words(B, H, T) 32-bit words of device scratch (ordering
+// counters and per-launch tickets), zeroed by the launcher on `st`.
+int launch_fa2_bwd_fused_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, Strided4 dO,
+                            const float* lse, const int64_t lse_s[3], const float* delta,
+                            float* dq, float* dk, float* dv, uint32_t* sync_words,
+                            const DeviceInfo& dev, cudaStream_t st);
+size_t fa2_bwd_fused_sync_words(int64_t B, int64_t H, int64_t T);
 // Whether the tensor-core kernels cover this problem (head dim / precision).
 bool fa2_fwd_tc_supported(const Fa2Problem& p);
 bool fa2_bwd_tc_supported(const Fa2Problem& p);
+bool fa2_bwd_fused_supported(const Fa2Problem& p);
 
 // CUDA-core FP32 kernels: any strides, head_dim in {32, 64, 128}.
 int launch_fa2_fwd_simt(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v, float* o,

@@ -296,15 +296,20 @@ __device__ __forceinline__ void mma_chain_mn2(uint32_t d, uint32_t a_hi, uint32_
 // not all stream the same tile at the same moment.  `heavy_first_desc` lists a
 // head's tiles from the last to the first (causal forward / dQ do the most
 // work on late query tiles; dK/dV on early key tiles keep ascending order).
-__device__ __forceinline__ void cta_tile(int n_tiles, int bh_total, int group,
-                                         bool heavy_first_desc, int& tile, int& bh) {
+// cta_tile_at takes the linear index explicitly (a ticket drawn at run time).
+__device__ __forceinline__ void cta_tile_at(unsigned idx, int n_tiles, int bh_total, int group,
+                                            bool heavy_first_desc, int& tile, int& bh) {
   const int per_group = group * n_tiles;
-  const int g = (int)(blockIdx.x / per_group);
-  const int r = (int)(blockIdx.x % per_group);
+  const int g = (int)(idx / per_group);
+  const int r = (int)(idx % per_group);
   const int gsize = min(group, bh_total - g * group);
   const int t = r / gsize;
   bh = g * group + r % gsize;
   tile = heavy_first_desc ? n_tiles - 1 - t : t;
+}
+__device__ __forceinline__ void cta_tile(int n_tiles, int bh_total, int group,
+                                         bool heavy_first_desc, int& tile, int& bh) {
+  cta_tile_at(blockIdx.x, n_tiles, bh_total, group, heavy_first_desc, tile, bh);
 }
 
 // Loads tile row block `r0` of head (h, b) into `dst`: one copy through a

@@ -85,6 +85,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (test_wait never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // try_wait with a suspend-time hint: a thread whose phase has not completed is
 // suspended by the hardware (woken when the phase completes or after at most
 // `hint_ns`) instead of spinning, so waiting warps leave their scheduler's
@@ -569,9 +582,11 @@ __device__ __forceinline__ void split_tile_smem_il(uint32_t base, uint32_t tid) 
 // SPLIT == 1 rounds both copies to the nearest TF32 (in place for the K-major
 // one); SPLIT == 3 keeps the raw values and writes the low parts x - trunc(x)
 // at +KLO (K-major) and +MLO (MN-major).  Each word moves within its row, so a
-// warp's stores stay free of bank conflicts.
+// warp's stores stay free of bank conflicts.  WRITE_K == false (SPLIT == 1):
+// the K-major copy is already rounded and is only read (the tensor core may be
+// reading it at the same time).
 template <int SPLIT, uint32_t BYTES, uint32_t NTHREADS, uint32_t BN, uint32_t KCH, uint32_t KLO,
-          uint32_t MLO>
+          uint32_t MLO, bool WRITE_K = true>
 __device__ __forceinline__ void derive_tile_smem(uint32_t k, uint32_t mn, uint32_t tid) {
   using P = TilePrep<BYTES, NTHREADS>;
   constexpr uint32_t CH = BN * 128u;
@@ -600,7 +615,7 @@ __device__ __forceinline__ void derive_tile_smem(uint32_t k, uint32_t mn, uint32
       } else {
         const float4 y = make_float4(tf32_round_finite(x[u].x), tf32_round_finite(x[u].y),
                                      tf32_round_finite(x[u].z), tf32_round_finite(x[u].w));
-        sts128(ka[u], y);
+        if constexpr (WRITE_K) sts128(ka[u], y);
         sts128(ma[u], y);
       }
     }

@@ -130,7 +130,9 @@ int ct_fa2_bwd_dkdv(const float* q, const int64_t q_stride[4],
                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
                     int causal, int precision, void* stream);
 
-/* Bytes of workspace ct_fa2_bwd needs (the delta vector). */
+/* Bytes of workspace ct_fa2_bwd and ct_fa2_bwd_fused need: the delta vector,
+ * then (from a 256-byte boundary) the one-kernel backward's ordering counters
+ * and launch tickets. */
 size_t ct_fa2_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq_len,
                                  int64_t head_dim);
 
@@ -148,6 +150,25 @@ int ct_fa2_bwd(const float* q, const int64_t q_stride[4],
                void* workspace, size_t workspace_bytes,
                int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
                int causal, int precision, void* stream);
+
+/* The same backward as ct_fa2_bwd in one key/value-stationary kernel after
+ * delta: P and dS are formed once per (key tile, query tile) and each CTA adds
+ * its dQ contribution into dQ in a fixed order of key tiles (per-tile counters
+ * in the workspace; bit-identical run to run).  TF32 precision and head dim 64
+ * only (CT_ERR_INVALID_ARGUMENT / CT_ERR_UNSUPPORTED_HEAD_DIM otherwise).  Not
+ * the default: on B200 it measures slower than ct_fa2_bwd's two kernels.  No
+ * reference counterpart (the reference's backward is two atomics-free kernels,
+ * Transformer_kernels/flash_attention.cuh:216-504). */
+int ct_fa2_bwd_fused(const float* q, const int64_t q_stride[4],
+                     const float* k, const int64_t k_stride[4],
+                     const float* v, const int64_t v_stride[4],
+                     const float* o, const int64_t o_stride[4],
+                     const float* d_o, const int64_t do_stride[4],
+                     const float* lse, const int64_t lse_stride[3],
+                     float* dq, float* dk, float* dv,
+                     void* workspace, size_t workspace_bytes,
+                     int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim,
+                     int causal, int precision, void* stream);
 
 /* Largest batch * heads * seq_len ct_fa2_bwd_noalloc accepts. */
 #define CT_FA2_BWD_NOALLOC_MAX_ROWS 2097152

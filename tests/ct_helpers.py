@@ -43,6 +43,38 @@ def fa2_bwd(q, k, v, o, do, lse, causal, precision=cb.PRECISION_3XTF32):
     return dq, dk, dv
 
 
+def fa2_bwd_fused(q, k, v, o, do, lse, causal, precision=cb.PRECISION_TF32):
+    """ct_fa2_bwd_fused: the one-kernel backward (TF32, head dim 64)."""
+    B, H, T, D = q.shape
+    dq, dk, dv = (torch.empty(B, H, T, D, device=q.device, dtype=torch.float32) for _ in range(3))
+    ws_bytes = cb.lib().ct_fa2_bwd_workspace_size(B, H, T, D)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+    rc = cb.lib().ct_fa2_bwd_fused(_p(q), cb.strides(q), _p(k), cb.strides(k), _p(v),
+                                   cb.strides(v), _p(o), cb.strides(o), _p(do), cb.strides(do),
+                                   _p(lse), cb.strides(lse), _p(dq), _p(dk), _p(dv), _p(ws),
+                                   ws_bytes, B, H, T, D, int(causal), precision, _stream())
+    cb.check(rc, "ct_fa2_bwd_fused")
+    return dq, dk, dv
+
+
+def fa2_bwd_split(q, k, v, o, do, lse, causal, precision=cb.PRECISION_3XTF32):
+    """The backward through its per-kernel entry points (delta, then the
+    query-stationary dQ kernel and the key/value-stationary dK/dV kernel),
+    never the one-kernel path ct_fa2_bwd may take."""
+    B, H, T, D = q.shape
+    dq, dk, dv = (torch.empty(B, H, T, D, device=q.device, dtype=torch.float32) for _ in range(3))
+    delta = fa2_delta(o, do)
+    cb.check(cb.lib().ct_fa2_bwd_dq(_p(q), cb.strides(q), _p(k), cb.strides(k), _p(v),
+                                    cb.strides(v), _p(do), cb.strides(do), _p(lse),
+                                    cb.strides(lse), _p(delta), _p(dq), B, H, T, D, int(causal),
+                                    precision, _stream()), "ct_fa2_bwd_dq")
+    cb.check(cb.lib().ct_fa2_bwd_dkdv(_p(q), cb.strides(q), _p(k), cb.strides(k), _p(v),
+                                      cb.strides(v), _p(do), cb.strides(do), _p(lse),
+                                      cb.strides(lse), _p(delta), _p(dk), _p(dv), B, H, T, D,
+                                      int(causal), precision, _stream()), "ct_fa2_bwd_dkdv")
+    return dq, dk, dv
+
+
 def fa2_delta(o, do):
     B, H, T, D = o.shape
     delta = torch.empty(B, H, T, device=o.device, dtype=torch.float32)

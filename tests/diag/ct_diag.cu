@@ -158,7 +158,8 @@ __device__ __forceinline__ void tmem_ld_16x32bx2_x16(uint32_t taddr, float (&v)[
 // TMEM (columns 128..159), else shared memory K-major; bit 1: L = 16 (the
 // upper half of each warp's lane quadrant), else 0; bit 2: D read with the
 // 16-lane 16x32bx2 shape (n = 32: threads 0-15 columns 0-15, threads 16-31
-// columns 16-31 of the same rows), else with 32x32b.
+// columns 16-31 of the same rows), else with 32x32b; bit 3: A and B both from
+// shared memory MN-major (a is [32 (k)][64 (m)], b is [32 (k)][n]).
 __global__ void __launch_bounds__(128, 1)
     umma_m64_kernel(int mode, const float* __restrict__ a, const float* __restrict__ b,
                     float* __restrict__ d, int n, uint32_t* status) {
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* gen = smem_raw + (base - smem_u32(smem_raw));
   const uint32_t sa = base, sb = base + 64u * 128u;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const bool a_tmem = (mode & 1) != 0, x2 = (mode & 4) != 0;
+  const bool a_tmem = (mode & 1) != 0, x2 = (mode & 4) != 0, mn = (mode & 8) != 0;
   const uint32_t L = (mode & 2) ? 16u : 0u;
   if (tid == 0) {
     mbar_init(smem_u32(&hs->bar), 1);
@@ -180,9 +181,11 @@ __global__ void __launch_bounds__(128, 1)
     tmem_relinquish();
   }
   for (int e = tid; e < 64 * 32; e += 128)
-    *reinterpret_cast<float*>(gen + sw128_offset(e / 32, e % 32, 64)) = a[e];
+    *reinterpret_cast<float*>(gen + (mn ? sw128_32b_offset(e / 64, e % 64, 32)
+                                        : sw128_offset(e / 32, e % 32, 64))) = a[e];
   for (int e = tid; e < n * 32; e += 128)
-    *reinterpret_cast<float*>(gen + (sb - sa) + sw128_offset(e / 32, e % 32, n)) = b[e];
+    *reinterpret_cast<float*>(gen + (sb - sa) + (mn ? sw128_32b_offset(e / n, e % n, 32)
+                                                    : sw128_offset(e / 32, e % 32, n))) = b[e];
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -201,11 +204,12 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   if (tid == 0) {
     tc_fence_after();
-    const uint32_t idesc = idesc_tf32(64, n, false, false);
+    const uint32_t idesc = idesc_tf32(64, n, mn, mn);
     const uint32_t dt = tmem + (L << 16);
     for (int k = 0; k < 4; ++k) {
-      const uint64_t bd = sdesc_kmajor(sb + k * 32u);
+      const uint64_t bd = mn ? sdesc_mnmajor(sb + k * 1024u, 32u * 128u) : sdesc_kmajor(sb + k * 32u);
       if (a_tmem) umma_tf32_ts(dt, tmem + (L << 16) + 128u + 8u * k, bd, idesc, k > 0);
+      else if (mn) umma_tf32_ss(dt, sdesc_mnmajor(sa + k * 1024u, 32u * 128u), bd, idesc, k > 0);
       else umma_tf32_ss(dt, sdesc_kmajor(sa + k * 32u), bd, idesc, k > 0);
     }
     umma_commit(smem_u32(&hs->bar));
@@ -373,7 +377,8 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
 }
 
 int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, void* stream) {
-  if (!a || !b || !d || mode < 0 || mode > 7 || !(n == 32 || n == 64) || ((mode & 4) && n != 32))
+  if (!a || !b || !d || mode < 0 || mode > 15 || !(n == 32 || n == 64) || ((mode & 4) && n != 32) ||
+      ((mode & 8) && (mode & 1)))
     return 1;
   uint32_t* status = ct::diag_status();
   if (!status) return 6;

@@ -24,7 +24,9 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
  * checking the M = 64 data-path layout of Tensor Memory (row r of D in lane
  * 32 * (r / 16) + r % 16 + L).  mode bit 0: A from TMEM (else shared memory);
  * bit 1: L = 16 (else 0); bit 2: D read with the 16-lane 16x32bx2 shape
- * (n = 32 only).  a is [64,32] row-major, b [n,32], d [64,n]; n in {32, 64}. */
+ * (n = 32 only); bit 3: A and B from shared memory MN-major (not with bit 0;
+ * a is then [32,64] = A^T and b [32,n] = B^T).  a is [64,32] row-major, b
+ * [n,32], d [64,n]; n in {32, 64}. */
 int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, void* stream);
 
 /* Tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in {32, 64, 128, 256}.

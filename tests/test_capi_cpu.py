@@ -73,7 +73,11 @@ def test_status_strings_and_version():
 
 def test_workspace_queries():
     lib = cb.lib()
-    assert lib.ct_fa2_bwd_workspace_size(4, 32, 4096, 64) == 4 * 32 * 4096 * 4
+    # delta, then the one-kernel backward's ordering counters (4 per 64-query
+    # tile) and one ticket per 4096-long segment
+    assert lib.ct_fa2_bwd_workspace_size(4, 32, 4096, 64) == 4 * 32 * 4096 * 4 + (128 * 64 * 4 + 1) * 4
+    assert lib.ct_fa2_bwd_workspace_size(1, 1, 8193, 64) == 33024 + (129 * 4 + 3) * 4
+    assert lib.ct_fa2_bwd_workspace_size(-1, 1, 1, 64) == 0
     assert lib.ct_bias_grad_workspace_size(1, 16384, 1536) >= 1536 * 4
     assert lib.ct_layernorm_bwd_workspace_size(16384, 384) >= 2 * 384 * 4
 
@@ -107,6 +111,14 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.ct_linear_fwd_ex(p, s3, p, s3, p, 1, p, 1, 4, 4, 4, 1, 0, 3, None, None, None, 0,
                                 None, 0, None) == cb.CT_ERR_INVALID_ARGUMENT
     assert lib.ct_cross_entropy_fwd_bwd(p, 4, 2, 8, p, -100, p, None) == cb.CT_ERR_INVALID_ARGUMENT
+    # the one-kernel backward covers TF32 at head dim 64 only
+    s3b = (ctypes.c_int64 * 3)(1, 1, 1)
+    for D, prec, want in ((32, cb.PRECISION_TF32, cb.CT_ERR_UNSUPPORTED_HEAD_DIM),
+                          (64, cb.PRECISION_3XTF32, cb.CT_ERR_INVALID_ARGUMENT),
+                          (64, cb.PRECISION_FP32, cb.CT_ERR_INVALID_ARGUMENT)):
+        rc = lib.ct_fa2_bwd_fused(p, s, p, s, p, s, p, s, p, s, p, s3b, p, p, p, p, 1 << 20,
+                                  1, 1, 64, D, 1, prec, None)
+        assert rc == want, (D, prec, rc)
     # LayerNorm rows are at most 8192 wide
     rc = lib.ct_layernorm_fwd(None, None, None, None, None, None, 1, 8193, ctypes.c_float(1e-5), None)
     assert rc == cb.CT_ERR_INVALID_ARGUMENT

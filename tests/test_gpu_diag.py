@@ -87,12 +87,13 @@ def test_mma_rate_probe_runs(cuda_device):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", range(8))
+@pytest.mark.parametrize("mode", [m for m in range(16) if not (m & 8 and m & 1)])
 @pytest.mark.parametrize("n", [32, 64])
 def test_umma_m64_layouts(cuda_device, mode, n):
     """M = 64 MMAs: rows in lanes 32*(r//16) + r%16 (+16 for the upper half of
-    each lane quadrant), A from shared memory or TMEM, D read with the 32x32b
-    or the 16-lane 16x32bx2 shape."""
+    each lane quadrant), A from shared memory (K-major, or MN-major together
+    with an MN-major B: the fused backward's dQ product) or TMEM, D read with
+    the 32x32b or the 16-lane 16x32bx2 shape."""
     from tests import diag
 
     if (mode & 4) and n != 32:
@@ -101,7 +102,8 @@ def test_umma_m64_layouts(cuda_device, mode, n):
     a = _tf32_exact((64, 32), g, cuda_device)
     b = _tf32_exact((n, 32), g, cuda_device)
     d = torch.full((64, n), float("nan"), device=cuda_device)
-    diag.check(diag.lib().ct_diag_umma_m64(mode, H._p(a), H._p(b), H._p(d), n, H._stream()),
+    aa, bb = (a.t().contiguous(), b.t().contiguous()) if mode & 8 else (a, b)
+    diag.check(diag.lib().ct_diag_umma_m64(mode, H._p(aa), H._p(bb), H._p(d), n, H._stream()),
                "ct_diag_umma_m64")
     torch.cuda.synchronize()
     assert diag.status() == 0

@@ -133,7 +133,8 @@ def test_no_out_of_bounds_writes(cuda_device, prec, D):
     cb.check(rc)
     grads = [guarded(numel) for _ in range(3)]
     dq, dk, dv = (g[1].view(B, Hh, T, D) for g in grads)
-    ws = torch.empty(B * Hh * T * 4, dtype=torch.uint8, device=cuda_device)
+    ws = torch.empty(cb.lib().ct_fa2_bwd_workspace_size(B, Hh, T, D), dtype=torch.uint8,
+                     device=cuda_device)
     rc = cb.lib().ct_fa2_bwd(H._p(q), cb.strides(q), H._p(k), cb.strides(k), H._p(v),
                              cb.strides(v), H._p(o), cb.strides(o), H._p(do), cb.strides(do),
                              H._p(lse), cb.strides(lse), H._p(dq), H._p(dk), H._p(dv), H._p(ws),
@@ -159,6 +160,37 @@ def test_deterministic(cuda_device, prec, D):
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
     for a, b in zip(g1, g2):
         assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,Hh,T,causal", [(2, 4, 256, True), (1, 3, 200, False),
+                                           (4, 8, 1024, True), (2, 16, 1024, False),
+                                           (1, 3, 4096, True), (1, 2, 1000, False)])
+def test_fused_backward(cuda_device, B, Hh, T, causal):
+    """ct_fa2_bwd_fused (TF32, head dim 64): the one-kernel backward, dQ added
+    across key tiles in a fixed order with CTAs waiting on one another's
+    counters.  Against the per-kernel path (dK and dV from the same MMA
+    sequence; dQ summed in another order), bit-identical over three calls
+    (the ordered reduction), and against the FP64 oracle.  The 256-CTA cases
+    exceed one wave of 148 SMs, so contributions cross waves."""
+    prec = cb.PRECISION_TF32
+    q, k, v, do = (_rand((B, Hh, T, 64), 70 + s, cuda_device) for s in range(4))
+    o, lse = H.fa2_fwd(q, k, v, causal, prec)
+    runs = [H.fa2_bwd_fused(q, k, v, o, do, lse, causal, prec) for _ in range(3)]
+    split = H.fa2_bwd_split(q, k, v, o, do, lse, causal, prec)
+    torch.cuda.synchronize()
+    for r in runs[1:]:
+        for a, b in zip(runs[0], r):
+            assert torch.equal(a, b)
+    dq, dk, dv = runs[0]
+    assert H.rel_err(dk, split[1]) < 1e-6 and H.rel_err(dv, split[2]) < 1e-6
+    assert H.rel_err(dq, split[0]) < TOL[prec]
+    qn, kn, vn, don = (t.detach().cpu().double().numpy() for t in (q, k, v, do))
+    o_ref, l_ref = orc.attention_fwd(qn, kn, vn, causal)
+    refs = orc.attention_bwd(qn, kn, vn, o_ref, don, l_ref, causal)
+    for name, got, ref in zip(("dQ", "dK", "dV"), (dq, dk, dv), refs):
+        assert H.rel_err(got, ref) < TOL[prec], (name, H.rel_err(got, ref))
+    H.assert_device_clean()
 
 
 @pytest.mark.gpu

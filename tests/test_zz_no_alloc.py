@@ -6,8 +6,11 @@ caller workspace.
 
 The GPU tests call it through the C ABI on two problems in a row (so a stale
 array left by the first call would show up in the second) and check it
-  * bit for bit against ct_fa2_bwd, which runs the same deterministic kernels
-    with a caller workspace, and
+  * bit for bit against the per-kernel entry points (ct_fa2_bwd_delta,
+    ct_fa2_bwd_dq, ct_fa2_bwd_dkdv), which run the same deterministic
+    kernels with caller-owned delta,
+  * bit for bit against ct_fa2_bwd, which runs the same kernels with a
+    caller workspace, and
   * against the FP64 oracle within the precision mode's tolerance,
 for every backward path it can reach: the tensor-core kernels (3xTF32 and
 TF32, head dim 64 and 128, including the two-pass head-dim-128 dK/dV) and
@@ -53,11 +56,13 @@ def test_noalloc_matches_workspace_entry_point_and_oracle(cuda_device, prec, D):
         g = torch.Generator().manual_seed(500 + i)
         q, k, v, do = (torch.randn(B, Hh, T, D, generator=g).to(cuda_device) for _ in range(4))
         o, lse = H.fa2_fwd(q, k, v, causal, prec)
-        ref = H.fa2_bwd(q, k, v, o, do, lse, causal, prec)
+        ref = H.fa2_bwd_split(q, k, v, o, do, lse, causal, prec)
+        ws_ref = H.fa2_bwd(q, k, v, o, do, lse, causal, prec)
         got = _noalloc(q, k, v, o, do, lse, causal, prec)
         torch.cuda.synchronize()
-        for name, a, b in zip(("dQ", "dK", "dV"), got, ref):
+        for name, a, b, c in zip(("dQ", "dK", "dV"), got, ref, ws_ref):
             assert torch.equal(a, b), (i, name, H.rel_err(a, b))
+            assert torch.equal(a, c), (i, name, H.rel_err(a, c))
         qn, kn, vn, dn = (t.cpu().double().numpy() for t in (q, k, v, do))
         o_ref, l_ref = orc.attention_fwd(qn, kn, vn, causal)
         grads = orc.attention_bwd(qn, kn, vn, o_ref, dn, l_ref, causal)
