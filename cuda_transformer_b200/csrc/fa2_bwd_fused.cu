@@ -59,7 +59,8 @@ constexpr int kFusedBN = 64;                 // queries per step (the dQ MMA's M
 // 640 threads launch with 96 registers each; the row groups take 104 and the
 // other three give up theirs down to 88 (setmaxnreg: 3 x 88 + 2 x 104 <=
 // 5 x 96; the launch count is checked against the compiled kernel before the
-// first launch).  ptxas fits every role in its share without spills.
+// first launch).  ptxas fits every role in its share, but for a few words of
+// the epilogue's two-step register queue that spill to local memory.
 constexpr int kFusedThreads = 640;
 constexpr int kFusedLaunchRegs = 96, kFusedLowRegs = 88, kFusedRowRegs = 104;
 static_assert(3 * kFusedLowRegs + 2 * kFusedRowRegs <= 5 * kFusedLaunchRegs, "register split");
@@ -107,7 +108,7 @@ struct FusedCfg {
 
 template <int NS1, int NS2>
 struct FusedBars {
-  uint64_t full1[NS1], rdy1[NS1], empty1[NS1];  // ring 1: landed, rounded, read (S^T, dP^T, copies)
+  uint64_t full1[NS1], rdy1[NS1], empty1[NS1];  // ring 1: landed, prepared, read (S^T, dP^T)
   uint64_t rdy2[NS2], empty2[NS2];              // ring 2 (+ LSE / delta): written, read (dV, dK)
   uint64_t s_full[2], p_full[2], dp_full, ds_full, dqd;
   uint64_t kmn_full, kmn_ready, dq_full[2], dq_free[2];

@@ -165,14 +165,17 @@ def test_deterministic(cuda_device, prec, D):
 @pytest.mark.gpu
 @pytest.mark.parametrize("B,Hh,T,causal", [(2, 4, 256, True), (1, 3, 200, False),
                                            (4, 8, 1024, True), (2, 16, 1024, False),
-                                           (1, 3, 4096, True), (1, 2, 1000, False)])
+                                           (1, 3, 4096, True), (1, 2, 1000, False),
+                                           (1, 2, 17, True), (1, 1, 1, False),
+                                           (1, 1, 4160, True), (1, 1, 4296, False)])
 def test_fused_backward(cuda_device, B, Hh, T, causal):
     """ct_fa2_bwd_fused (TF32, head dim 64): the one-kernel backward, dQ added
     across key tiles in a fixed order with CTAs waiting on one another's
     counters.  Against the per-kernel path (dK and dV from the same MMA
     sequence; dQ summed in another order), bit-identical over three calls
     (the ordered reduction), and against the FP64 oracle.  The 256-CTA cases
-    exceed one wave of 148 SMs, so contributions cross waves."""
+    exceed one wave of 148 SMs, so contributions cross waves; T > 4096 runs
+    two query segments (dK, dV added across launches, dQ complete in each)."""
     prec = cb.PRECISION_TF32
     q, k, v, do = (_rand((B, Hh, T, 64), 70 + s, cuda_device) for s in range(4))
     o, lse = H.fa2_fwd(q, k, v, causal, prec)
