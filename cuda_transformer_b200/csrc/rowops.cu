@@ -701,6 +701,38 @@ __global__ void __launch_bounds__(256)
   if (row < rows && sub == 0) delta[row] = acc;
 }
 
+// The same sums for dense [B,H,T,D] O and dO (unit head-dim stride, rows D
+// apart): the flat row index addresses both tensors, so no index division, and
+// every lane has four float4 of each tensor in flight.  Lane l's u-th load is
+// float4 u*32 + l of its warp's block of 128/(D/4) rows; each row is still
+// summed as four products per lane and a butterfly over the row's D/4 lanes,
+// the order fa2_delta_kernel uses (identical results).
+template <int D>
+__global__ void __launch_bounds__(256)
+    fa2_delta_dense_kernel(const float4* __restrict__ o, const float4* __restrict__ g,
+                           float* __restrict__ delta, int64_t rows) {
+  constexpr int F = D / 4;        // float4 per row
+  constexpr int RW = 128 / F;     // rows per warp
+  const int lane = threadIdx.x & 31;
+  const int64_t r0 = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * RW;
+  const int64_t n4 = rows * F;
+  float4 x[4], y[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t i = r0 * F + u * 32 + lane;
+    x[u] = i < n4 ? __ldg(o + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    y[u] = i < n4 ? __ldg(g + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    float acc = x[u].x * y[u].x + x[u].y * y[u].y + x[u].z * y[u].z + x[u].w * y[u].w;
+#pragma unroll
+    for (int off = F / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off, F);
+    const int64_t row = r0 + (u * 32 + lane) / F;
+    if ((lane % F) == 0 && row < rows) delta[row] = acc;
+  }
+}
+
 template <int THREADS, int V>
 int softmax_dispatch_fwd(const float* x, float* y, int64_t rows, int64_t n, bool vec,
                          cudaStream_t st) {
@@ -928,6 +960,23 @@ int launch_fa2_delta(const Fa2Problem& p, Strided4 o, Strided4 dO, float* delta,
   const bool vec = o.s[3] == 1 && dO.s[3] == 1 && aligned16(o.ptr) && aligned16(dO.ptr) &&
                    o.s[0] % 4 == 0 && o.s[1] % 4 == 0 && o.s[2] % 4 == 0 && dO.s[0] % 4 == 0 &&
                    dO.s[1] % 4 == 0 && dO.s[2] % 4 == 0;
+  const auto dense = [&](const Strided4& t) {
+    return t.s[3] == 1 && t.s[2] == p.D && t.s[1] == p.T * p.D && t.s[0] == p.H * p.T * p.D &&
+           aligned16(t.ptr);
+  };
+  if (dense(o) && dense(dO)) {
+    const int64_t rows_per_cta = 8 * (128 / (p.D / 4));
+    const unsigned g = (unsigned)((rows + rows_per_cta - 1) / rows_per_cta);
+    const float4* o4 = reinterpret_cast<const float4*>(o.ptr);
+    const float4* g4 = reinterpret_cast<const float4*>(dO.ptr);
+    switch (p.D) {
+      case 32: fa2_delta_dense_kernel<32><<<g, 256, 0, st>>>(o4, g4, delta, rows); break;
+      case 64: fa2_delta_dense_kernel<64><<<g, 256, 0, st>>>(o4, g4, delta, rows); break;
+      case 128: fa2_delta_dense_kernel<128><<<g, 256, 0, st>>>(o4, g4, delta, rows); break;
+      default: return CT_ERR_UNSUPPORTED_HEAD_DIM;
+    }
+    return check_launch();
+  }
   const int64_t threads = rows * (p.D / 4);
   const unsigned grid = (unsigned)((threads + 255) / 256);
 #define CT_DELTA(DD)                                                                          \
