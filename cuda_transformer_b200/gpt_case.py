@@ -15,7 +15,8 @@ small-vocabulary loss are torch's.
 Default shape (the data-parallel benchmark configuration): 6 blocks,
 d_model 384, 6 heads of 64, context 256, vocabulary 65 with the lm_head tied to
 the token embedding, 64 sequences per GPU, AdamW lr 3e-4, weights
-N(0, 0.02).  Tokens are uniform in [0, vocab), seeded per rank, staged in
+N(0, 0.02).  gpt/gpt.py's own shape: --layers 1 --d 512 --heads 4 --vocab 100256
+--untied.  Tokens are uniform in [0, vocab), seeded per rank, staged in
 pinned host memory and copied to the GPU inside every timed step (as the
 reference's Generate_Batch does, gpt/gpt.py:39-45).
 
@@ -197,6 +198,8 @@ def main() -> None:
     ap.add_argument("--lr", type=float, default=3e-4)
     ap.add_argument("--gpus", type=int, default=None,
                     help="expected number of ranks (launch N > 1 with torchrun)")
+    ap.add_argument("--untied", action="store_true",
+                    help="separate lm_head weights and bias, as gpt/gpt.py has them")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -214,7 +217,7 @@ def main() -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     torch.manual_seed(1234)  # identical initial weights on every rank
-    model = GPT(a.layers, a.d, a.heads, a.ctx, a.vocab).to(dev)
+    model = GPT(a.layers, a.d, a.heads, a.ctx, a.vocab, tied=not a.untied).to(dev)
     params = n_params(model)
     net = model
     if world > 1:
@@ -281,7 +284,7 @@ def main() -> None:
             "loss_uniform": math.log(a.vocab), "communication": comm,
             "config": {"layers": a.layers, "d_model": a.d, "heads": a.heads, "ctx": a.ctx,
                        "vocab": a.vocab, "batch_per_gpu": a.batch, "global_batch": a.batch * world,
-                       "tied": True, "optimizer": "AdamW(fused) lr %g" % a.lr,
+                       "tied": not a.untied, "optimizer": "AdamW(fused) lr %g" % a.lr,
                        "grad_sync": "DDP bucketed NCCL all-reduce" if world > 1 else "none"},
             "data": "synthetic uniform tokens, pinned host -> device each step"}), flush=True)
     if world > 1:
