@@ -140,8 +140,16 @@ def n_params(model: nn.Module) -> int:
     return sum(p.numel() for p in model.parameters())
 
 
+def matmul_params(model: "GPT") -> int:
+    """Parameters that enter a matrix product: all but the position table and,
+    when the lm_head has its own weights, the token table (a lookup)."""
+    skip = model.pos.weight.numel() + (0 if model.tied else model.tok.weight.numel())
+    return n_params(model) - skip
+
+
 def step_flops(params: int, layers: int, d: int, ctx: int, tokens: int) -> float:
-    """Training FLOPs of one step: 6 * params * tokens for the dense layers,
+    """Training FLOPs of one step: 6 * params * tokens for the dense layers
+    (params: matmul_params),
     plus causal attention (2 * 2 * T * d per token per layer forward, half of
     it masked, x3 for forward + backward)."""
     return 6.0 * params * tokens + 3.0 * 2.0 * layers * ctx * d * tokens
@@ -275,7 +283,7 @@ def main() -> None:
                 "allreduce_busbw_gbs": 2.0 * (world - 1) / world * params * 4 / (ar_ms * 1e-3) / 1e9}
     tokens = tokens_per_step(world, a.batch, a.ctx)
     if rank == 0:
-        flops = step_flops(params, a.layers, a.d, a.ctx, tokens)
+        flops = step_flops(matmul_params(model), a.layers, a.d, a.ctx, tokens)
         print(json.dumps({
             "metric": "GPT DP training tokens/s", "value": tokens * a.steps / (ms * 1e-3),
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms / a.steps, "steps": a.steps,
