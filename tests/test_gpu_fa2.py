@@ -208,11 +208,20 @@ def test_config2_length_subset(cuda_device, prec):
 
 
 @pytest.mark.gpu
-def test_delta_kernel(cuda_device):
-    o, do = (_rand((2, 3, 77, 64), 60 + s, cuda_device) for s in range(2))
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_delta_kernel(cuda_device, D):
+    """Dense O, dO (the flat-index kernel), rows of a (B, T, H, D) layout
+    (unit head-dim stride, the strided 128-bit kernel; bit for bit the same
+    sums, the per-row order being the same) and a non-unit head-dim stride
+    (scalar loads)."""
+    o, do = (_rand((2, 3, 77, D), 60 + s, cuda_device) for s in range(2))
     d = H.fa2_delta(o, do)
     ref = orc.attention_bwd_delta(o.cpu().numpy(), do.cpu().numpy())
     assert H.rel_err(d, ref) < 1e-6
+    # rows of a (B, T, H, D) tensor: head-dim stride 1, the others not dense
+    ob = o.transpose(1, 2).contiguous().transpose(1, 2)
+    assert ob.stride(3) == 1 and not ob.is_contiguous()
+    assert torch.equal(H.fa2_delta(ob, do), d)
     # strided inputs (non-unit head-dim stride)
     ot = o.transpose(2, 3).contiguous().transpose(2, 3)
     d2 = H.fa2_delta(ot, do)
