@@ -441,6 +441,322 @@ int run_fwd(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, 
   return check_launch();
 }
 
+// ------------------------------------------- TF32: two query tiles per CTA
+// The TF32 forward at head dims 32 and 64 keeps two 128-row query tiles (A,
+// B) per CTA instead of splitting one tile's score columns between the two
+// row warpgroups.  Each warpgroup owns a whole tile: it takes every column of
+// its S, so no row maximum is exchanged between warps, and the K / V tiles a
+// stage lands serve 256 query rows.  Each tile has its own issuing thread
+// (warp 1: tile A, warp 10: tile B) and two S / P buffers:
+//   S_t(j+1) = Q_t K_{j+1}^T runs while the rows turn S_t(j) into P_t(j);
+//   O_t += P_t(j) V_j, then S_t(j+2) into P_t(j)'s buffer (same thread, in
+//   order), so while one group forms P the tensor core works for the other.
+// TMEM: Q_A | Q_B | O_A | O_B | S_A x 2 | S_B x 2.  The rows rescale O_t (when
+// the maximum grows by more than 2^8) once O_t += P_t(j-1) V_{j-1} is done
+// (pv_done).
+template <int D_, int BN_, int NS_>
+struct FwdPairCfg {
+  static constexpr int D = D_, BN = BN_, NS = NS_;
+  static constexpr uint32_t TILE = (uint32_t)BN * D_ * 4u;
+  static constexpr uint32_t STAGE = 2u * TILE, OFF_K = 0, OFF_V = TILE;
+  // Q_t at t * D, O_t at 2D + t * D, S buffer bb of tile t at 4D + (2t + bb) * BN
+  static constexpr uint32_t TC_Q = 0, TC_O = 2u * D_, TC_S = 4u * D_;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(TC_S + 4u * BN <= TMEM_COLS, "TMEM budget");
+  static_assert(BN == 64, "the row warps keep a step's 64 scores in registers");
+};
+
+template <int NS>
+struct FwdPairBars {
+  uint64_t full_k[NS], full_v[NS], ready_k[NS], ready_v[NS], empty_k[NS], empty_v[NS];
+  uint64_t s_full[2][2], p_full[2][2], pv_done[2], o_done[2], q_ready, mma_final[2];
+  CtaCtl ctl;
+};
+
+template <class C>
+constexpr size_t fwd_pair_smem_bytes() {
+  constexpr size_t head = (sizeof(FwdPairBars<C::NS>) + 1023) / 1024 * 1024 + 1024;
+  static_assert(head + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
+  return head + (size_t)C::NS * C::STAGE;
+}
+
+template <class C>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    fa2_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  constexpr int D = C::D, BN = C::BN, NS = C::NS;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (status_raised(p.status)) return;
+  auto* bars = reinterpret_cast<FwdPairBars<NS>*>(smem_raw);
+  const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(FwdPairBars<NS>) + 1023u) & ~1023u;
+  CtaCtl* ctl = &bars->ctl;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // Head-major order (L2 reuse of K / V), last query-tile pairs of a head first.
+  int qp, bh;
+  cta_tile(p.n_qt, p.bh_total, p.head_group, true, qp, bh);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qp * 2 * kRows;  // tile t covers rows q0 + t * 128 ..
+  const int T = p.T;
+  auto steps = [&](int t) {  // key tiles query tile t reads
+    const int last = min(q0 + (t + 1) * kRows - 1, T - 1);
+    return p.causal ? last / BN + 1 : (T + BN - 1) / BN;
+  };
+  const int n_a = steps(0), n_b = steps(1);
+  const int n_kv = max(n_a, n_b);
+
+  auto B = [&](const uint64_t& x) { return smem_u32(&x); };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(B(bars->full_k[s]), 1);
+      mbar_init(B(bars->full_v[s]), 1);
+      mbar_init(B(bars->ready_k[s]), kPrepWarps);
+      mbar_init(B(bars->ready_v[s]), kPrepWarps);
+      mbar_init(B(bars->empty_k[s]), 2);  // both tiles' S MMAs read K_j
+      mbar_init(B(bars->empty_v[s]), 2);  // both tiles' P.V MMAs read V_j
+    }
+    for (int t = 0; t < 2; ++t) {
+      for (int bb = 0; bb < 2; ++bb) {
+        mbar_init(B(bars->s_full[t][bb]), 1);
+        mbar_init(B(bars->p_full[t][bb]), 4);  // the tile's row warps
+      }
+      mbar_init(B(bars->pv_done[t]), 1);
+      mbar_init(B(bars->o_done[t]), 1);
+      mbar_init(B(bars->mma_final[t]), 1);
+    }
+    mbar_init(B(bars->q_ready), 8);  // all row warps
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int last_k[NS], last_v[NS];
+      for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % NS, r = j / NS;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (r > 0 && !mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status)) break;
+        mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
+        tma_load_tile<true, D>(st + C::OFF_K, &tmK, B(bars->full_k[s]), j * BN, h, b, BN * 128u);
+        last_k[s] = r;
+        if (r > 0 && !mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status)) break;
+        mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
+        tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_v[s]), j * BN, h, b, BN * 128u);
+        last_v[s] = r;
+      }
+      if (ctl->abort) {  // let every issued copy land before the CTA exits
+        for (int s = 0; s < NS; ++s) {
+          if (last_k[s] >= 0) mbar_drain(B(bars->full_k[s]), last_k[s] & 1);
+          if (last_v[s] >= 0) mbar_drain(B(bars->full_v[s]), last_v[s] & 1);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1 || warp == kIssuer2Warp) {
+    // ------------------------------------- tile t's issuer: S, then P.V
+    // Past its last key tile a tile still releases the stages (commits with
+    // nothing new in flight), so the producer's two-issuer count holds.
+    if (lane == 0) {
+      const int t = warp == 1 ? 0 : 1;
+      const int n_mine = t ? n_b : n_a;
+      constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
+      constexpr uint32_t idO = idesc_tf32(128, D, false, true);
+      const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);
+      const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
+      const uint32_t sb0 = tmem + C::TC_S + (uint32_t)(2 * t) * BN;
+      auto issue_S = [&](int j) -> bool {  // S_t(j) into buffer j % 2
+        const int s = j % NS;
+        if (j < n_mine) {
+          if (!mbar_wait(B(bars->ready_k[s]), (j / NS) & 1, ctl, p.status)) return false;
+          tc_fence_after();
+          mma_chain<1, D, false, BN, C::TILE>(sb0 + (uint32_t)(j & 1) * BN,
+                                              tmem + C::TC_Q + (uint32_t)t * D, 0,
+                                              kd0 + (s * C::STAGE >> 4), idS, false);
+          umma_commit(B(bars->s_full[t][j & 1]));
+        }
+        umma_commit(B(bars->empty_k[s]));
+        return true;
+      };
+      bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status) && issue_S(0) &&
+                (n_kv < 2 || issue_S(1));
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % NS;
+        if (j < n_mine) {
+          if (!(ok = mbar_wait(B(bars->p_full[t][j & 1]), (j >> 1) & 1, ctl, p.status))) break;
+          if (!(ok = mbar_wait(B(bars->ready_v[s]), (j / NS) & 1, ctl, p.status))) break;
+          tc_fence_after();
+          mma_chain<1, BN, true, BN, C::TILE>(tmem + C::TC_O + (uint32_t)t * D,
+                                              sb0 + (uint32_t)(j & 1) * BN, 0,
+                                              vd0 + (s * C::STAGE >> 4), idO, j > 0);
+          umma_commit(B(bars->pv_done[t]));
+        }
+        umma_commit(B(bars->empty_v[s]));
+        if (j + 2 < n_kv && !(ok = issue_S(j + 2))) break;
+      }
+      if (ok) umma_commit(B(bars->o_done[t]));
+      umma_commit(B(bars->mma_final[t]));  // nothing of this thread in flight after this
+      mbar_drain(B(bars->mma_final[t]), 0);
+    }
+    __syncwarp();
+  } else if (is_prep_warp(warp)) {
+    // ----------------------------------------------- TF32 rounding warps
+    const uint32_t tid = prep_tid();
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j % NS, r = j / NS;
+      const uint32_t st = tiles + s * C::STAGE;
+      if (!warp_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
+      round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_K, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_k[s]));
+      if (!warp_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
+      round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_V, tid);
+      fence_proxy_async_smem();
+      warp_arrive(B(bars->ready_v[s]));
+    }
+  } else {
+    // --------------------------------------------------------- row warps
+    // Warps 4-7 own tile A, warps 11-14 tile B: thread (quad, lane) owns
+    // query row quad*32 + lane of its tile (TMEM lane quarter quad) and all
+    // BN score columns of a step, kept in registers between the maximum and
+    // the exponentials.
+    const int t = warp >= kFwdRowWarp1 ? 1 : 0;
+    const int n_mine = t ? n_b : n_a;
+    const int quad = warp & 3;
+    const int qt0 = q0 + t * kRows;
+    const int row = qt0 + quad * 32 + lane;
+    const bool valid = row < T;
+    const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
+    const uint32_t sc0 = lb + C::TC_S + (uint32_t)(2 * t) * BN;
+    const uint32_t oc = lb + C::TC_O + (uint32_t)t * D;
+    {
+      const float* qrow = p.q.row(b, h, valid ? row : 0);
+      const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
+      row_to_tmem<D, 1>(p.q, qrow, valid, vec, lb, C::TC_Q + (uint32_t)t * D);
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive(B(bars->q_ready));
+    }
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; ok && j < n_mine; ++j) {
+      const int bb = j & 1;
+      const uint32_t sc = sc0 + (uint32_t)bb * BN;
+      if (!(ok = warp_wait(B(bars->s_full[t][bb]), (j >> 1) & 1, ctl, p.status))) break;
+      tc_fence_after();
+      const int kv0 = j * BN;
+      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > qt0);
+      float sv[BN];
+      float mraw = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float x[32];
+        tmem_ld32(sc + 32 * c, x);
+        if (need_mask) mask_cols32(x, kv0 + 32 * c, T, p.causal, row);
+        mraw = fmaxf(mraw, max32(x));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[32 * c + i] = x[i];
+      }
+      // scale_log2 > 0, so scaling after the maximum is exact
+      const float m_new = fmaxf(m_used, mraw * p.scale_log2);
+      const bool resc = m_new > m_used + 8.0f;
+      const bool any_resc = __any_sync(0xffffffffu, resc);
+      const float alpha = resc ? ex2_approx(m_used - m_new) : 1.0f;
+      if (resc) m_used = m_new;
+      l *= alpha;
+      const float neg_m = -m_used;
+      float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float a0, a1;
+          ffma2(a0, a1, sv[32 * c + i], sv[32 * c + i + 1], p.scale_log2, p.scale_log2, neg_m,
+                neg_m);
+          const float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
+          fadd2(ls0, ls1, ls0, ls1, e0, e1);
+          x[i] = tf32_round_finite(e0);
+          x[i + 1] = tf32_round_finite(e1);
+        }
+        tmem_st32(sc + 32 * c, x);
+      }
+      l += ls0 + ls1;
+      // O_t rescaled to the new maximum once O_t += P_t(j-1) V_{j-1} is done
+      // (the scores are out of the registers by now)
+      if (any_resc && j > 0) {
+        if (!(ok = warp_wait(B(bars->pv_done[t]), (j - 1) & 1, ctl, p.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float ov[32];
+          tmem_ld32(oc + 32 * c, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(oc + 32 * c, ov);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive(B(bars->p_full[t][bb]));
+    }
+    if (ok && warp_wait(B(bars->o_done[t]), 0, ctl, p.status)) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;
+      tmem_cols_to_global<D>(lb, C::TC_O + (uint32_t)t * D, inv_l, orow, valid);
+      if (valid) p.lse[(int64_t)bh * T + row] = (m_used + log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <class C>
+int run_fwd_pair(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float* o, float* lse,
+                 const DeviceInfo& dev, cudaStream_t st) {
+  static unsigned long long attr_done = 0;
+  CUtensorMap tmK, tmV;
+  int rc = make_tmap_bhtd_whole(&tmK, k, pr, C::BN);
+  if (rc != CT_OK) return rc;
+  rc = make_tmap_bhtd_whole(&tmV, v, pr, C::BN, /*mn_major=*/true);
+  if (rc != CT_OK) return rc;
+  const size_t smem = fwd_pair_smem_bytes<C>();
+  rc = ensure_smem_attr(fa2_fwd_pair_kernel<C>, smem, dev.device, &attr_done);
+  if (rc != CT_OK) return rc;
+  FwdParams p;
+  p.q = Ptr4{q.ptr, q.s[0], q.s[1], q.s[2], q.s[3]};
+  p.o = o;
+  p.lse = lse;
+  p.H = (int)pr.H;
+  p.T = (int)pr.T;
+  p.n_qt = (int)((pr.T + 2 * kRows - 1) / (2 * kRows));  // query-tile pairs
+  p.bh_total = (int)(pr.B * pr.H);
+  p.head_group = fa2_head_group(p.bh_total);
+  p.causal = pr.causal ? 1 : 0;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
+  p.status = dev.status;
+  const int64_t grid = (int64_t)p.n_qt * p.bh_total;
+  fa2_fwd_pair_kernel<C><<<(unsigned)grid, kFwdThreads, smem, st>>>(tmK, tmV, p);
+  return check_launch();
+}
+
 }  // namespace
 
 bool fa2_fwd_tc_supported(const Fa2Problem& p) {
@@ -457,10 +773,10 @@ int launch_fa2_fwd_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, 
   switch (pr.D) {
     case 32:
       return split ? run_fwd<FwdCfg<32, 64, 3, 4, 3>>(pr, q, k, v, o, lse, dev, st)
-                   : run_fwd<FwdCfg<32, 128, 1, 4, 3>>(pr, q, k, v, o, lse, dev, st);
+                   : run_fwd_pair<FwdPairCfg<32, 64, 8>>(pr, q, k, v, o, lse, dev, st);
     case 64:
       return split ? run_fwd<FwdCfg<64, 64, 3, 3, 2>>(pr, q, k, v, o, lse, dev, st)
-                   : run_fwd<FwdCfg<64, 128, 1, 3, 3>>(pr, q, k, v, o, lse, dev, st);
+                   : run_fwd_pair<FwdPairCfg<64, 64, 6>>(pr, q, k, v, o, lse, dev, st);
     case 128:
       return split ? run_fwd<FwdCfg<128, 32, 3, 3, 2>>(pr, q, k, v, o, lse, dev, st)
                    : run_fwd<FwdCfg<128, 64, 1, 3, 3>>(pr, q, k, v, o, lse, dev, st);
