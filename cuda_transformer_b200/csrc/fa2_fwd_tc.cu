@@ -23,6 +23,9 @@
 // maximum grows by more than 2^8 (exact: l and O always share the stale
 // maximum).  3xTF32 forms hi*hi and hi*lo of S, and of P V, with one MMA
 // (mma_chain_kil, mma_chain_mn2).
+// TF32 mode at head dims 32 and 64 runs fa2_fwd_pair_kernel instead: two
+// query tiles per CTA, one row warpgroup and one issuing thread per tile
+// (see there).
 #include "fa2_common.cuh"
 
 namespace ct {
