@@ -376,7 +376,7 @@ def timed_steps(runner, steps: int, warmup: int, dist, world: int):
 
 
 def e2e_steps(pairs: int, dev, precision: int, steps: int, dist, world: int, seed: int,
-              chunks: int = 16) -> dict:
+              chunks: int = 4) -> dict:
     """Same metric through the torch operators, every step's inputs copied from
     pinned host memory and its results (O, LSE, dQ, dK, dV) copied back inside
     the timed region.  The rank's (b,h) pairs are cut into `chunks` slices that
