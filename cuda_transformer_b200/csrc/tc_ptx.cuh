@@ -428,6 +428,125 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// ------------------------------------------------- CTA pairs (cta_group::2)
+// A cluster of two CTAs on two SMs runs one tensor-core product of M = 256:
+// rows 0-127 of A and D live in the even CTA's Tensor Memory and rows 128-255
+// in the odd CTA's (same TMEM address in both); B's N rows are split, rows
+// [0, N/2) in the even CTA's shared memory and [N/2, N) in the odd CTA's, both
+// at the address the descriptor names.  The even CTA's thread issues, and its
+// commits arrive on the barrier at the same address in both CTAs.  Kernels
+// using these run every tcgen05 instruction with cta_group::2 (TMEM allocation
+// included) and are launched with cluster dimension 2.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The address in CTA `rank` of this cluster of the shared-memory word at
+// `addr` (a shared::cta address of the calling CTA).
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrives on an mbarrier of any CTA of the cluster (address from mapa_shared),
+// releasing the calling thread's earlier writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// try_wait acquiring at cluster scope (the phase may have been completed by
+// arrivals from the other CTA of the pair).
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar, uint32_t parity,
+                                                       uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait with cluster-scope acquire (same bound, same abort handling).
+static __device__ __noinline__ bool mbar_wait_cl_slow(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                                      uint32_t* status) {
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_sleep_cl(bar, parity, 100000u)) return true;
+    if ((i & 15u) == 0u) {
+      if (ctl->abort) return false;
+      if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
+        ctl->abort = 1u;
+        return false;
+      }
+      if (globaltimer_ns() - t0 > limit) {
+        ctl->abort = 1u;
+        atomicOr(status, CT_DEVSTAT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, CtaCtl* ctl,
+                                             uint32_t* status) {
+  if (__builtin_expect(mbar_try_wait_cl(bar, parity), 1)) return true;
+  return mbar_wait_cl_slow(bar, parity, ctl, status);
+}
+// Barrier over every thread of both CTAs of the cluster (each thread arrives
+// once per use).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Pair allocation: the same warp index of both CTAs calls each of these, with
+// the same destination address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D (+)= A * B over the CTA pair (M = 256), A from both CTAs' TMEM.
+__device__ __forceinline__ void umma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem,
+                                                  uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on the barrier at `bar` in both CTAs of the pair when all
+// previously issued tcgen05 operations of the calling thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  const uint16_t both = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(both)
+      : "memory");
+}
+
 // --------------------------------------------------------- TF32 helpers
 // Round-to-nearest (ties away) to TF32; the low 13 bits of the result are 0.
 __device__ __forceinline__ float tf32_round(float x) {

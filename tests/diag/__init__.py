@@ -14,6 +14,7 @@ _int = ctypes.c_int
 SIGNATURES = {
     "ct_diag_umma_tf32": [_int, _fp, _fp, _fp, _int, _fp],
     "ct_diag_umma_m64": [_int, _fp, _fp, _fp, _int, _fp],
+    "ct_diag_umma_pair": [_int, _fp, _fp, _fp, _int, _fp],
     "ct_diag_mma_rate": [_int, _int, _int, _int, _fp, _fp],
     "ct_diag_status": [ctypes.POINTER(ctypes.c_uint)],
 }

@@ -6,6 +6,8 @@
 //   FlashAttention and GEMM kernels rely on: K-major and MN-major shared-memory
 //   operands in the 128-byte swizzle, A read from Tensor Memory, and how the
 //   tensor core treats the 13 low mantissa bits of an FP32 operand.
+// * ct_diag_umma_pair: the same check for a CTA pair (cta_group::2, M = 256):
+//   which rows of A, B and D each CTA of the pair holds.
 // * ct_diag_mma_rate: a throughput probe -- back-to-back kind::tf32 MMAs of one
 //   shape, timed in SM cycles on every SM (the tensor-pipe ceiling the tile
 //   shapes of the product kernels are chosen against).
@@ -128,6 +130,92 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
+  }
+}
+
+// A CTA pair (cluster of two, cta_group::2): D[256 x n] = A[256 x 64] B^T over
+// K = 64 in eight MMAs of M = 256 issued by the even CTA.  A from Tensor
+// Memory: CTA r holds rows 128r..128r+127 in its lanes (columns 128..191).  B
+// split along N: CTA r holds B's rows [r n/2, (r+1) n/2) in its shared memory
+// at the same address, K-major (mode 0: b is [n][64]) or MN-major (mode 1: b is
+// [64][n]).  The odd CTA reports its operands ready with a remote arrival on
+// the even CTA's barrier; the commit arrives on both CTAs' barriers.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
+    umma_pair_diag_kernel(int mode, const float* __restrict__ a, const float* __restrict__ b,
+                          float* __restrict__ d, int n, uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DiagSmem* hs = reinterpret_cast<DiagSmem*>(smem_raw);
+  const uint32_t base = (smem_u32(smem_raw) + sizeof(DiagSmem) + 1023u) & ~1023u;
+  uint8_t* sbp = smem_raw + (base - smem_u32(smem_raw));
+  const int tid = threadIdx.x, warp = tid / 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool b_mn = mode == 1;
+  const int nh = n / 2;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&hs->bar), 1);   // the pair's commit
+    mbar_init(smem_u32(&hs->bar2), 2);  // operands ready: one arrival per CTA
+    hs->ctl.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(smem_u32(&hs->ctl.tmem_base), 256);
+    tmem_relinquish_pair();
+  }
+  for (int e = tid; e < nh * 64; e += 128) {
+    if (b_mn) {  // rows k, 128-byte rows of 32 n values, n chunks of 64 rows
+      const int kk = e / nh, nl = e % nh;
+      *reinterpret_cast<float*>(sbp + sw128_32b_offset(kk, nl, 64)) = b[kk * n + rank * nh + nl];
+    } else {  // rows n, 128-byte rows of 32 k values, k chunks of nh rows
+      const int nl = e / 64, kk = e % 64;
+      *reinterpret_cast<float*>(sbp + sw128_offset(nl, kk, nh)) = b[(rank * nh + nl) * 64 + kk];
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = hs->ctl.tmem_base;
+  const uint32_t lane_base = tmem_addr(tmem, 32u * warp, 0);
+  for (int h = 0; h < 2; ++h) {
+    float row[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) row[i] = a[(128 * rank + tid) * 64 + 32 * h + i];
+    tmem_st32(lane_base + 128u + 32u * h, row);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&hs->bar2), 0));
+  if (rank == 0 && tid == 0) {
+    if (mbar_wait_cl(smem_u32(&hs->bar2), 0, &hs->ctl, status)) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_tf32(256, n, false, b_mn);
+      for (int k = 0; k < 8; ++k) {
+        const uint64_t bd =
+            b_mn ? sdesc_mnmajor(base + k * 1024u, 64u * 128u)
+                 : sdesc_kmajor(base + (uint32_t)(k / 4) * nh * 128u + (uint32_t)(k % 4) * 32u);
+        umma_tf32_ts_pair(tmem, tmem + 128u + 8u * k, bd, idesc, k > 0);
+      }
+      umma_commit_pair(smem_u32(&hs->bar));
+    }
+  }
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_cl(smem_u32(&hs->bar), 0, &hs->ctl, status));
+  if (ok) {
+    tc_fence_after();
+    for (int c = 0; c < n; c += 32) {
+      float v[32];
+      tmem_ld32(lane_base + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) d[(128 * rank + tid) * n + c + i] = v[i];
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no MMA, load or remote arrival of either CTA still pending
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 256);
   }
 }
 
@@ -388,6 +476,19 @@ int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, 
     return 6;
   ct::umma_m64_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mode, a, b, d, n,
                                                                                 status);
+  return ct::launch_ok();
+}
+
+int ct_diag_umma_pair(int mode, const float* a, const float* b, float* d, int n, void* stream) {
+  if (!a || !b || !d || mode < 0 || mode > 1 || !(n == 64 || n == 128)) return 1;
+  uint32_t* status = ct::diag_status();
+  if (!status) return 6;
+  const size_t smem = 1024 + 1024 + (size_t)(n / 2) * 64 * 4;
+  if (cudaFuncSetAttribute(ct::umma_pair_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return 6;
+  ct::umma_pair_diag_kernel<<<2, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mode, a, b,
+                                                                                      d, n, status);
   return ct::launch_ok();
 }
 

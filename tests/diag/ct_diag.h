@@ -29,6 +29,13 @@ int ct_diag_umma_tf32(int mode, const float* a, const float* b, float* d, int n,
  * [n,32], d [64,n]; n in {32, 64}. */
 int ct_diag_umma_m64(int mode, const float* a, const float* b, float* d, int n, void* stream);
 
+/* One M = 256 TF32 product D[256 x n] = A[256 x 64] B^T on a CTA pair
+ * (cluster of two, cta_group::2).  A from Tensor Memory (CTA r: rows
+ * 128r..128r+127); B split along N between the two CTAs' shared memory:
+ * mode 0 K-major (b is [n,64]), mode 1 MN-major (b is [64,n]).  a is [256,64]
+ * row-major, d [256,n]; n in {64, 128}. */
+int ct_diag_umma_pair(int mode, const float* a, const float* b, float* d, int n, void* stream);
+
 /* Tensor-pipe throughput of kind::tf32 MMAs, M = 128, N in {32, 64, 128, 256}.
  * `flags`: bit 0 A from TMEM (else shared memory), bit 1 B MN-major (else
  * K-major), bit 2 two issuing threads in different warps, each with its own

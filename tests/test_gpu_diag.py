@@ -109,3 +109,26 @@ def test_umma_m64_layouts(cuda_device, mode, n):
     assert diag.status() == 0
     ref = a.double() @ b.double().t()
     assert H.rel_err(d, ref) < 1e-6, mode
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("n", [64, 128])
+def test_umma_pair_layouts(cuda_device, mode, n):
+    """CTA pair (cta_group::2, M = 256): each CTA holds 128 rows of A and D in
+    its own Tensor Memory and half of B's N rows in its shared memory (K-major
+    or MN-major); the odd CTA's readiness reaches the issuing even CTA by a
+    remote barrier arrival and the commit completes both CTAs' barriers."""
+    from tests import diag
+
+    g = torch.Generator().manual_seed(500 + 10 * mode + n)
+    a = _tf32_exact((256, 64), g, cuda_device)
+    b = _tf32_exact((n, 64), g, cuda_device)  # [n][k]
+    d = torch.full((256, n), float("nan"), device=cuda_device)
+    bb = b.t().contiguous() if mode == 1 else b
+    diag.check(diag.lib().ct_diag_umma_pair(mode, H._p(a), H._p(bb), H._p(d), n, H._stream()),
+               "ct_diag_umma_pair")
+    torch.cuda.synchronize()
+    assert diag.status() == 0
+    ref = a.double() @ b.double().t()
+    assert H.rel_err(d, ref) < 1e-6, mode
