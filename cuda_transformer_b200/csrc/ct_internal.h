@@ -96,6 +96,13 @@ int launch_fa2_bwd_fused_tc(const Fa2Problem& p, Strided4 q, Strided4 k, Strided
                             float* dq, float* dk, float* dv, uint32_t* sync_words,
                             const DeviceInfo& dev, cudaStream_t st);
 size_t fa2_bwd_fused_sync_words(int64_t B, int64_t H, int64_t T);
+// dK/dV on CTA pairs (TF32, head dim 64; fa2_bwd_pair.cu): the default for
+// that case unless CT_FA2_PAIR_DKDV=0.
+int launch_fa2_bwd_dkdv_pair(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v,
+                             Strided4 dO, const float* lse, const int64_t lse_s[3],
+                             const float* delta, float* dk, float* dv, const DeviceInfo& dev,
+                             cudaStream_t st);
+bool fa2_bwd_pair_supported(const Fa2Problem& p);
 // Whether the tensor-core kernels cover this problem (head dim / precision).
 bool fa2_fwd_tc_supported(const Fa2Problem& p);
 bool fa2_bwd_tc_supported(const Fa2Problem& p);

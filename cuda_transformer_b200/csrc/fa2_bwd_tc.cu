@@ -1246,6 +1246,8 @@ int launch_fa2_bwd_dkdv_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided
                            float* dv, const DeviceInfo& dev, cudaStream_t st) {
   if (!fa2_tma_ok(q) || !fa2_tma_ok(g)) return CT_ERR_UNSUPPORTED_LAYOUT;
   const bool split = pr.precision == CT_PRECISION_3XTF32;
+  if (fa2_bwd_pair_supported(pr))  // TF32, D = 64: 256-key tiles on CTA pairs
+    return launch_fa2_bwd_dkdv_pair(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);
   if (pr.D == 64)
     return split ? run_dkdv<DkvCfg<64, 32, 3, 3>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st)
                  : run_dkdv<DkvCfg<64, 64, 1, 3, 2>>(pr, q, k, v, g, lse, ls, delta, dk, dv, dev, st);

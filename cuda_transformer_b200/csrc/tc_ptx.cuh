@@ -450,61 +450,16 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return r;
 }
 // Arrives on an mbarrier of any CTA of the cluster (address from mapa_shared),
-// releasing the calling thread's earlier writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+// with the arrive's default release at CTA scope.  The pair kernels publish
+// only data that lives in the arriving CTA itself -- its shared memory
+// (after fence.proxy.async) or its Tensor Memory (after tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync) -- for tensor-core operations that the
+// other CTA issues once it has seen the arrival; the same protocol as the
+// CUTLASS sm100 pair pipelines.  A cluster-scope release would cost a
+// cluster fence (~320 cycles per arrival, measured on B200; this arrive: ~6).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
-}
-// try_wait acquiring at cluster scope (the phase may have been completed by
-// arrivals from the other CTA of the pair).
-__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar, uint32_t parity,
-                                                       uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-// mbar_wait with cluster-scope acquire (same bound, same abort handling).
-static __device__ __noinline__ bool mbar_wait_cl_slow(uint32_t bar, uint32_t parity, CtaCtl* ctl,
-                                                      uint32_t* status) {
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit_ns(status);
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_sleep_cl(bar, parity, 100000u)) return true;
-    if ((i & 15u) == 0u) {
-      if (ctl->abort) return false;
-      if (*reinterpret_cast<volatile uint32_t*>(status) != 0u) {
-        ctl->abort = 1u;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > limit) {
-        ctl->abort = 1u;
-        atomicOr(status, CT_DEVSTAT_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, CtaCtl* ctl,
-                                             uint32_t* status) {
-  if (__builtin_expect(mbar_try_wait_cl(bar, parity), 1)) return true;
-  return mbar_wait_cl_slow(bar, parity, ctl, status);
 }
 // Barrier over every thread of both CTAs of the cluster (each thread arrives
 // once per use).

@@ -186,9 +186,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
   tmem_wait_st();
   tc_fence_before();
   __syncthreads();
-  if (tid == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&hs->bar2), 0));
+  if (tid == 0) mbar_arrive_remote(mapa_shared(smem_u32(&hs->bar2), 0));
   if (rank == 0 && tid == 0) {
-    if (mbar_wait_cl(smem_u32(&hs->bar2), 0, &hs->ctl, status)) {
+    if (mbar_wait(smem_u32(&hs->bar2), 0, &hs->ctl, status)) {
       tc_fence_after();
       const uint32_t idesc = idesc_tf32(256, n, false, b_mn);
       for (int k = 0; k < 8; ++k) {
@@ -201,7 +201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
     }
   }
   __syncwarp();
-  const bool ok = __all_sync(0xffffffffu, mbar_wait_cl(smem_u32(&hs->bar), 0, &hs->ctl, status));
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&hs->bar), 0, &hs->ctl, status));
   if (ok) {
     tc_fence_after();
     for (int c = 0; c < n; c += 32) {

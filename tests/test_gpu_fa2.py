@@ -296,3 +296,30 @@ def test_segment_boundaries(cuda_device, prec, T, causal):
     for a, b in zip(g1, g2):
         assert torch.equal(a, b)
     H.assert_device_clean()
+
+
+_ONE_CTA_CHILD = r"""
+import torch
+from tests import test_gpu_fa2 as T
+import cuda_transformer_b200 as cb
+dev = torch.device("cuda", 0)
+for (B, Hh, N, causal) in [(2, 4, 257, True), (1, 2, 300, False), (1, 2, 1024, True)]:
+    q, k, v, do = (T._rand((B, Hh, N, 64), 70 + s, dev) for s in range(4))
+    T._check_fwd_bwd(q, k, v, do, causal, cb.PRECISION_TF32)
+print("ONE_CTA_OK")
+"""
+
+
+@pytest.mark.gpu
+def test_one_cta_dkdv_tf32(cuda_device):
+    """TF32 at head dim 64 runs dK/dV on CTA pairs by default; CT_FA2_PAIR_DKDV=0
+    selects the one-CTA kernel.  The library reads the variable once, so the
+    one-CTA path runs in a child process, against the same oracle."""
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, CT_FA2_PAIR_DKDV="0")
+    r = subprocess.run([sys.executable, "-c", _ONE_CTA_CHILD], cwd=str(ROOT), env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ONE_CTA_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
