@@ -74,8 +74,8 @@ constexpr size_t pair_smem_bytes() {
 
 constexpr int kPairRowWarps = 16;  // both CTAs' row warps arrive on the even CTA's barriers
 
-// full_a: TMA landed (local); ready_a / ready_b: K-major halves rounded /
-// MN-major chunks written (both CTAs' preparation warps, on the even CTA);
+// full_a: TMA landed (local); ready_a: K-major halves rounded and MN-major
+// chunks written (both CTAs' preparation warps, on the even CTA);
 // empty_a: the stage's MMAs finished (both issuers' commits, in both CTAs).
 template <class C>
 __device__ __forceinline__ void init_pair_bars(BwdBars<C::NS>* bars) {
@@ -83,7 +83,6 @@ __device__ __forceinline__ void init_pair_bars(BwdBars<C::NS>* bars) {
   for (int s = 0; s < C::NS; ++s) {
     mbar_init(B(bars->full_a[s]), 1);
     mbar_init(B(bars->ready_a[s]), 2 * kPrepWarps);
-    mbar_init(B(bars->ready_b[s]), 2 * kPrepWarps);
     mbar_init(B(bars->empty_a[s]), 2);
     mbar_init(B(bars->vec_full[s]), 1);
   }
@@ -160,6 +159,45 @@ __device__ __forceinline__ void pair_derive_mn(uint32_t t, uint32_t mn, uint32_t
   }
 }
 
+// One 256-key tile of a persistent cluster: (head, keys [k0, k0 + 256)) and
+// its query tiles [j0, j1) in this launch's segment.
+struct PairTile {
+  int b, h, bh, k0, kb, j0, j1, n;
+  bool exists;
+};
+// The clusters' static schedule.  A unit is the tile pair (kp, NT-1-kp) of one
+// head (NT tiles per head): under the causal mask their step counts add up to
+// the same total for every kp, so units have equal work, and cluster c takes
+// units c, c + G, c + 2G, ... (units in the head-grouped order of cta_tile_at,
+// so the heads in flight share L2).  Tile m of cluster c is half m % 2 of its
+// unit m / 2.  Returns false past the cluster's last unit; t.exists is false
+// for the missing second half of the middle unit when NT is odd.
+__device__ __forceinline__ bool pair_tile_at(const BwdParams& p, int c, int G, int m,
+                                             uint32_t rank, PairTile& t) {
+  constexpr int BN = 64;
+  const int U = (p.n_tiles + 1) / 2;
+  const int u = c + (m >> 1) * G;
+  if (u >= U * p.bh_total) return false;
+  int k;
+  cta_tile_at((unsigned)u, U, p.bh_total, p.head_group, false, k, t.bh);
+  const int kp = (m & 1) ? p.n_tiles - 1 - k : k;
+  t.exists = !((m & 1) && kp == k);
+  t.b = t.bh / p.H;
+  t.h = t.bh % p.H;
+  t.k0 = kp * 2 * kRows;
+  t.kb = t.k0 + (int)rank * kRows;
+  t.j0 = max(p.causal ? t.k0 / BN : 0, p.seg_lo / BN);
+  t.j1 = min((p.T + BN - 1) / BN, (p.seg_hi + BN - 1) / BN);
+  t.n = t.exists ? max(0, t.j1 - t.j0) : 0;
+  return true;
+}
+
+// Persistent: each cluster loops over tiles.  The producer, preparation warps
+// and issuers run on across tile boundaries (one step counter g for the stage
+// ring and the S^T / dP^T buffers), so the next tile's tiles are landed and
+// prepared while the current one finishes; per tile only the rows' dK / dV
+// write-out and the load of the next K / V rows into TMEM sit between the
+// last MMA of one tile and the first of the next.
 template <class C>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     fa2_bwd_dkdv_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -175,16 +213,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-
-  int kp, bh;  // the pair's 256-key tile; same (tile, head) order as the one-CTA kernel
-  cta_tile_at(blockIdx.x / 2, p.n_tiles, p.bh_total, p.head_group, false, kp, bh);
-  const int b = bh / p.H, h = bh % p.H;
-  const int k0 = kp * 2 * kRows, T = p.T;
-  const int kb = k0 + (int)rank * kRows;  // this CTA's first key
-  const int j0 = max(p.causal ? k0 / BN : 0, p.seg_lo / BN);
-  const int j1 = min((T + BN - 1) / BN, (p.seg_hi + BN - 1) / BN);
-  const int n = max(0, j1 - j0);
-  if (n == 0 && p.accumulate_out) return;  // the same for both CTAs of the pair
+  const int T = p.T;
+  const int G = (int)(gridDim.x / 2), cl = (int)(blockIdx.x / 2);
 
   if (threadIdx.x == 0) init_pair_bars<C>(bars);
   if (warp == 1) {
@@ -195,54 +225,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
   cluster_sync_all();  // both CTAs' barriers initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  auto stg = [&](int i) { return (uint64_t)(((i % NS) * C::STAGE) >> 4); };
+  auto stg = [&](int g) { return (uint64_t)(((g % NS) * C::STAGE) >> 4); };
 
   if (warp == 0) {
-    // Producer: Q_j and dO_j (two 32-row copies each: own rows to half 0),
-    // then the step's LSE * -log2(e) and delta into the stage's vector slot.
-    constexpr int NV = BN / 32;
-    const float* lse_bh = p.lse + b * p.l0 + h * p.l1;
-    const float* del_bh = p.delta + (int64_t)bh * T;
-    float vl[NV], vd[NV];
-    auto load_vec = [&](int j) {
-#pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        const int q = j * BN + 32 * u + lane;
-        const bool in = j < j1 && q < T;
-        vl[u] = in ? ldg_nc_early(lse_bh + (int64_t)q * p.l2) : 0.0f;
-        vd[u] = in ? ldg_nc_early(del_bh + q) : 0.0f;
-      }
-    };
+    // Producer: per step, Q_j and dO_j (two 32-row copies each: own rows to
+    // half 0), then the step's LSE * -log2(e) and delta into the stage's
+    // vector slot (loaded before the stage wait, so the load overlaps it).
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmG);
     }
     int last[NS];
     for (int s = 0; s < NS; ++s) last[s] = -1;
-    load_vec(j0);
-    for (int j = j0; j < j1; ++j) {
-      const int i = j - j0, s = i % NS, r = i / NS;
-      const uint32_t st = tiles + s * C::STAGE;
-      if (r > 0 && !warp_wait(B(bars->empty_a[s]), (r - 1) & 1, ctl, p.status)) break;
-      if (lane == 0) {
-        const uint32_t fb = B(bars->full_a[s]);
-        const int own = j * BN + 32 * (int)rank, other = j * BN + 32 * (int)(rank ^ 1u);
-        mbar_arrive_expect_tx(fb, C::TX);
-        tma_load_5d(st + C::OFF_Q, &tmQ, fb, 0, own, 0, h, b);
-        tma_load_5d(st + C::OFF_Q + C::HALF, &tmQ, fb, 0, other, 0, h, b);
-        tma_load_5d(st + C::OFF_G, &tmG, fb, 0, own, 0, h, b);
-        tma_load_5d(st + C::OFF_G + C::HALF, &tmG, fb, 0, other, 0, h, b);
-      }
-      last[s] = r;
-      float* vs = vec + s * 2 * BN;
+    bool ok = true;
+    int g = 0;
+    PairTile t;
+    for (int m = 0; ok && pair_tile_at(p, cl, G, m, rank, t); ++m) {
+      const float* lse_bh = p.lse + t.b * p.l0 + t.h * p.l1;
+      const float* del_bh = p.delta + (int64_t)t.bh * T;
+      for (int i = 0; i < t.n; ++i) {
+        const int gs = g + i, s = gs % NS, rr = gs / NS, j = t.j0 + i;
+        float vl[BN / 32], vd[BN / 32];
 #pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        vs[32 * u + lane] = vl[u] * -kLog2e;
-        vs[BN + 32 * u + lane] = vd[u];
+        for (int u = 0; u < BN / 32; ++u) {
+          const int q = j * BN + 32 * u + lane;
+          vl[u] = q < T ? ldg_nc_early(lse_bh + (int64_t)q * p.l2) : 0.0f;
+          vd[u] = q < T ? ldg_nc_early(del_bh + q) : 0.0f;
+        }
+        if (rr > 0 && !(ok = warp_wait(B(bars->empty_a[s]), (rr - 1) & 1, ctl, p.status))) break;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (lane == 0) {
+          const uint32_t fb = B(bars->full_a[s]);
+          const int own = j * BN + 32 * (int)rank, other = j * BN + 32 * (int)(rank ^ 1u);
+          mbar_arrive_expect_tx(fb, C::TX);
+          tma_load_5d(st + C::OFF_Q, &tmQ, fb, 0, own, 0, t.h, t.b);
+          tma_load_5d(st + C::OFF_Q + C::HALF, &tmQ, fb, 0, other, 0, t.h, t.b);
+          tma_load_5d(st + C::OFF_G, &tmG, fb, 0, own, 0, t.h, t.b);
+          tma_load_5d(st + C::OFF_G + C::HALF, &tmG, fb, 0, other, 0, t.h, t.b);
+        }
+        last[s] = rr;
+        float* vs = vec + s * 2 * BN;
+#pragma unroll
+        for (int u = 0; u < BN / 32; ++u) {
+          vs[32 * u + lane] = vl[u] * -kLog2e;
+          vs[BN + 32 * u + lane] = vd[u];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B(bars->vec_full[s]));
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(B(bars->vec_full[s]));
-      load_vec(j + 1);
+      g += t.n;
     }
     __syncwarp();
     if (ctl->abort && lane == 0) {
@@ -254,6 +285,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     // into P_i's buffer.  Warp 10: dP^T_i -> dp_full; [dS_i] dK += dS_i^T Q_i;
     // dP^T_{i+2} into dS_i's buffer.  Each reuses a buffer in its own issue
     // order; a stage is released after both issuers' last MMA reading it.
+    // Per tile: wait until both CTAs' rows have written out the previous
+    // tile's dK / dV and loaded this tile's K / V (rows_ready); commit `done`
+    // after the tile's last MMAs.
     if (leader && lane == 0) {
       const bool first = warp == 1;
       const uint32_t tc_x = first ? C::TC_K : C::TC_V;        // stationary operand
@@ -263,37 +297,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
       const uint64_t md0 = sdesc_mnmajor(tiles + (first ? C::OFF_GM : C::OFF_QM), 64u * 128u);
       uint64_t* full = first ? bars->s_full : bars->dp_full;
       uint64_t* rows = first ? bars->p_full : bars->ds_full;
-      auto issue_x = [&](int i) {
-        pair_chain_k<C>(tmem + tc_b + (uint32_t)(i % 2) * C::SB, tmem + tc_x, kd0 + stg(i));
-        umma_commit_pair(B(full[i % 2]));
+      auto issue_x = [&](int gs) {
+        pair_chain_k<C>(tmem + tc_b + (uint32_t)(gs % 2) * C::SB, tmem + tc_x, kd0 + stg(gs));
+        umma_commit_pair(B(full[gs % 2]));
       };
-      bool ok = n > 0 && mbar_wait(B(bars->rows_ready), 0, ctl, p.status) &&
-                mbar_wait(B(bars->ready_a[0]), 0, ctl, p.status);
-      if (ok) {
-        tc_fence_after();
-        issue_x(0);
-        if (n > 1) {
-          ok = mbar_wait(B(bars->ready_a[1 % NS]), (1 / NS) & 1, ctl, p.status);
-          if (ok) {
+      bool ok = true;
+      int g = 0, tn = 0;
+      PairTile t;
+      for (int m = 0; ok && pair_tile_at(p, cl, G, m, rank, t); ++m) {
+        const int n = t.n;
+        if (n == 0) continue;
+        if (!(ok = mbar_wait(B(bars->rows_ready), tn & 1, ctl, p.status))) break;
+        for (int i0 = 0; ok && i0 < 2 && i0 < n; ++i0) {
+          const int gs = g + i0;
+          if ((ok = mbar_wait(B(bars->ready_a[gs % NS]), (gs / NS) & 1, ctl, p.status))) {
             tc_fence_after();
-            issue_x(1);
+            issue_x(gs);
           }
         }
         for (int i = 0; ok && i < n; ++i) {
-          const int bi = i % 2, nx = i + 2;
-          if (!(ok = mbar_wait(B(rows[bi]), (i / 2) & 1, ctl, p.status))) break;
-          if (!(ok = mbar_wait(B(bars->ready_b[i % NS]), (i / NS) & 1, ctl, p.status))) break;
+          const int gi = g + i, bi = gi % 2, nx = i + 2, gx = gi + 2;
+          // Both waits of the step together (a second wait on a completed
+          // phase costs the issuing thread little more than the first; the
+          // preparation runs steps ahead, so waiting for stage i+2 here does
+          // not delay dV_i).  Stage i's MN-major chunk is covered by this
+          // thread's wait on ready_a before S^T_i / dP^T_i.
+          if (!(ok = mbar_wait(B(rows[bi]), (gi / 2) & 1, ctl, p.status))) break;
+          if (nx < n &&
+              !(ok = mbar_wait(B(bars->ready_a[gx % NS]), (gx / NS) & 1, ctl, p.status)))
+            break;
           tc_fence_after();
-          pair_chain_mn(tmem + tc_acc, tmem + tc_b + (uint32_t)bi * C::SB, md0 + stg(i), i > 0);
-          umma_commit_pair(B(bars->empty_a[i % NS]));
-          if (nx < n) {
-            if (!(ok = mbar_wait(B(bars->ready_a[nx % NS]), (nx / NS) & 1, ctl, p.status)))
-              break;
-            tc_fence_after();
-            issue_x(nx);
-          }
+          pair_chain_mn(tmem + tc_acc, tmem + tc_b + (uint32_t)bi * C::SB, md0 + stg(gi), i > 0);
+          umma_commit_pair(B(bars->empty_a[gi % NS]));
+          if (nx < n) issue_x(gx);
         }
         if (ok) umma_commit_pair(B(bars->done));
+        g += n;
+        ++tn;
       }
       const uint32_t fin = B(first ? bars->mma_final : bars->mma_final2);
       umma_commit_pair(fin);  // nothing of this thread in flight after this
@@ -303,23 +343,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
   } else if (warp == kIssuer3Warp) {
     // idle
   } else if (is_prep_warp(warp)) {
-    // Per stage: round the own halves of Q_j and dO_j in place (S^T / dP^T
-    // operands) -> ready_a; write the MN-major chunks (dK / dV operands) ->
-    // ready_b.  Rounding is idempotent, so the MN pass may read half 0 before
-    // or after its rounding.
+    // Per step: round the own halves of Q_j and dO_j in place (S^T / dP^T
+    // operands) and write the MN-major chunks (dK / dV operands), then one
+    // arrival on ready_a: each issuing thread waits once per step.  Rounding
+    // is idempotent, so the MN pass may read half 0 before or after its
+    // rounding.
     const uint32_t tid = prep_tid();
-    for (int i = 0; i < n; ++i) {
-      const int s = i % NS, r = i / NS;
-      const uint32_t st = tiles + s * C::STAGE;
-      if (!warp_wait(B(bars->full_a[s]), r & 1, ctl, p.status)) break;
-      round_tile_smem<C::HALF, kSplitThreads>(st + C::OFF_Q, tid);
-      round_tile_smem<C::HALF, kSplitThreads>(st + C::OFF_G, tid);
-      fence_proxy_async_smem();
-      warp_arrive_remote(L(bars->ready_a[s]));
-      pair_derive_mn(st + C::OFF_Q, st + C::OFF_QM, rank, tid);
-      pair_derive_mn(st + C::OFF_G, st + C::OFF_GM, rank, tid);
-      fence_proxy_async_smem();
-      warp_arrive_remote(L(bars->ready_b[s]));
+    bool ok = true;
+    int g = 0;
+    PairTile t;
+    for (int m = 0; ok && pair_tile_at(p, cl, G, m, rank, t); ++m) {
+      const int n = t.n;
+      for (int i = 0; i < n; ++i) {
+        const int gs = g + i, s = gs % NS;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (!(ok = warp_wait(B(bars->full_a[s]), (gs / NS) & 1, ctl, p.status))) break;
+        round_tile_smem<C::HALF, kSplitThreads>(st + C::OFF_Q, tid);
+        round_tile_smem<C::HALF, kSplitThreads>(st + C::OFF_G, tid);
+        pair_derive_mn(st + C::OFF_Q, st + C::OFF_QM, rank, tid);
+        pair_derive_mn(st + C::OFF_G, st + C::OFF_GM, rank, tid);
+        fence_proxy_async_smem();
+        warp_arrive_remote(L(bars->ready_a[s]));
+      }
+      g += n;
     }
   } else {
     // Row warps 4-7 (group 0) and 11-14 (group 1): thread (quad, lane) owns key
@@ -330,89 +376,142 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     const int quad = warp & 3;
     const int grp = warp >= kBwdRowWarp1 ? 1 : 0;
     const int c0 = grp * HB;
-    const int row = kb + quad * 32 + lane;
-    const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    {
-      const Ptr4& src = grp ? p.st1 : p.st0;
-      const float* r = src.row(b, h, valid ? row : 0);
-      const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0);
-      row_to_tmem<D, 1>(src, r, valid, vr, lb, grp ? C::TC_V : C::TC_K);
-      tmem_wait_st();
-    }
-    tc_fence_before();
-    warp_arrive_remote(L(bars->rows_ready));
-    bool ok = n > 0;
-    for (int i = 0; ok && i < n; ++i) {
-      const int qs = (j0 + i) * BN + c0;
-      const int bi = i % 2;
-      const uint32_t par = (uint32_t)(i / 2) & 1u;
-      const uint32_t sc = lb + C::TC_S + (uint32_t)bi * C::SB + c0;
-      const uint32_t dc = lb + C::TC_DP + (uint32_t)bi * C::SB + c0;
-      if (!(ok = warp_wait(B(bars->vec_full[i % NS]), (i / NS) & 1, ctl, p.status))) break;
-      const float* vl = vec + (i % NS) * 2 * BN + c0;
-      if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
-      tc_fence_after();
-      const bool need_mask = !valid || (qs + HB > T) || (p.causal && qs < kb + kRows - 1);
-      float pv[HB];
-      {
-        float t[HB], lv[HB];
-        tmem_ldn<HB>(sc, t);
-        load_vecn<HB>(vl, lv);  // -LSE * log2(e)
-#pragma unroll
-        for (int x = 0; x < HB; x += 2) {
-          float a0, a1;
-          ffma2(a0, a1, t[x], t[x + 1], p.scale_log2, p.scale_log2, lv[x], lv[x + 1]);
-          t[x] = ex2_approx(a0);
-          t[x + 1] = ex2_approx(a1);
-        }
-        if (need_mask) {
-#pragma unroll
-          for (int x = 0; x < HB; ++x) {
-            const int q = qs + x;
-            t[x] = (valid && q < T && (!p.causal || q >= row)) ? t[x] : 0.0f;
-          }
-        }
-#pragma unroll
-        for (int x = 0; x < HB; ++x) {
-          pv[x] = t[x];
-          t[x] = tf32_round_finite(t[x]);
-        }
-        tmem_stn<HB>(sc, t);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      warp_arrive_remote(L(bars->p_full[bi]));  // S^T_i read, P^T_i written
-      if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
-      tc_fence_after();
-      {
-        float t[HB], dv[HB];
-        tmem_ldn<HB>(dc, t);
-        load_vecn<HB>(vl + BN, dv);
-#pragma unroll
-        for (int x = 0; x < HB; x += 2) {
-          float u0, u1, d0, d1;
-          fsub2(u0, u1, t[x], t[x + 1], dv[x], dv[x + 1]);
-          fmul2(d0, d1, pv[x], pv[x + 1], u0, u1);  // dS^T = P^T (dP^T - delta)
-          t[x] = tf32_round_finite(d0);
-          t[x + 1] = tf32_round_finite(d1);
-        }
-        tmem_stn<HB>(dc, t);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      warp_arrive_remote(L(bars->ds_full[bi]));
-    }
-    const int64_t orow = ((int64_t)bh * T + (valid ? row : 0)) * D;
+    const Ptr4& src = grp ? p.st1 : p.st0;
     float* out = grp ? p.out1 : p.out0;
-    if (n == 0) {  // no query of the first segment reaches these keys
-      if (valid) {
-        for (int d = 0; d < D; ++d) out[orow + d] = 0.0f;
+    // Tile boundary: the next tile's K / V row is loaded into registers
+    // before the wait for the previous tile's `done`; once that completes
+    // (no MMA reads K / V any more) it goes into TMEM and rows_ready lets the
+    // issuers start S^T_0 / dP^T_0 while the rows write out the previous dK /
+    // dV (the first dV / dK MMAs, which overwrite the accumulators, wait for
+    // P_0 / dS_0, formed after the write-out).
+    bool ok = true, pending = false;
+    int g = 0, tn = 0;
+    int64_t prev_orow = 0;
+    bool prev_valid = false;
+    auto write_out = [&]() {
+      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale,
+                            out + prev_orow, prev_valid, p.accumulate_out != 0);
+      tc_fence_before();  // TMEM reads done before the next arrival
+    };
+    PairTile t;
+    for (int m = 0; ok && pair_tile_at(p, cl, G, m, rank, t); ++m) {
+      if (!t.exists) continue;
+      const int row = t.kb + quad * 32 + lane;
+      const bool valid = row < T;
+      const int64_t orow = ((int64_t)t.bh * T + (valid ? row : 0)) * D;
+      if (t.n == 0) {  // no query of the first segment reaches these keys
+        if (valid && !p.accumulate_out) {
+          for (int d = 0; d < D; ++d) out[orow + d] = 0.0f;
+        }
+        continue;
       }
-    } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
+      float x0[32], x1[32];
+      {
+        const float* rp = src.row(t.b, t.h, valid ? row : 0);
+        const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(rp) & 15u) == 0);
+        load_row32(src, rp, 0, valid, vr, x0);
+        load_row32(src, rp, 32, valid, vr, x1);
+      }
+      if (pending && !(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
       tc_fence_after();
-      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid,
-                            p.accumulate_out != 0);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        x0[e] = tf32_round(x0[e]);
+        x1[e] = tf32_round(x1[e]);
+      }
+      const uint32_t kv = lb + (grp ? C::TC_V : C::TC_K);
+      tmem_st32(kv, x0);
+      tmem_st32(kv + 32, x1);
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive_remote(L(bars->rows_ready));
+      if (pending) write_out();
+      {  // the next tile's K / V row into L2 while this tile runs
+        PairTile nt;
+        for (int m2 = m + 1; m2 <= m + 2; ++m2) {
+          if (!pair_tile_at(p, cl, G, m2, rank, nt)) break;
+          if (!nt.exists || nt.n == 0) continue;
+          const int nrow = nt.kb + quad * 32 + lane;
+          if (nrow < T && src.s3 == 1) {
+            const float* np = src.row(nt.b, nt.h, nrow);
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(np));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(np + 32));
+          }
+          break;
+        }
+      }
+      for (int i = 0; ok && i < t.n; ++i) {
+        const int gi = g + i;
+        const int qs = (t.j0 + i) * BN + c0;
+        const int bi = gi % 2;
+        const uint32_t par = (uint32_t)(gi / 2) & 1u;
+        const uint32_t sc = lb + C::TC_S + (uint32_t)bi * C::SB + c0;
+        const uint32_t dc = lb + C::TC_DP + (uint32_t)bi * C::SB + c0;
+        if (!(ok = warp_wait(B(bars->vec_full[gi % NS]), (gi / NS) & 1, ctl, p.status))) break;
+        const float* vl = vec + (gi % NS) * 2 * BN + c0;
+        if (!(ok = warp_wait(B(bars->s_full[bi]), par, ctl, p.status))) break;
+        tc_fence_after();
+        const bool need_mask =
+            !valid || (qs + HB > T) || (p.causal && qs < t.kb + kRows - 1);
+        float pv[HB];
+        {
+          float x[HB], lv[HB];
+          tmem_ldn<HB>(sc, x);
+          load_vecn<HB>(vl, lv);  // -LSE * log2(e)
+#pragma unroll
+          for (int e = 0; e < HB; e += 2) {
+            float a0, a1;
+            ffma2(a0, a1, x[e], x[e + 1], p.scale_log2, p.scale_log2, lv[e], lv[e + 1]);
+            x[e] = ex2_approx(a0);
+            x[e + 1] = ex2_approx(a1);
+          }
+          if (need_mask) {
+#pragma unroll
+            for (int e = 0; e < HB; ++e) {
+              const int q = qs + e;
+              x[e] = (valid && q < T && (!p.causal || q >= row)) ? x[e] : 0.0f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < HB; ++e) {
+            pv[e] = x[e];
+            x[e] = tf32_round_finite(x[e]);
+          }
+          tmem_stn<HB>(sc, x);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive_remote(L(bars->p_full[bi]));  // S^T_i read, P^T_i written
+        if (!(ok = warp_wait(B(bars->dp_full[bi]), par, ctl, p.status))) break;
+        tc_fence_after();
+        {
+          float x[HB], dv[HB];
+          tmem_ldn<HB>(dc, x);
+          load_vecn<HB>(vl + BN, dv);
+#pragma unroll
+          for (int e = 0; e < HB; e += 2) {
+            float u0, u1, d0, d1;
+            fsub2(u0, u1, x[e], x[e + 1], dv[e], dv[e + 1]);
+            fmul2(d0, d1, pv[e], pv[e + 1], u0, u1);  // dS^T = P^T (dP^T - delta)
+            x[e] = tf32_round_finite(d0);
+            x[e + 1] = tf32_round_finite(d1);
+          }
+          tmem_stn<HB>(dc, x);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive_remote(L(bars->ds_full[bi]));
+      }
+      pending = ok;
+      prev_orow = orow;
+      prev_valid = valid;
+      g += t.n;
+      ++tn;
+    }
+    if (ok && pending && warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status)) {
+      tc_fence_after();
+      write_out();
     }
   }
 
@@ -438,12 +537,14 @@ int run_dkdv_pair(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Stri
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
   p.n_tiles = (int)((pr.T + 2 * kRows - 1) / (2 * kRows));  // 256-key pair tiles
-  const int64_t grid = 2 * (int64_t)p.n_tiles * p.bh_total;
+  const int64_t units = (int64_t)((p.n_tiles + 1) / 2) * p.bh_total;
+  // persistent: one cluster per two SMs (one CTA per SM fits), at most one per unit
+  const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(units, dev.sm_count / 2));
   for (int64_t s0 = 0; s0 < pr.T; s0 += kSegLen) {  // one launch per query segment
     p.seg_lo = (int)s0;
     p.seg_hi = (int)std::min<int64_t>(s0 + kSegLen, pr.T);
     p.accumulate_out = s0 > 0;
-    fa2_bwd_dkdv_pair_kernel<C><<<(unsigned)grid, kBwdThreads, smem, st>>>(tq, tg, p);
+    fa2_bwd_dkdv_pair_kernel<C><<<(unsigned)(2 * clusters), kBwdThreads, smem, st>>>(tq, tg, p);
     rc = check_launch();
     if (rc != CT_OK) return rc;
   }
