@@ -64,12 +64,16 @@ struct PairCfg {
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
+// Write-out staging: per row warp 32 rows x 16 columns, rows padded to 17
+// floats (conflict-free column writes and row reads).
+constexpr uint32_t kPairWbufFloats = 32 * 17;
+
 template <class C>
 constexpr size_t pair_smem_bytes() {
-  static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + (size_t)C::NS * 2 * C::BN * 4 <=
-                    227 * 1024,
-                "shared memory budget");
-  return 1024 + 1024 + (size_t)C::NS * C::STAGE + (size_t)C::NS * 2 * C::BN * 4;
+  constexpr size_t bytes = 1024 + 1024 + (size_t)C::NS * C::STAGE + (size_t)C::NS * 2 * C::BN * 4 +
+                           8 * kPairWbufFloats * 4;
+  static_assert(bytes <= 227 * 1024, "shared memory budget");
+  return bytes;
 }
 
 constexpr int kPairRowWarps = 16;  // both CTAs' row warps arrive on the even CTA's barriers
@@ -387,11 +391,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     // P_0 / dS_0, formed after the write-out).
     bool ok = true, pending = false;
     int g = 0, tn = 0;
-    int64_t prev_orow = 0;
-    bool prev_valid = false;
+    // dK / dV rows leave through a per-warp shared-memory buffer, 16 columns
+    // at a time, so each store instruction writes two 64-byte row segments
+    // (a thread storing its own row would scatter 16-byte pieces over 32 rows).
+    int64_t prev_row0 = 0;  // global row index (b h T + key) of this warp's first row
+    int prev_nrows = 0;     // rows of the warp that lie inside the sequence
+    float* wbuf = vec + NS * 2 * BN + (warp - 4 - (grp ? 3 : 0)) * kPairWbufFloats;
     auto write_out = [&]() {
-      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale,
-                            out + prev_orow, prev_valid, p.accumulate_out != 0);
+      const float scale = grp ? 1.0f : p.scale;
+      const uint32_t col = grp ? C::TC_DV : C::TC_DK;
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        float x[16];
+        tmem_ldn<16>(lb + col + 16 * c, x);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) wbuf[lane * 17 + e] = x[e] * scale;
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int r = 2 * k + (lane >> 4), cc = lane & 15;
+          if (r < prev_nrows) {
+            float* dst = out + (prev_row0 + r) * D + 16 * c + cc;
+            const float v = wbuf[r * 17 + cc];
+            *dst = p.accumulate_out ? *dst + v : v;
+          }
+        }
+        __syncwarp();
+      }
       tc_fence_before();  // TMEM reads done before the next arrival
     };
     PairTile t;
@@ -504,8 +530,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
         warp_arrive_remote(L(bars->ds_full[bi]));
       }
       pending = ok;
-      prev_orow = orow;
-      prev_valid = valid;
+      prev_row0 = (int64_t)t.bh * T + t.kb + quad * 32;
+      prev_nrows = max(0, min(32, T - (t.kb + quad * 32)));
       g += t.n;
       ++tn;
     }
