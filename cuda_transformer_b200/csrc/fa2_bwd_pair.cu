@@ -64,14 +64,10 @@ struct PairCfg {
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
-// Write-out staging: per row warp 32 rows x 16 columns, rows padded to 17
-// floats (conflict-free column writes and row reads).
-constexpr uint32_t kPairWbufFloats = 32 * 17;
-
 template <class C>
 constexpr size_t pair_smem_bytes() {
   constexpr size_t bytes = 1024 + 1024 + (size_t)C::NS * C::STAGE + (size_t)C::NS * 2 * C::BN * 4 +
-                           8 * kPairWbufFloats * 4;
+                           kRowWbufBytes;
   static_assert(bytes <= 227 * 1024, "shared memory budget");
   return bytes;
 }
@@ -391,33 +387,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     // P_0 / dS_0, formed after the write-out).
     bool ok = true, pending = false;
     int g = 0, tn = 0;
-    // dK / dV rows leave through a per-warp shared-memory buffer, 16 columns
-    // at a time, so each store instruction writes two 64-byte row segments
-    // (a thread storing its own row would scatter 16-byte pieces over 32 rows).
+    // dK / dV rows leave through a per-warp shared-memory buffer
+    // (warp_rows_to_global: coalesced stores).
     int64_t prev_row0 = 0;  // global row index (b h T + key) of this warp's first row
     int prev_nrows = 0;     // rows of the warp that lie inside the sequence
-    float* wbuf = vec + NS * 2 * BN + (warp - 4 - (grp ? 3 : 0)) * kPairWbufFloats;
+    float* wbuf = vec + NS * 2 * BN + (warp - 4 - (grp ? 3 : 0)) * kRowWbufFloats;
     auto write_out = [&]() {
-      const float scale = grp ? 1.0f : p.scale;
-      const uint32_t col = grp ? C::TC_DV : C::TC_DK;
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        float x[16];
-        tmem_ldn<16>(lb + col + 16 * c, x);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) wbuf[lane * 17 + e] = x[e] * scale;
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int r = 2 * k + (lane >> 4), cc = lane & 15;
-          if (r < prev_nrows) {
-            float* dst = out + (prev_row0 + r) * D + 16 * c + cc;
-            const float v = wbuf[r * 17 + cc];
-            *dst = p.accumulate_out ? *dst + v : v;
-          }
-        }
-        __syncwarp();
-      }
+      warp_rows_to_global<D>(lb + (grp ? C::TC_DV : C::TC_DK), grp ? 1.0f : p.scale, wbuf,
+                             out + prev_row0 * D, prev_nrows, D, p.accumulate_out != 0);
       tc_fence_before();  // TMEM reads done before the next arrival
     };
     PairTile t;

@@ -296,9 +296,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_cols_to_global<D / 2>(lb, C::TC_DQ + grp * (D / 2), p.scale,
-                                 p.out0 + ((int64_t)bh * T + (valid ? row : 0)) * D + grp * (D / 2),
-                                 valid, p.accumulate_out != 0);
+      // coalesced through the warp's shared-memory buffer
+      float* wbuf = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
+                                             NS * C::STAGE + NS * 2 * BN * 4) +
+                    (warp - 4 - (grp ? 3 : 0)) * kRowWbufFloats;
+      const int r0 = q0 + quad * 32;
+      warp_rows_to_global<D / 2>(lb + C::TC_DQ + grp * (D / 2), p.scale, wbuf,
+                                 p.out0 + ((int64_t)bh * T + r0) * D + grp * (D / 2),
+                                 max(0, min(32, T - r0)), D, p.accumulate_out != 0);
     }
   }
 
@@ -1140,7 +1145,7 @@ int run_dq(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 g,
   if (rc == CT_OK)
     rc = C::KILB ? make_tmap_bhtd(&tv, v, pr, C::BN) : make_tmap_bhtd_whole(&tv, v, pr, C::BN);
   if (rc != CT_OK) return rc;
-  const size_t smem = bwd_smem_bytes<C>();
+  const size_t smem = bwd_smem_bytes_wbuf<C>();
   rc = ensure_smem_attr(fa2_bwd_dq_tc_kernel<C>, smem, dev.device, &attr_done);
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, q, g, lse, ls, delta, dq, nullptr, dev);
