@@ -103,6 +103,13 @@ int launch_fa2_bwd_dkdv_pair(const Fa2Problem& p, Strided4 q, Strided4 k, Stride
                              const float* delta, float* dk, float* dv, const DeviceInfo& dev,
                              cudaStream_t st);
 bool fa2_bwd_pair_supported(const Fa2Problem& p);
+// Persistent dQ (TF32, head dim 64; fa2_bwd_dq_persist.cu): the default for
+// that case unless CT_FA2_PERSIST_DQ=0.
+int launch_fa2_bwd_dq_persist(const Fa2Problem& p, Strided4 q, Strided4 k, Strided4 v,
+                              Strided4 dO, const float* lse, const int64_t lse_s[3],
+                              const float* delta, float* dq, const DeviceInfo& dev,
+                              cudaStream_t st);
+bool fa2_bwd_dq_persist_supported(const Fa2Problem& p);
 // Whether the tensor-core kernels cover this problem (head dim / precision).
 bool fa2_fwd_tc_supported(const Fa2Problem& p);
 bool fa2_bwd_tc_supported(const Fa2Problem& p);

@@ -1234,6 +1234,8 @@ int launch_fa2_bwd_dq_tc(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 
                          const DeviceInfo& dev, cudaStream_t st) {
   if (!fa2_tma_ok(k) || !fa2_tma_ok(v)) return CT_ERR_UNSUPPORTED_LAYOUT;
   const bool split = pr.precision == CT_PRECISION_3XTF32;
+  if (fa2_bwd_dq_persist_supported(pr))  // TF32, D = 64: persistent CTAs
+    return launch_fa2_bwd_dq_persist(pr, q, k, v, g, lse, ls, delta, dq, dev, st);
   if (pr.D == 64)
     return split ? run_dq<DqCfg<64, 64, 3, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st)
                  : run_dq<DqCfg<64, 64, 1, 4, 2>>(pr, q, k, v, g, lse, ls, delta, dq, dev, st);

@@ -312,14 +312,15 @@ print("ONE_CTA_OK")
 
 @pytest.mark.gpu
 def test_one_cta_dkdv_tf32(cuda_device):
-    """TF32 at head dim 64 runs dK/dV on CTA pairs by default; CT_FA2_PAIR_DKDV=0
-    selects the one-CTA kernel.  The library reads the variable once, so the
-    one-CTA path runs in a child process, against the same oracle."""
+    """TF32 at head dim 64 runs dK/dV on persistent CTA pairs and dQ on
+    persistent CTAs by default; CT_FA2_PAIR_DKDV=0 and CT_FA2_PERSIST_DQ=0
+    select the one-CTA-per-tile kernels.  The library reads the variables once,
+    so those run in a child process, against the same oracle."""
     import os
     import subprocess
     import sys
 
-    env = dict(os.environ, CT_FA2_PAIR_DKDV="0")
+    env = dict(os.environ, CT_FA2_PAIR_DKDV="0", CT_FA2_PERSIST_DQ="0")
     r = subprocess.run([sys.executable, "-c", _ONE_CTA_CHILD], cwd=str(ROOT), env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ONE_CTA_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
