@@ -70,11 +70,6 @@ struct BwdParams {
   uint32_t* status;
 };
 
-// Row warps' write-out buffer: 32 rows x 16 columns per warp, rows padded to
-// 17 floats (conflict-free column writes and row reads); eight row warps.
-constexpr uint32_t kRowWbufFloats = 32 * 17;
-constexpr size_t kRowWbufBytes = 8 * (size_t)kRowWbufFloats * 4;
-
 // Bytes of the per-stage vector slots (log-sum-exp and delta of BN queries).
 template <class C>
 constexpr size_t bwd_vec_bytes() {
@@ -92,38 +87,6 @@ constexpr size_t bwd_smem_bytes() {
   static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>() <= 227 * 1024,
                 "shared memory budget");
   return 1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>();
-}
-
-// Writes TMEM columns [col, col + NC) of a row warp's 32 lanes (lane r = row
-// r), times `scale`, to rows 0 .. nrows-1 of `out` (row stride ld floats),
-// 16 columns at a time through the warp's buffer: each store instruction then
-// writes two 64-byte row segments, where a thread storing its own row would
-// scatter 16-byte pieces over 32 rows.  `accumulate` adds to what out holds.
-// All 32 lanes call it.
-template <int NC>
-__device__ __forceinline__ void warp_rows_to_global(uint32_t col, float scale, float* wbuf,
-                                                    float* out, int nrows, int64_t ld,
-                                                    bool accumulate) {
-  static_assert(NC % 16 == 0, "column count");
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int c = 0; c < NC / 16; ++c) {
-    float x[16];
-    tmem_ld16(col + 16 * c, x);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) wbuf[lane * 17 + e] = x[e] * scale;
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int r = 2 * k + (lane >> 4), cc = lane & 15;
-      if (r < nrows) {
-        float* dst = out + (int64_t)r * ld + 16 * c + cc;
-        const float v = wbuf[r * 17 + cc];
-        *dst = accumulate ? *dst + v : v;
-      }
-    }
-    __syncwarp();
-  }
 }
 
 // empty_count: MMA issuers that read a stage; done_count: issuers whose

@@ -221,6 +221,43 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t lane_base, uint32_t 
   tmem_cols_to_global<D>(lane_base, col, scale, dst, valid, add_partial);
 }
 
+// Row warps' write-out buffer: 32 rows x 16 columns per warp, rows padded to
+// 17 floats (conflict-free column writes and row reads); eight row warps.
+constexpr uint32_t kRowWbufFloats = 32 * 17;
+constexpr size_t kRowWbufBytes = 8 * (size_t)kRowWbufFloats * 4;
+
+// Writes TMEM columns [col, col + NC) of a row warp's 32 lanes (lane r = row
+// r), times `scale`, to rows 0 .. nrows-1 of `out` (row stride ld floats),
+// 16 columns at a time through the warp's buffer: each store instruction then
+// writes two 64-byte row segments, where a thread storing its own row would
+// scatter 16-byte pieces over 32 rows.  `accumulate` adds to what out holds.
+// `scale` may differ per lane (row).  All 32 lanes call it.
+template <int NC>
+__device__ __forceinline__ void warp_rows_to_global(uint32_t col, float scale, float* wbuf,
+                                                    float* out, int nrows, int64_t ld,
+                                                    bool accumulate) {
+  static_assert(NC % 16 == 0, "column count");
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < NC / 16; ++c) {
+    float x[16];
+    tmem_ld16(col + 16 * c, x);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) wbuf[lane * 17 + e] = x[e] * scale;
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int r = 2 * k + (lane >> 4), cc = lane & 15;
+      if (r < nrows) {
+        float* dst = out + (int64_t)r * ld + 16 * c + cc;
+        const float v = wbuf[r * 17 + cc];
+        *dst = accumulate ? *dst + v : v;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // Long reductions.  The tensor core adds each MMA's products into its FP32
 // accumulator with a rounding biased toward zero: the relative error of a
 // gradient grows with the reduction length (measured in 3xTF32: ~4e-5 at

@@ -472,41 +472,66 @@ struct FwdPairCfg {
 template <int NS>
 struct FwdPairBars {
   uint64_t full_k[NS], full_v[NS], ready_k[NS], ready_v[NS], empty_k[NS], empty_v[NS];
-  uint64_t s_full[2][2], p_full[2][2], pv_done[2], o_done[2], q_ready, mma_final[2];
+  uint64_t s_full[2][2], p_full[2][2], pv_done[2], o_done[2], q_ready[2], mma_final[2];
   CtaCtl ctl;
 };
 
 template <class C>
-constexpr size_t fwd_pair_smem_bytes() {
+constexpr size_t fwd_pair_smem_bytes() {  // with the row warps' write-out buffer
   constexpr size_t head = (sizeof(FwdPairBars<C::NS>) + 1023) / 1024 * 1024 + 1024;
-  static_assert(head + (size_t)C::NS * C::STAGE <= 227 * 1024, "shared memory budget");
-  return head + (size_t)C::NS * C::STAGE;
+  static_assert(head + (size_t)C::NS * C::STAGE + kRowWbufBytes <= 227 * 1024,
+                "shared memory budget");
+  return head + (size_t)C::NS * C::STAGE + kRowWbufBytes;
 }
 
+// One unit tile of a persistent CTA: query-tile pair qp of head bh (tiles A
+// and B, rows q0 .. q0 + 255), with n_a / n_b key tiles each and n_kv the
+// larger.
+struct FwdUnitTile {
+  int b, h, bh, q0, n_a, n_b, n_kv;
+};
+// Tile m of CTA c (of G): half m % 2 of unit c + (m / 2) G, a unit being the
+// tile pairs (qp, NQ-1-qp) of one head (NQ pairs per head), whose causal key
+// counts add up to the same total for every qp.  Returns false past the CTA's
+// last unit and skips the missing half of the middle unit when NQ is odd.
+__device__ __forceinline__ bool fwd_tile_at(const FwdParams& p, int c, int G, int& m,
+                                            FwdUnitTile& u) {
+  constexpr int BN = 64;
+  const int U = (p.n_qt + 1) / 2;
+  for (;; ++m) {
+    const int un = c + (m >> 1) * G;
+    if (un >= U * p.bh_total) return false;
+    int k;
+    cta_tile_at((unsigned)un, U, p.bh_total, p.head_group, false, k, u.bh);
+    const int qp = (m & 1) ? p.n_qt - 1 - k : k;
+    if ((m & 1) && qp == k) continue;
+    u.b = u.bh / p.H;
+    u.h = u.bh % p.H;
+    u.q0 = qp * 2 * kRows;
+    auto steps = [&](int t) {
+      const int last = min(u.q0 + (t + 1) * kRows - 1, p.T - 1);
+      return p.causal ? last / BN + 1 : (p.T + BN - 1) / BN;
+    };
+    u.n_a = steps(0);
+    u.n_b = steps(1);
+    u.n_kv = max(u.n_a, u.n_b);
+    return true;
+  }
+}
+
+// Persistent: each CTA loops over unit tiles; the producer and rounding warps
+// run across tile boundaries (one step counter for the stage ring).
 template <class C>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fa2_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   constexpr int D = C::D, BN = C::BN, NS = C::NS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  if (status_raised(p.status)) return;
   auto* bars = reinterpret_cast<FwdPairBars<NS>*>(smem_raw);
   const uint32_t tiles = (smem_u32(smem_raw) + (uint32_t)sizeof(FwdPairBars<NS>) + 1023u) & ~1023u;
   CtaCtl* ctl = &bars->ctl;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-  // Head-major order (L2 reuse of K / V), last query-tile pairs of a head first.
-  int qp, bh;
-  cta_tile(p.n_qt, p.bh_total, p.head_group, true, qp, bh);
-  const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qp * 2 * kRows;  // tile t covers rows q0 + t * 128 ..
-  const int T = p.T;
-  auto steps = [&](int t) {  // key tiles query tile t reads
-    const int last = min(q0 + (t + 1) * kRows - 1, T - 1);
-    return p.causal ? last / BN + 1 : (T + BN - 1) / BN;
-  };
-  const int n_a = steps(0), n_b = steps(1);
-  const int n_kv = max(n_a, n_b);
+  const int T = p.T, G = (int)gridDim.x, cta = (int)blockIdx.x;
 
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   if (threadIdx.x == 0) {
@@ -526,8 +551,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(B(bars->pv_done[t]), 1);
       mbar_init(B(bars->o_done[t]), 1);
       mbar_init(B(bars->mma_final[t]), 1);
+      mbar_init(B(bars->q_ready[t]), 4);  // the tile's row warps
     }
-    mbar_init(B(bars->q_ready), 8);  // all row warps
     ctl->abort = 0;
     fence_barrier_init();
   }
@@ -547,17 +572,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tmV);
       int last_k[NS], last_v[NS];
       for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % NS, r = j / NS;
-        const uint32_t st = tiles + s * C::STAGE;
-        if (r > 0 && !mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status)) break;
-        mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
-        tma_load_tile<true, D>(st + C::OFF_K, &tmK, B(bars->full_k[s]), j * BN, h, b, BN * 128u);
-        last_k[s] = r;
-        if (r > 0 && !mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status)) break;
-        mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
-        tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_v[s]), j * BN, h, b, BN * 128u);
-        last_v[s] = r;
+      bool ok = true;
+      int g = 0;
+      FwdUnitTile u;
+      for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
+        for (int j = 0; j < u.n_kv; ++j) {
+          const int gs = g + j, s = gs % NS, r = gs / NS;
+          const uint32_t st = tiles + s * C::STAGE;
+          if (r > 0 && !(ok = mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status))) break;
+          mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
+          tma_load_tile<true, D>(st + C::OFF_K, &tmK, B(bars->full_k[s]), j * BN, u.h, u.b,
+                                 BN * 128u);
+          last_k[s] = r;
+          if (r > 0 && !(ok = mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status))) break;
+          mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
+          tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_v[s]), j * BN, u.h, u.b,
+                                 BN * 128u);
+          last_v[s] = r;
+        }
+        g += u.n_kv;
       }
       if (ctl->abort) {  // let every issued copy land before the CTA exits
         for (int s = 0; s < NS; ++s) {
@@ -570,45 +603,57 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 1 || warp == kIssuer2Warp) {
     // ------------------------------------- tile t's issuer: S, then P.V
     // Past its last key tile a tile still releases the stages (commits with
-    // nothing new in flight), so the producer's two-issuer count holds.
+    // nothing new in flight), so the producer's two-issuer count holds.  g
+    // counts the CTA's key steps (stage ring), gt this tile's own steps (S /
+    // P buffers, pv_done); per unit tile: wait for the rows' Q (q_ready),
+    // commit o_done after the last P.V.
     if (lane == 0) {
       const int t = warp == 1 ? 0 : 1;
-      const int n_mine = t ? n_b : n_a;
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
       constexpr uint32_t idO = idesc_tf32(128, D, false, true);
       const uint64_t kd0 = sdesc_kmajor(tiles + C::OFF_K);
       const uint64_t vd0 = sdesc_mnmajor(tiles + C::OFF_V, BN * 128);
       const uint32_t sb0 = tmem + C::TC_S + (uint32_t)(2 * t) * BN;
-      auto issue_S = [&](int j) -> bool {  // S_t(j) into buffer j % 2
-        const int s = j % NS;
-        if (j < n_mine) {
-          if (!mbar_wait(B(bars->ready_k[s]), (j / NS) & 1, ctl, p.status)) return false;
-          tc_fence_after();
-          mma_chain<1, D, false, BN, C::TILE>(sb0 + (uint32_t)(j & 1) * BN,
-                                              tmem + C::TC_Q + (uint32_t)t * D, 0,
-                                              kd0 + (s * C::STAGE >> 4), idS, false);
-          umma_commit(B(bars->s_full[t][j & 1]));
+      bool ok = true;
+      int g = 0, gt = 0, tn = 0;
+      FwdUnitTile u;
+      for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
+        const int n_mine = t ? u.n_b : u.n_a, n_kv = u.n_kv;
+        auto issue_S = [&](int j) -> bool {  // S_t(j) into buffer (gt + j) % 2
+          const int gs = g + j, s = gs % NS;
+          if (j < n_mine) {
+            if (!mbar_wait(B(bars->ready_k[s]), (gs / NS) & 1, ctl, p.status)) return false;
+            tc_fence_after();
+            mma_chain<1, D, false, BN, C::TILE>(sb0 + (uint32_t)((gt + j) & 1) * BN,
+                                                tmem + C::TC_Q + (uint32_t)t * D, 0,
+                                                kd0 + (s * C::STAGE >> 4), idS, false);
+            umma_commit(B(bars->s_full[t][(gt + j) & 1]));
+          }
+          umma_commit(B(bars->empty_k[s]));
+          return true;
+        };
+        ok = mbar_wait(B(bars->q_ready[t]), tn & 1, ctl, p.status) && issue_S(0) &&
+             (n_kv < 2 || issue_S(1));
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int gs = g + j, s = gs % NS;
+          if (j < n_mine) {
+            const int gb = gt + j;
+            if (!(ok = mbar_wait(B(bars->p_full[t][gb & 1]), (gb >> 1) & 1, ctl, p.status))) break;
+            if (!(ok = mbar_wait(B(bars->ready_v[s]), (gs / NS) & 1, ctl, p.status))) break;
+            tc_fence_after();
+            mma_chain<1, BN, true, BN, C::TILE>(tmem + C::TC_O + (uint32_t)t * D,
+                                                sb0 + (uint32_t)(gb & 1) * BN, 0,
+                                                vd0 + (s * C::STAGE >> 4), idO, j > 0);
+            umma_commit(B(bars->pv_done[t]));
+          }
+          umma_commit(B(bars->empty_v[s]));
+          if (j + 2 < n_kv && !(ok = issue_S(j + 2))) break;
         }
-        umma_commit(B(bars->empty_k[s]));
-        return true;
-      };
-      bool ok = mbar_wait(B(bars->q_ready), 0, ctl, p.status) && issue_S(0) &&
-                (n_kv < 2 || issue_S(1));
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % NS;
-        if (j < n_mine) {
-          if (!(ok = mbar_wait(B(bars->p_full[t][j & 1]), (j >> 1) & 1, ctl, p.status))) break;
-          if (!(ok = mbar_wait(B(bars->ready_v[s]), (j / NS) & 1, ctl, p.status))) break;
-          tc_fence_after();
-          mma_chain<1, BN, true, BN, C::TILE>(tmem + C::TC_O + (uint32_t)t * D,
-                                              sb0 + (uint32_t)(j & 1) * BN, 0,
-                                              vd0 + (s * C::STAGE >> 4), idO, j > 0);
-          umma_commit(B(bars->pv_done[t]));
-        }
-        umma_commit(B(bars->empty_v[s]));
-        if (j + 2 < n_kv && !(ok = issue_S(j + 2))) break;
+        if (ok) umma_commit(B(bars->o_done[t]));
+        g += n_kv;
+        gt += n_mine;
+        ++tn;
       }
-      if (ok) umma_commit(B(bars->o_done[t]));
       umma_commit(B(bars->mma_final[t]));  // nothing of this thread in flight after this
       mbar_drain(B(bars->mma_final[t]), 0);
     }
@@ -616,17 +661,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (is_prep_warp(warp)) {
     // ----------------------------------------------- TF32 rounding warps
     const uint32_t tid = prep_tid();
-    for (int j = 0; j < n_kv; ++j) {
-      const int s = j % NS, r = j / NS;
-      const uint32_t st = tiles + s * C::STAGE;
-      if (!warp_wait(B(bars->full_k[s]), r & 1, ctl, p.status)) break;
-      round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_K, tid);
-      fence_proxy_async_smem();
-      warp_arrive(B(bars->ready_k[s]));
-      if (!warp_wait(B(bars->full_v[s]), r & 1, ctl, p.status)) break;
-      round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_V, tid);
-      fence_proxy_async_smem();
-      warp_arrive(B(bars->ready_v[s]));
+    bool ok = true;
+    int g = 0;
+    FwdUnitTile u;
+    for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
+      for (int j = 0; j < u.n_kv; ++j) {
+        const int gs = g + j, s = gs % NS, r = gs / NS;
+        const uint32_t st = tiles + s * C::STAGE;
+        if (!(ok = warp_wait(B(bars->full_k[s]), r & 1, ctl, p.status))) break;
+        round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_K, tid);
+        fence_proxy_async_smem();
+        warp_arrive(B(bars->ready_k[s]));
+        if (!(ok = warp_wait(B(bars->full_v[s]), r & 1, ctl, p.status))) break;
+        round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_V, tid);
+        fence_proxy_async_smem();
+        warp_arrive(B(bars->ready_v[s]));
+      }
+      g += u.n_kv;
     }
   } else {
     // --------------------------------------------------------- row warps
@@ -634,92 +685,134 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // query row quad*32 + lane of its tile (TMEM lane quarter quad) and all
     // BN score columns of a step, kept in registers between the maximum and
     // the exponentials.
+    // Unit-tile boundary: the next Q row is loaded into registers before the
+    // wait for the previous tile's o_done; once that completes (no MMA reads
+    // Q_t any more) it goes into TMEM and q_ready lets the tile's issuer start
+    // S while the rows write out the previous O_t and LSE (the first P.V,
+    // which overwrites the accumulator, waits for P(0), formed after the
+    // write-out).
     const int t = warp >= kFwdRowWarp1 ? 1 : 0;
-    const int n_mine = t ? n_b : n_a;
     const int quad = warp & 3;
-    const int qt0 = q0 + t * kRows;
-    const int row = qt0 + quad * 32 + lane;
-    const bool valid = row < T;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
-    const uint32_t sc0 = lb + C::TC_S + (uint32_t)(2 * t) * BN;
-    const uint32_t oc = lb + C::TC_O + (uint32_t)t * D;
-    {
-      const float* qrow = p.q.row(b, h, valid ? row : 0);
-      const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
-      row_to_tmem<D, 1>(p.q, qrow, valid, vec, lb, C::TC_Q + (uint32_t)t * D);
-      tmem_wait_st();
-      tc_fence_before();
-      warp_arrive(B(bars->q_ready));
-    }
-    float m_used = -INFINITY, l = 0.0f;
-    bool ok = true;
-    for (int j = 0; ok && j < n_mine; ++j) {
-      const int bb = j & 1;
-      const uint32_t sc = sc0 + (uint32_t)bb * BN;
-      if (!(ok = warp_wait(B(bars->s_full[t][bb]), (j >> 1) & 1, ctl, p.status))) break;
-      tc_fence_after();
-      const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > qt0);
-      float sv[BN];
-      float mraw = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float x[32];
-        tmem_ld32(sc + 32 * c, x);
-        if (need_mask) mask_cols32(x, kv0 + 32 * c, T, p.causal, row);
-        mraw = fmaxf(mraw, max32(x));
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[32 * c + i] = x[i];
-      }
-      // scale_log2 > 0, so scaling after the maximum is exact
-      const float m_new = fmaxf(m_used, mraw * p.scale_log2);
-      const bool resc = m_new > m_used + 8.0f;
-      const bool any_resc = __any_sync(0xffffffffu, resc);
-      const float alpha = resc ? ex2_approx(m_used - m_new) : 1.0f;
-      if (resc) m_used = m_new;
-      l *= alpha;
-      const float neg_m = -m_used;
-      float ls0 = 0.0f, ls1 = 0.0f;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float x[32];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float a0, a1;
-          ffma2(a0, a1, sv[32 * c + i], sv[32 * c + i + 1], p.scale_log2, p.scale_log2, neg_m,
-                neg_m);
-          const float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
-          fadd2(ls0, ls1, ls0, ls1, e0, e1);
-          x[i] = tf32_round_finite(e0);
-          x[i + 1] = tf32_round_finite(e1);
-        }
-        tmem_st32(sc + 32 * c, x);
-      }
-      l += ls0 + ls1;
-      // O_t rescaled to the new maximum once O_t += P_t(j-1) V_{j-1} is done
-      // (the scores are out of the registers by now)
-      if (any_resc && j > 0) {
-        if (!(ok = warp_wait(B(bars->pv_done[t]), (j - 1) & 1, ctl, p.status))) break;
+    float* wbuf = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
+                                           NS * C::STAGE) +
+                  (t * 4 + quad) * kRowWbufFloats;
+    bool ok = true, pending = false;
+    int gt = 0, tn = 0;
+    int64_t prev_row0 = 0;
+    int prev_nrows = 0;
+    bool prev_valid = false;
+    int64_t prev_lse = 0;
+    float prev_inv_l = 0.0f, prev_lse_val = 0.0f;
+    auto write_out = [&]() {
+      warp_rows_to_global<D>(lb + C::TC_O + (uint32_t)t * D, prev_inv_l, wbuf,
+                             p.o + prev_row0 * D, prev_nrows, D, false);
+      if (prev_valid) p.lse[prev_lse] = prev_lse_val;
+      tc_fence_before();  // TMEM reads done before the next arrival
+    };
+    FwdUnitTile u;
+    for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
+      const int n_mine = t ? u.n_b : u.n_a;
+      const int qt0 = u.q0 + t * kRows;
+      const int row = qt0 + quad * 32 + lane;
+      const bool valid = row < T;
+      const uint32_t sc0 = lb + C::TC_S + (uint32_t)(2 * t) * BN;
+      const uint32_t oc = lb + C::TC_O + (uint32_t)t * D;
+      {
+        const float* qrow = p.q.row(u.b, u.h, valid ? row : 0);
+        const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
+        float x0[32];
+        load_row32(p.q, qrow, 0, valid, vec, x0);
+        if (pending && !(ok = warp_wait(B(bars->o_done[t]), (tn - 1) & 1, ctl, p.status))) break;
         tc_fence_after();
+        const uint32_t qa = lb + C::TC_Q + (uint32_t)t * D;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          float ov[32];
-          tmem_ld32(oc + 32 * c, ov);
+          if (c > 0) load_row32(p.q, qrow, 32 * c, valid, vec, x0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(oc + 32 * c, ov);
+          for (int e = 0; e < 32; ++e) x0[e] = tf32_round(x0[e]);
+          tmem_st32(qa + 32 * c, x0);
         }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive(B(bars->q_ready[t]));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      warp_arrive(B(bars->p_full[t][bb]));
+      if (pending) write_out();
+      float m_used = -INFINITY, l = 0.0f;
+      for (int j = 0; ok && j < n_mine; ++j) {
+        const int gb = gt + j, bb = gb & 1;
+        const uint32_t sc = sc0 + (uint32_t)bb * BN;
+        if (!(ok = warp_wait(B(bars->s_full[t][bb]), (gb >> 1) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        const int kv0 = j * BN;
+        const bool need_mask = (kv0 + BN > T) || (p.causal && kv0 + BN - 1 > qt0);
+        float sv[BN];
+        float mraw = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32];
+          tmem_ld32(sc + 32 * c, x);
+          if (need_mask) mask_cols32(x, kv0 + 32 * c, T, p.causal, row);
+          mraw = fmaxf(mraw, max32(x));
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[32 * c + i] = x[i];
+        }
+        // scale_log2 > 0, so scaling after the maximum is exact
+        const float m_new = fmaxf(m_used, mraw * p.scale_log2);
+        const bool resc = m_new > m_used + 8.0f;
+        const bool any_resc = __any_sync(0xffffffffu, resc);
+        const float alpha = resc ? ex2_approx(m_used - m_new) : 1.0f;
+        if (resc) m_used = m_new;
+        l *= alpha;
+        const float neg_m = -m_used;
+        float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float a0, a1;
+            ffma2(a0, a1, sv[32 * c + i], sv[32 * c + i + 1], p.scale_log2, p.scale_log2, neg_m,
+                  neg_m);
+            const float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
+            fadd2(ls0, ls1, ls0, ls1, e0, e1);
+            x[i] = tf32_round_finite(e0);
+            x[i + 1] = tf32_round_finite(e1);
+          }
+          tmem_st32(sc + 32 * c, x);
+        }
+        l += ls0 + ls1;
+        // O_t rescaled to the new maximum once O_t += P_t(j-1) V_{j-1} is done
+        // (the scores are out of the registers by now)
+        if (any_resc && j > 0) {
+          if (!(ok = warp_wait(B(bars->pv_done[t]), (gb - 1) & 1, ctl, p.status))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            tmem_ld32(oc + 32 * c, ov);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(oc + 32 * c, ov);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive(B(bars->p_full[t][bb]));
+      }
+      pending = ok;
+      prev_row0 = (int64_t)u.bh * T + qt0 + quad * 32;
+      prev_nrows = max(0, min(32, T - (qt0 + quad * 32)));
+      prev_valid = valid;
+      prev_lse = (int64_t)u.bh * T + row;
+      prev_inv_l = 1.0f / l;
+      prev_lse_val = (m_used + log2f(l)) * kLn2;
+      gt += n_mine;
+      ++tn;
     }
-    if (ok && warp_wait(B(bars->o_done[t]), 0, ctl, p.status)) {
+    if (ok && pending && warp_wait(B(bars->o_done[t]), (tn - 1) & 1, ctl, p.status)) {
       tc_fence_after();
-      const float inv_l = 1.0f / l;
-      float* orow = p.o + ((int64_t)bh * T + (valid ? row : 0)) * D;
-      tmem_cols_to_global<D>(lb, C::TC_O + (uint32_t)t * D, inv_l, orow, valid);
-      if (valid) p.lse[(int64_t)bh * T + row] = (m_used + log2f(l)) * kLn2;
+      write_out();
     }
   }
 
@@ -755,7 +848,9 @@ int run_fwd_pair(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, float
   p.causal = pr.causal ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)pr.D));
   p.status = dev.status;
-  const int64_t grid = (int64_t)p.n_qt * p.bh_total;
+  // persistent: one CTA per SM (one fits), at most one per unit
+  const int64_t units = (int64_t)((p.n_qt + 1) / 2) * p.bh_total;
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units, dev.sm_count));
   fa2_fwd_pair_kernel<C><<<(unsigned)grid, kFwdThreads, smem, st>>>(tmK, tmV, p);
   return check_launch();
 }
