@@ -286,23 +286,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       const float* rp = src.row(t.b, t.h, valid ? row : 0);
       const bool vr = src.s3 == 1 && ((reinterpret_cast<uintptr_t>(rp) & 15u) == 0);
-      float x0[32];
+      float x0[32], x1[32];
       load_row32(src, rp, 0, valid, vr, x0);
+      load_row32(src, rp, 32, valid, vr, x1);
       float l2 = 0.0f, dl = 0.0f;
       if (valid) {
-        l2 = __ldg(p.lse + t.b * p.l0 + t.h * p.l1 + (int64_t)row * p.l2) * kLog2e;
-        dl = __ldg(p.delta + (int64_t)t.bh * T + row);
+        l2 = ldg_nc_early(p.lse + t.b * p.l0 + t.h * p.l1 + (int64_t)row * p.l2);
+        dl = ldg_nc_early(p.delta + (int64_t)t.bh * T + row);
       }
       if (pending && !(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
       tc_fence_after();
+      l2 *= kLog2e;
       const uint32_t qa = lb + (grp ? C::TC_G : C::TC_Q);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) x0[e] = tf32_round(x0[e]);
+      for (int e = 0; e < 32; ++e) {
+        x0[e] = tf32_round(x0[e]);
+        x1[e] = tf32_round(x1[e]);
+      }
       tmem_st32(qa, x0);
-      load_row32(src, rp, 32, valid, vr, x0);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) x0[e] = tf32_round(x0[e]);
-      tmem_st32(qa + 32, x0);
+      tmem_st32(qa + 32, x1);
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(B(bars->rows_ready));

@@ -721,17 +721,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       {
         const float* qrow = p.q.row(u.b, u.h, valid ? row : 0);
         const bool vec = p.q.s3 == 1 && ((reinterpret_cast<uintptr_t>(qrow) & 15u) == 0);
-        float x0[32];
-        load_row32(p.q, qrow, 0, valid, vec, x0);
+        float xq[D / 32][32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) load_row32(p.q, qrow, 32 * c, valid, vec, xq[c]);
         if (pending && !(ok = warp_wait(B(bars->o_done[t]), (tn - 1) & 1, ctl, p.status))) break;
         tc_fence_after();
         const uint32_t qa = lb + C::TC_Q + (uint32_t)t * D;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          if (c > 0) load_row32(p.q, qrow, 32 * c, valid, vec, x0);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) x0[e] = tf32_round(x0[e]);
-          tmem_st32(qa + 32 * c, x0);
+          for (int e = 0; e < 32; ++e) xq[c][e] = tf32_round(xq[c][e]);
+          tmem_st32(qa + 32 * c, xq[c]);
         }
         tmem_wait_st();
         tc_fence_before();
