@@ -48,6 +48,10 @@ METRIC = "FA2 fwd+bwd TFLOPS (B4,H32,N4096,D64) at 1/2/4/8 B200; % of TF32 peak"
 # kernel's algorithmic bytes: reads Q, K, V, dO (4 x 128 MiB) + LSE, delta, writes dK, dV.
 DKDV_TRAFFIC_BYTES = 2 * 377.0e6
 # the dK/dV kernel instance that capture measured (recaptured whenever it changes)
+# kind::tf32 tensor-pipe ceiling on this pool's B200s, TFLOP/s: N >= 128 MMAs
+# issued back to back on every SM by the test-only probe ct_diag_mma_rate
+# (tests/diag); a tighter denominator than half the BF16 GEMM rate.
+TF32_PIPE_CEILING = 1190.0
 DKDV_TRAFFIC_KERNEL = "fa2_bwd_dkdv_tc_kernel<DkvCfg<64, 32, 3, 3>> (3xTF32, D = 64)"
 DKDV_ALGO_BYTES = 4 * 134217728 + 2 * 2097152 + 2 * 134217728
 WORKLOAD = "FA2 fwd+bwd B4 H32 N4096 D64 causal fp32 (BASELINE config 2)"
@@ -571,6 +575,7 @@ def main() -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp32", "precision": args.precision,
             "frac_of_tf32_peak": value / tf32_peak,
+            "frac_of_tf32_pipe_ceiling": value / TF32_PIPE_CEILING,
             "data": "synthetic: Q, K, V, dO ~ N(0,1) fp32, seeded per (b,h) slice",
             "config": {"workload": WORKLOAD, "B": B_FULL, "H": H_FULL, "N": N, "D": D,
                        "causal": CAUSAL, "pairs_per_rank": pairs,
@@ -591,7 +596,9 @@ def main() -> None:
             "alt_precision": {"precision": "tf32" if alt == cb.PRECISION_TF32 else "3xtf32",
                               "value": value_alt, "unit": "TFLOPS",
                               "ms_per_step": ms_alt / max(5, args.steps // 2),
-                              "frac_of_tf32_peak": value_alt / tf32_peak, "kernel_ms": kern_alt},
+                              "frac_of_tf32_peak": value_alt / tf32_peak,
+                              "frac_of_tf32_pipe_ceiling": value_alt / TF32_PIPE_CEILING,
+                              "kernel_ms": kern_alt},
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -75,6 +75,13 @@ template <class C>
 constexpr size_t bwd_vec_bytes() {
   return (size_t)C::NS * 2 * C::BN * sizeof(float);
 }
+// Whether the row warps' write-out buffer fits beside the stage ring.
+template <class C>
+__host__ __device__ constexpr bool bwd_wbuf_fits() {
+  return 1024 + 1024 + (size_t)C::NS * C::STAGE + (size_t)C::NS * 2 * C::BN * sizeof(float) +
+             kRowWbufBytes <=
+         227 * 1024;
+}
 template <class C>
 constexpr size_t bwd_smem_bytes_wbuf() {  // with the row warps' write-out buffer
   static_assert(1024 + 1024 + (size_t)C::NS * C::STAGE + bwd_vec_bytes<C>() + kRowWbufBytes <=

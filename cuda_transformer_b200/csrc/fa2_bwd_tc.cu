@@ -693,8 +693,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (ok && warp_wait(B(bars->done), 0, ctl, p.status)) {
       tc_fence_after();
-      tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow, valid,
-                            p.accumulate_out != 0);
+      if constexpr (bwd_wbuf_fits<C>()) {  // coalesced through the warp's buffer
+        float* wbuf = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)) +
+                                               NS * C::STAGE + NS * 2 * BN * 4) +
+                      (warp - 4 - (grp ? 3 : 0)) * kRowWbufFloats;
+        const int r0 = k0 + quad * 32;
+        warp_rows_to_global<D>(lb + (grp ? C::TC_DV : C::TC_DK), grp ? 1.0f : p.scale, wbuf,
+                               out + ((int64_t)bh * T + r0) * D, max(0, min(32, T - r0)), D,
+                               p.accumulate_out != 0);
+      } else {
+        tmem_row_to_global<D>(lb, grp ? C::TC_DV : C::TC_DK, grp ? 1.0f : p.scale, out + orow,
+                              valid, p.accumulate_out != 0);
+      }
     }
   }
 
@@ -1172,7 +1182,8 @@ int run_dkdv(const Fa2Problem& pr, Strided4 q, Strided4 k, Strided4 v, Strided4 
     rc = C::KILB ? make_tmap_bhtd(&tg, g, pr, C::BN)
                  : make_tmap_bhtd_whole(&tg, g, pr, C::BN, C::BMN);
   if (rc != CT_OK) return rc;
-  const size_t smem = bwd_smem_bytes<C>();
+  size_t smem = bwd_smem_bytes<C>();
+  if constexpr (bwd_wbuf_fits<C>()) smem = bwd_smem_bytes_wbuf<C>();
   rc = ensure_smem_attr(fa2_bwd_dkdv_tc_kernel<C>, smem, dev.device, &attr_done);
   if (rc != CT_OK) return rc;
   BwdParams p = make_params(pr, k, v, lse, ls, delta, dk, dv, dev);
