@@ -248,10 +248,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // [32g, 32g + 32) of every step, loads Q (g = 0) or dO (g = 1) into TMEM,
     // and writes dQ columns [32g, 32g + 32).
     // Tile boundary: the next tile's Q / dO row (and the row's LSE and delta)
-    // is loaded into registers before the wait for the previous tile's
-    // `done`; once that completes (no MMA reads Q / dO any more) it goes into
-    // TMEM and rows_ready lets the S and dP issuers start while the rows write
-    // out the previous dQ (the first dQ MMA, which overwrites the
+    // goes into TMEM as soon as the previous tile's last S and dP have
+    // completed, and rows_ready lets the S and dP issuers start while the
+    // previous tile's dQ MMAs drain; the rows then wait for its `done` and
+    // write out the previous dQ (the first dQ MMA, which overwrites the
     // accumulator, waits for dS_0, formed after the write-out).
     constexpr int HB = BN / 2;
     const int quad = warp & 3;
@@ -294,7 +294,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         l2 = ldg_nc_early(p.lse + t.b * p.l0 + t.h * p.l1 + (int64_t)row * p.l2);
         dl = ldg_nc_early(p.delta + (int64_t)t.bh * T + row);
       }
-      if (pending && !(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
+      // No wait for the previous tile's `done` here: only its S and dP MMAs read
+      // Q / dO, and this warp saw them complete (s_full, dp_full of its last
+      // step); the previous dQ accumulator is written out after rows_ready.
       tc_fence_after();
       l2 *= kLog2e;
       const uint32_t qa = lb + (grp ? C::TC_G : C::TC_Q);
@@ -308,7 +310,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(B(bars->rows_ready));
-      if (pending) write_out();
+      if (pending) {
+        if (!(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        write_out();
+      }
       {  // the next tile's row into L2 while this tile runs
         DqTile nt;
         for (int m2 = m + 1; m2 <= m + 2; ++m2) {

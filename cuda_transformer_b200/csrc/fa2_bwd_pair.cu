@@ -379,12 +379,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
     const Ptr4& src = grp ? p.st1 : p.st0;
     float* out = grp ? p.out1 : p.out0;
-    // Tile boundary: the next tile's K / V row is loaded into registers
-    // before the wait for the previous tile's `done`; once that completes
-    // (no MMA reads K / V any more) it goes into TMEM and rows_ready lets the
-    // issuers start S^T_0 / dP^T_0 while the rows write out the previous dK /
-    // dV (the first dV / dK MMAs, which overwrite the accumulators, wait for
-    // P_0 / dS_0, formed after the write-out).
+    // Tile boundary: the next tile's K / V row goes into TMEM as soon as the
+    // previous tile's last S^T and dP^T have completed, and rows_ready lets
+    // the issuers start S^T_0 / dP^T_0 while the previous dV / dK MMAs drain;
+    // the rows then wait for `done` and write out the previous dK / dV (the
+    // first dV / dK MMAs, which overwrite the accumulators, wait for P_0 /
+    // dS_0, formed after the write-out).
     bool ok = true, pending = false;
     int g = 0, tn = 0;
     // dK / dV rows leave through a per-warp shared-memory buffer
@@ -416,7 +416,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
         load_row32(src, rp, 0, valid, vr, x0);
         load_row32(src, rp, 32, valid, vr, x1);
       }
-      if (pending && !(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
+      // K / V are read only by the S^T / dP^T MMAs, which this warp saw
+      // complete (s_full, dp_full of its last step): no wait for the previous
+      // tile's `done` before replacing them.
       tc_fence_after();
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
@@ -429,7 +431,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBwdThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       warp_arrive_remote(L(bars->rows_ready));
-      if (pending) write_out();
+      if (pending) {
+        if (!(ok = warp_wait(B(bars->done), (tn - 1) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        write_out();
+      }
       {  // the next tile's K / V row into L2 while this tile runs
         PairTile nt;
         for (int m2 = m + 1; m2 <= m + 2; ++m2) {

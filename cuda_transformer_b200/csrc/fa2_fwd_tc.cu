@@ -603,7 +603,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 1 || warp == kIssuer2Warp) {
     // ------------------------------------- tile t's issuer: S, then P.V
     // Past its last key tile a tile still releases the stages (commits with
-    // nothing new in flight), so the producer's two-issuer count holds.  g
+    // nothing new in flight, after the stage has landed), so the producer's
+    // two-issuer count holds.  g
     // counts the CTA's key steps (stage ring), gt this tile's own steps (S /
     // P buffers, pv_done); per unit tile: wait for the rows' Q (q_ready),
     // commit o_done after the last P.V.
@@ -619,10 +620,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       FwdUnitTile u;
       for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
         const int n_mine = t ? u.n_b : u.n_a, n_kv = u.n_kv;
+        // Past its last key tile a tile still releases each stage, but only
+        // once the stage holds that step's tiles (ready_k / ready_v): an early
+        // release would count toward the stage's previous round, which the
+        // other tile may still be reading.
         auto issue_S = [&](int j) -> bool {  // S_t(j) into buffer (gt + j) % 2
           const int gs = g + j, s = gs % NS;
+          if (!mbar_wait(B(bars->ready_k[s]), (gs / NS) & 1, ctl, p.status)) return false;
           if (j < n_mine) {
-            if (!mbar_wait(B(bars->ready_k[s]), (gs / NS) & 1, ctl, p.status)) return false;
             tc_fence_after();
             mma_chain<1, D, false, BN, C::TILE>(sb0 + (uint32_t)((gt + j) & 1) * BN,
                                                 tmem + C::TC_Q + (uint32_t)t * D, 0,
@@ -639,7 +644,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (j < n_mine) {
             const int gb = gt + j;
             if (!(ok = mbar_wait(B(bars->p_full[t][gb & 1]), (gb >> 1) & 1, ctl, p.status))) break;
-            if (!(ok = mbar_wait(B(bars->ready_v[s]), (gs / NS) & 1, ctl, p.status))) break;
+          }
+          if (!(ok = mbar_wait(B(bars->ready_v[s]), (gs / NS) & 1, ctl, p.status))) break;
+          if (j < n_mine) {
+            const int gb = gt + j;
             tc_fence_after();
             mma_chain<1, BN, true, BN, C::TILE>(tmem + C::TC_O + (uint32_t)t * D,
                                                 sb0 + (uint32_t)(gb & 1) * BN, 0,
@@ -685,12 +693,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // query row quad*32 + lane of its tile (TMEM lane quarter quad) and all
     // BN score columns of a step, kept in registers between the maximum and
     // the exponentials.
-    // Unit-tile boundary: the next Q row is loaded into registers before the
-    // wait for the previous tile's o_done; once that completes (no MMA reads
-    // Q_t any more) it goes into TMEM and q_ready lets the tile's issuer start
-    // S while the rows write out the previous O_t and LSE (the first P.V,
-    // which overwrites the accumulator, waits for P(0), formed after the
-    // write-out).
+    // Unit-tile boundary: the next Q row goes into TMEM as soon as the
+    // previous tile's last S has completed, and q_ready lets the tile's issuer
+    // start S while the previous P.V drains; the rows then wait for o_done and
+    // write out the previous O_t and LSE (the first P.V, which overwrites the
+    // accumulator, waits for P(0), formed after the write-out).
     const int t = warp >= kFwdRowWarp1 ? 1 : 0;
     const int quad = warp & 3;
     const uint32_t lb = tmem_addr(tmem, 32u * quad, 0);
@@ -724,7 +731,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         float xq[D / 32][32];
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) load_row32(p.q, qrow, 32 * c, valid, vec, xq[c]);
-        if (pending && !(ok = warp_wait(B(bars->o_done[t]), (tn - 1) & 1, ctl, p.status))) break;
+        // Q_t is read only by the S MMAs, which this warp saw complete
+        // (s_full of its last step): no wait for o_done before replacing it.
         tc_fence_after();
         const uint32_t qa = lb + C::TC_Q + (uint32_t)t * D;
 #pragma unroll
@@ -737,7 +745,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_before();
         warp_arrive(B(bars->q_ready[t]));
       }
-      if (pending) write_out();
+      if (pending) {
+        if (!(ok = warp_wait(B(bars->o_done[t]), (tn - 1) & 1, ctl, p.status))) break;
+        tc_fence_after();
+        write_out();
+      }
       float m_used = -INFINITY, l = 0.0f;
       for (int j = 0; ok && j < n_mine; ++j) {
         const int gb = gt + j, bb = gb & 1;
