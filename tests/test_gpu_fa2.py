@@ -171,8 +171,9 @@ def test_deterministic(cuda_device, prec, D):
 def test_fused_backward(cuda_device, B, Hh, T, causal):
     """ct_fa2_bwd_fused (TF32, head dim 64): the one-kernel backward, dQ added
     across key tiles in a fixed order with CTAs waiting on one another's
-    counters.  Against the per-kernel path (dK and dV from the same MMA
-    sequence; dQ summed in another order), bit-identical over three calls
+    counters.  Against the per-kernel path (dK and dV from the one-CTA dK/dV
+    kernel's MMA sequence, within 1e-6 of the default CTA-pair kernel; dQ
+    summed in another order), bit-identical over three calls
     (the ordered reduction), and against the FP64 oracle.  The 256-CTA cases
     exceed one wave of 148 SMs, so contributions cross waves; T > 4096 runs
     two query segments (dK, dV added across launches, dQ complete in each)."""
