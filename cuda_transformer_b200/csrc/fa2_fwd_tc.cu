@@ -536,12 +536,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   auto B = [&](const uint64_t& x) { return smem_u32(&x); };
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
+      // one landing, one readiness and one release barrier per stage (K_j, V_j)
       mbar_init(B(bars->full_k[s]), 1);
-      mbar_init(B(bars->full_v[s]), 1);
       mbar_init(B(bars->ready_k[s]), kPrepWarps);
-      mbar_init(B(bars->ready_v[s]), kPrepWarps);
-      mbar_init(B(bars->empty_k[s]), 2);  // both tiles' S MMAs read K_j
-      mbar_init(B(bars->empty_v[s]), 2);  // both tiles' P.V MMAs read V_j
+      mbar_init(B(bars->empty_k[s]), 2);  // both tiles' S and P.V MMAs read the stage
     }
     for (int t = 0; t < 2; ++t) {
       for (int bb = 0; bb < 2; ++bb) {
@@ -570,8 +568,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      int last_k[NS], last_v[NS];
-      for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+      int last_k[NS];
+      for (int s = 0; s < NS; ++s) last_k[s] = -1;
       bool ok = true;
       int g = 0;
       FwdUnitTile u;
@@ -579,35 +577,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int j = 0; j < u.n_kv; ++j) {
           const int gs = g + j, s = gs % NS, r = gs / NS;
           const uint32_t st = tiles + s * C::STAGE;
+          // K_j and V_j share one stage release and one landing barrier
           if (r > 0 && !(ok = mbar_wait(B(bars->empty_k[s]), (r - 1) & 1, ctl, p.status))) break;
-          mbar_arrive_expect_tx(B(bars->full_k[s]), C::TILE);
+          mbar_arrive_expect_tx(B(bars->full_k[s]), 2 * C::TILE);
           tma_load_tile<true, D>(st + C::OFF_K, &tmK, B(bars->full_k[s]), j * BN, u.h, u.b,
                                  BN * 128u);
-          last_k[s] = r;
-          if (r > 0 && !(ok = mbar_wait(B(bars->empty_v[s]), (r - 1) & 1, ctl, p.status))) break;
-          mbar_arrive_expect_tx(B(bars->full_v[s]), C::TILE);
-          tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_v[s]), j * BN, u.h, u.b,
+          tma_load_tile<true, D>(st + C::OFF_V, &tmV, B(bars->full_k[s]), j * BN, u.h, u.b,
                                  BN * 128u);
-          last_v[s] = r;
+          last_k[s] = r;
         }
         g += u.n_kv;
       }
       if (ctl->abort) {  // let every issued copy land before the CTA exits
-        for (int s = 0; s < NS; ++s) {
+        for (int s = 0; s < NS; ++s)
           if (last_k[s] >= 0) mbar_drain(B(bars->full_k[s]), last_k[s] & 1);
-          if (last_v[s] >= 0) mbar_drain(B(bars->full_v[s]), last_v[s] & 1);
-        }
       }
     }
     __syncwarp();
   } else if (warp == 1 || warp == kIssuer2Warp) {
     // ------------------------------------- tile t's issuer: S, then P.V
-    // Past its last key tile a tile still releases the stages (commits with
-    // nothing new in flight, after the stage has landed), so the producer's
-    // two-issuer count holds.  g
-    // counts the CTA's key steps (stage ring), gt this tile's own steps (S /
-    // P buffers, pv_done); per unit tile: wait for the rows' Q (q_ready),
-    // commit o_done after the last P.V.
+    // One readiness wait per step (ready_k covers K_j and V_j; S(j) waits on
+    // it, P.V(j) follows on the same thread) and one stage release (empty_k,
+    // committed after P.V(j), so it also covers S(j)).  Past its last key
+    // tile a tile still releases the stages (commits with nothing new in
+    // flight, after the stage has landed), so the producer's two-issuer count
+    // holds.  g counts the CTA's key steps (stage ring), gt this tile's own
+    // steps (S / P buffers, pv_done); per unit tile: wait for the rows' Q
+    // (q_ready), commit o_done after the last P.V.
     if (lane == 0) {
       const int t = warp == 1 ? 0 : 1;
       constexpr uint32_t idS = idesc_tf32(128, BN, false, false);
@@ -621,9 +617,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int m = 0; ok && fwd_tile_at(p, cta, G, m, u); ++m) {
         const int n_mine = t ? u.n_b : u.n_a, n_kv = u.n_kv;
         // Past its last key tile a tile still releases each stage, but only
-        // once the stage holds that step's tiles (ready_k / ready_v): an early
-        // release would count toward the stage's previous round, which the
-        // other tile may still be reading.
+        // once the stage holds that step's tiles (the wait on ready_k below,
+        // two steps before the release): an early release would count toward
+        // the stage's previous round, which the other tile may still be
+        // reading.
         auto issue_S = [&](int j) -> bool {  // S_t(j) into buffer (gt + j) % 2
           const int gs = g + j, s = gs % NS;
           if (!mbar_wait(B(bars->ready_k[s]), (gs / NS) & 1, ctl, p.status)) return false;
@@ -634,7 +631,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                                                 kd0 + (s * C::STAGE >> 4), idS, false);
             umma_commit(B(bars->s_full[t][(gt + j) & 1]));
           }
-          umma_commit(B(bars->empty_k[s]));
           return true;
         };
         ok = mbar_wait(B(bars->q_ready[t]), tn & 1, ctl, p.status) && issue_S(0) &&
@@ -644,17 +640,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (j < n_mine) {
             const int gb = gt + j;
             if (!(ok = mbar_wait(B(bars->p_full[t][gb & 1]), (gb >> 1) & 1, ctl, p.status))) break;
-          }
-          if (!(ok = mbar_wait(B(bars->ready_v[s]), (gs / NS) & 1, ctl, p.status))) break;
-          if (j < n_mine) {
-            const int gb = gt + j;
             tc_fence_after();
             mma_chain<1, BN, true, BN, C::TILE>(tmem + C::TC_O + (uint32_t)t * D,
                                                 sb0 + (uint32_t)(gb & 1) * BN, 0,
                                                 vd0 + (s * C::STAGE >> 4), idO, j > 0);
             umma_commit(B(bars->pv_done[t]));
           }
-          umma_commit(B(bars->empty_v[s]));
+          umma_commit(B(bars->empty_k[s]));  // K_j and V_j read for the last time
           if (j + 2 < n_kv && !(ok = issue_S(j + 2))) break;
         }
         if (ok) umma_commit(B(bars->o_done[t]));
@@ -678,12 +670,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t st = tiles + s * C::STAGE;
         if (!(ok = warp_wait(B(bars->full_k[s]), r & 1, ctl, p.status))) break;
         round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_K, tid);
-        fence_proxy_async_smem();
-        warp_arrive(B(bars->ready_k[s]));
-        if (!(ok = warp_wait(B(bars->full_v[s]), r & 1, ctl, p.status))) break;
         round_tile_smem<C::TILE, kSplitThreads>(st + C::OFF_V, tid);
         fence_proxy_async_smem();
-        warp_arrive(B(bars->ready_v[s]));
+        warp_arrive(B(bars->ready_k[s]));  // K_j and V_j
       }
       g += u.n_kv;
     }
